@@ -1,0 +1,172 @@
+/*
+ * visionattn.h — C ABI of the B200-native (sm_100a) attention hot path of
+ * spinorml/vision-rs.
+ *
+ * Drop-in boundary.  In the reference every hot-path node is a teenygrad
+ * `RuntimeOp` whose `pack_args` pushes kernel arguments through an
+ * `ArgVisitor` and whose `grid()` derives the launch size from the output
+ * shape (src/models/yolo/kernels/attention/psa.rs).  Each entry point below
+ * takes exactly the pointer/int/float arguments that `pack_args` pushes, in
+ * the same order, followed by the sizes that the reference's `grid()` reads
+ * from the output shape (batch, head count, head dim), followed by the
+ * stream.  A Rust `RuntimeOp` shim therefore replaces
+ * `visitor.visit_*(…); launch(grid, block)` by a single call here.
+ *
+ * Conventions (all entry points):
+ *   - device pointers only; the library never allocates, frees or
+ *     synchronises inside these calls, and every launch goes on `stream`;
+ *   - return 0 (VA_OK) or a VA_ERR_* code; `va_get_last_error_string()`
+ *     describes the last failure on the calling thread;
+ *   - bf16 tensors are passed as raw 16-bit words (`va_bf16`);
+ *   - "accumulates" means `+=` into caller-zeroed memory, as the reference's
+ *     backward kernels do with `atomic_add` (psa.rs:232, :279-280, :700, :723).
+ */
+#ifndef VISIONATTN_H
+#define VISIONATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define VA_API __attribute__((visibility("default")))
+#else
+#define VA_API
+#endif
+
+typedef uint16_t va_bf16;
+typedef struct CUstream_st *va_stream_t;
+
+enum {
+  VA_OK = 0,
+  VA_ERR_SHAPE = 1,       /* unsupported or inconsistent sizes */
+  VA_ERR_LAUNCH = 2,      /* CUDA launch / runtime error */
+  VA_ERR_TIMEOUT = 3,     /* a bounded device-side wait gave up */
+  VA_ERR_ALIGN = 4,       /* pointer alignment the kernel needs is not met */
+  VA_ERR_UNSUPPORTED = 5, /* device or configuration not supported */
+  VA_ERR_WORKSPACE = 6,   /* workspace missing or too small */
+  VA_ERR_NCCL = 7         /* collective failed or timed out */
+};
+
+/* Library identity and diagnostics. */
+VA_API int va_version(void);
+VA_API const char *va_get_last_error_string(void);
+/* Number of kernels this library has launched in this process (all threads). */
+VA_API uint64_t va_launch_count(void);
+
+/* ── Shape inference (CustomOp::infer_output_shape). -1 = dynamic dim. ─────
+ * Return the output rank, or -1 on a bad input rank. */
+/* psa.rs:766-776 — [B,qkv_h,H,W] → [B,4,nh,N,kd] */
+VA_API int va_psa_pack_qkv_infer_output_shape(const int64_t *in, int rank, int num_heads, int64_t *out);
+/* psa.rs:809-812 — [B,qkv_h,H,W] → [B,qkv_h/2,H,W] */
+VA_API int va_psa_extract_v_infer_output_shape(const int64_t *in, int rank, int64_t *out);
+/* psa.rs:853-863 — [B,nh,N,kd] → [B,nh*2*kd,H,W] (H, W fixed at construction) */
+VA_API int va_psa_merge_attn_infer_output_shape(const int64_t *in, int rank, int num_heads, int64_t H,
+                                         int64_t W, int64_t *out);
+/* psa.rs:901-905 — [B,4,nh,N,kd] → [B,nh,N,kd] */
+VA_API int va_flash_attention2_infer_output_shape(const int64_t *in, int rank, int64_t *out);
+
+/* ── PSA layout kernels ───────────────────────────────────────────────────── */
+/* psa_pack_qkv (psa.rs:58-94; args psa.rs:371-377):
+ * NCHW [B,qkv_h,H,W] → flat [4, B*nh, H*W, kd], kd = qkv_h/(4*nh). */
+VA_API int va_psa_pack_qkv_f32(const float *qkv, float *out, int qkv_h, int H, int W, int B,
+                        int num_heads, va_stream_t stream);
+VA_API int va_psa_pack_qkv_bf16(const va_bf16 *qkv, va_bf16 *out, int qkv_h, int H, int W, int B,
+                         int num_heads, va_stream_t stream);
+/* psa_pack_qkv_backward (psa.rs:201-233; args :411-417): accumulates into d_qkv. */
+VA_API int va_psa_pack_qkv_backward_f32(const float *d_packed, float *d_qkv, int qkv_h, int H, int W,
+                                 int B, int num_heads, va_stream_t stream);
+/* psa_extract_v_nchw (psa.rs:105-142; args :472-478; B from grid() :483-488):
+ * V channels of each head → NCHW [B,c,H,W], c = nh*2*kd. */
+VA_API int va_psa_extract_v_nchw_f32(const float *qkv, float *v, int qkv_h, int c, int H, int W,
+                              int num_heads, int B, va_stream_t stream);
+VA_API int va_psa_extract_v_nchw_bf16(const va_bf16 *qkv, va_bf16 *v, int qkv_h, int c, int H, int W,
+                               int num_heads, int B, va_stream_t stream);
+/* psa_extract_v_backward (psa.rs:244-281; args :512-518): accumulates into d_qkv. */
+VA_API int va_psa_extract_v_backward_f32(const float *d_v, float *d_qkv, int qkv_h, int c, int H,
+                                  int W, int num_heads, int B, va_stream_t stream);
+/* psa_merge_attn_nchw (psa.rs:153-189; args :575-581; B from grid() :586-591):
+ * two [B*nh, N, kd] halves → NCHW [B,c,H,W]. */
+VA_API int va_psa_merge_attn_nchw_f32(const float *lo, const float *hi, float *out, int c, int H, int W,
+                               int num_heads, int B, va_stream_t stream);
+VA_API int va_psa_merge_attn_nchw_bf16(const va_bf16 *lo, const va_bf16 *hi, va_bf16 *out, int c,
+                                int H, int W, int num_heads, int B, va_stream_t stream);
+/* psa_merge_attn_backward (psa.rs:292-327; args :614-620): stores d_lo, d_hi. */
+VA_API int va_psa_merge_attn_backward_f32(const float *d_merged, float *d_lo, float *d_hi, int c, int H,
+                                   int W, int num_heads, int B, va_stream_t stream);
+
+/* ── Flash attention on [BH, N, head_dim] row-major ───────────────────────── */
+/* flash_attention2_forward (flash_attn2.rs:54-121; args psa.rs:988-996;
+ * grid (n_ctx_q, BH) psa.rs:999-1004).  l = m + ln(sum exp) per query row.
+ * q/k/v may be offsets into the packed buffer exactly as psa.rs:982-985
+ * computes them.  head_dim ∈ {16, 32, 64}.  The bf16 variant reads bf16
+ * q/k/v, writes bf16 o and an f32 l. */
+VA_API int va_flash_attention2_forward_f32(const float *q, const float *k, const float *v, float *o,
+                                    float *l, int n_ctx_q, int n_ctx_k, float softmax_scale,
+                                    float neg_inf, int bh, int head_dim, va_stream_t stream);
+VA_API int va_flash_attention2_forward_bf16(const va_bf16 *q, const va_bf16 *k, const va_bf16 *v,
+                                     va_bf16 *o, float *l, int n_ctx_q, int n_ctx_k,
+                                     float softmax_scale, float neg_inf, int bh, int head_dim,
+                                     va_stream_t stream);
+/* flash_attention2_backward_dq (flash_attn2.rs:129-187): stores dq. */
+VA_API int va_flash_attention2_backward_dq_f32(const float *q, const float *k, const float *v,
+                                        const float *o, const float *d_o, const float *l,
+                                        float *dq, int n_ctx_q, int n_ctx_k, float softmax_scale,
+                                        int bh, int head_dim, va_stream_t stream);
+/* flash_attention2_backward_dkv (flash_attn2.rs:195-260): stores dk, dv. */
+VA_API int va_flash_attention2_backward_dkv_f32(const float *q, const float *k, const float *v,
+                                         const float *o, const float *d_o, const float *l,
+                                         float *dk, float *dv, int n_ctx_q, int n_ctx_k,
+                                         float softmax_scale, int bh, int head_dim,
+                                         va_stream_t stream);
+/* psa_fa2_backward (psa.rs:650-725; args psa.rs:1044-1054): dq and dk
+ * accumulate (the lo and hi calls share them), dv is stored.  Deterministic:
+ * no atomics — each output row is owned by one thread. */
+VA_API int va_psa_fa2_backward_f32(const float *q, const float *k, const float *v, const float *o,
+                            const float *d_o, const float *l, float *dq, float *dk, float *dv,
+                            int N, float softmax_scale, int bh, int head_dim, va_stream_t stream);
+
+/* ── Convolution pieces of the PSA block (conv_bn, conv.rs:53-69) ─────────── */
+/* Eval-mode BN folded into the conv (host function, no GPU):
+ * w_out = w*g/sqrt(var+eps); b_out = beta - mean*g/sqrt(var+eps). */
+VA_API int va_fold_bn_f32(const float *w, const float *gamma, const float *beta, const float *mean,
+                   const float *var, float eps, int c_out, int k_per_out, float *w_out,
+                   float *b_out);
+/* 1×1 conv + bias, NCHW: y[b,o,n] = sum_i w[o,i] x[b,i,n] + bias[o]. */
+VA_API int va_conv1x1_bias_f32(const float *x, const float *w, const float *bias, float *y, int B,
+                        int c_in, int c_out, int HW, va_stream_t stream);
+/* depthwise 3×3, stride 1, pad 1, + bias (the PE conv, c2psa.rs:66). */
+VA_API int va_dwconv3x3_bias_f32(const float *x, const float *w, const float *bias, float *y, int B,
+                          int C, int H, int W, va_stream_t stream);
+/* its backward: stores dx; stores dw [C,1,3,3] (deterministic reduction). */
+VA_API int va_dwconv3x3_backward_f32(const float *x, const float *w, const float *dy, float *dx,
+                              float *dw, int B, int C, int H, int W, va_stream_t stream);
+
+/* ── Fused PSA Attention forward (c2psa.rs:61-116, BN folded) ─────────────── *
+ * y = proj(merge(FA(pack(qkv(x)))) + pe(extract_v(qkv(x)))), x/y NCHW [B,C,H,W].
+ * Weights: w_qkv [nh*4*kd, C], w_pe [C,1,3,3], w_proj [C, C]; biases f32.
+ * f32 variant: f32 everything (SIMT FFMA path, max-abs 1e-5 class).
+ * bf16 variant: x, y and weights bf16, biases f32, f32 accumulation
+ * (tcgen05/TMEM tensor-core path).  Supported: C = nh*2*kd, kd = 32.
+ * `workspace` holds the qkv/attention intermediates; size from
+ * va_psa_attention_workspace_bytes().  dtype: 0 = f32, 1 = bf16. */
+VA_API size_t va_psa_attention_workspace_bytes(int B, int C, int H, int W, int num_heads, int key_dim,
+                                        int dtype);
+VA_API int va_psa_attention_fwd_f32(const float *x, const float *w_qkv, const float *b_qkv,
+                             const float *w_pe, const float *b_pe, const float *w_proj,
+                             const float *b_proj, float *y, int B, int C, int H, int W,
+                             int num_heads, int key_dim, void *workspace, size_t ws_bytes,
+                             va_stream_t stream);
+VA_API int va_psa_attention_fwd_bf16(const va_bf16 *x, const va_bf16 *w_qkv, const float *b_qkv,
+                              const va_bf16 *w_pe, const float *b_pe, const va_bf16 *w_proj,
+                              const float *b_proj, va_bf16 *y, int B, int C, int H, int W,
+                              int num_heads, int key_dim, void *workspace, size_t ws_bytes,
+                              va_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VISIONATTN_H */

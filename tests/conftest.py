@@ -1,0 +1,55 @@
+"""Shared fixtures for the visionattn test-suite.
+
+Markers: ``gpu`` — needs a CUDA device (a B200).  Everything else runs on CPU.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
+
+
+def load_golden(name):
+    return dict(np.load(os.path.join(GOLDEN, name)))
+
+
+STAGES = ["cv1", "cv2", "m0_attn_qkv", "m0_attn_proj", "m0_attn_pe", "m0_ffn0", "m0_ffn1"]
+
+
+def stage_params(g):
+    return {s: tuple(g[f"{s}_{p}"] for p in ("conv_w", "bn_w", "bn_b", "bn_rm", "bn_rv")) for s in STAGES}
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def max_abs(a, b):
+    return float(np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64)).max())
+
+
+# Tolerances stated by the north star: f32 mode max-abs 1e-5; bf16 mode
+# rel-L2 2e-3 and max-abs 1e-2 against the f32 reference.
+F32_MAX_ABS = 1e-5
+BF16_REL_L2 = 2e-3
+BF16_MAX_ABS = 1e-2
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")

@@ -1,0 +1,105 @@
+"""The C-ABI library on CPU: it loads, exports every symbol the header
+declares, and its host-only functions (shape inference, BN folding, argument
+validation that fails before any launch) behave like the reference's
+CustomOp methods.  No compute calls: there is no GPU here."""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+from oracle import psa_oracle as po
+from vision_rs_b200 import _lib
+from vision_rs_b200 import psa as vp
+
+HEADER = os.path.join(ROOT, "include", "visionattn.h")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(va_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared_symbols()
+    assert len(names) >= 20
+    for n in names:
+        assert hasattr(lib, n), n
+    # the binding table covers exactly the header
+    assert sorted(_lib.SIGNATURES) == names
+
+
+def _shape(fn, inp, *extra, out_len=5):
+    a = (C.c_int64 * len(inp))(*inp)
+    o = (C.c_int64 * out_len)()
+    r = fn(a, len(inp), *extra, o) if extra else fn(a, len(inp), o)
+    return r, list(o)[:max(r, 0)]
+
+
+def test_shape_inference_matches_reference_customops():
+    lib = _lib.lib()
+    # psa.rs:766-776 (test_c2psa_yolo26.rs:128: [2,4,2,256,32] at B=2, 16x16)
+    r, s = _shape(lib.va_psa_pack_qkv_infer_output_shape, [2, 256, 16, 16], 2)
+    assert (r, s) == (5, [2, 4, 2, 256, 32])
+    r, s = _shape(lib.va_psa_pack_qkv_infer_output_shape, [-1, 256, 16, 16], 2)
+    assert s[0] == -1
+    r, s = _shape(lib.va_psa_extract_v_infer_output_shape, [2, 256, 16, 16])
+    assert s == [2, 128, 16, 16]
+    a = (C.c_int64 * 4)(2, 2, 256, 32)
+    o = (C.c_int64 * 4)()
+    assert lib.va_psa_merge_attn_infer_output_shape(a, 4, 2, 16, 16, o) == 4
+    assert list(o) == [2, 128, 16, 16]   # test_c2psa_yolo26.rs:132
+    r, s = _shape(lib.va_flash_attention2_infer_output_shape, [2, 4, 2, 256, 32])
+    assert s == [2, 2, 256, 32]
+    # bad rank
+    r, _ = _shape(lib.va_psa_extract_v_infer_output_shape, [2, 256, 16])
+    assert r == -1
+
+
+def test_python_customop_mirror_shapes():
+    assert vp.PsaPackQkvOp(32, 2).infer_output_shape([[None, 256, 20, 20]]) == [None, 4, 2, 400, 32]
+    assert vp.PsaExtractVOp(32, 2).infer_output_shape([[2, 256, 20, 20]]) == [2, 128, 20, 20]
+    assert vp.PsaMergeAttnOp(32, 2, 20, 20).infer_output_shape([[2, 2, 400, 32]]) == [2, 128, 20, 20]
+    assert vp.FlashAttn2PsaOp.new_lo(32).infer_output_shape([[2, 4, 2, 400, 32]]) == [2, 2, 400, 32]
+    assert vp.FlashAttn2PsaOp.new_hi(32).inner.v_section == 3
+    names = [vp.PsaPackQkvOp(32, 2).name(), vp.FlashAttn2PsaOp.new_lo(32).name(),
+             vp.PsaMergeAttnOp(32, 2, 4, 4).name(), vp.PsaExtractVOp(32, 2).name()]
+    assert names == ["psa_pack_qkv", "flash_attention2_forward", "psa_merge_attn_nchw", "psa_extract_v_nchw"]
+    assert vp.FlashAttn2PsaOp.new_lo(32).inner.param_shapes([[2, 4, 2, 400, 32]], None) == [[1600]]
+
+
+def test_fold_bn_host_function_matches_oracle():
+    rng = np.random.default_rng(3)
+    w = rng.standard_normal((256, 128, 1, 1)).astype(np.float32)
+    g, b, m = (rng.standard_normal(256).astype(np.float32) for _ in range(3))
+    v = rng.uniform(0.5, 2, 256).astype(np.float32)
+    import torch
+    wf, bf = vp.fold_bn(torch.tensor(w), g, b, m, v, 1e-3)
+    wo, bo = po.fold_bn(w, g, b, m, v, 1e-3)
+    assert np.abs(wf.numpy() - wo).max() < 1e-5
+    assert np.abs(bf.numpy() - bo).max() < 1e-5
+
+
+def test_argument_validation_fails_before_launch():
+    lib = _lib.lib()
+    # qkv_h not a multiple of 4*num_heads → VA_ERR_SHAPE, message set, nothing launched
+    rc = lib.va_psa_pack_qkv_f32(None, None, 250, 4, 4, 2, 2, None)
+    assert rc == 1
+    assert b"multiple" in lib.va_get_last_error_string()
+    rc = lib.va_flash_attention2_forward_f32(None, None, None, None, None, 16, 16, 0.1, float("-inf"), 4, 48, None)
+    assert rc == 1 and b"head_dim" in lib.va_get_last_error_string()
+    rc = lib.va_psa_attention_fwd_bf16(*([None] * 8), 2, 128, 4, 4, 2, 32, None, 0, None)
+    assert rc == 6  # workspace missing
+    with pytest.raises(_lib.VisionAttnError):
+        _lib.call("va_psa_merge_attn_nchw_f32", None, None, None, 127, 4, 4, 2, 2, None)
+
+
+def test_workspace_query():
+    lib = _lib.lib()
+    n32 = lib.va_psa_attention_workspace_bytes(2, 128, 20, 20, 2, 32, 0)
+    n16 = lib.va_psa_attention_workspace_bytes(2, 128, 20, 20, 2, 32, 1)
+    assert n32 > 0 and n16 > 0 and n16 < n32
+    assert lib.va_psa_attention_workspace_bytes(0, 128, 20, 20, 2, 32, 0) == 0

@@ -1,0 +1,235 @@
+"""PSA attention path on the GPU, through the C ABI, against the CPU oracle
+and the reference's golden fixtures.
+
+Tolerances: layout ops are permutations → bit-exact; f32 kernels max-abs
+1e-5 (the north star's f32 bound); bf16 paths rel-L2 ≤ 2e-3 and max-abs ≤
+1e-2 against the f32 oracle evaluated on the same bf16-rounded inputs."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import BF16_MAX_ABS, BF16_REL_L2, F32_MAX_ABS, load_golden, max_abs, rel_l2
+from oracle import psa_oracle as po
+from vision_rs_b200 import psa as vp
+
+pytestmark = pytest.mark.gpu
+SCALE = 1.0 / math.sqrt(32.0)
+
+
+def dev(a, dtype=torch.float32):
+    return torch.as_tensor(np.asarray(a)).to("cuda", dtype).contiguous()
+
+
+def host(t):
+    return t.float().cpu().numpy()
+
+
+def bf16_round(a):
+    return torch.as_tensor(np.asarray(a, np.float32)).bfloat16().float().numpy()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,H,W", [(2, 4, 4), (1, 20, 20), (3, 7, 9), (2, 40, 40)])
+def test_layout_ops_exact(cuda, dtype, B, H, W):
+    nh, kd = 2, 32
+    rng = np.random.default_rng(B * 100 + H)
+    qkv = bf16_round(rng.standard_normal((B, nh * 4 * kd, H, W)).astype(np.float32))
+    x = dev(qkv, dtype)
+    pk = vp.PsaPackQkvOp(kd, nh)
+    shp = pk.infer_output_shape([list(x.shape)])
+    packed = torch.empty(4, B * nh, H * W, kd, device="cuda", dtype=dtype)
+    pk.inner.launch([(x, shp)], [], packed)
+    ref = po.pack_qkv(qkv, nh)
+    assert np.array_equal(host(packed), ref)
+    v = torch.empty(B, nh * 2 * kd, H, W, device="cuda", dtype=dtype)
+    vp.PsaExtractVOp(kd, nh).inner.launch([x], [], v)
+    assert np.array_equal(host(v), po.extract_v_nchw(qkv, nh))
+    merged = torch.empty_like(v)
+    vp.PsaMergeAttnOp(kd, nh, H, W).inner.launch([packed[2], packed[3]], [], merged)
+    assert np.array_equal(host(merged), po.merge_attn_nchw(ref[2], ref[3], nh, H, W))
+
+
+@pytest.mark.parametrize("B,H,W", [(2, 4, 4), (2, 9, 7)])
+def test_layout_backwards_exact(cuda, B, H, W):
+    nh, kd = 2, 32
+    qkv_h, c = nh * 4 * kd, nh * 2 * kd
+    rng = np.random.default_rng(7)
+    d_packed = rng.standard_normal((4, B * nh, H * W, kd)).astype(np.float32)
+    d0 = rng.standard_normal((B, qkv_h, H, W)).astype(np.float32)
+    d_qkv = dev(d0)
+    x = torch.zeros(B, qkv_h, H, W, device="cuda")
+    vp.PsaPackQkvOp(kd, nh).inner.launch_backward([x], [], None, dev(d_packed), [d_qkv])
+    ref = po.pack_qkv_backward(d_packed, B, qkv_h, H, W, nh, d_qkv=d0)
+    assert np.array_equal(host(d_qkv), ref)
+    d_v = rng.standard_normal((B, c, H, W)).astype(np.float32)
+    vp.PsaExtractVOp(kd, nh).inner.launch_backward([x], [], None, dev(d_v), [d_qkv])
+    ref = po.extract_v_backward(d_v, qkv_h, nh, d_qkv=ref)
+    assert np.array_equal(host(d_qkv), ref)
+    dm = rng.standard_normal((B, c, H, W)).astype(np.float32)
+    dlo = torch.empty(B * nh, H * W, kd, device="cuda")
+    dhi = torch.empty_like(dlo)
+    out = torch.empty(B, c, H, W, device="cuda")
+    vp.PsaMergeAttnOp(kd, nh, H, W).inner.launch_backward([dlo, dhi], [], out, dev(dm), [dlo, dhi])
+    rlo, rhi = po.merge_attn_backward(dm, nh)
+    assert np.array_equal(host(dlo), rlo) and np.array_equal(host(dhi), rhi)
+
+
+def test_fa_forward_golden_fixture(cuda):
+    """Direct FA known-answer test: the reference's backward fixture dumps
+    Q, K, V_lo, V_hi, O_lo, O_hi, LSE in [4,16,32] (generate_backward.py:202-208)."""
+    g = load_golden("c2psa_bwd.npz")
+    for half in ("lo", "hi"):
+        o, l = vp.flash_attention2_forward(dev(g["attn_q"]), dev(g["attn_k"]), dev(g[f"attn_v_{half}"]), SCALE)
+        assert max_abs(host(o), g[f"attn_o_{half}"]) < F32_MAX_ABS
+        assert max_abs(host(l), g["attn_l"]) < F32_MAX_ABS
+
+
+@pytest.mark.parametrize("bh,nq,nk,d", [(2, 400, 400, 32), (4, 37, 129, 32), (1, 1601, 1601, 64),
+                                        (3, 100, 100, 64), (2, 1, 5, 16)])
+def test_fa_forward_f32_vs_oracle(cuda, bh, nq, nk, d):
+    rng = np.random.default_rng(nq + nk)
+    q, k, v = (rng.standard_normal((bh, n, d)).astype(np.float32) for n in (nq, nk, nk))
+    o, l = vp.flash_attention2_forward(dev(q), dev(k), dev(v), 1 / math.sqrt(d))
+    ro, rl = po.flash_attention2_forward(q, k, v, 1 / math.sqrt(d))
+    assert max_abs(host(o), ro) < F32_MAX_ABS
+    assert max_abs(host(l), rl) < 1e-4  # LSE magnitude ~log(N)+|s|
+
+
+def test_fa_forward_bf16_vs_oracle(cuda):
+    rng = np.random.default_rng(5)
+    q, k, v = (bf16_round(rng.standard_normal((4, 400, 32))) for _ in range(3))
+    o, l = vp.flash_attention2_forward(dev(q, torch.bfloat16), dev(k, torch.bfloat16), dev(v, torch.bfloat16), SCALE)
+    ro, rl = po.flash_attention2_forward(q, k, v, SCALE)
+    assert rel_l2(host(o), ro) < BF16_REL_L2 and max_abs(host(o), ro) < BF16_MAX_ABS
+
+
+@pytest.mark.parametrize("bh,n,d", [(4, 16, 32), (2, 400, 32), (3, 77, 16), (2, 130, 64)])
+def test_psa_fa2_backward_f32(cuda, bh, n, d):
+    """psa_fa2_backward (psa.rs:650-725): dq/dk accumulate, dv stored."""
+    rng = np.random.default_rng(n)
+    q, k, v, do = (rng.standard_normal((bh, n, d)).astype(np.float32) for _ in range(4))
+    o, l = po.flash_attention2_forward(q, k, v, 1 / math.sqrt(d))
+    dq0, dk0 = (rng.standard_normal((bh, n, d)).astype(np.float32) for _ in range(2))
+    dq, dk, dv = dev(dq0), dev(dk0), torch.empty(bh, n, d, device="cuda")
+    from vision_rs_b200 import _lib
+    sp = lambda t: t.data_ptr()
+    st = torch.cuda.current_stream().cuda_stream
+    args = [dev(a) for a in (q, k, v, o, do, l)]
+    _lib.call("va_psa_fa2_backward_f32", *map(sp, args), sp(dq), sp(dk), sp(dv), n, 1 / math.sqrt(d), bh, d, st)
+    rq, rk, rv = po.psa_fa2_backward(q, k, v, o, do, l, 1 / math.sqrt(d), dq_acc=dq0, dk_acc=dk0)
+    assert max_abs(host(dq), rq) < 1e-4 and max_abs(host(dk), rk) < 1e-4 and max_abs(host(dv), rv) < 1e-4
+    # split kernels (flash_attn2.rs:129-260) store instead of accumulating
+    dq2, dk2, dv2 = (torch.empty(bh, n, d, device="cuda") for _ in range(3))
+    _lib.call("va_flash_attention2_backward_dq_f32", *map(sp, args), sp(dq2), n, n, 1 / math.sqrt(d), bh, d, st)
+    _lib.call("va_flash_attention2_backward_dkv_f32", *map(sp, args), sp(dk2), sp(dv2), n, n, 1 / math.sqrt(d),
+              bh, d, st)
+    assert max_abs(host(dq2), rq - dq0) < 1e-4 and max_abs(host(dk2), rk - dk0) < 1e-4
+    assert max_abs(host(dv2), rv) < 1e-4
+
+
+def test_dwconv_golden_fixture(cuda):
+    g = load_golden("dwconv_depthwise.npz")
+    from vision_rs_b200 import _lib
+    st = torch.cuda.current_stream().cuda_stream
+    x, w, dy = dev(g["x"]), dev(g["conv_w"]), dev(g["dy"])
+    y = torch.empty_like(x)
+    _lib.call("va_dwconv3x3_bias_f32", x.data_ptr(), w.data_ptr(), None, y.data_ptr(), 2, 128, 4, 4, st)
+    assert max_abs(host(y), g["expected_output"]) < 1e-5
+    dx, dw = torch.empty_like(x), torch.empty_like(w)
+    _lib.call("va_dwconv3x3_backward_f32", x.data_ptr(), w.data_ptr(), dy.data_ptr(), dx.data_ptr(), dw.data_ptr(),
+              2, 128, 4, 4, st)
+    assert max_abs(host(dx), g["dx_expected"]) < 1e-4
+    assert max_abs(host(dw), g["dw_expected"]) < 1e-4
+
+
+def _op(p, dtype):
+    return vp.PsaAttention(p["w_qkv"], p["b_qkv"], p["w_pe"], p["b_pe"], p["w_proj"], p["b_proj"], num_heads=2,
+                           key_dim=32, dtype=dtype)
+
+
+def _oracle(p):
+    return po.psa_attention(p["x"], p["w_qkv"], p["b_qkv"], p["w_pe"], p["b_pe"], p["w_proj"], p["b_proj"], 2, 32)
+
+
+def test_fused_f32_golden_case(cuda):
+    g = load_golden("psa_attn_case.npz")
+    y = _op(g, torch.float32)(dev(g["x"]))
+    assert max_abs(host(y), g["y"]) < F32_MAX_ABS
+
+
+@pytest.mark.parametrize("B,H,W", [(1, 20, 20), (2, 7, 9), (1, 40, 40)])
+def test_fused_f32_vs_oracle(cuda, B, H, W):
+    """cfg1 shape (1×128×20×20) and ragged shapes, f32 max-abs 1e-5."""
+    p = po.psa_synthetic(B, H, W, seed=B + H)
+    y = _op(p, torch.float32)(dev(p["x"]))
+    assert max_abs(host(y), _oracle(p)) < F32_MAX_ABS
+
+
+def _bf16_inputs(p):
+    q = dict(p)
+    for k in ("x", "w_qkv", "w_pe", "w_proj"):
+        q[k] = bf16_round(p[k])
+    return q
+
+
+@pytest.mark.parametrize("B,H,W", [(2, 4, 4), (2, 40, 40), (3, 20, 20), (1, 13, 11), (1, 3, 50)])
+def test_fused_bf16_vs_oracle(cuda, B, H, W):
+    p = _bf16_inputs(po.psa_synthetic(B, H, W, seed=7 + B * H))
+    y = _op(p, torch.bfloat16)(dev(p["x"], torch.bfloat16))
+    ref = _oracle(p)
+    assert rel_l2(host(y), ref) < BF16_REL_L2
+    assert max_abs(host(y), ref) < BF16_MAX_ABS
+
+
+def test_fused_bf16_full_cfg2_batch(cuda):
+    """cfg2 at full size (64×128×40×40): images 0, 31 and 63 against the oracle,
+    and a batch-consistency property (an image's output does not depend on its
+    batch neighbours)."""
+    p = _bf16_inputs(po.psa_synthetic(64, 40, 40, seed=2))
+    op = _op(p, torch.bfloat16)
+    x = dev(p["x"], torch.bfloat16)
+    y = host(op(x))
+    for i in (0, 31, 63):
+        q = dict(p)
+        q["x"] = p["x"][i:i + 1]
+        ref = _oracle(q)
+        assert rel_l2(y[i:i + 1], ref) < BF16_REL_L2 and max_abs(y[i:i + 1], ref) < BF16_MAX_ABS
+    y_single = host(op(x[5:6].contiguous()))
+    assert np.array_equal(y_single, y[5:6])
+
+
+def test_reference_node_sequence_matches_fused(cuda):
+    """The reference graph's node sequence (c2psa.rs:74-114) run through the
+    RuntimeOp mirror equals the fused entry point (f32)."""
+    g = load_golden("psa_attn_case.npz")
+    B, C, H, W = g["x"].shape
+    nh, kd = 2, 32
+    from vision_rs_b200 import _lib
+    st = torch.cuda.current_stream().cuda_stream
+    x = dev(g["x"])
+    qkv = torch.empty(B, 256, H, W, device="cuda")
+    _lib.call("va_conv1x1_bias_f32", x.data_ptr(), dev(g["w_qkv"]).data_ptr(), dev(g["b_qkv"]).data_ptr(),
+              qkv.data_ptr(), B, C, 256, H * W, st)
+    pk = vp.PsaPackQkvOp(kd, nh)
+    shp = pk.infer_output_shape([list(qkv.shape)])
+    packed = torch.empty(4, B * nh, H * W, kd, device="cuda")
+    pk.inner.launch([(qkv, shp)], [], packed)
+    lse = torch.empty(*vp.FlashAttn2PsaOp.new_lo(kd).inner.param_shapes([shp], None)[0], device="cuda")
+    lo = torch.empty(B * nh, H * W, kd, device="cuda")
+    hi = torch.empty_like(lo)
+    vp.FlashAttn2PsaOp.new_lo(kd).inner.launch([(packed, shp)], [lse], lo)
+    vp.FlashAttn2PsaOp.new_hi(kd).inner.launch([(packed, shp)], [lse], hi)
+    merged = torch.empty(B, C, H, W, device="cuda")
+    vp.PsaMergeAttnOp(kd, nh, H, W).inner.launch([lo, hi], [], merged)
+    v = torch.empty(B, C, H, W, device="cuda")
+    vp.PsaExtractVOp(kd, nh).inner.launch([qkv], [], v)
+    pe = torch.empty_like(v)
+    _lib.call("va_dwconv3x3_bias_f32", v.data_ptr(), dev(g["w_pe"]).data_ptr(), dev(g["b_pe"]).data_ptr(),
+              pe.data_ptr(), B, C, H, W, st)
+    y = torch.empty_like(v)
+    s = (merged + pe).contiguous()
+    _lib.call("va_conv1x1_bias_f32", s.data_ptr(), dev(g["w_proj"]).data_ptr(), dev(g["b_proj"]).data_ptr(),
+              y.data_ptr(), B, C, C, H * W, st)
+    assert max_abs(host(y), g["y"]) < F32_MAX_ABS

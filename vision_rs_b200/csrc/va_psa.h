@@ -1,0 +1,34 @@
+// Internal declarations shared between the visionattn translation units.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace va {
+
+size_t psa_workspace_bytes(int B, int C, int H, int W, int nh, int kd, int dtype);
+
+int psa_attention_fwd_f32(const float* x, const float* w_qkv, const float* b_qkv, const float* w_pe,
+                          const float* b_pe, const float* w_proj, const float* b_proj, float* y, int B, int C,
+                          int H, int W, int nh, int kd, void* ws, size_t ws_bytes, cudaStream_t st);
+
+int psa_attention_fwd_bf16(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,
+                           const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
+                           const float* b_proj, __nv_bfloat16* y, int B, int C, int H, int W, int nh, int kd,
+                           void* ws, size_t ws_bytes, cudaStream_t st);
+
+int fa_fwd_f32(const float* q, const float* k, const float* v, float* o, float* l, int nq, int nk, float scale,
+               int bh, int hd, cudaStream_t st);
+int fa_fwd_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, __nv_bfloat16* o,
+                float* l, int nq, int nk, float scale, int bh, int hd, cudaStream_t st);
+
+template <typename T, typename TW>
+int conv1x1(const T* x, const T* x2, const TW* w, const float* bias, T* y, int B, int cin, int cout, int HW,
+            cudaStream_t st);
+template <typename T, typename TW>
+int dwconv3x3(const T* x, const TW* w, const float* bias, T* y, int B, int C, int H, int W, cudaStream_t st);
+
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace va
