@@ -149,8 +149,11 @@ VA_API int va_dwconv3x3_backward_f32(const float *x, const float *w, const float
  * y = proj(merge(FA(pack(qkv(x)))) + pe(extract_v(qkv(x)))), x/y NCHW [B,C,H,W].
  * Weights: w_qkv [nh*4*kd, C], w_pe [C,1,3,3], w_proj [C, C]; biases f32.
  * f32 variant: f32 everything (SIMT FFMA path, max-abs 1e-5 class).
- * bf16 variant: x, y and weights bf16, biases f32, f32 accumulation
- * (tcgen05/TMEM tensor-core path).  Supported: C = nh*2*kd, kd = 32.
+ * bf16 variant: x, y and weights bf16, biases f32 (tcgen05/TMEM tensor-core
+ * path: bf16 qkv GEMM, f16 attention operands, f32 accumulation); it
+ * supports the YOLO26 PSA shape C = 128, nh = 2, kd = 32 and any H, W
+ * (returns VA_ERR_SHAPE otherwise); x, w_qkv, w_proj 16-byte aligned,
+ * workspace 256-byte aligned.  f32 variant: any C = nh*2*kd.
  * `workspace` holds the qkv/attention intermediates; size from
  * va_psa_attention_workspace_bytes().  dtype: 0 = f32, 1 = bf16. */
 VA_API size_t va_psa_attention_workspace_bytes(int B, int C, int H, int W, int num_heads, int key_dim,
@@ -165,6 +168,22 @@ VA_API int va_psa_attention_fwd_bf16(const va_bf16 *x, const va_bf16 *w_qkv, con
                               const float *b_proj, va_bf16 *y, int B, int C, int H, int W,
                               int num_heads, int key_dim, void *workspace, size_t ws_bytes,
                               va_stream_t stream);
+
+/* The attention core of the bf16 path on its own (tcgen05, one launch):
+ * O = softmax(Q·Kᵀ/√32)·V per (b, head) with the full 64-wide V — the two
+ * reference flash_attention2_forward calls (psa.rs:930-944) in one pass.
+ * Layouts (f16): qk = [2][B*nh][N][32] (psa_pack_qkv sections 0 and 1),
+ * v and o = [B][nh*64][Np] channel-major with row pitch Np = roundup(N, 8)
+ * (psa_extract_v_nchw / psa_merge_attn_nchw layouts, padded); lse optional
+ * [B*nh][N] f32.  nh = 2 only. */
+VA_API int va_psa_flash_attention_fwd_f16(const void *qk, const void *v, void *o, float *lse, int B,
+                                          int num_heads, int H, int W, va_stream_t stream);
+
+/* Device status word of the tensor-core kernels: 0, or 1000+site of the
+ * first bounded wait that gave up.  read: copies it to *status (synchronises
+ * `stream`); clear: resets it to 0. */
+VA_API int va_device_status_read(int *status, va_stream_t stream);
+VA_API int va_device_status_clear(va_stream_t stream);
 
 #ifdef __cplusplus
 }

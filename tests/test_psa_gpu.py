@@ -208,10 +208,10 @@ def test_reference_node_sequence_matches_fused(cuda):
     nh, kd = 2, 32
     from vision_rs_b200 import _lib
     st = torch.cuda.current_stream().cuda_stream
-    x = dev(g["x"])
+    # keep every device tensor referenced while its raw pointer is in use
+    x, wq, bq, wpe, bpe, wpr, bpr = (dev(g[k]) for k in ("x", "w_qkv", "b_qkv", "w_pe", "b_pe", "w_proj", "b_proj"))
     qkv = torch.empty(B, 256, H, W, device="cuda")
-    _lib.call("va_conv1x1_bias_f32", x.data_ptr(), dev(g["w_qkv"]).data_ptr(), dev(g["b_qkv"]).data_ptr(),
-              qkv.data_ptr(), B, C, 256, H * W, st)
+    _lib.call("va_conv1x1_bias_f32", x.data_ptr(), wq.data_ptr(), bq.data_ptr(), qkv.data_ptr(), B, C, 256, H * W, st)
     pk = vp.PsaPackQkvOp(kd, nh)
     shp = pk.infer_output_shape([list(qkv.shape)])
     packed = torch.empty(4, B * nh, H * W, kd, device="cuda")
@@ -226,10 +226,40 @@ def test_reference_node_sequence_matches_fused(cuda):
     v = torch.empty(B, C, H, W, device="cuda")
     vp.PsaExtractVOp(kd, nh).inner.launch([qkv], [], v)
     pe = torch.empty_like(v)
-    _lib.call("va_dwconv3x3_bias_f32", v.data_ptr(), dev(g["w_pe"]).data_ptr(), dev(g["b_pe"]).data_ptr(),
-              pe.data_ptr(), B, C, H, W, st)
+    _lib.call("va_dwconv3x3_bias_f32", v.data_ptr(), wpe.data_ptr(), bpe.data_ptr(), pe.data_ptr(), B, C, H, W, st)
     y = torch.empty_like(v)
     s = (merged + pe).contiguous()
-    _lib.call("va_conv1x1_bias_f32", s.data_ptr(), dev(g["w_proj"]).data_ptr(), dev(g["b_proj"]).data_ptr(),
-              y.data_ptr(), B, C, C, H * W, st)
+    _lib.call("va_conv1x1_bias_f32", s.data_ptr(), wpr.data_ptr(), bpr.data_ptr(), y.data_ptr(), B, C, C, H * W, st)
     assert max_abs(host(y), g["y"]) < F32_MAX_ABS
+
+
+@pytest.mark.parametrize("B,H,W", [(1, 4, 4), (2, 20, 20), (2, 40, 40), (1, 13, 11), (3, 16, 16), (1, 8, 25)])
+def test_tc_attention_core_vs_oracle(cuda, B, H, W):
+    """The tcgen05 attention kernel alone (va_psa_flash_attention_fwd_f16):
+    O = softmax(QKᵀ/√32)·V with 64-wide V, f16 operands, against the f64
+    oracle on the same f16 values; LSE against the oracle's."""
+    from vision_rs_b200 import _lib
+    nh, N = 2, H * W
+    Np = (N + 7) // 8 * 8
+    rng = np.random.default_rng(N + B)
+    f16 = lambda a: np.asarray(a, np.float32).astype(np.float16)
+    qk = f16(rng.standard_normal((2, B * nh, N, 32)) * 0.6)
+    vv = f16(rng.standard_normal((B, 128, N)))
+    vpad = np.zeros((B, 128, Np), np.float16)
+    vpad[:, :, :N] = vv
+    qk_d = torch.as_tensor(qk).cuda()
+    v_d = torch.as_tensor(vpad).cuda()
+    o_d = torch.zeros(B, 128, Np, dtype=torch.float16, device="cuda")
+    l_d = torch.zeros(B * nh, N, dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.call("va_psa_flash_attention_fwd_f16", qk_d.data_ptr(), v_d.data_ptr(), o_d.data_ptr(), l_d.data_ptr(),
+              B, nh, H, W, st)
+    o = o_d.float().cpu().numpy()[:, :, :N]
+    v_t = vv.astype(np.float32).reshape(B, nh, 64, N).transpose(0, 1, 3, 2).reshape(B * nh, N, 64)
+    ro, rl = po.flash_attention2_forward(qk[0].astype(np.float32), qk[1].astype(np.float32), v_t, SCALE)
+    ro = ro.reshape(B, nh, N, 64).transpose(0, 1, 3, 2).reshape(B, 128, N)
+    assert rel_l2(o, ro) < 2e-3 and max_abs(o, ro) < 1e-2
+    assert max_abs(l_d.cpu().numpy(), rl) < 2e-3
+    status = __import__("ctypes").c_int(-1)
+    _lib.call("va_device_status_read", __import__("ctypes").byref(status), st)
+    assert status.value == 0

@@ -114,4 +114,16 @@ int va_psa_attention_fwd_bf16(const va_bf16* x, const va_bf16* w_qkv, const floa
                                 (__nv_bfloat16*)y, B, C, H, W, num_heads, key_dim, ws, ws_bytes, (cudaStream_t)s);
 }
 
+int va_psa_flash_attention_fwd_f16(const void* qk, const void* v, void* o, float* lse, int B, int nh, int H, int W,
+                                   va_stream_t s) {
+  return psa_attention_core_tc(qk, v, o, lse, B, nh, H, W, (cudaStream_t)s);
+}
+
+int va_device_status_read(int* status, va_stream_t s) {
+  if (!status) return set_error(VA_ERR_SHAPE, "device_status_read: null output");
+  return tc_status_read(status, (cudaStream_t)s);
+}
+
+int va_device_status_clear(va_stream_t s) { return tc_status_clear((cudaStream_t)s); }
+
 }  // extern "C"

@@ -29,6 +29,17 @@ int conv1x1(const T* x, const T* x2, const TW* w, const float* bias, T* y, int B
 template <typename T, typename TW>
 int dwconv3x3(const T* x, const TW* w, const float* bias, T* y, int B, int C, int H, int W, cudaStream_t st);
 
+size_t psa_tc_workspace_bytes(int B, int H, int W, int nh);
+bool psa_tc_supported(int C, int nh, int kd);
+int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,
+                         const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
+                         const float* b_proj, __nv_bfloat16* y, int B, int C, int H, int W, int nh, int kd,
+                         void* ws, size_t ws_bytes, cudaStream_t st, float* lse_out);
+int psa_attention_core_tc(const void* qk, const void* v, void* o, float* lse, int B, int nh, int H, int W,
+                          cudaStream_t st);
+int tc_status_read(int* out, cudaStream_t st);
+int tc_status_clear(cudaStream_t st);
+
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 }  // namespace va

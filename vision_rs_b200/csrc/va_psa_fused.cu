@@ -4,7 +4,7 @@
 //   v = extract_v(qkv) → pe = dw3x3(v)+b → y = conv1x1(merged + pe)+b
 //
 // f32: the reference's node sequence on the FFMA kernels, intermediates in the
-// caller's workspace.
+// caller's workspace.  bf16: the tensor-core path in va_tc_psa.cu.
 #include "va_common.cuh"
 #include "va_psa.h"
 
@@ -51,7 +51,8 @@ int check_common(int B, int C, int H, int W, int nh, int kd, void* ws, size_t ws
 }  // namespace
 
 size_t psa_workspace_bytes(int B, int C, int H, int W, int nh, int kd, int dtype) {
-  return layout(B, C, H, W, nh, kd, dtype == 0 ? 4 : 2).total;
+  if (dtype == 0) return layout(B, C, H, W, nh, kd, 4).total;
+  return psa_tc_supported(C, nh, kd) ? psa_tc_workspace_bytes(B, H, W, nh) : 0;
 }
 
 #define VA_TRY(expr)          \
@@ -93,31 +94,8 @@ int psa_attention_fwd_bf16(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, c
                            const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
                            const float* b_proj, __nv_bfloat16* y, int B, int C, int H, int W, int nh, int kd,
                            void* ws, size_t ws_bytes, cudaStream_t st) {
-  typedef __nv_bfloat16 bf;
-  const PsaWs L = layout(B, C, H, W, nh, kd, 2);
-  VA_TRY(check_common(B, C, H, W, nh, kd, ws, ws_bytes, L.total));
-  char* base = (char*)ws;
-  bf* qkv = (bf*)(base + L.qkv);
-  bf* packed = (bf*)(base + L.packed);
-  bf* lo = (bf*)(base + L.lo);
-  bf* hi = (bf*)(base + L.hi);
-  bf* merged = (bf*)(base + L.merged);
-  bf* v = (bf*)(base + L.v);
-  bf* pe = (bf*)(base + L.pe);
-  float* lse = (float*)(base + L.lse);
-  const int N = H * W, qkv_h = nh * 4 * kd, BH = B * nh;
-  const size_t sec = (size_t)BH * N * kd;
-  const float scale = 1.0f / sqrtf((float)kd);
-  va_stream_t s = (va_stream_t)st;
-  VA_TRY((conv1x1<bf, bf>(x, nullptr, w_qkv, b_qkv, qkv, B, C, qkv_h, N, st)));
-  VA_TRY(va_psa_pack_qkv_bf16((const va_bf16*)qkv, (va_bf16*)packed, qkv_h, H, W, B, nh, s));
-  VA_TRY(fa_fwd_bf16(packed, packed + sec, packed + 2 * sec, lo, lse, N, N, scale, BH, kd, st));
-  VA_TRY(fa_fwd_bf16(packed, packed + sec, packed + 3 * sec, hi, lse, N, N, scale, BH, kd, st));
-  VA_TRY(va_psa_merge_attn_nchw_bf16((const va_bf16*)lo, (const va_bf16*)hi, (va_bf16*)merged, C, H, W, nh, B, s));
-  VA_TRY(va_psa_extract_v_nchw_bf16((const va_bf16*)qkv, (va_bf16*)v, qkv_h, C, H, W, nh, B, s));
-  VA_TRY((dwconv3x3<bf, bf>(v, w_pe, b_pe, pe, B, C, H, W, st)));
-  VA_TRY((conv1x1<bf, bf>(merged, pe, w_proj, b_proj, y, B, C, C, N, st)));
-  return VA_OK;
+  return psa_attention_fwd_tc(x, w_qkv, b_qkv, w_pe, b_pe, w_proj, b_proj, y, B, C, H, W, nh, kd, ws, ws_bytes, st,
+                              nullptr);
 }
 
 }  // namespace va

@@ -1,0 +1,709 @@
+// PSA Attention forward on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// The reference graph (src/models/yolo/yolo26/blocks/c2psa.rs:61-116) runs
+// 7 nodes: qkv conv+BN, psa_pack_qkv, flash attention ×2 (V split into two
+// 32-wide halves, psa.rs:930-944), psa_merge_attn_nchw, psa_extract_v_nchw,
+// pe dw-conv+BN, add, proj conv+BN.  Here it is three kernels:
+//
+//  1. qkv_proj_kernel  — D[128 tok × 256 ch] = xᵀ·W_qkvᵀ on tcgen05 (x tile is
+//     the MN-major A operand read straight from NCHW by TMA).  The epilogue
+//     adds the folded-BN bias and writes exactly the layouts the next kernel
+//     reads: Q and K token-major [2][B·nh][N][32] (psa_pack_qkv sections 0/1)
+//     and V channel-major [B][C][Np] (psa_extract_v_nchw's output), f16.
+//  2. attn_kernel      — flash attention per (b, h, 128-query tile):
+//     S = Q·Kᵀ (TMEM), online softmax in registers (one thread per query
+//     row), P → smem (f16), O += P·V with the full 64-wide V in one MMA (no
+//     lo/hi split).  O is written channel-major [B][C][Np] — the layout
+//     psa_merge_attn_nchw produces.
+//  3. pe_proj_kernel   — A = O + dw3×3(V) + b_pe built in smem as the MN-major
+//     operand, D = A·W_projᵀ on tcgen05, + b_proj, y stored NCHW bf16.
+//
+// Precision: x, weights and y are bf16; the qkv GEMM runs bf16×bf16; the
+// attention operands Q, K, V, P, O and the proj A operand are f16 (3 more
+// mantissa bits than bf16 for values whose range is small: |qkv| is clamped
+// to ±65504, P ∈ [0, 256]); every accumulation is f32 in TMEM or registers.
+//
+// Every mbarrier wait is bounded (sm100::mbar_wait); a timeout records a code
+// in g_tc_status and the kernel unwinds, releasing its TMEM.
+#include <cudaTypedefs.h>
+
+#include "va_common.cuh"
+#include "va_psa.h"
+#include "va_sm100.cuh"
+
+namespace va {
+using namespace sm100;
+
+__device__ int g_tc_status;
+
+namespace {
+
+constexpr int kC = 128;      // PSA hidden channels supported by the tensor-core path
+constexpr int kQKV = 256;    // nh*4*kd
+constexpr int kKD = 32;      // key_dim
+constexpr int kHD = 64;      // head_dim (V width)
+constexpr int kTile = 128;   // tokens per tile (UMMA M)
+
+// ── Kernel 1: qkv projection ────────────────────────────────────────────────
+struct QkvSmem {
+  uint8_t a[2][kC * 128];      // xᵀ tile, MN-major SW128: 2 blocks of 64 tokens × 128 channel rows (16 KB each)
+  uint8_t w[2][kQKV * 128];    // W_qkv K-major SW128: 2 blocks of 64 in-channels × 256 rows (32 KB each)
+  uint64_t full_bar;
+  uint64_t mma_bar;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __launch_bounds__(128, 1)
+qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                const float* __restrict__ bias, __half* __restrict__ qk, __half* __restrict__ vbuf, int N, int Np,
+                int nh) {
+  extern __shared__ uint8_t smem_raw[];
+  QkvSmem& sm = *reinterpret_cast<QkvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * kTile, b = blockIdx.y;
+
+  if (tid == 0) {
+    mbar_init(&sm.full_bar, 1);
+    mbar_init(&sm.mma_bar, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&sm.tmem_base, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (tid == 0) {
+    tma_prefetch_desc(&map_x);
+    tma_prefetch_desc(&map_w);
+    mbar_arrive_expect_tx(&sm.full_bar, 2 * kC * 128 + 2 * kQKV * 128);
+    tma_load_2d(sm.a[0], &map_x, &sm.full_bar, n0, b * kC);
+    tma_load_2d(sm.a[1], &map_x, &sm.full_bar, n0 + 64, b * kC);
+    tma_load_2d(sm.w[0], &map_w, &sm.full_bar, 0, 0);
+    tma_load_2d(sm.w[1], &map_w, &sm.full_bar, 64, 0);
+    if (mbar_wait(&sm.full_bar, 0, &sm.abort, &g_tc_status, 1)) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_f32acc(128, kQKV, AB_BF16, /*a_mn=*/true, /*b_mn=*/false);
+      const uint32_t a0 = smem_u32(sm.a[0]), w0 = smem_u32(sm.w[0]);
+#pragma unroll
+      for (int s = 0; s < kC / 16; ++s) {
+        uint64_t ad = sdesc(a0 + s * 16 * 128, /*lbo=*/kC * 128, /*sbo=*/1024, SW_128B);
+        uint64_t bd = sdesc(w0 + (s >> 2) * (kQKV * 128) + (s & 3) * 32, 16, 1024, SW_128B);
+        mma_ss(tmem, ad, bd, idesc, s > 0);
+      }
+    } else {
+      // the TMA loads may still land: wait for them (bounded) before leaving
+      const long long t0 = clock64();
+      while (!mbar_try_wait(&sm.full_bar, 0) && clock64() - t0 < kSpinCycles) {
+      }
+    }
+    mma_commit(&sm.mma_bar);
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(&sm.mma_bar, 0, &sm.abort, &g_tc_status, 2) && !sm.abort;
+  tc_fence_after();
+
+  if (ok) {
+    const int n = n0 + warp * 32 + lane;
+    const int BH = gridDim.y * nh;
+#pragma unroll 1
+    for (int c = 0; c < kQKV / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
+      tmem_ld_wait();
+      const int h = c >> 2, sec = c & 3;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + __ldg(bias + c * 32 + i);
+      if (n < N) {
+        if (sec < 2) {
+          // Q / K row: 32 contiguous f16 in [sec][b*nh+h][n][:]
+          uint4* dst = reinterpret_cast<uint4*>(qk + (((size_t)sec * BH + (size_t)b * nh + h) * N + n) * kKD);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 u;
+            u.x = pack_f16x2_sat(v[q * 8 + 0], v[q * 8 + 1]);
+            u.y = pack_f16x2_sat(v[q * 8 + 2], v[q * 8 + 3]);
+            u.z = pack_f16x2_sat(v[q * 8 + 4], v[q * 8 + 5]);
+            u.w = pack_f16x2_sat(v[q * 8 + 6], v[q * 8 + 7]);
+            dst[q] = u;
+          }
+        } else {
+          // V channels h*64 + (sec-2)*32 + i, channel-major
+          __half* dst = vbuf + ((size_t)b * kC + h * kHD + (sec - 2) * 32) * Np + n;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            uint32_t p = pack_f16x2_sat(v[i], 0.f);
+            dst[(size_t)i * Np] = __ushort_as_half((unsigned short)(p & 0xFFFF));
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ── Kernel 2: flash attention ───────────────────────────────────────────────
+struct AttnSmem {
+  uint8_t q[kTile * 64];           // Q tile [128 rows × 32] f16, K-major SW64 (8 KB)
+  uint8_t k[2][kTile * 64];        // K tiles, 2 stages (8 KB each)
+  uint8_t v[2][2][kHD * 128];      // V tiles: stage × key-block (64 keys) × [64 ch rows × 128 B] SW128
+  uint8_t p[2][kTile * 128];       // P [128 rows × 128 keys] f16, K-major SW128: 2 key-blocks × 16 KB
+  uint64_t q_full, kv_full[2], kv_empty[2], s_full, s_free, p_full, o_done, fin;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr int kAttnThreads = 160;  // warps 0-3: softmax (one thread per query row); warp 4: TMA + MMA issue
+constexpr uint32_t kColS = 0, kColO = 128;
+
+__device__ __forceinline__ void attn_load_kv(AttnSmem& sm, const CUtensorMap* mqk, const CUtensorMap* mv, int t,
+                                             int stage, int BH, int bh, int vrow) {
+  mbar_arrive_expect_tx(&sm.kv_full[stage], kTile * 64 + 2 * kHD * 128);
+  tma_load_3d(sm.k[stage], mqk, &sm.kv_full[stage], 0, t * kTile, BH + bh);
+  tma_load_2d(sm.v[stage][0], mv, &sm.kv_full[stage], t * kTile, vrow);
+  tma_load_2d(sm.v[stage][1], mv, &sm.kv_full[stage], t * kTile + 64, vrow);
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 2)
+attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v,
+            __half* __restrict__ obuf, float* __restrict__ lse, int N, int Np, int nh, float scale_log2) {
+  extern __shared__ uint8_t smem_raw[];
+  AttnSmem& sm = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q0 = blockIdx.x * kTile, bh = blockIdx.y;
+  const int BH = gridDim.y, b = bh / nh, h = bh % nh;
+  const int nkv = (N + kTile - 1) / kTile;
+  const int vrow = b * kC + h * kHD;
+
+  if (tid == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.kv_full[i], 1);
+      mbar_init(&sm.kv_empty[i], 1);
+    }
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.s_free, 128);
+    mbar_init(&sm.p_full, 128);
+    mbar_init(&sm.o_done, 1);
+    mbar_init(&sm.fin, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&sm.tmem_base, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // ── control thread: TMA producer and MMA issuer ──
+      int issued = 0;  // KV tiles whose loads were issued
+      tma_prefetch_desc(&map_qk);
+      tma_prefetch_desc(&map_v);
+      mbar_arrive_expect_tx(&sm.q_full, kTile * 64);
+      tma_load_3d(sm.q, &map_qk, &sm.q_full, 0, q0, bh);
+      for (; issued < 2 && issued < nkv; ++issued) attn_load_kv(sm, &map_qk, &map_v, issued, issued, BH, bh, vrow);
+
+      constexpr uint32_t idS = idesc_f32acc(128, kTile, AB_F16, false, false);
+      constexpr uint32_t idO = idesc_f32acc(128, kHD, AB_F16, false, false);
+      const uint32_t qa = smem_u32(sm.q), pa = smem_u32(sm.p[0]);
+      auto issue_s = [&](int stage) {
+        const uint32_t ka = smem_u32(sm.k[stage]);
+#pragma unroll
+        for (int s = 0; s < kKD / 16; ++s)
+          mma_ss(tmem + kColS, sdesc(qa + s * 32, 16, 512, SW_64B), sdesc(ka + s * 32, 16, 512, SW_64B), idS, s > 0);
+      };
+      auto issue_o = [&](int stage, bool acc) {
+        const uint32_t va0 = smem_u32(sm.v[stage][0]);
+#pragma unroll
+        for (int s = 0; s < kTile / 16; ++s) {
+          uint64_t ad = sdesc(pa + (s >> 2) * (kTile * 128) + (s & 3) * 32, 16, 1024, SW_128B);
+          uint64_t bd = sdesc(va0 + (s >> 2) * (kHD * 128) + (s & 3) * 32, 16, 1024, SW_128B);
+          mma_ss(tmem + kColO, ad, bd, idO, (acc || s > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(&sm.q_full, 0, &sm.abort, &g_tc_status, 10) &&
+                mbar_wait(&sm.kv_full[0], 0, &sm.abort, &g_tc_status, 11);
+      int consumed = ok ? 1 : 0;  // KV tiles whose full barrier was observed
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+        mma_commit(&sm.s_full);
+      }
+      for (int j = 0; ok && j < nkv; ++j) {
+        if (j + 1 < nkv) {
+          ok = mbar_wait(&sm.kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, &sm.abort, &g_tc_status, 12) &&
+               mbar_wait(&sm.s_free, j & 1, &sm.abort, &g_tc_status, 13);
+          if (!ok) break;
+          consumed = j + 2;
+          tc_fence_after();
+          issue_s((j + 1) & 1);
+          mma_commit(&sm.s_full);
+        }
+        if (!(ok = mbar_wait(&sm.p_full, j & 1, &sm.abort, &g_tc_status, 14))) break;
+        tc_fence_after();
+        issue_o(j & 1, j > 0);
+        mma_commit(&sm.o_done);
+        mma_commit(&sm.kv_empty[j & 1]);
+        if (j + 2 < nkv) {
+          if (!(ok = mbar_wait(&sm.kv_empty[j & 1], (j >> 1) & 1, &sm.abort, &g_tc_status, 15))) break;
+          attn_load_kv(sm, &map_qk, &map_v, j + 2, j & 1, BH, bh, vrow);
+          ++issued;
+        }
+      }
+      // teardown: every issued TMA load has landed and every MMA has completed
+      for (int t = consumed; t < issued; ++t) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&sm.kv_full[t & 1], (t >> 1) & 1) && clock64() - t0 < kSpinCycles) {
+        }
+      }
+      if (!ok) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&sm.q_full, 0) && clock64() - t0 < kSpinCycles) {
+        }
+      }
+      mma_commit(&sm.fin);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(&sm.fin, 0) && clock64() - t0 < kSpinCycles) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // ── softmax warps: thread = query row (TMEM lane) ──
+    const int row = tid;  // 0..127
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    uint8_t* prow0 = sm.p[0] + row * 128;
+    uint8_t* prow1 = sm.p[1] + row * 128;
+    const int rsw = row & 7;
+    for (int j = 0; j < nkv; ++j) {
+      if (!(ok = mbar_wait(&sm.s_full, j & 1, &sm.abort, &g_tc_status, 20))) break;
+      tc_fence_after();
+      float x[kTile];
+#pragma unroll
+      for (int c = 0; c < kTile / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + kColS + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[i]) * scale_log2;
+      }
+      tc_fence_before();
+      mbar_arrive(&sm.s_free);
+      const int kvalid = N - j * kTile;
+      if (kvalid < kTile) {
+#pragma unroll
+        for (int i = 0; i < kTile; ++i)
+          if (i >= kvalid) x[i] = -INFINITY;
+      }
+      float mx = x[0];
+#pragma unroll
+      for (int i = 1; i < kTile; ++i) mx = fmaxf(mx, x[i]);
+      const float m_new = fmaxf(m, mx);
+      // Rescale only when the running max grew by more than 2^8 (the stale
+      // max keeps p ≤ 256, exact after the final 1/l normalisation).
+      const bool resc = (j == 0) || (m_new > m + 8.0f);
+      const float m_use = resc ? m_new : m;
+      const float alpha = resc ? ex2(m - m_use) : 1.0f;
+      if (j > 0) {
+        if (!(ok = mbar_wait(&sm.o_done, (j - 1) & 1, &sm.abort, &g_tc_status, 21))) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll
+          for (int c = 0; c < kHD / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tmem + lane_off + kColO + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(tmem + lane_off + kColO + c * 32, r);
+          }
+          tmem_st_wait();
+        }
+      }
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < kTile / 8; ++c) {  // 16 chunks of 8 keys = 16 bytes of f16
+        float p[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          p[e] = ex2(x[c * 8 + e] - m_use);
+          rs += p[e];
+        }
+        uint4 u;
+        u.x = pack_f16x2_sat(p[0], p[1]);
+        u.y = pack_f16x2_sat(p[2], p[3]);
+        u.z = pack_f16x2_sat(p[4], p[5]);
+        u.w = pack_f16x2_sat(p[6], p[7]);
+        uint8_t* base = (c < 8) ? prow0 : prow1;
+        *reinterpret_cast<uint4*>(base + (((c & 7) ^ rsw) << 4)) = u;
+      }
+      l = l * alpha + rs;
+      m = m_use;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&sm.p_full);
+    }
+    if (ok) ok = mbar_wait(&sm.o_done, (nkv - 1) & 1, &sm.abort, &g_tc_status, 22);
+    if (ok) {
+      tc_fence_after();
+      const int n = q0 + row;
+      const float inv = 1.0f / l;
+#pragma unroll
+      for (int c = 0; c < kHD / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + kColO + c * 32, r);
+        tmem_ld_wait();
+        if (n < N) {
+          __half* dst = obuf + ((size_t)b * kC + h * kHD + c * 32) * Np + n;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            uint32_t pk = pack_f16x2_sat(__uint_as_float(r[i]) * inv, 0.f);
+            dst[(size_t)i * Np] = __ushort_as_half((unsigned short)(pk & 0xFFFF));
+          }
+        }
+      }
+      if (lse && n < N) lse[(size_t)bh * N + n] = (m + __log2f(l)) * 0.6931471805599453f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ── Kernel 3: positional encoding + add + output projection ─────────────────
+struct ProjSmem {
+  uint8_t a[2][kC * 128];   // (O+PE)ᵀ tile, MN-major SW128: 2 blocks of 64 tokens × 128 channel rows
+  uint8_t w[2][kC * 128];   // W_proj f16, K-major SW128: 2 blocks of 64 in-channels × 128 rows
+  float wpe[kC * 9];
+  float bpe[kC];
+  uint64_t mma_bar;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __launch_bounds__(128, 1)
+pe_proj_kernel(const __half* __restrict__ obuf, const __half* __restrict__ vbuf,
+               const __nv_bfloat16* __restrict__ w_pe, const float* __restrict__ b_pe,
+               const __nv_bfloat16* __restrict__ w_proj, const float* __restrict__ b_proj,
+               __nv_bfloat16* __restrict__ y, int H, int W, int Np) {
+  extern __shared__ uint8_t smem_raw[];
+  ProjSmem& sm = *reinterpret_cast<ProjSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int N = H * W;
+  const int n0 = blockIdx.x * kTile, b = blockIdx.y;
+
+  if (tid == 0) {
+    mbar_init(&sm.mma_bar, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&sm.tmem_base, 128);
+    tmem_relinquish();
+  }
+  for (int i = tid; i < kC * 9; i += 128) sm.wpe[i] = __bfloat162float(w_pe[i]);
+  for (int i = tid; i < kC; i += 128) sm.bpe[i] = b_pe[i];
+  // W_proj (bf16, [out][in]) → f16 K-major SW128
+  for (int i = tid; i < kC * kC / 8; i += 128) {
+    const int o = i / (kC / 8), chunk = i % (kC / 8);  // 16 chunks of 8 in-channels per row
+    const uint4 src = __ldg(reinterpret_cast<const uint4*>(w_proj + (size_t)o * kC) + chunk);
+    const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&src);
+    uint4 u;
+    uint32_t* uu = &u.x;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __bfloat1622float2(s2[e]);
+      uu[e] = pack_f16x2_sat(f.x, f.y);
+    }
+    const int kb = chunk >> 3, c8 = chunk & 7;
+    *reinterpret_cast<uint4*>(sm.w[kb] + o * 128 + ((c8 ^ (o & 7)) << 4)) = u;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  // A tile: item = (channel c, group g of 8 tokens)
+  const __half* ob = obuf + (size_t)b * kC * Np;
+  const __half* vb = vbuf + (size_t)b * kC * Np;
+  for (int it = tid; it < kC * (kTile / 8); it += 128) {
+    const int c = it / (kTile / 8), g = it % (kTile / 8);
+    const int nb = n0 + g * 8;
+    float acc[8];
+    if (nb + 8 <= Np) {
+      const uint4 ou = __ldg(reinterpret_cast<const uint4*>(ob + (size_t)c * Np + nb));
+      const __half2* o2 = reinterpret_cast<const __half2*>(&ou);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __half22float2(o2[e]);
+        acc[2 * e] = f.x;
+        acc[2 * e + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    }
+    const float* wc = sm.wpe + c * 9;
+    const __half* vc = vb + (size_t)c * Np;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int n = nb + e;
+      if (n >= N) {
+        acc[e] = 0.f;
+        continue;
+      }
+      const int i = n / W, jj = n - i * W;
+      float pe = sm.bpe[c];
+#pragma unroll
+      for (int di = 0; di < 3; ++di) {
+        const int ii = i + di - 1;
+        if (ii < 0 || ii >= H) continue;
+#pragma unroll
+        for (int dj = 0; dj < 3; ++dj) {
+          const int j2 = jj + dj - 1;
+          if (j2 < 0 || j2 >= W) continue;
+          pe = fmaf(wc[di * 3 + dj], __half2float(vc[ii * W + j2]), pe);
+        }
+      }
+      acc[e] += pe;
+    }
+    uint4 u;
+    u.x = pack_f16x2_sat(acc[0], acc[1]);
+    u.y = pack_f16x2_sat(acc[2], acc[3]);
+    u.z = pack_f16x2_sat(acc[4], acc[5]);
+    u.w = pack_f16x2_sat(acc[6], acc[7]);
+    const int blk = g >> 3, ch = g & 7;
+    *reinterpret_cast<uint4*>(sm.a[blk] + c * 128 + ((ch ^ (c & 7)) << 4)) = u;
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    tc_fence_after();
+    constexpr uint32_t idesc = idesc_f32acc(128, kC, AB_F16, /*a_mn=*/true, /*b_mn=*/false);
+    const uint32_t a0 = smem_u32(sm.a[0]), w0 = smem_u32(sm.w[0]);
+#pragma unroll
+    for (int s = 0; s < kC / 16; ++s) {
+      uint64_t ad = sdesc(a0 + s * 16 * 128, kC * 128, 1024, SW_128B);
+      uint64_t bd = sdesc(w0 + (s >> 2) * (kC * 128) + (s & 3) * 32, 16, 1024, SW_128B);
+      mma_ss(tmem, ad, bd, idesc, s > 0);
+    }
+    mma_commit(&sm.mma_bar);
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(&sm.mma_bar, 0, &sm.abort, &g_tc_status, 30);
+  tc_fence_after();
+  if (ok) {
+    const int n = n0 + warp * 32 + lane;
+#pragma unroll 1
+    for (int c = 0; c < kC / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
+      tmem_ld_wait();
+      if (n < N) {
+        __nv_bfloat16* dst = y + ((size_t)b * kC + c * 32) * N + n;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dst[(size_t)i * N] = __float2bfloat16_rn(__uint_as_float(r[i]) + __ldg(b_proj + c * 32 + i));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
+// x with a row pitch that TMA cannot address (N*2 bytes not a multiple of 16)
+// is first copied into a padded buffer.
+__global__ void pad_rows_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ xp, int rows, int N,
+                                int Np) {
+  const long long total = (long long)rows * Np;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / Np;
+    const int n = (int)(i - r * Np);
+    xp[i] = n < N ? x[r * N + n] : __float2bfloat16_rn(0.f);
+  }
+}
+
+// ── host side ───────────────────────────────────────────────────────────────
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+             const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz, const char* what) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(VA_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+  uint32_t es[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(m, dt, rank, const_cast<void*>(base), dims, strides_bytes, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(VA_ERR_ALIGN, "tensor map for %s rejected (CUresult %d)", what, (int)r);
+  return VA_OK;
+}
+
+struct TcWs {
+  size_t qk, v, o, xpad, total;
+};
+
+TcWs tc_layout(int B, int H, int W, int nh) {
+  const size_t N = (size_t)H * W, Np = (N + 7) / 8 * 8, BH = (size_t)B * nh;
+  TcWs w;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
+  w.qk = take(2 * BH * N * kKD * 2);
+  w.v = take((size_t)B * kC * Np * 2);
+  w.o = take((size_t)B * kC * Np * 2);
+  w.xpad = (N % 8) ? take((size_t)B * kC * Np * 2) : (size_t)-1;
+  w.total = off;
+  return w;
+}
+
+template <typename K>
+int set_smem(K kernel, size_t bytes) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  return VA_OK;
+}
+
+}  // namespace
+
+size_t psa_tc_workspace_bytes(int B, int H, int W, int nh) { return tc_layout(B, H, W, nh).total; }
+
+bool psa_tc_supported(int C, int nh, int kd) { return C == kC && nh * 4 * kd == kQKV && kd == kKD; }
+
+int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,
+                         const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
+                         const float* b_proj, __nv_bfloat16* y, int B, int C, int H, int W, int nh, int kd,
+                         void* ws, size_t ws_bytes, cudaStream_t st, float* lse_out) {
+  VA_CHECK_ARG(psa_tc_supported(C, nh, kd), "psa_attention bf16: tensor-core path needs C=128, nh=2, kd=32");
+  VA_CHECK_ARG(B > 0 && H > 0 && W > 0 && B <= 65535, "psa_attention bf16: bad sizes");
+  const TcWs L = tc_layout(B, H, W, nh);
+  if (!ws || ws_bytes < L.total)
+    return set_error(VA_ERR_WORKSPACE, "psa_attention bf16: workspace %zu < %zu bytes", ws_bytes, L.total);
+  if ((reinterpret_cast<uintptr_t>(ws) & 255) || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(w_qkv) & 15) || (reinterpret_cast<uintptr_t>(w_proj) & 15))
+    return set_error(VA_ERR_ALIGN, "psa_attention bf16: x/w_qkv/w_proj need 16-byte, workspace 256-byte alignment");
+  const int N = H * W, Np = (N + 7) / 8 * 8, BH = B * nh;
+  char* base = static_cast<char*>(ws);
+  __half* qk = reinterpret_cast<__half*>(base + L.qk);
+  __half* vb = reinterpret_cast<__half*>(base + L.v);
+  __half* ob = reinterpret_cast<__half*>(base + L.o);
+  const __nv_bfloat16* xs = x;
+  if (N % 8) {
+    __nv_bfloat16* xp = reinterpret_cast<__nv_bfloat16*>(base + L.xpad);
+    const long long total = (long long)B * kC * Np;
+    pad_rows_kernel<<<(int)std::min<long long>((total + 255) / 256, 148LL * 8), 256, 0, st>>>(x, xp, B * kC, N, Np);
+    if (int rc = check_launch("psa pad")) return rc;
+    xs = xp;
+  }
+  CUtensorMap mx, mw, mqk, mv;
+  {
+    uint64_t d[2] = {(uint64_t)N, (uint64_t)B * kC}, s[1] = {(uint64_t)Np * 2};
+    uint32_t bx[2] = {64, kC};
+    if (int rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xs, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B, "x"))
+      return rc;
+  }
+  {
+    uint64_t d[2] = {(uint64_t)kC, (uint64_t)kQKV}, s[1] = {(uint64_t)kC * 2};
+    uint32_t bx[2] = {64, kQKV};
+    if (int rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_qkv, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B,
+                          "w_qkv"))
+      return rc;
+  }
+  {
+    uint64_t d[3] = {(uint64_t)kKD, (uint64_t)N, (uint64_t)2 * BH}, s[2] = {(uint64_t)kKD * 2, (uint64_t)N * kKD * 2};
+    uint32_t bx[3] = {kKD, kTile, 1};
+    if (int rc = make_map(&mqk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, qk, d, s, bx, CU_TENSOR_MAP_SWIZZLE_64B, "qk"))
+      return rc;
+  }
+  {
+    uint64_t d[2] = {(uint64_t)N, (uint64_t)B * kC}, s[1] = {(uint64_t)Np * 2};
+    uint32_t bx[2] = {64, kHD};
+    if (int rc = make_map(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, vb, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B, "v"))
+      return rc;
+  }
+  const int ntile = (N + kTile - 1) / kTile;
+  const size_t sm1 = sizeof(QkvSmem) + 1024, sm2 = sizeof(AttnSmem) + 1024, sm3 = sizeof(ProjSmem) + 1024;
+  static bool attr_done = false;
+  if (!attr_done) {
+    if (int rc = set_smem(qkv_proj_kernel, sm1)) return rc;
+    if (int rc = set_smem(attn_kernel, sm2)) return rc;
+    if (int rc = set_smem(pe_proj_kernel, sm3)) return rc;
+    attr_done = true;
+  }
+  qkv_proj_kernel<<<dim3(ntile, B), 128, sm1, st>>>(mx, mw, b_qkv, qk, vb, N, Np, nh);
+  if (int rc = check_launch("psa qkv_proj")) return rc;
+  const float scale_log2 = (1.0f / sqrtf((float)kd)) * 1.4426950408889634f;
+  attn_kernel<<<dim3(ntile, BH), kAttnThreads, sm2, st>>>(mqk, mv, ob, lse_out, N, Np, nh, scale_log2);
+  if (int rc = check_launch("psa attention")) return rc;
+  pe_proj_kernel<<<dim3(ntile, B), 128, sm3, st>>>(ob, vb, w_pe, b_pe, w_proj, b_proj, y, H, W, Np);
+  return check_launch("psa pe_proj");
+}
+
+int tc_status_read(int* out, cudaStream_t st) {
+  cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_tc_status, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "device status read: %s", cudaGetErrorString(e));
+  return VA_OK;
+}
+
+int tc_status_clear(cudaStream_t st) {
+  static const int zero = 0;
+  cudaError_t e = cudaMemcpyToSymbolAsync(g_tc_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "device status clear: %s", cudaGetErrorString(e));
+  return VA_OK;
+}
+
+}  // namespace va
+
+namespace va {
+
+int psa_attention_core_tc(const void* qk, const void* v, void* o, float* lse, int B, int nh, int H, int W,
+                          cudaStream_t st) {
+  VA_CHECK_ARG(nh == 2 && B > 0 && H > 0 && W > 0 && B * nh <= 65535, "psa flash attention: need nh=2, B,H,W > 0");
+  if ((reinterpret_cast<uintptr_t>(qk) & 15) || (reinterpret_cast<uintptr_t>(v) & 15) ||
+      (reinterpret_cast<uintptr_t>(o) & 15))
+    return set_error(VA_ERR_ALIGN, "psa flash attention: qk/v/o need 16-byte alignment");
+  const int N = H * W, Np = (N + 7) / 8 * 8, BH = B * nh;
+  CUtensorMap mqk, mv;
+  {
+    uint64_t d[3] = {(uint64_t)kKD, (uint64_t)N, (uint64_t)2 * BH}, s[2] = {(uint64_t)kKD * 2, (uint64_t)N * kKD * 2};
+    uint32_t bx[3] = {kKD, kTile, 1};
+    if (int rc = make_map(&mqk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, qk, d, s, bx, CU_TENSOR_MAP_SWIZZLE_64B, "qk"))
+      return rc;
+  }
+  {
+    uint64_t d[2] = {(uint64_t)N, (uint64_t)B * kC}, s[1] = {(uint64_t)Np * 2};
+    uint32_t bx[2] = {64, kHD};
+    if (int rc = make_map(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B, "v"))
+      return rc;
+  }
+  const size_t sm2 = sizeof(AttnSmem) + 1024;
+  if (int rc = set_smem(attn_kernel, sm2)) return rc;
+  const float scale_log2 = (1.0f / sqrtf((float)kKD)) * 1.4426950408889634f;
+  attn_kernel<<<dim3((N + kTile - 1) / kTile, BH), kAttnThreads, sm2, st>>>(mqk, mv, static_cast<__half*>(o), lse, N,
+                                                                            Np, nh, scale_log2);
+  return check_launch("psa flash attention");
+}
+
+}  // namespace va
