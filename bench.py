@@ -67,7 +67,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                          "-lms", "50", "-i", str(self.idx)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -130,7 +130,7 @@ def run_reference(args, ws, rank):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    n_img = 4
+    n_img = B_PER_GPU  # one step = the whole 64-image batch of the workload
     vals = []
     for _ in range(args.warmup):
         cpu_sample(n_img, threads)
@@ -142,10 +142,11 @@ def run_reference(args, ws, rank):
         "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * n_img / val,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg2: C2PSA PSA attention fwd 64x128x40x40 (sample of 4 images per step)",
+        "config": {"workload": "cfg2: C2PSA PSA attention fwd, 128x40x40 (1600 tokens), nh=2, kd=32, hd=64",
                    "global_batch": n_img, "seq_len": N_TOK, "parallelism": "host threads"},
         "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{n_img} images of 128x40x40 per step, torch-CPU f32 restatement"},
+                         "sample": f"{n_img} images of 128x40x40 per step, torch-CPU f32 restatement of the "
+                                   "reference maths (the reference has no CPU path)"},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -164,7 +165,7 @@ def run_ours(args, ws, rank, local):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     rng = np.random.default_rng(1000 + rank)
-    B = B_PER_GPU
+    B = args.batch
     f = lambda *s, std=1.0: torch.tensor((rng.standard_normal(s) * std).astype(np.float32))
     x = f(B, C, H, W).to(dev, torch.bfloat16)
     op = vp.PsaAttention(f(NH * 4 * KD, C, std=0.02), f(NH * 4 * KD, std=0.02), f(C, 1, 3, 3, std=0.02),
@@ -179,21 +180,27 @@ def run_ours(args, ws, rank, local):
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
+    clk = ClockSampler(local).__enter__()
+    t_w = time.perf_counter()
+    nw = 0
+    while nw < args.warmup or time.perf_counter() - t_w < args.min_warm_s:
         op.forward_into(x, y)
+        nw += 1
+        if nw % 50 == 0:
+            torch.cuda.synchronize()
     barrier()
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     lc0 = _lib.lib().va_launch_count()
     barrier()
-    with ClockSampler(local) as clk:
-        for i in range(args.steps):
-            flush.fill_(float(i))  # evict L2 between timed steps (outside the events)
-            starts[i].record(stream)
-            op.forward_into(x, y)
-            ends[i].record(stream)
-        barrier()
+    for i in range(args.steps):
+        flush.fill_(float(i))  # evict L2 between timed steps (outside the events)
+        starts[i].record(stream)
+        op.forward_into(x, y)
+        ends[i].record(stream)
+    barrier()
+    clk.__exit__(None, None, None)
     launches = _lib.lib().va_launch_count() - lc0
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     ms = statistics.mean(step_ms)
@@ -201,7 +208,31 @@ def run_ours(args, ws, rank, local):
     # dominant kernel (flash attention) timed alone on the same stream
     dom = time_dominant(op, x, args, stream)
 
-    # end-to-end through the public API with host buffers
+    if args.no_e2e:
+        e2e_ms = float("nan")
+    else:
+        e2e_ms = time_e2e(op, x, y, args, stream, barrier)
+
+    t = torch.tensor([ms, e2e_ms, dom["ms"]], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, dom_ms = t.tolist()
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_sample()
+
+    if rank == 0:
+        emit(args, ws, B, ms, e2e_ms, dom, dom_ms, launches, cpu, clk, x, y)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def time_e2e(op, x, y, args, stream, barrier):
+    """Same metric through the public API with host buffers: every step copies
+    the batch from pinned host memory, runs the op and copies y back."""
+    import torch
     xh = x.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
     for _ in range(max(1, args.warmup)):
@@ -217,73 +248,86 @@ def run_ours(args, ws, rank, local):
         yh.copy_(y, non_blocking=True)
         e_e[i].record(stream)
     barrier()
-    e2e_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(e_s, e_e))
+    return statistics.mean(s.elapsed_time(e) for s, e in zip(e_s, e_e))
 
-    t = torch.tensor([ms, e2e_ms, dom["ms"]], device=dev, dtype=torch.float64)
-    if ws > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, dom_ms = t.tolist()
 
-    cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        v, dt = cpu_sample(2, threads)
-        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"2 images of 128x40x40 (one call, {dt:.2f} s), torch-CPU f32 restatement"}
+def cpu_baseline_sample():
+    """The torch-CPU f32 restatement on this host's cores: whole 64-image
+    batches, repeated until ≥10 s of CPU time."""
+    threads = os.cpu_count() or 1
+    tot_img, tot_s = 0, 0.0
+    while tot_s < 10.0:
+        v, dt = cpu_sample(B_PER_GPU, threads)
+        tot_img += B_PER_GPU
+        tot_s += dt
+    return {"value": tot_img / tot_s, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{tot_img} images of 128x40x40 in {tot_s:.1f} s (64-image calls), torch-CPU f32 "
+                      "restatement of the reference maths (the reference has no CPU path)"}
 
-    if rank == 0:
-        pk, src = peaks()
-        achieved = dom["flop"] / (dom_ms * 1e-3) / 1e12
-        peak = pk["bf16_tflops"]
-        line = {
-            "metric": METRIC, "value": B * ws / (ms * 1e-3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg2: C2PSA PSA attention fwd, 128x40x40 (1600 tokens), nh=2, kd=32, hd=64",
-                       "global_batch": B * ws, "per_gpu_batch": B, "seq_len": N_TOK,
-                       "parallelism": f"image shards x{ws}, no collective",
-                       "l2": "flushed between timed steps (256 MB write)"},
-            "e2e": {"value": B * ws / (e2e_ms * 1e-3), "unit": UNIT,
-                    "h2d_bytes_per_step": x.numel() * x.element_size(),
-                    "d2h_bytes_per_step": y.numel() * y.element_size()},
-            "gpu_launches": int(launches),
-            "roofline": {"bound": "tensor", "kernel": dom["name"], "achieved": achieved, "peak": peak,
-                         "unit": "TFLOP/s", "frac": achieved / peak, "peak_source": f"{src} bf16_tflops (burst)",
-                         "traffic": None, "flop_per_launch": dom["flop"], "ms_per_launch": dom_ms},
-            "cpu_baseline": cpu,
-            "clocks": clk.summary(),
-            "tflops_whole_op": FLOP_IMG * B / (ms * 1e-3) / 1e12,
-        }
-        print(json.dumps(line), flush=True)
-    if ws > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+
+def emit(args, ws, B, ms, e2e_ms, dom, dom_ms, launches, cpu, clk, x, y):
+    pk, src = peaks()
+    achieved = dom["flop"] / (dom_ms * 1e-3) / 1e12
+    peak = pk["bf16_tflops"]
+    line = {
+        "metric": METRIC, "value": B * ws / (ms * 1e-3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "cfg2: C2PSA PSA attention fwd, 128x40x40 (1600 tokens), nh=2, kd=32, hd=64",
+                   "global_batch": B * ws, "per_gpu_batch": B, "seq_len": N_TOK,
+                   "parallelism": f"image shards x{ws}, no collective",
+                   "l2": "flushed between timed steps (256 MB write)",
+                   "precision": "bf16 I/O and qkv GEMM; f16 attention operands; f32 accumulation"},
+        "e2e": None if math.isnan(e2e_ms) else {
+            "value": B * ws / (e2e_ms * 1e-3), "unit": UNIT,
+            "h2d_bytes_per_step": x.numel() * x.element_size(),
+            "d2h_bytes_per_step": y.numel() * y.element_size()},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "kernel": dom["name"], "achieved": achieved, "peak": peak,
+                     "unit": "TFLOP/s", "frac": achieved / peak, "peak_source": f"{src} bf16_tflops (burst)",
+                     "traffic": None, "flop_per_launch": dom["flop"], "ms_per_launch": dom_ms},
+        "cpu_baseline": cpu,
+        "clocks": clk.summary(),
+        "tflops_whole_op": FLOP_IMG * B / (ms * 1e-3) / 1e12,
+    }
+    print(json.dumps(line), flush=True)
 
 
 def time_dominant(op, x, args, stream):
-    """Average duration of the flash-attention kernel on this workload,
-    timed alone with CUDA events on the launching stream."""
+    """Average duration of the dominant kernel — the tcgen05 flash-attention
+    kernel — timed alone with CUDA events on the launching stream, on the
+    op's own intermediates (Q/K/V as the qkv kernel left them in the
+    workspace)."""
     import torch
-    from vision_rs_b200 import psa as vp
+    from vision_rs_b200 import _lib
     B = x.shape[0]
-    # the bf16 path's attention step: [BH, N, kd] flash attention, lo and hi halves
-    g = torch.Generator(device=x.device).manual_seed(7)
-    q = torch.randn(B * NH, N_TOK, KD, device=x.device, generator=g).bfloat16()
-    k = torch.randn_like(q)
-    v = torch.randn_like(q)
+    y = torch.empty_like(x)
+    op.forward_into(x, y)  # fills the workspace: qk at offset 0, then v, then o
+    ws = op.workspace(B, H, W, x.device)
+    Np = (N_TOK + 7) // 8 * 8
+    al = lambda n: (n + 255) // 256 * 256
+    qk_off = 0
+    v_off = qk_off + al(2 * B * NH * N_TOK * KD * 2)
+    o_off = v_off + al(B * C * Np * 2)
+    base = ws.data_ptr()
+    st = stream.cuda_stream
+    call = lambda: _lib.call("va_psa_flash_attention_fwd_f16", base + qk_off, base + v_off, base + o_off, None,
+                             B, NH, H, W, st)
     for _ in range(args.warmup):
-        vp.flash_attention2_forward(q, k, v)
+        call()
     torch.cuda.synchronize()
-    n = max(3, args.steps)
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record(stream)
-    for _ in range(n):
-        vp.flash_attention2_forward(q, k, v)
-    e.record(stream)
+    n = max(5, args.steps)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=x.device)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    for i in range(n):
+        flush.fill_(float(i))
+        evs[i][0].record(stream)
+        call()
+        evs[i][1].record(stream)
     torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / n
-    flop = 2 * B * NH * N_TOK * N_TOK * KD * 2  # QK^T + P·V_half per launch
-    return {"name": "flash_attention2_forward_bf16 (FFMA)", "ms": ms, "flop": flop}
+    ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    return {"name": "attn_kernel (tcgen05 flash attention, QK^T + PV, 64-wide V)", "ms": ms,
+            "flop": B * FLOP_ATTN_IMG}
 
 
 def main():
@@ -293,6 +337,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--min-warm-s", type=float, default=1.5,
+                    help="keep warming up at least this long so the clock sampler sees the load")
+    ap.add_argument("--batch", type=int, default=B_PER_GPU, help="per-GPU batch (profiling of smaller cases)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
