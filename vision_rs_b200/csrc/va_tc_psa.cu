@@ -385,6 +385,12 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
 }
 
 // ── Kernel 3: positional encoding + add + output projection ─────────────────
+// 256 threads.  Per 64-channel half, the tile's V rows plus one halo row above
+// and below are staged in shared memory with 16-byte loads; the 3×3 stencil
+// then reads shared memory only.
+constexpr int kProjThreads = 256;
+constexpr int kMaxW = 192;  // widest image row the staged-V layout supports
+
 struct ProjSmem {
   uint8_t a[2][kC * 128];   // (O+PE)ᵀ tile, MN-major SW128: 2 blocks of 64 tokens × 128 channel rows
   uint8_t w[2][kC * 128];   // W_proj f16, K-major SW128: 2 blocks of 64 in-channels × 128 rows
@@ -393,18 +399,27 @@ struct ProjSmem {
   uint64_t mma_bar;
   uint32_t tmem_base;
   int abort;
+  // followed by the staged V rows: [64 channels][vpitch] f16
 };
 
-__global__ void __launch_bounds__(128, 1)
+// f16 elements staged per channel for a 128-token tile of a W-wide image
+__host__ __device__ inline int proj_vpitch(int W) {
+  const int rows = (kTile + W - 1) / W + 3;
+  return ((rows * W + 8) + 7) / 8 * 8 + 8;
+}
+
+__global__ void __launch_bounds__(kProjThreads, 1)
 pe_proj_kernel(const __half* __restrict__ obuf, const __half* __restrict__ vbuf,
                const __nv_bfloat16* __restrict__ w_pe, const float* __restrict__ b_pe,
                const __nv_bfloat16* __restrict__ w_proj, const float* __restrict__ b_proj,
                __nv_bfloat16* __restrict__ y, int H, int W, int Np) {
   extern __shared__ uint8_t smem_raw[];
   ProjSmem& sm = *reinterpret_cast<ProjSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __half* vs = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(&sm) + ((sizeof(ProjSmem) + 15) & ~size_t(15)));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int N = H * W;
   const int n0 = blockIdx.x * kTile, b = blockIdx.y;
+  const int vpitch = proj_vpitch(W);
 
   if (tid == 0) {
     mbar_init(&sm.mma_bar, 1);
@@ -415,10 +430,10 @@ pe_proj_kernel(const __half* __restrict__ obuf, const __half* __restrict__ vbuf,
     tmem_alloc(&sm.tmem_base, 128);
     tmem_relinquish();
   }
-  for (int i = tid; i < kC * 9; i += 128) sm.wpe[i] = __bfloat162float(w_pe[i]);
-  for (int i = tid; i < kC; i += 128) sm.bpe[i] = b_pe[i];
+  for (int i = tid; i < kC * 9; i += kProjThreads) sm.wpe[i] = __bfloat162float(w_pe[i]);
+  for (int i = tid; i < kC; i += kProjThreads) sm.bpe[i] = b_pe[i];
   // W_proj (bf16, [out][in]) → f16 K-major SW128
-  for (int i = tid; i < kC * kC / 8; i += 128) {
+  for (int i = tid; i < kC * kC / 8; i += kProjThreads) {
     const int o = i / (kC / 8), chunk = i % (kC / 8);  // 16 chunks of 8 in-channels per row
     const uint4 src = __ldg(reinterpret_cast<const uint4*>(w_proj + (size_t)o * kC) + chunk);
     const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&src);
@@ -437,57 +452,76 @@ pe_proj_kernel(const __half* __restrict__ obuf, const __half* __restrict__ vbuf,
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  // A tile: item = (channel c, group g of 8 tokens)
+  // rows of the image this tile touches, plus one halo row on each side
+  const int nlast = min(n0 + kTile, N) - 1;
+  const int r_lo = max(0, n0 / W - 1), r_hi = min(H - 1, nlast / W + 1);
+  const int e0 = (r_lo * W) & ~7;                 // 16-byte aligned start of the staged run
+  const int e1 = min(Np, ((r_hi + 1) * W + 7) & ~7);
+  const int nchunk = (e1 - e0) >> 3;
+
   const __half* ob = obuf + (size_t)b * kC * Np;
   const __half* vb = vbuf + (size_t)b * kC * Np;
-  for (int it = tid; it < kC * (kTile / 8); it += 128) {
-    const int c = it / (kTile / 8), g = it % (kTile / 8);
-    const int nb = n0 + g * 8;
-    float acc[8];
-    if (nb + 8 <= Np) {
-      const uint4 ou = __ldg(reinterpret_cast<const uint4*>(ob + (size_t)c * Np + nb));
-      const __half2* o2 = reinterpret_cast<const __half2*>(&ou);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float2 f = __half22float2(o2[e]);
-        acc[2 * e] = f.x;
-        acc[2 * e + 1] = f.y;
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    const int cbase = half * 64;
+    // stage V[cbase .. cbase+64)[e0 .. e1) → vs[c][0 .. e1-e0)
+    for (int i = tid; i < 64 * nchunk; i += kProjThreads) {
+      const int c = i / nchunk, k = i - c * nchunk;
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(vb + (size_t)(cbase + c) * Np + e0) + k);
+      *reinterpret_cast<uint4*>(vs + c * vpitch + k * 8) = u;
     }
-    const float* wc = sm.wpe + c * 9;
-    const __half* vc = vb + (size_t)c * Np;
+    __syncthreads();
+    // items: (channel c of this half, group g of 8 tokens)
+    for (int it = tid; it < 64 * (kTile / 8); it += kProjThreads) {
+      const int cl = it >> 4, g = it & 15, c = cbase + cl;
+      const int nb = n0 + g * 8;
+      float acc[8];
+      if (nb < N) {
+        const uint4 ou = __ldg(reinterpret_cast<const uint4*>(ob + (size_t)c * Np + nb));
+        const __half2* o2 = reinterpret_cast<const __half2*>(&ou);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int n = nb + e;
-      if (n >= N) {
-        acc[e] = 0.f;
-        continue;
-      }
-      const int i = n / W, jj = n - i * W;
-      float pe = sm.bpe[c];
-#pragma unroll
-      for (int di = 0; di < 3; ++di) {
-        const int ii = i + di - 1;
-        if (ii < 0 || ii >= H) continue;
-#pragma unroll
-        for (int dj = 0; dj < 3; ++dj) {
-          const int j2 = jj + dj - 1;
-          if (j2 < 0 || j2 >= W) continue;
-          pe = fmaf(wc[di * 3 + dj], __half2float(vc[ii * W + j2]), pe);
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(o2[e]);
+          acc[2 * e] = f.x;
+          acc[2 * e + 1] = f.y;
         }
       }
-      acc[e] += pe;
+      const float* wc = sm.wpe + c * 9;
+      const float bias = sm.bpe[c];
+      const __half* vc = vs + cl * vpitch - e0;   // vc[n] = V[c][n] for staged n
+      int i = nb / W, j = nb - (nb / W) * W;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int n = nb + e;
+        if (n < N) {
+          float pe = bias;
+#pragma unroll
+          for (int di = 0; di < 3; ++di) {
+            const int ii = i + di - 1;
+            if (ii < 0 || ii >= H) continue;
+            const __half* vr = vc + ii * W;
+#pragma unroll
+            for (int dj = 0; dj < 3; ++dj) {
+              const int j2 = j + dj - 1;
+              if (j2 < 0 || j2 >= W) continue;
+              pe = fmaf(wc[di * 3 + dj], __half2float(vr[j2]), pe);
+            }
+          }
+          acc[e] += pe;
+        } else {
+          acc[e] = 0.f;
+        }
+        if (++j == W) { j = 0; ++i; }
+      }
+      uint4 u;
+      u.x = pack_f16x2_sat(acc[0], acc[1]);
+      u.y = pack_f16x2_sat(acc[2], acc[3]);
+      u.z = pack_f16x2_sat(acc[4], acc[5]);
+      u.w = pack_f16x2_sat(acc[6], acc[7]);
+      const int blk = g >> 3, ch = g & 7;
+      *reinterpret_cast<uint4*>(sm.a[blk] + c * 128 + ((ch ^ (c & 7)) << 4)) = u;
     }
-    uint4 u;
-    u.x = pack_f16x2_sat(acc[0], acc[1]);
-    u.y = pack_f16x2_sat(acc[2], acc[3]);
-    u.z = pack_f16x2_sat(acc[4], acc[5]);
-    u.w = pack_f16x2_sat(acc[6], acc[7]);
-    const int blk = g >> 3, ch = g & 7;
-    *reinterpret_cast<uint4*>(sm.a[blk] + c * 128 + ((ch ^ (c & 7)) << 4)) = u;
+    __syncthreads();
   }
   fence_proxy_async_smem();
   __syncthreads();
@@ -507,16 +541,19 @@ pe_proj_kernel(const __half* __restrict__ obuf, const __half* __restrict__ vbuf,
   const bool ok = mbar_wait(&sm.mma_bar, 0, &sm.abort, &g_tc_status, 30);
   tc_fence_after();
   if (ok) {
-    const int n = n0 + warp * 32 + lane;
+    // warp w reads TMEM lanes 32*(w%4) (its sub-partition), columns (w/4)*64 .. +64
+    const int n = n0 + (warp & 3) * 32 + lane;
 #pragma unroll 1
-    for (int c = 0; c < kC / 32; ++c) {
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c = (warp >> 2) * 2 + cc;
       uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
+      tmem_ld32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + c * 32, r);
       tmem_ld_wait();
       if (n < N) {
         __nv_bfloat16* dst = y + ((size_t)b * kC + c * 32) * N + n;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) dst[(size_t)i * N] = __float2bfloat16_rn(__uint_as_float(r[i]) + __ldg(b_proj + c * 32 + i));
+        for (int i = 0; i < 32; ++i)
+          dst[(size_t)i * N] = __float2bfloat16_rn(__uint_as_float(r[i]) + __ldg(b_proj + c * 32 + i));
       }
     }
   }
@@ -597,6 +634,7 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
                          void* ws, size_t ws_bytes, cudaStream_t st, float* lse_out) {
   VA_CHECK_ARG(psa_tc_supported(C, nh, kd), "psa_attention bf16: tensor-core path needs C=128, nh=2, kd=32");
   VA_CHECK_ARG(B > 0 && H > 0 && W > 0 && B <= 65535, "psa_attention bf16: bad sizes");
+  VA_CHECK_ARG(W <= kMaxW, "psa_attention bf16: image width %d > %d unsupported", W, kMaxW);
   const TcWs L = tc_layout(B, H, W, nh);
   if (!ws || ws_bytes < L.total)
     return set_error(VA_ERR_WORKSPACE, "psa_attention bf16: workspace %zu < %zu bytes", ws_bytes, L.total);
@@ -643,12 +681,14 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
       return rc;
   }
   const int ntile = (N + kTile - 1) / kTile;
-  const size_t sm1 = sizeof(QkvSmem) + 1024, sm2 = sizeof(AttnSmem) + 1024, sm3 = sizeof(ProjSmem) + 1024;
+  const size_t sm1 = sizeof(QkvSmem) + 1024, sm2 = sizeof(AttnSmem) + 1024;
+  const size_t sm3 = ((sizeof(ProjSmem) + 15) & ~size_t(15)) + (size_t)64 * proj_vpitch(W) * 2 + 1024;
   static bool attr_done = false;
   if (!attr_done) {
     if (int rc = set_smem(qkv_proj_kernel, sm1)) return rc;
     if (int rc = set_smem(attn_kernel, sm2)) return rc;
-    if (int rc = set_smem(pe_proj_kernel, sm3)) return rc;
+    if (int rc = set_smem(pe_proj_kernel, ((sizeof(ProjSmem) + 15) & ~size_t(15)) + 64 * proj_vpitch(kMaxW) * 2 + 1024))
+      return rc;
     attr_done = true;
   }
   qkv_proj_kernel<<<dim3(ntile, B), 128, sm1, st>>>(mx, mw, b_qkv, qk, vb, N, Np, nh);
@@ -656,7 +696,7 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   const float scale_log2 = (1.0f / sqrtf((float)kd)) * 1.4426950408889634f;
   attn_kernel<<<dim3(ntile, BH), kAttnThreads, sm2, st>>>(mqk, mv, ob, lse_out, N, Np, nh, scale_log2);
   if (int rc = check_launch("psa attention")) return rc;
-  pe_proj_kernel<<<dim3(ntile, B), 128, sm3, st>>>(ob, vb, w_pe, b_pe, w_proj, b_proj, y, H, W, Np);
+  pe_proj_kernel<<<dim3(ntile, B), kProjThreads, sm3, st>>>(ob, vb, w_pe, b_pe, w_proj, b_proj, y, H, W, Np);
   return check_launch("psa pe_proj");
 }
 
