@@ -116,6 +116,7 @@ qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
       uint32_t r[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
       tmem_ld_wait();
+      reg_fence(r);
       const int h = c >> 2, sec = c & 3;
       float v[32];
 #pragma unroll
@@ -151,18 +152,32 @@ qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
 }
 
 // ── Kernel 2: flash attention ───────────────────────────────────────────────
+// One CTA = two 128-query tiles of one (b, h), sharing every K/V tile.
+//   warps 0-3: softmax for query tile 0, warps 4-7: query tile 1 (thread =
+//              query row = TMEM lane); warp 8 lane 0: TMA producer + MMA issuer.
+// TMEM (512 columns): S_i = Q_i·Kᵀ at cols 128·i (f32), overwritten in place
+// by P_i as packed f16 (64 cols) which the P·V MMA reads as its A operand
+// straight from TMEM; O_i at 256 + 80·i: 64 output columns plus column 64 =
+// Σ_k P (V carries a row of ones), so the row sum comes out of the tensor
+// core already consistent with the f16 P it multiplied.
+// The two softmax warpgroups run ping-pong against the MMA pipe: the issuer
+// starts S_0(j+1) as soon as P_0(j)·V is queued, while group 1 still works
+// on tile j.
+constexpr int kStages = 4;
+constexpr int kVRows = 80;                 // 64 V channels + ones row + 15 zero rows (UMMA N = 80)
+constexpr int kVBlk = kVRows * 128;        // one 64-key block of the V operand (10 KB)
+constexpr int kAttnThreads = 288;
+__device__ __forceinline__ uint32_t col_s(int i) { return (uint32_t)i * 128u; }        // S_i / P_i
+__device__ __forceinline__ uint32_t col_o(int i) { return 256u + (uint32_t)i * 80u; }  // O_i (+ row sum at +64)
+
 struct AttnSmem {
-  uint8_t q[kTile * 64];           // Q tile [128 rows × 32] f16, K-major SW64 (8 KB)
-  uint8_t k[2][kTile * 64];        // K tiles, 2 stages (8 KB each)
-  uint8_t v[2][2][kHD * 128];      // V tiles: stage × key-block (64 keys) × [64 ch rows × 128 B] SW128
-  uint8_t p[2][kTile * 128];       // P [128 rows × 128 keys] f16, K-major SW128: 2 key-blocks × 16 KB
-  uint64_t q_full, kv_full[2], kv_empty[2], s_full, s_free, p_full, o_done, fin;
+  uint8_t q[2][kTile * 64];                // Q tiles [128 rows × 32] f16, K-major SW64 (8 KB each)
+  uint8_t k[kStages][kTile * 64];          // K tiles (8 KB each)
+  uint8_t v[kStages][2][kVBlk];            // V: stage × key-block; rows 0-63 by TMA, 64 = ones, 65-79 = 0
+  uint64_t q_full, kv_full[kStages], kv_empty[kStages], s_full[2], p_full[2], o_done[2], fin;
   uint32_t tmem_base;
   int abort;
 };
-
-constexpr int kAttnThreads = 160;  // warps 0-3: softmax (one thread per query row); warp 4: TMA + MMA issue
-constexpr uint32_t kColS = 0, kColO = 128;
 
 __device__ __forceinline__ void attn_load_kv(AttnSmem& sm, const CUtensorMap* mqk, const CUtensorMap* mv, int t,
                                              int stage, int BH, int bh, int vrow) {
@@ -172,33 +187,42 @@ __device__ __forceinline__ void attn_load_kv(AttnSmem& sm, const CUtensorMap* mq
   tma_load_2d(sm.v[stage][1], mv, &sm.kv_full[stage], t * kTile + 64, vrow);
 }
 
-__global__ void __launch_bounds__(kAttnThreads, 2)
+__global__ void __launch_bounds__(kAttnThreads, 1)
 attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v,
             __half* __restrict__ obuf, float* __restrict__ lse, int N, int Np, int nh, float scale_log2) {
   extern __shared__ uint8_t smem_raw[];
   AttnSmem& sm = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int q0 = blockIdx.x * kTile, bh = blockIdx.y;
+  const int q0 = blockIdx.x * 2 * kTile, bh = blockIdx.y;
   const int BH = gridDim.y, b = bh / nh, h = bh % nh;
   const int nkv = (N + kTile - 1) / kTile;
+  const bool has1 = q0 + kTile < N;
   const int vrow = b * kC + h * kHD;
 
   if (tid == 0) {
     mbar_init(&sm.q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.kv_full[i], 1);
       mbar_init(&sm.kv_empty[i], 1);
     }
-    mbar_init(&sm.s_full, 1);
-    mbar_init(&sm.s_free, 128);
-    mbar_init(&sm.p_full, 128);
-    mbar_init(&sm.o_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.s_full[i], 1);
+      mbar_init(&sm.p_full[i], 128);
+      mbar_init(&sm.o_done[i], 1);
+    }
     mbar_init(&sm.fin, 1);
     sm.abort = 0;
     fence_mbar_init();
   }
+  // constant rows 64..79 of every V block: row 64 = 1.0 (f16 0x3C00), the rest 0
+  for (int i = tid; i < kStages * 2 * 16 * 8; i += kAttnThreads) {
+    const int blk = i >> 7, rr = (i >> 3) & 15, ch = i & 7;
+    const uint32_t val = rr == 0 ? 0x3C003C00u : 0u;
+    *reinterpret_cast<uint4*>(&sm.v[0][0][0] + blk * kVBlk + (64 + rr) * 128 + ch * 16) = make_uint4(val, val, val, val);
+  }
+  fence_proxy_async_smem();
   if (warp == 0) {
-    tmem_alloc(&sm.tmem_base, 256);
+    tmem_alloc(&sm.tmem_base, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -206,67 +230,82 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       // ── control thread: TMA producer and MMA issuer ──
-      int issued = 0;  // KV tiles whose loads were issued
       tma_prefetch_desc(&map_qk);
       tma_prefetch_desc(&map_v);
-      mbar_arrive_expect_tx(&sm.q_full, kTile * 64);
-      tma_load_3d(sm.q, &map_qk, &sm.q_full, 0, q0, bh);
-      for (; issued < 2 && issued < nkv; ++issued) attn_load_kv(sm, &map_qk, &map_v, issued, issued, BH, bh, vrow);
+      mbar_arrive_expect_tx(&sm.q_full, (has1 ? 2 : 1) * kTile * 64);
+      tma_load_3d(sm.q[0], &map_qk, &sm.q_full, 0, q0, bh);
+      if (has1) tma_load_3d(sm.q[1], &map_qk, &sm.q_full, 0, q0 + kTile, bh);
+      int issued = 0;
+      for (; issued < kStages && issued < nkv; ++issued)
+        attn_load_kv(sm, &map_qk, &map_v, issued, issued, BH, bh, vrow);
 
       constexpr uint32_t idS = idesc_f32acc(128, kTile, AB_F16, false, false);
-      constexpr uint32_t idO = idesc_f32acc(128, kHD, AB_F16, false, false);
-      const uint32_t qa = smem_u32(sm.q), pa = smem_u32(sm.p[0]);
-      auto issue_s = [&](int stage) {
-        const uint32_t ka = smem_u32(sm.k[stage]);
+      constexpr uint32_t idO = idesc_f32acc(128, kVRows, AB_F16, false, false);
+      auto issue_s = [&](int i, int stage) {
+        const uint32_t qa = smem_u32(sm.q[i]), ka = smem_u32(sm.k[stage]);
 #pragma unroll
         for (int s = 0; s < kKD / 16; ++s)
-          mma_ss(tmem + kColS, sdesc(qa + s * 32, 16, 512, SW_64B), sdesc(ka + s * 32, 16, 512, SW_64B), idS, s > 0);
+          mma_ss(tmem + col_s(i), sdesc(qa + s * 32, 16, 512, SW_64B), sdesc(ka + s * 32, 16, 512, SW_64B), idS,
+                 s > 0);
       };
-      auto issue_o = [&](int stage, bool acc) {
+      auto issue_o = [&](int i, int stage, bool acc) {
         const uint32_t va0 = smem_u32(sm.v[stage][0]);
 #pragma unroll
-        for (int s = 0; s < kTile / 16; ++s) {
-          uint64_t ad = sdesc(pa + (s >> 2) * (kTile * 128) + (s & 3) * 32, 16, 1024, SW_128B);
-          uint64_t bd = sdesc(va0 + (s >> 2) * (kHD * 128) + (s & 3) * 32, 16, 1024, SW_128B);
-          mma_ss(tmem + kColO, ad, bd, idO, (acc || s > 0) ? 1u : 0u);
-        }
+        for (int s = 0; s < kTile / 16; ++s)
+          mma_ts(tmem + col_o(i), tmem + col_s(i) + s * 8,
+                 sdesc(va0 + (s >> 2) * kVBlk + (s & 3) * 32, 16, 1024, SW_128B), idO, (acc || s > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(&sm.q_full, 0, &sm.abort, &g_tc_status, 10) &&
                 mbar_wait(&sm.kv_full[0], 0, &sm.abort, &g_tc_status, 11);
-      int consumed = ok ? 1 : 0;  // KV tiles whose full barrier was observed
+      int consumed = ok ? 1 : 0;
       if (ok) {
         tc_fence_after();
-        issue_s(0);
-        mma_commit(&sm.s_full);
+        issue_s(0, 0);
+        mma_commit(&sm.s_full[0]);
+        if (has1) {
+          issue_s(1, 0);
+          mma_commit(&sm.s_full[1]);
+        }
       }
       for (int j = 0; ok && j < nkv; ++j) {
+        const int st = j % kStages, stn = (j + 1) % kStages;
+        if (!(ok = mbar_wait(&sm.p_full[0], j & 1, &sm.abort, &g_tc_status, 12))) break;
+        tc_fence_after();
+        issue_o(0, st, j > 0);
+        mma_commit(&sm.o_done[0]);
         if (j + 1 < nkv) {
-          ok = mbar_wait(&sm.kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, &sm.abort, &g_tc_status, 12) &&
-               mbar_wait(&sm.s_free, j & 1, &sm.abort, &g_tc_status, 13);
-          if (!ok) break;
+          if (!(ok = mbar_wait(&sm.kv_full[stn], ((j + 1) / kStages) & 1, &sm.abort, &g_tc_status, 13))) break;
           consumed = j + 2;
           tc_fence_after();
-          issue_s((j + 1) & 1);
-          mma_commit(&sm.s_full);
+          issue_s(0, stn);
+          mma_commit(&sm.s_full[0]);
         }
-        if (!(ok = mbar_wait(&sm.p_full, j & 1, &sm.abort, &g_tc_status, 14))) break;
-        tc_fence_after();
-        issue_o(j & 1, j > 0);
-        mma_commit(&sm.o_done);
-        mma_commit(&sm.kv_empty[j & 1]);
-        if (j + 2 < nkv) {
-          if (!(ok = mbar_wait(&sm.kv_empty[j & 1], (j >> 1) & 1, &sm.abort, &g_tc_status, 15))) break;
-          attn_load_kv(sm, &map_qk, &map_v, j + 2, j & 1, BH, bh, vrow);
+        if (has1) {
+          if (!(ok = mbar_wait(&sm.p_full[1], j & 1, &sm.abort, &g_tc_status, 14))) break;
+          tc_fence_after();
+          issue_o(1, st, j > 0);
+          mma_commit(&sm.o_done[1]);
+          if (j + 1 < nkv) {
+            issue_s(1, stn);
+            mma_commit(&sm.s_full[1]);
+          }
+        }
+        mma_commit(&sm.kv_empty[st]);
+        // refill the stage tile j-1 used (its MMAs finished long ago) with tile j+3
+        if (j >= 1 && j + kStages - 1 < nkv) {
+          const int sp = (j - 1) % kStages;
+          if (!(ok = mbar_wait(&sm.kv_empty[sp], ((j - 1) / kStages) & 1, &sm.abort, &g_tc_status, 15))) break;
+          attn_load_kv(sm, &map_qk, &map_v, j + kStages - 1, sp, BH, bh, vrow);
           ++issued;
         }
       }
       // teardown: every issued TMA load has landed and every MMA has completed
       for (int t = consumed; t < issued; ++t) {
         const long long t0 = clock64();
-        while (!mbar_try_wait(&sm.kv_full[t & 1], (t >> 1) & 1) && clock64() - t0 < kSpinCycles) {
+        while (!mbar_try_wait(&sm.kv_full[t % kStages], (t / kStages) & 1) && clock64() - t0 < kSpinCycles) {
         }
       }
       if (!ok) {
@@ -280,100 +319,110 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       }
     }
     __syncwarp();
-  } else {
-    // ── softmax warps: thread = query row (TMEM lane) ──
-    const int row = tid;  // 0..127
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    float m = -INFINITY, l = 0.f;
+  } else if (warp < 4 || has1) {
+    // ── softmax warpgroup g: thread = query row (TMEM lane) ──
+    const int g = warp >> 2, row = tid & 127;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t sc = tmem + lane_off + col_s(g), oc = tmem + lane_off + col_o(g);
+    float m = -INFINITY;
     bool ok = true;
-    uint8_t* prow0 = sm.p[0] + row * 128;
-    uint8_t* prow1 = sm.p[1] + row * 128;
-    const int rsw = row & 7;
     for (int j = 0; j < nkv; ++j) {
-      if (!(ok = mbar_wait(&sm.s_full, j & 1, &sm.abort, &g_tc_status, 20))) break;
+      if (!(ok = mbar_wait(&sm.s_full[g], j & 1, &sm.abort, &g_tc_status, 20 + g))) break;
       tc_fence_after();
-      float x[kTile];
-#pragma unroll
-      for (int c = 0; c < kTile / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_off + kColS + c * 32, r);
+      float sv[kTile];
+      {
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld32(sc + 0, r0);
+        tmem_ld32(sc + 32, r1);
+        tmem_ld32(sc + 64, r2);
+        tmem_ld32(sc + 96, r3);
         tmem_ld_wait();
+        reg_fence(r0);
+        reg_fence(r1);
+        reg_fence(r2);
+        reg_fence(r3);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[i]) * scale_log2;
+        for (int i = 0; i < 32; ++i) {
+          sv[i] = __uint_as_float(r0[i]);
+          sv[32 + i] = __uint_as_float(r1[i]);
+          sv[64 + i] = __uint_as_float(r2[i]);
+          sv[96 + i] = __uint_as_float(r3[i]);
+        }
       }
-      tc_fence_before();
-      mbar_arrive(&sm.s_free);
       const int kvalid = N - j * kTile;
       if (kvalid < kTile) {
 #pragma unroll
         for (int i = 0; i < kTile; ++i)
-          if (i >= kvalid) x[i] = -INFINITY;
+          if (i >= kvalid) sv[i] = -INFINITY;
       }
-      float mx = x[0];
+      float mx[8];
 #pragma unroll
-      for (int i = 1; i < kTile; ++i) mx = fmaxf(mx, x[i]);
-      const float m_new = fmaxf(m, mx);
-      // Rescale only when the running max grew by more than 2^8 (the stale
-      // max keeps p ≤ 256, exact after the final 1/l normalisation).
+      for (int u = 0; u < 8; ++u) mx[u] = max3(sv[u], sv[8 + u], sv[16 + u]);
+#pragma unroll
+      for (int i = 24; i + 16 <= kTile; i += 16)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mx[u] = max3(mx[u], sv[i + u], sv[i + 8 + u]);
+      mx[0] = max3(mx[0], mx[1], mx[2]);
+      mx[3] = max3(mx[3], mx[4], mx[5]);
+      mx[6] = max3(mx[6], mx[7], sv[kTile - 8]);  // kTile-8.. covered by the loop up to i=120; harmless repeat
+      const float m_new = fmaxf(m, max3(mx[0], mx[3], mx[6]) * scale_log2);
+      // Rescale only when the running max grew by more than 2^8 (the stale max
+      // keeps P ≤ 256; exact after the final division by the row sum).
       const bool resc = (j == 0) || (m_new > m + 8.0f);
       const float m_use = resc ? m_new : m;
-      const float alpha = resc ? ex2(m - m_use) : 1.0f;
       if (j > 0) {
-        if (!(ok = mbar_wait(&sm.o_done, (j - 1) & 1, &sm.abort, &g_tc_status, 21))) break;
+        if (!(ok = mbar_wait(&sm.o_done[g], (j - 1) & 1, &sm.abort, &g_tc_status, 22 + g))) break;
         tc_fence_after();
         if (__any_sync(0xffffffffu, resc)) {
-#pragma unroll
-          for (int c = 0; c < kHD / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tmem + lane_off + kColO + c * 32, r);
+          const float alpha = resc ? ex2(m - m_use) : 1.0f;
+#pragma unroll 1
+          for (int c = 0; c < kVRows / 16; ++c) {  // 64 outputs + row sum (+ zero columns)
+            uint32_t o16[16];
+            tmem_ld16(oc + c * 16, o16);
             tmem_ld_wait();
+            reg_fence(o16);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(tmem + lane_off + kColO + c * 32, r);
+            for (int i = 0; i < 16; ++i) o16[i] = __float_as_uint(__uint_as_float(o16[i]) * alpha);
+            tmem_st16(oc + c * 16, o16);
           }
           tmem_st_wait();
         }
       }
-      float rs = 0.f;
+      const float nm = -m_use;
 #pragma unroll
-      for (int c = 0; c < kTile / 8; ++c) {  // 16 chunks of 8 keys = 16 bytes of f16
-        float p[8];
+      for (int c = 0; c < kTile / 32; ++c) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          p[e] = ex2(x[c * 8 + e] - m_use);
-          rs += p[e];
-        }
-        uint4 u;
-        u.x = pack_f16x2_sat(p[0], p[1]);
-        u.y = pack_f16x2_sat(p[2], p[3]);
-        u.z = pack_f16x2_sat(p[4], p[5]);
-        u.w = pack_f16x2_sat(p[6], p[7]);
-        uint8_t* base = (c < 8) ? prow0 : prow1;
-        *reinterpret_cast<uint4*>(base + (((c & 7) ^ rsw) << 4)) = u;
+        for (int e = 0; e < 16; ++e)
+          pk[e] = pack_f16x2(ex2(fmaf(sv[c * 32 + 2 * e], scale_log2, nm)),
+                             ex2(fmaf(sv[c * 32 + 2 * e + 1], scale_log2, nm)));
+        tmem_st16(sc + c * 16, pk);
       }
-      l = l * alpha + rs;
+      tmem_st_wait();
       m = m_use;
-      fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&sm.p_full);
+      mbar_arrive(&sm.p_full[g]);
     }
-    if (ok) ok = mbar_wait(&sm.o_done, (nkv - 1) & 1, &sm.abort, &g_tc_status, 22);
+    if (ok) ok = mbar_wait(&sm.o_done[g], (nkv - 1) & 1, &sm.abort, &g_tc_status, 24 + g);
     if (ok) {
       tc_fence_after();
-      const int n = q0 + row;
+      const int n = q0 + g * kTile + row;
+      uint32_t o16[16];
+      tmem_ld16(oc + 64, o16);
+      tmem_ld_wait();
+      reg_fence(o16);
+      const float l = __uint_as_float(o16[0]);
       const float inv = 1.0f / l;
 #pragma unroll
       for (int c = 0; c < kHD / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_off + kColO + c * 32, r);
+        uint32_t o[32];
+        tmem_ld32(oc + c * 32, o);
         tmem_ld_wait();
+        reg_fence(o);
         if (n < N) {
           __half* dst = obuf + ((size_t)b * kC + h * kHD + c * 32) * Np + n;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            uint32_t pk = pack_f16x2_sat(__uint_as_float(r[i]) * inv, 0.f);
-            dst[(size_t)i * Np] = __ushort_as_half((unsigned short)(pk & 0xFFFF));
-          }
+          for (int i = 0; i < 32; ++i) dst[(size_t)i * Np] = __float2half_rn(__uint_as_float(o[i]) * inv);
         }
       }
       if (lse && n < N) lse[(size_t)bh * N + n] = (m + __log2f(l)) * 0.6931471805599453f;
@@ -381,7 +430,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 256);
+  if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 // ── Kernel 3: positional encoding + add + output projection ─────────────────
@@ -549,6 +598,7 @@ pe_proj_kernel(const __half* __restrict__ obuf, const __half* __restrict__ vbuf,
       uint32_t r[32];
       tmem_ld32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + c * 32, r);
       tmem_ld_wait();
+      reg_fence(r);
       if (n < N) {
         __nv_bfloat16* dst = y + ((size_t)b * kC + c * 32) * N + n;
 #pragma unroll
@@ -694,7 +744,7 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   qkv_proj_kernel<<<dim3(ntile, B), 128, sm1, st>>>(mx, mw, b_qkv, qk, vb, N, Np, nh);
   if (int rc = check_launch("psa qkv_proj")) return rc;
   const float scale_log2 = (1.0f / sqrtf((float)kd)) * 1.4426950408889634f;
-  attn_kernel<<<dim3(ntile, BH), kAttnThreads, sm2, st>>>(mqk, mv, ob, lse_out, N, Np, nh, scale_log2);
+  attn_kernel<<<dim3((ntile + 1) / 2, BH), kAttnThreads, sm2, st>>>(mqk, mv, ob, lse_out, N, Np, nh, scale_log2);
   if (int rc = check_launch("psa attention")) return rc;
   pe_proj_kernel<<<dim3(ntile, B), kProjThreads, sm3, st>>>(ob, vb, w_pe, b_pe, w_proj, b_proj, y, H, W, Np);
   return check_launch("psa pe_proj");
@@ -741,8 +791,9 @@ int psa_attention_core_tc(const void* qk, const void* v, void* o, float* lse, in
   const size_t sm2 = sizeof(AttnSmem) + 1024;
   if (int rc = set_smem(attn_kernel, sm2)) return rc;
   const float scale_log2 = (1.0f / sqrtf((float)kKD)) * 1.4426950408889634f;
-  attn_kernel<<<dim3((N + kTile - 1) / kTile, BH), kAttnThreads, sm2, st>>>(mqk, mv, static_cast<__half*>(o), lse, N,
-                                                                            Np, nh, scale_log2);
+  const int ntile = (N + kTile - 1) / kTile;
+  attn_kernel<<<dim3((ntile + 1) / 2, BH), kAttnThreads, sm2, st>>>(mqk, mv, static_cast<__half*>(o), lse, N, Np, nh,
+                                                                    scale_log2);
   return check_launch("psa flash attention");
 }
 
