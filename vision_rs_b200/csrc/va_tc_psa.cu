@@ -155,33 +155,31 @@ qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
 // One CTA = two 128-query tiles of one (b, h), sharing every K/V tile.
 //   warps 0-3: softmax for query tile 0, warps 4-7: query tile 1 (thread =
 //              query row = TMEM lane); warp 8 lane 0: TMA producer + MMA issuer.
-// TMEM (512 columns): S_i = Q_i·Kᵀ at cols 128·i (f32), overwritten in place
-// by P_i as packed f16 (64 cols) which the P·V MMA reads as its A operand
-// straight from TMEM; O_i at 256 + 80·i: 64 output columns plus column 64 =
-// Σ_k P (V carries a row of ones), so the row sum comes out of the tensor
-// core already consistent with the f16 P it multiplied.
-// The two softmax warpgroups run ping-pong against the MMA pipe: the issuer
-// starts S_0(j+1) as soon as P_0(j)·V is queued, while group 1 still works
-// on tile j.
+// TMEM (512 columns), per query tile g at 256·g: S (f32, 128 cols), P (packed
+// f16, 64 cols) read by the P·V MMA as its A operand straight from TMEM, and
+// O (f32, 64 cols).  Because P has its own columns, S(j+1) = Q·K(j+1)ᵀ is
+// issued as soon as the softmax has copied S(j) into registers, so the next
+// tile's scores are ready when the exponentials of this one are done.
 constexpr int kStages = 4;
-constexpr int kVRows = 80;                 // 64 V channels + ones row + 15 zero rows (UMMA N = 80)
-constexpr int kVBlk = kVRows * 128;        // one 64-key block of the V operand (10 KB)
+constexpr int kVBlk = kHD * 128;           // one 64-key block of V: [64 channel rows × 128 B] SW128 (8 KB)
 constexpr int kAttnThreads = 288;
-__device__ __forceinline__ uint32_t col_s(int i) { return (uint32_t)i * 128u; }        // S_i / P_i
-__device__ __forceinline__ uint32_t col_o(int i) { return 256u + (uint32_t)i * 80u; }  // O_i (+ row sum at +64)
+
+__device__ __forceinline__ uint32_t col_s(int g) { return (uint32_t)g * 256u; }
+__device__ __forceinline__ uint32_t col_p(int g) { return (uint32_t)g * 256u + 128u; }
+__device__ __forceinline__ uint32_t col_o(int g) { return (uint32_t)g * 256u + 192u; }
 
 struct AttnSmem {
   uint8_t q[2][kTile * 64];                // Q tiles [128 rows × 32] f16, K-major SW64 (8 KB each)
   uint8_t k[kStages][kTile * 64];          // K tiles (8 KB each)
-  uint8_t v[kStages][2][kVBlk];            // V: stage × key-block; rows 0-63 by TMA, 64 = ones, 65-79 = 0
-  uint64_t q_full, kv_full[kStages], kv_empty[kStages], s_full[2], p_full[2], o_done[2], fin;
+  uint8_t v[kStages][2][kVBlk];            // V: stage × key-block
+  uint64_t q_full, kv_full[kStages], kv_empty[kStages], s_full[2], s_free[2], p_full[2], o_done[2], fin;
   uint32_t tmem_base;
   int abort;
 };
 
 __device__ __forceinline__ void attn_load_kv(AttnSmem& sm, const CUtensorMap* mqk, const CUtensorMap* mv, int t,
                                              int stage, int BH, int bh, int vrow) {
-  mbar_arrive_expect_tx(&sm.kv_full[stage], kTile * 64 + 2 * kHD * 128);
+  mbar_arrive_expect_tx(&sm.kv_full[stage], kTile * 64 + 2 * kVBlk);
   tma_load_3d(sm.k[stage], mqk, &sm.kv_full[stage], 0, t * kTile, BH + bh);
   tma_load_2d(sm.v[stage][0], mv, &sm.kv_full[stage], t * kTile, vrow);
   tma_load_2d(sm.v[stage][1], mv, &sm.kv_full[stage], t * kTile + 64, vrow);
@@ -207,6 +205,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.s_full[i], 1);
+      mbar_init(&sm.s_free[i], 128);
       mbar_init(&sm.p_full[i], 128);
       mbar_init(&sm.o_done[i], 1);
     }
@@ -214,13 +213,6 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
     sm.abort = 0;
     fence_mbar_init();
   }
-  // constant rows 64..79 of every V block: row 64 = 1.0 (f16 0x3C00), the rest 0
-  for (int i = tid; i < kStages * 2 * 16 * 8; i += kAttnThreads) {
-    const int blk = i >> 7, rr = (i >> 3) & 15, ch = i & 7;
-    const uint32_t val = rr == 0 ? 0x3C003C00u : 0u;
-    *reinterpret_cast<uint4*>(&sm.v[0][0][0] + blk * kVBlk + (64 + rr) * 128 + ch * 16) = make_uint4(val, val, val, val);
-  }
-  fence_proxy_async_smem();
   if (warp == 0) {
     tmem_alloc(&sm.tmem_base, 512);
     tmem_relinquish();
@@ -243,19 +235,20 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
         attn_load_kv(sm, &map_qk, &map_v, issued, issued, BH, bh, vrow);
 
       constexpr uint32_t idS = idesc_f32acc(128, kTile, AB_F16, false, false);
-      constexpr uint32_t idO = idesc_f32acc(128, kVRows, AB_F16, false, false);
-      auto issue_s = [&](int i, int stage) {
-        const uint32_t qa = smem_u32(sm.q[i]), ka = smem_u32(sm.k[stage]);
+      constexpr uint32_t idO = idesc_f32acc(128, kHD, AB_F16, false, false);
+      const int ng = has1 ? 2 : 1;
+      auto issue_s = [&](int g, int stage) {
+        const uint32_t qa = smem_u32(sm.q[g]), ka = smem_u32(sm.k[stage]);
 #pragma unroll
         for (int s = 0; s < kKD / 16; ++s)
-          mma_ss(tmem + col_s(i), sdesc(qa + s * 32, 16, 512, SW_64B), sdesc(ka + s * 32, 16, 512, SW_64B), idS,
+          mma_ss(tmem + col_s(g), sdesc(qa + s * 32, 16, 512, SW_64B), sdesc(ka + s * 32, 16, 512, SW_64B), idS,
                  s > 0);
       };
-      auto issue_o = [&](int i, int stage, bool acc) {
+      auto issue_o = [&](int g, int stage, bool acc) {
         const uint32_t va0 = smem_u32(sm.v[stage][0]);
 #pragma unroll
         for (int s = 0; s < kTile / 16; ++s)
-          mma_ts(tmem + col_o(i), tmem + col_s(i) + s * 8,
+          mma_ts(tmem + col_o(g), tmem + col_p(g) + s * 8,
                  sdesc(va0 + (s >> 2) * kVBlk + (s & 3) * 32, 16, 1024, SW_128B), idO, (acc || s > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(&sm.q_full, 0, &sm.abort, &g_tc_status, 10) &&
@@ -263,36 +256,31 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       int consumed = ok ? 1 : 0;
       if (ok) {
         tc_fence_after();
-        issue_s(0, 0);
-        mma_commit(&sm.s_full[0]);
-        if (has1) {
-          issue_s(1, 0);
-          mma_commit(&sm.s_full[1]);
+        for (int g = 0; g < ng; ++g) {
+          issue_s(g, 0);
+          mma_commit(&sm.s_full[g]);
         }
       }
       for (int j = 0; ok && j < nkv; ++j) {
         const int st = j % kStages, stn = (j + 1) % kStages;
-        if (!(ok = mbar_wait(&sm.p_full[0], j & 1, &sm.abort, &g_tc_status, 12))) break;
-        tc_fence_after();
-        issue_o(0, st, j > 0);
-        mma_commit(&sm.o_done[0]);
         if (j + 1 < nkv) {
-          if (!(ok = mbar_wait(&sm.kv_full[stn], ((j + 1) / kStages) & 1, &sm.abort, &g_tc_status, 13))) break;
+          if (!(ok = mbar_wait(&sm.kv_full[stn], ((j + 1) / kStages) & 1, &sm.abort, &g_tc_status, 12))) break;
           consumed = j + 2;
-          tc_fence_after();
-          issue_s(0, stn);
-          mma_commit(&sm.s_full[0]);
-        }
-        if (has1) {
-          if (!(ok = mbar_wait(&sm.p_full[1], j & 1, &sm.abort, &g_tc_status, 14))) break;
-          tc_fence_after();
-          issue_o(1, st, j > 0);
-          mma_commit(&sm.o_done[1]);
-          if (j + 1 < nkv) {
-            issue_s(1, stn);
-            mma_commit(&sm.s_full[1]);
+          for (int g = 0; g < ng && ok; ++g) {
+            if (!(ok = mbar_wait(&sm.s_free[g], j & 1, &sm.abort, &g_tc_status, 13))) break;
+            tc_fence_after();
+            issue_s(g, stn);
+            mma_commit(&sm.s_full[g]);
           }
+          if (!ok) break;
         }
+        for (int g = 0; g < ng && ok; ++g) {
+          if (!(ok = mbar_wait(&sm.p_full[g], j & 1, &sm.abort, &g_tc_status, 14))) break;
+          tc_fence_after();
+          issue_o(g, st, j > 0);
+          mma_commit(&sm.o_done[g]);
+        }
+        if (!ok) break;
         mma_commit(&sm.kv_empty[st]);
         // refill the stage tile j-1 used (its MMAs finished long ago) with tile j+3
         if (j >= 1 && j + kStages - 1 < nkv) {
@@ -323,8 +311,8 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
     // ── softmax warpgroup g: thread = query row (TMEM lane) ──
     const int g = warp >> 2, row = tid & 127;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t sc = tmem + lane_off + col_s(g), oc = tmem + lane_off + col_o(g);
-    float m = -INFINITY;
+    const uint32_t sc = tmem + lane_off + col_s(g), pc = tmem + lane_off + col_p(g), oc = tmem + lane_off + col_o(g);
+    float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       if (!(ok = mbar_wait(&sm.s_full[g], j & 1, &sm.abort, &g_tc_status, 20 + g))) break;
@@ -349,6 +337,8 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
           sv[96 + i] = __uint_as_float(r3[i]);
         }
       }
+      tc_fence_before();
+      mbar_arrive(&sm.s_free[g]);  // S columns may now take the next tile's scores
       const int kvalid = N - j * kTile;
       if (kvalid < kTile) {
 #pragma unroll
@@ -364,19 +354,20 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
         for (int u = 0; u < 8; ++u) mx[u] = max3(mx[u], sv[i + u], sv[i + 8 + u]);
       mx[0] = max3(mx[0], mx[1], mx[2]);
       mx[3] = max3(mx[3], mx[4], mx[5]);
-      mx[6] = max3(mx[6], mx[7], sv[kTile - 8]);  // kTile-8.. covered by the loop up to i=120; harmless repeat
+      mx[6] = fmaxf(mx[6], mx[7]);
       const float m_new = fmaxf(m, max3(mx[0], mx[3], mx[6]) * scale_log2);
       // Rescale only when the running max grew by more than 2^8 (the stale max
       // keeps P ≤ 256; exact after the final division by the row sum).
       const bool resc = (j == 0) || (m_new > m + 8.0f);
       const float m_use = resc ? m_new : m;
+      const float alpha = resc ? ex2(m - m_use) : 1.0f;
       if (j > 0) {
+        // P·V(j-1) done: the P columns are free and O is stable
         if (!(ok = mbar_wait(&sm.o_done[g], (j - 1) & 1, &sm.abort, &g_tc_status, 22 + g))) break;
         tc_fence_after();
         if (__any_sync(0xffffffffu, resc)) {
-          const float alpha = resc ? ex2(m - m_use) : 1.0f;
 #pragma unroll 1
-          for (int c = 0; c < kVRows / 16; ++c) {  // 64 outputs + row sum (+ zero columns)
+          for (int c = 0; c < kHD / 16; ++c) {
             uint32_t o16[16];
             tmem_ld16(oc + c * 16, o16);
             tmem_ld_wait();
@@ -385,20 +376,25 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
             for (int i = 0; i < 16; ++i) o16[i] = __float_as_uint(__uint_as_float(o16[i]) * alpha);
             tmem_st16(oc + c * 16, o16);
           }
-          tmem_st_wait();
         }
       }
       const float nm = -m_use;
+      float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
       for (int c = 0; c < kTile / 32; ++c) {
         uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          pk[e] = pack_f16x2(ex2(fmaf(sv[c * 32 + 2 * e], scale_log2, nm)),
-                             ex2(fmaf(sv[c * 32 + 2 * e + 1], scale_log2, nm)));
-        tmem_st16(sc + c * 16, pk);
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], scale_log2, nm));
+          const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], scale_log2, nm));
+          ls0 += p0;
+          ls1 += p1;
+          pk[e] = pack_f16x2(p0, p1);
+        }
+        tmem_st16(pc + c * 16, pk);
       }
       tmem_st_wait();
+      l = l * alpha + (ls0 + ls1);
       m = m_use;
       tc_fence_before();
       mbar_arrive(&sm.p_full[g]);
@@ -407,11 +403,6 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
     if (ok) {
       tc_fence_after();
       const int n = q0 + g * kTile + row;
-      uint32_t o16[16];
-      tmem_ld16(oc + 64, o16);
-      tmem_ld_wait();
-      reg_fence(o16);
-      const float l = __uint_as_float(o16[0]);
       const float inv = 1.0f / l;
 #pragma unroll
       for (int c = 0; c < kHD / 32; ++c) {
