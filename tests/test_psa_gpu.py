@@ -263,3 +263,41 @@ def test_tc_attention_core_vs_oracle(cuda, B, H, W):
     status = __import__("ctypes").c_int(-1)
     _lib.call("va_device_status_read", __import__("ctypes").byref(status), st)
     assert status.value == 0
+
+
+@pytest.mark.parametrize("B,H,W", [(1, 20, 20), (2, 40, 40), (1, 11, 13)])
+def test_tc_attention_core_peaked(cuda, B, H, W):
+    """Strongly peaked attention (one dominant key per query, at every key
+    position mod 128, incl. the ragged last tile): exercises the running-max
+    rescale and the row max over every column of a tile."""
+    from vision_rs_b200 import _lib
+    nh, N = 2, H * W
+    Np = (N + 7) // 8 * 8
+    rng = np.random.default_rng(11)
+    q = rng.standard_normal((B * nh, N, 32)) * 0.1
+    k = rng.standard_normal((B * nh, N, 32)) * 0.1
+    # queries and a third of the keys point in 2-D directions with norm 10:
+    # scores up to 100 (≈25 in scaled log2 units) against ~0 elsewhere, the
+    # arg-max key varying with the query
+    th = rng.uniform(0, 2 * np.pi, (B * nh, N))
+    q[:, :, 0], q[:, :, 1] = 10 * np.cos(th), 10 * np.sin(th)
+    hot = rng.permutation(N)[: max(1, N // 3)]
+    ph = rng.uniform(0, 2 * np.pi, (B * nh, hot.size))
+    k[:, hot, 0], k[:, hot, 1] = 10 * np.cos(ph), 10 * np.sin(ph)
+    qk = np.stack([q, k]).astype(np.float16)
+    vv = rng.standard_normal((B, 128, N)).astype(np.float16)
+    vpad = np.zeros((B, 128, Np), np.float16)
+    vpad[:, :, :N] = vv
+    qk_d, v_d = torch.as_tensor(qk).cuda(), torch.as_tensor(vpad).cuda()
+    o_d = torch.zeros(B, 128, Np, dtype=torch.float16, device="cuda")
+    l_d = torch.zeros(B * nh, N, dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.call("va_psa_flash_attention_fwd_f16", qk_d.data_ptr(), v_d.data_ptr(), o_d.data_ptr(), l_d.data_ptr(),
+              B, nh, H, W, st)
+    o = o_d.float().cpu().numpy()[:, :, :N]
+    assert np.isfinite(o).all()
+    v_t = vv.astype(np.float32).reshape(B, nh, 64, N).transpose(0, 1, 3, 2).reshape(B * nh, N, 64)
+    ro, rl = po.flash_attention2_forward(qk[0].astype(np.float32), qk[1].astype(np.float32), v_t, SCALE)
+    ro = ro.reshape(B, nh, N, 64).transpose(0, 1, 3, 2).reshape(B, 128, N)
+    assert rel_l2(o, ro) < 2e-3 and max_abs(o, ro) < 1e-2
+    assert max_abs(l_d.cpu().numpy(), rl) < 2e-3

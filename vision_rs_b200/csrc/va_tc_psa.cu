@@ -345,13 +345,16 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
         for (int i = 0; i < kTile; ++i)
           if (i >= kvalid) sv[i] = -INFINITY;
       }
+      // row max over all 128 scores: 8 interleaved chains of 3-input max
       float mx[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) mx[u] = max3(sv[u], sv[8 + u], sv[16 + u]);
 #pragma unroll
-      for (int i = 24; i + 16 <= kTile; i += 16)
+      for (int i = 24; i < kTile - 8; i += 16)
 #pragma unroll
         for (int u = 0; u < 8; ++u) mx[u] = max3(mx[u], sv[i + u], sv[i + 8 + u]);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mx[u] = fmaxf(mx[u], sv[kTile - 8 + u]);
       mx[0] = max3(mx[0], mx[1], mx[2]);
       mx[3] = max3(mx[3], mx[4], mx[5]);
       mx[6] = fmaxf(mx[6], mx[7]);
