@@ -427,177 +427,179 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-// ── Kernel 3: positional encoding + add + output projection ─────────────────
-// 256 threads.  Per 64-channel half, the tile's V rows plus one halo row above
-// and below are staged in shared memory with 16-byte loads; the 3×3 stencil
-// then reads shared memory only.
-constexpr int kProjThreads = 256;
-constexpr int kMaxW = 192;  // widest image row the staged-V layout supports
+// ── Kernel 3: positional encoding (depthwise 3×3 + bias) ───────────────────
+// One CTA per (image, group of kPeCh channels).  Each channel plane is read
+// with 16-byte loads (all in flight at once), widened to f32 into a zero-
+// bordered [H+2][W+2] shared-memory plane, and every thread then produces
+// consecutive outputs (conflict-free shared reads, coalesced stores).  PE is
+// stored f16 [B][C][Np], the layout the projection kernel reads with TMA.
+// CTA 0 also converts W_proj (bf16) to the f16 operand the projection uses.
+constexpr int kPeCh = 4;
+constexpr int kPeThreads = 256;
+constexpr int kMaxPlane = 12288;   // (H+2)(W+2) floats per staged channel
 
-struct ProjSmem {
-  uint8_t a[2][kC * 128];   // (O+PE)ᵀ tile, MN-major SW128: 2 blocks of 64 tokens × 128 channel rows
-  uint8_t w[2][kC * 128];   // W_proj f16, K-major SW128: 2 blocks of 64 in-channels × 128 rows
-  float wpe[kC * 9];
-  float bpe[kC];
-  uint64_t mma_bar;
-  uint32_t tmem_base;
-  int abort;
-  // followed by the staged V rows: [64 channels][vpitch] f16
-};
-
-// f16 elements staged per channel for a 128-token tile of a W-wide image
-__host__ __device__ inline int proj_vpitch(int W) {
-  const int rows = (kTile + W - 1) / W + 3;
-  return ((rows * W + 8) + 7) / 8 * 8 + 8;
+__global__ void __launch_bounds__(kPeThreads)
+pe_dwconv_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __restrict__ w_pe,
+                 const float* __restrict__ b_pe, __half* __restrict__ pebuf,
+                 const __nv_bfloat16* __restrict__ w_proj, __half* __restrict__ wproj16, int H, int W, int Np) {
+  extern __shared__ float plane[];   // [kPeCh][(H+2)*(W+2)]
+  const int tid = threadIdx.x;
+  const int N = H * W, W2 = W + 2, P2 = (H + 2) * W2;
+  const int cg = blockIdx.x, b = blockIdx.y;
+  if (cg == 0 && b == 0) {
+    for (int i = tid; i < kC * kC / 8; i += kPeThreads) {
+      const uint4 src = __ldg(reinterpret_cast<const uint4*>(w_proj) + i);
+      const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&src);
+      uint4 u;
+      uint32_t* uu = &u.x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(s2[e]);
+        uu[e] = pack_f16x2_sat(f.x, f.y);
+      }
+      reinterpret_cast<uint4*>(wproj16)[i] = u;
+    }
+  }
+  // zero border, then the interior from global (16-byte loads, batched)
+  for (int i = tid; i < kPeCh * P2; i += kPeThreads) plane[i] = 0.f;
+  __syncthreads();
+  const int nchunk = Np >> 3;
+  const __half* vb = vbuf + ((size_t)b * kC + (size_t)cg * kPeCh) * Np;
+  constexpr int kBatch = 4;
+  for (int base = tid; base < kPeCh * nchunk; base += kPeThreads * kBatch) {
+    uint4 u[kBatch];
+#pragma unroll
+    for (int q = 0; q < kBatch; ++q) {
+      const int i = base + q * kPeThreads;
+      if (i < kPeCh * nchunk) {
+        const int c = i / nchunk, k = i - c * nchunk;
+        u[q] = __ldg(reinterpret_cast<const uint4*>(vb + (size_t)c * Np) + k);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kBatch; ++q) {
+      const int i = base + q * kPeThreads;
+      if (i < kPeCh * nchunk) {
+        const int c = i / nchunk, k = i - c * nchunk;
+        const __half* h = reinterpret_cast<const __half*>(&u[q]);
+        int n = k * 8, r = n / W, j = n - r * W;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (n + e < N) plane[c * P2 + (r + 1) * W2 + j + 1] = __half2float(h[e]);
+          if (++j == W) { j = 0; ++r; }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  for (int c = 0; c < kPeCh; ++c) {
+    const int ch = cg * kPeCh + c;
+    float w[9];
+#pragma unroll
+    for (int t = 0; t < 9; ++t) w[t] = __bfloat162float(w_pe[ch * 9 + t]);
+    const float bias = b_pe[ch];
+    const float* pl = plane + c * P2;
+    __half* out = pebuf + ((size_t)b * kC + ch) * Np;
+    for (int n = tid; n < N; n += kPeThreads) {
+      const int r = n / W, j = n - r * W;
+      const float* p = pl + r * W2 + j;   // top-left of the 3×3 window
+      float acc = bias;
+      acc = fmaf(w[0], p[0], acc);
+      acc = fmaf(w[1], p[1], acc);
+      acc = fmaf(w[2], p[2], acc);
+      acc = fmaf(w[3], p[W2], acc);
+      acc = fmaf(w[4], p[W2 + 1], acc);
+      acc = fmaf(w[5], p[W2 + 2], acc);
+      acc = fmaf(w[6], p[2 * W2], acc);
+      acc = fmaf(w[7], p[2 * W2 + 1], acc);
+      acc = fmaf(w[8], p[2 * W2 + 2], acc);
+      out[n] = __float2half_rn(acc);
+    }
+  }
 }
 
-__global__ void __launch_bounds__(kProjThreads, 1)
-pe_proj_kernel(const __half* __restrict__ obuf, const __half* __restrict__ vbuf,
-               const __nv_bfloat16* __restrict__ w_pe, const float* __restrict__ b_pe,
-               const __nv_bfloat16* __restrict__ w_proj, const float* __restrict__ b_proj,
-               __nv_bfloat16* __restrict__ y, int H, int W, int Np) {
+// ── Kernel 4: output projection y = W_proj·(O + PE) + b_proj ───────────────
+// Both O and PE tiles arrive by TMA as MN-major operands; the sum O + PE is
+// formed by the tensor core itself: D = Oᵀ·W_projᵀ, then D += PEᵀ·W_projᵀ
+// into the same TMEM accumulator (16 k-steps).
+struct ProjSmem {
+  uint8_t o[2][kC * 128];    // Oᵀ tile, MN-major SW128: 2 blocks of 64 tokens × 128 channel rows
+  uint8_t pe[2][kC * 128];   // PEᵀ tile, same layout
+  uint8_t w[2][kC * 128];    // W_proj f16, K-major SW128: 2 blocks of 64 in-channels × 128 rows
+  float bias[kC];
+  uint64_t full_bar, mma_bar;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __launch_bounds__(128, 1)
+proj_kernel(const __grid_constant__ CUtensorMap map_o, const __grid_constant__ CUtensorMap map_pe,
+            const __grid_constant__ CUtensorMap map_w, const float* __restrict__ b_proj,
+            __nv_bfloat16* __restrict__ y, int N) {
   extern __shared__ uint8_t smem_raw[];
   ProjSmem& sm = *reinterpret_cast<ProjSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __half* vs = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(&sm) + ((sizeof(ProjSmem) + 15) & ~size_t(15)));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int N = H * W;
   const int n0 = blockIdx.x * kTile, b = blockIdx.y;
-  const int vpitch = proj_vpitch(W);
-
   if (tid == 0) {
+    mbar_init(&sm.full_bar, 1);
     mbar_init(&sm.mma_bar, 1);
     sm.abort = 0;
     fence_mbar_init();
   }
+  sm.bias[tid] = b_proj[tid];
   if (warp == 0) {
     tmem_alloc(&sm.tmem_base, 128);
     tmem_relinquish();
-  }
-  for (int i = tid; i < kC * 9; i += kProjThreads) sm.wpe[i] = __bfloat162float(w_pe[i]);
-  for (int i = tid; i < kC; i += kProjThreads) sm.bpe[i] = b_pe[i];
-  // W_proj (bf16, [out][in]) → f16 K-major SW128
-  for (int i = tid; i < kC * kC / 8; i += kProjThreads) {
-    const int o = i / (kC / 8), chunk = i % (kC / 8);  // 16 chunks of 8 in-channels per row
-    const uint4 src = __ldg(reinterpret_cast<const uint4*>(w_proj + (size_t)o * kC) + chunk);
-    const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&src);
-    uint4 u;
-    uint32_t* uu = &u.x;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float2 f = __bfloat1622float2(s2[e]);
-      uu[e] = pack_f16x2_sat(f.x, f.y);
-    }
-    const int kb = chunk >> 3, c8 = chunk & 7;
-    *reinterpret_cast<uint4*>(sm.w[kb] + o * 128 + ((c8 ^ (o & 7)) << 4)) = u;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-
-  // rows of the image this tile touches, plus one halo row on each side
-  const int nlast = min(n0 + kTile, N) - 1;
-  const int r_lo = max(0, n0 / W - 1), r_hi = min(H - 1, nlast / W + 1);
-  const int e0 = (r_lo * W) & ~7;                 // 16-byte aligned start of the staged run
-  const int e1 = min(Np, ((r_hi + 1) * W + 7) & ~7);
-  const int nchunk = (e1 - e0) >> 3;
-
-  const __half* ob = obuf + (size_t)b * kC * Np;
-  const __half* vb = vbuf + (size_t)b * kC * Np;
-#pragma unroll 1
-  for (int half = 0; half < 2; ++half) {
-    const int cbase = half * 64;
-    // stage V[cbase .. cbase+64)[e0 .. e1) → vs[c][0 .. e1-e0)
-    for (int i = tid; i < 64 * nchunk; i += kProjThreads) {
-      const int c = i / nchunk, k = i - c * nchunk;
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(vb + (size_t)(cbase + c) * Np + e0) + k);
-      *reinterpret_cast<uint4*>(vs + c * vpitch + k * 8) = u;
-    }
-    __syncthreads();
-    // items: (channel c of this half, group g of 8 tokens)
-    for (int it = tid; it < 64 * (kTile / 8); it += kProjThreads) {
-      const int cl = it >> 4, g = it & 15, c = cbase + cl;
-      const int nb = n0 + g * 8;
-      float acc[8];
-      if (nb < N) {
-        const uint4 ou = __ldg(reinterpret_cast<const uint4*>(ob + (size_t)c * Np + nb));
-        const __half2* o2 = reinterpret_cast<const __half2*>(&ou);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __half22float2(o2[e]);
-          acc[2 * e] = f.x;
-          acc[2 * e + 1] = f.y;
-        }
-      }
-      const float* wc = sm.wpe + c * 9;
-      const float bias = sm.bpe[c];
-      const __half* vc = vs + cl * vpitch - e0;   // vc[n] = V[c][n] for staged n
-      int i = nb / W, j = nb - (nb / W) * W;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int n = nb + e;
-        if (n < N) {
-          float pe = bias;
-#pragma unroll
-          for (int di = 0; di < 3; ++di) {
-            const int ii = i + di - 1;
-            if (ii < 0 || ii >= H) continue;
-            const __half* vr = vc + ii * W;
-#pragma unroll
-            for (int dj = 0; dj < 3; ++dj) {
-              const int j2 = j + dj - 1;
-              if (j2 < 0 || j2 >= W) continue;
-              pe = fmaf(wc[di * 3 + dj], __half2float(vr[j2]), pe);
-            }
-          }
-          acc[e] += pe;
-        } else {
-          acc[e] = 0.f;
-        }
-        if (++j == W) { j = 0; ++i; }
-      }
-      uint4 u;
-      u.x = pack_f16x2_sat(acc[0], acc[1]);
-      u.y = pack_f16x2_sat(acc[2], acc[3]);
-      u.z = pack_f16x2_sat(acc[4], acc[5]);
-      u.w = pack_f16x2_sat(acc[6], acc[7]);
-      const int blk = g >> 3, ch = g & 7;
-      *reinterpret_cast<uint4*>(sm.a[blk] + c * 128 + ((ch ^ (c & 7)) << 4)) = u;
-    }
-    __syncthreads();
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
   if (tid == 0) {
-    tc_fence_after();
-    constexpr uint32_t idesc = idesc_f32acc(128, kC, AB_F16, /*a_mn=*/true, /*b_mn=*/false);
-    const uint32_t a0 = smem_u32(sm.a[0]), w0 = smem_u32(sm.w[0]);
+    tma_prefetch_desc(&map_o);
+    tma_prefetch_desc(&map_pe);
+    tma_prefetch_desc(&map_w);
+    mbar_arrive_expect_tx(&sm.full_bar, 6 * kC * 128);
+    tma_load_2d(sm.o[0], &map_o, &sm.full_bar, n0, b * kC);
+    tma_load_2d(sm.o[1], &map_o, &sm.full_bar, n0 + 64, b * kC);
+    tma_load_2d(sm.pe[0], &map_pe, &sm.full_bar, n0, b * kC);
+    tma_load_2d(sm.pe[1], &map_pe, &sm.full_bar, n0 + 64, b * kC);
+    tma_load_2d(sm.w[0], &map_w, &sm.full_bar, 0, 0);
+    tma_load_2d(sm.w[1], &map_w, &sm.full_bar, 64, 0);
+    if (mbar_wait(&sm.full_bar, 0, &sm.abort, &g_tc_status, 30)) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_f32acc(128, kC, AB_F16, /*a_mn=*/true, /*b_mn=*/false);
+      const uint32_t o0 = smem_u32(sm.o[0]), p0 = smem_u32(sm.pe[0]), w0 = smem_u32(sm.w[0]);
 #pragma unroll
-    for (int s = 0; s < kC / 16; ++s) {
-      uint64_t ad = sdesc(a0 + s * 16 * 128, kC * 128, 1024, SW_128B);
-      uint64_t bd = sdesc(w0 + (s >> 2) * (kC * 128) + (s & 3) * 32, 16, 1024, SW_128B);
-      mma_ss(tmem, ad, bd, idesc, s > 0);
+      for (int s = 0; s < 2 * kC / 16; ++s) {
+        const int k = s & 7;
+        const uint32_t a0 = s < 8 ? o0 : p0;
+        uint64_t ad = sdesc(a0 + k * 16 * 128, kC * 128, 1024, SW_128B);
+        uint64_t bd = sdesc(w0 + (k >> 2) * (kC * 128) + (k & 3) * 32, 16, 1024, SW_128B);
+        mma_ss(tmem, ad, bd, idesc, s > 0);
+      }
+    } else {
+      const long long t0 = clock64();
+      while (!mbar_try_wait(&sm.full_bar, 0) && clock64() - t0 < kSpinCycles) {
+      }
     }
     mma_commit(&sm.mma_bar);
   }
   __syncwarp();
-  const bool ok = mbar_wait(&sm.mma_bar, 0, &sm.abort, &g_tc_status, 30);
+  const bool ok = mbar_wait(&sm.mma_bar, 0, &sm.abort, &g_tc_status, 31) && !sm.abort;
   tc_fence_after();
   if (ok) {
-    // warp w reads TMEM lanes 32*(w%4) (its sub-partition), columns (w/4)*64 .. +64
-    const int n = n0 + (warp & 3) * 32 + lane;
+    const int n = n0 + warp * 32 + lane;
 #pragma unroll 1
-    for (int cc = 0; cc < 2; ++cc) {
-      const int c = (warp >> 2) * 2 + cc;
+    for (int c = 0; c < kC / 32; ++c) {
       uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + c * 32, r);
+      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
       tmem_ld_wait();
       reg_fence(r);
       if (n < N) {
         __nv_bfloat16* dst = y + ((size_t)b * kC + c * 32) * N + n;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          dst[(size_t)i * N] = __float2bfloat16_rn(__uint_as_float(r[i]) + __ldg(b_proj + c * 32 + i));
+        for (int i = 0; i < 32; ++i) dst[(size_t)i * N] = __float2bfloat16_rn(__uint_as_float(r[i]) + sm.bias[c * 32 + i]);
       }
     }
   }
@@ -643,7 +645,7 @@ int make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base,
 }
 
 struct TcWs {
-  size_t qk, v, o, xpad, total;
+  size_t qk, v, o, pe, wproj, xpad, total;
 };
 
 TcWs tc_layout(int B, int H, int W, int nh) {
@@ -654,6 +656,8 @@ TcWs tc_layout(int B, int H, int W, int nh) {
   w.qk = take(2 * BH * N * kKD * 2);
   w.v = take((size_t)B * kC * Np * 2);
   w.o = take((size_t)B * kC * Np * 2);
+  w.pe = take((size_t)B * kC * Np * 2);
+  w.wproj = take((size_t)kC * kC * 2);
   w.xpad = (N % 8) ? take((size_t)B * kC * Np * 2) : (size_t)-1;
   w.total = off;
   return w;
@@ -678,7 +682,7 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
                          void* ws, size_t ws_bytes, cudaStream_t st, float* lse_out) {
   VA_CHECK_ARG(psa_tc_supported(C, nh, kd), "psa_attention bf16: tensor-core path needs C=128, nh=2, kd=32");
   VA_CHECK_ARG(B > 0 && H > 0 && W > 0 && B <= 65535, "psa_attention bf16: bad sizes");
-  VA_CHECK_ARG(W <= kMaxW, "psa_attention bf16: image width %d > %d unsupported", W, kMaxW);
+  VA_CHECK_ARG((H + 2) * (W + 2) <= kMaxPlane, "psa_attention bf16: image %dx%d larger than supported", H, W);
   const TcWs L = tc_layout(B, H, W, nh);
   if (!ws || ws_bytes < L.total)
     return set_error(VA_ERR_WORKSPACE, "psa_attention bf16: workspace %zu < %zu bytes", ws_bytes, L.total);
@@ -725,23 +729,43 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
       return rc;
   }
   const int ntile = (N + kTile - 1) / kTile;
-  const size_t sm1 = sizeof(QkvSmem) + 1024, sm2 = sizeof(AttnSmem) + 1024;
-  const size_t sm3 = ((sizeof(ProjSmem) + 15) & ~size_t(15)) + (size_t)64 * proj_vpitch(W) * 2 + 1024;
+  const size_t sm1 = sizeof(QkvSmem) + 1024, sm2 = sizeof(AttnSmem) + 1024, sm4 = sizeof(ProjSmem) + 1024;
+  const size_t sm3 = (size_t)kPeCh * (H + 2) * (W + 2) * sizeof(float);
   static bool attr_done = false;
   if (!attr_done) {
     if (int rc = set_smem(qkv_proj_kernel, sm1)) return rc;
     if (int rc = set_smem(attn_kernel, sm2)) return rc;
-    if (int rc = set_smem(pe_proj_kernel, ((sizeof(ProjSmem) + 15) & ~size_t(15)) + 64 * proj_vpitch(kMaxW) * 2 + 1024))
-      return rc;
+    if (int rc = set_smem(pe_dwconv_kernel, (size_t)kPeCh * kMaxPlane * sizeof(float))) return rc;
+    if (int rc = set_smem(proj_kernel, sm4)) return rc;
     attr_done = true;
+  }
+  __half* peb = reinterpret_cast<__half*>(base + L.pe);
+  __half* wp16 = reinterpret_cast<__half*>(base + L.wproj);
+  CUtensorMap mo, mpe, mwp;
+  {
+    uint64_t d[2] = {(uint64_t)N, (uint64_t)B * kC}, s[1] = {(uint64_t)Np * 2};
+    uint32_t bx[2] = {64, kC};
+    if (int rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ob, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B, "o"))
+      return rc;
+    if (int rc = make_map(&mpe, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, peb, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B, "pe"))
+      return rc;
+  }
+  {
+    uint64_t d[2] = {(uint64_t)kC, (uint64_t)kC}, s[1] = {(uint64_t)kC * 2};
+    uint32_t bx[2] = {64, kC};
+    if (int rc = make_map(&mwp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, wp16, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B,
+                          "w_proj"))
+      return rc;
   }
   qkv_proj_kernel<<<dim3(ntile, B), 128, sm1, st>>>(mx, mw, b_qkv, qk, vb, N, Np, nh);
   if (int rc = check_launch("psa qkv_proj")) return rc;
   const float scale_log2 = (1.0f / sqrtf((float)kd)) * 1.4426950408889634f;
   attn_kernel<<<dim3((ntile + 1) / 2, BH), kAttnThreads, sm2, st>>>(mqk, mv, ob, lse_out, N, Np, nh, scale_log2);
   if (int rc = check_launch("psa attention")) return rc;
-  pe_proj_kernel<<<dim3(ntile, B), kProjThreads, sm3, st>>>(ob, vb, w_pe, b_pe, w_proj, b_proj, y, H, W, Np);
-  return check_launch("psa pe_proj");
+  pe_dwconv_kernel<<<dim3(kC / kPeCh, B), kPeThreads, sm3, st>>>(vb, w_pe, b_pe, peb, w_proj, wp16, H, W, Np);
+  if (int rc = check_launch("psa pe")) return rc;
+  proj_kernel<<<dim3(ntile, B), 128, sm4, st>>>(mo, mpe, mwp, b_proj, y, N);
+  return check_launch("psa proj");
 }
 
 int tc_status_read(int* out, cudaStream_t st) {
