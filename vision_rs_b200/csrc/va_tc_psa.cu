@@ -237,19 +237,25 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       constexpr uint32_t idS = idesc_f32acc(128, kTile, AB_F16, false, false);
       constexpr uint32_t idO = idesc_f32acc(128, kHD, AB_F16, false, false);
       const int ng = has1 ? 2 : 1;
+      // Descriptors are built once; inside the loop a stage / k-step only moves
+      // the start-address field (bits 0-13, address >> 4), a plain add that
+      // cannot carry out of the field for shared-memory addresses.
+      const uint64_t dq0 = sdesc(smem_u32(sm.q[0]), 16, 512, SW_64B);
+      const uint64_t dk0 = sdesc(smem_u32(sm.k[0]), 16, 512, SW_64B);
+      const uint64_t dv0 = sdesc(smem_u32(sm.v[0][0]), 16, 1024, SW_128B);
+      constexpr uint32_t kQStep = (kTile * 64) >> 4, kKStage = (kTile * 64) >> 4, kVStage = (2 * kVBlk) >> 4;
       auto issue_s = [&](int g, int stage) {
-        const uint32_t qa = smem_u32(sm.q[g]), ka = smem_u32(sm.k[stage]);
+        const uint32_t d = tmem + col_s(g);
+        const uint64_t qd = dq0 + (uint64_t)(g * kQStep), kd_ = dk0 + (uint64_t)(stage * kKStage);
 #pragma unroll
-        for (int s = 0; s < kKD / 16; ++s)
-          mma_ss(tmem + col_s(g), sdesc(qa + s * 32, 16, 512, SW_64B), sdesc(ka + s * 32, 16, 512, SW_64B), idS,
-                 s > 0);
+        for (int s = 0; s < kKD / 16; ++s) mma_ss(d, qd + (uint64_t)(s * 2), kd_ + (uint64_t)(s * 2), idS, s > 0);
       };
       auto issue_o = [&](int g, int stage, bool acc) {
-        const uint32_t va0 = smem_u32(sm.v[stage][0]);
+        const uint32_t d = tmem + col_o(g), a = tmem + col_p(g);
+        const uint64_t vd = dv0 + (uint64_t)(stage * kVStage);
 #pragma unroll
         for (int s = 0; s < kTile / 16; ++s)
-          mma_ts(tmem + col_o(g), tmem + col_p(g) + s * 8,
-                 sdesc(va0 + (s >> 2) * kVBlk + (s & 3) * 32, 16, 1024, SW_128B), idO, (acc || s > 0) ? 1u : 0u);
+          mma_ts(d, a + s * 8, vd + (uint64_t)((((s >> 2) * kVBlk) + (s & 3) * 32) >> 4), idO, (acc || s > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(&sm.q_full, 0, &sm.abort, &g_tc_status, 10) &&
                 mbar_wait(&sm.kv_full[0], 0, &sm.abort, &g_tc_status, 11);
@@ -436,7 +442,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
 // CTA 0 also converts W_proj (bf16) to the f16 operand the projection uses.
 constexpr int kPeCh = 4;
 constexpr int kPeThreads = 256;
-constexpr int kMaxPlane = 12288;   // (H+2)(W+2) floats per staged channel
+constexpr int kMaxPlane = 12288;   // (H+2)·pitch floats per staged channel
 
 __global__ void __launch_bounds__(kPeThreads)
 pe_dwconv_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __restrict__ w_pe,
@@ -444,7 +450,7 @@ pe_dwconv_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __restric
                  const __nv_bfloat16* __restrict__ w_proj, __half* __restrict__ wproj16, int H, int W, int Np) {
   extern __shared__ float plane[];   // [kPeCh][(H+2)*(W+2)]
   const int tid = threadIdx.x;
-  const int N = H * W, W2 = W + 2, P2 = (H + 2) * W2;
+  const int N = H * W, W2 = (W + 10) | 1, P2 = (H + 2) * W2;   // odd pitch; 8 zero columns of slack
   const int cg = blockIdx.x, b = blockIdx.y;
   if (cg == 0 && b == 0) {
     for (int i = tid; i < kC * kC / 8; i += kPeThreads) {
@@ -492,28 +498,44 @@ pe_dwconv_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __restric
     }
   }
   __syncthreads();
-  for (int c = 0; c < kPeCh; ++c) {
-    const int ch = cg * kPeCh + c;
+  // items: (channel, 8-column group, row) with the row fastest across threads
+  // (odd plane pitch → conflict-free shared reads); 8 outputs per item from a
+  // 3×10 register window
+  const int ngrp = (W + 7) >> 3;
+  const bool vec_store = (W & 7) == 0;
+  for (int it = tid; it < kPeCh * ngrp * H; it += kPeThreads) {
+    const int r = it % H, rest = it / H;
+    const int g = rest % ngrp, c = rest / ngrp;
+    const int ch = cg * kPeCh + c, j0 = g * 8;
+    const float* p = plane + c * P2 + r * W2 + j0;   // window top-left: image (r-1, j0-1)
     float w[9];
 #pragma unroll
     for (int t = 0; t < 9; ++t) w[t] = __bfloat162float(w_pe[ch * 9 + t]);
+    float acc[8];
     const float bias = b_pe[ch];
-    const float* pl = plane + c * P2;
-    __half* out = pebuf + ((size_t)b * kC + ch) * Np;
-    for (int n = tid; n < N; n += kPeThreads) {
-      const int r = n / W, j = n - r * W;
-      const float* p = pl + r * W2 + j;   // top-left of the 3×3 window
-      float acc = bias;
-      acc = fmaf(w[0], p[0], acc);
-      acc = fmaf(w[1], p[1], acc);
-      acc = fmaf(w[2], p[2], acc);
-      acc = fmaf(w[3], p[W2], acc);
-      acc = fmaf(w[4], p[W2 + 1], acc);
-      acc = fmaf(w[5], p[W2 + 2], acc);
-      acc = fmaf(w[6], p[2 * W2], acc);
-      acc = fmaf(w[7], p[2 * W2 + 1], acc);
-      acc = fmaf(w[8], p[2 * W2 + 2], acc);
-      out[n] = __float2half_rn(acc);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = bias;
+#pragma unroll
+    for (int di = 0; di < 3; ++di) {
+      float x[10];
+#pragma unroll
+      for (int q = 0; q < 10; ++q) x[q] = p[di * W2 + q];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        acc[e] = fmaf(w[di * 3], x[e], fmaf(w[di * 3 + 1], x[e + 1], fmaf(w[di * 3 + 2], x[e + 2], acc[e])));
+    }
+    __half* out = pebuf + ((size_t)b * kC + ch) * Np + (size_t)r * W + j0;
+    if (vec_store) {
+      uint4 u;
+      u.x = pack_f16x2(acc[0], acc[1]);
+      u.y = pack_f16x2(acc[2], acc[3]);
+      u.z = pack_f16x2(acc[4], acc[5]);
+      u.w = pack_f16x2(acc[6], acc[7]);
+      *reinterpret_cast<uint4*>(out) = u;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (j0 + e < W) out[e] = __float2half_rn(acc[e]);
     }
   }
 }
@@ -682,7 +704,7 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
                          void* ws, size_t ws_bytes, cudaStream_t st, float* lse_out) {
   VA_CHECK_ARG(psa_tc_supported(C, nh, kd), "psa_attention bf16: tensor-core path needs C=128, nh=2, kd=32");
   VA_CHECK_ARG(B > 0 && H > 0 && W > 0 && B <= 65535, "psa_attention bf16: bad sizes");
-  VA_CHECK_ARG((H + 2) * (W + 2) <= kMaxPlane, "psa_attention bf16: image %dx%d larger than supported", H, W);
+  VA_CHECK_ARG((H + 2) * ((W + 10) | 1) <= kMaxPlane, "psa_attention bf16: image %dx%d larger than supported", H, W);
   const TcWs L = tc_layout(B, H, W, nh);
   if (!ws || ws_bytes < L.total)
     return set_error(VA_ERR_WORKSPACE, "psa_attention bf16: workspace %zu < %zu bytes", ws_bytes, L.total);
@@ -730,7 +752,7 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   }
   const int ntile = (N + kTile - 1) / kTile;
   const size_t sm1 = sizeof(QkvSmem) + 1024, sm2 = sizeof(AttnSmem) + 1024, sm4 = sizeof(ProjSmem) + 1024;
-  const size_t sm3 = (size_t)kPeCh * (H + 2) * (W + 2) * sizeof(float);
+  const size_t sm3 = (size_t)kPeCh * (H + 2) * ((W + 10) | 1) * sizeof(float);
   static bool attr_done = false;
   if (!attr_done) {
     if (int rc = set_smem(qkv_proj_kernel, sm1)) return rc;
