@@ -155,24 +155,26 @@ qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
 // One CTA = two 128-query tiles of one (b, h), sharing every K/V tile.
 //   warps 0-3: softmax for query tile 0, warps 4-7: query tile 1 (thread =
 //              query row = TMEM lane); warp 8 lane 0: TMA producer + MMA issuer.
-// TMEM (512 columns), per query tile g at 256·g: S (f32, 128 cols), P (packed
-// f16, 64 cols) read by the P·V MMA as its A operand straight from TMEM, and
-// O (f32, 64 cols).  Because P has its own columns, S(j+1) = Q·K(j+1)ᵀ is
-// issued as soon as the softmax has copied S(j) into registers, so the next
-// tile's scores are ready when the exponentials of this one are done.
+// Keys are processed in 64-key units u (two per 128-key K/V stage).  TMEM per
+// query tile g (192 columns at 192·g): two score buffers S[u%2] (f32, 64
+// cols) and O (f32, 64 cols).  The softmax writes P(u) as packed f16 over the
+// first 32 columns of the S buffer it just read; the P·V MMA reads it from
+// there (TMEM A operand).  S(u+2) reuses that buffer and is issued right
+// after P(u)·V, so the in-order tensor pipe orders the reuse and the softmax
+// of unit u+1 finds its scores computed a whole unit earlier.
 constexpr int kStages = 4;
+constexpr int kUnit = 64;                  // keys per softmax step
 constexpr int kVBlk = kHD * 128;           // one 64-key block of V: [64 channel rows × 128 B] SW128 (8 KB)
 constexpr int kAttnThreads = 288;
 
-__device__ __forceinline__ uint32_t col_s(int g) { return (uint32_t)g * 256u; }
-__device__ __forceinline__ uint32_t col_p(int g) { return (uint32_t)g * 256u + 128u; }
-__device__ __forceinline__ uint32_t col_o(int g) { return (uint32_t)g * 256u + 192u; }
+__device__ __forceinline__ uint32_t col_s(int g, int buf) { return (uint32_t)g * 192u + (uint32_t)buf * 64u; }
+__device__ __forceinline__ uint32_t col_o(int g) { return (uint32_t)g * 192u + 128u; }
 
 struct AttnSmem {
   uint8_t q[2][kTile * 64];                // Q tiles [128 rows × 32] f16, K-major SW64 (8 KB each)
-  uint8_t k[kStages][kTile * 64];          // K tiles (8 KB each)
-  uint8_t v[kStages][2][kVBlk];            // V: stage × key-block
-  uint64_t q_full, kv_full[kStages], kv_empty[kStages], s_full[2], s_free[2], p_full[2], o_done[2], fin;
+  uint8_t k[kStages][kTile * 64];          // K tiles: 128 keys (8 KB each)
+  uint8_t v[kStages][2][kVBlk];            // V: stage × 64-key block
+  uint64_t q_full, kv_full[kStages], kv_empty[kStages], s_full[2][2], p_full[2], o_done[2], fin;
   uint32_t tmem_base;
   int abort;
 };
@@ -193,7 +195,8 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int q0 = blockIdx.x * 2 * kTile, bh = blockIdx.y;
   const int BH = gridDim.y, b = bh / nh, h = bh % nh;
-  const int nkv = (N + kTile - 1) / kTile;
+  const int ntl = (N + kTile - 1) / kTile;   // 128-key K/V tiles
+  const int nu = (N + kUnit - 1) / kUnit;    // 64-key units
   const bool has1 = q0 + kTile < N;
   const int vrow = b * kC + h * kHD;
 
@@ -203,11 +206,11 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       mbar_init(&sm.kv_full[i], 1);
       mbar_init(&sm.kv_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.s_full[i], 1);
-      mbar_init(&sm.s_free[i], 128);
-      mbar_init(&sm.p_full[i], 128);
-      mbar_init(&sm.o_done[i], 1);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&sm.s_full[g][0], 1);
+      mbar_init(&sm.s_full[g][1], 1);
+      mbar_init(&sm.p_full[g], 128);
+      mbar_init(&sm.o_done[g], 1);
     }
     mbar_init(&sm.fin, 1);
     sm.abort = 0;
@@ -231,69 +234,73 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       tma_load_3d(sm.q[0], &map_qk, &sm.q_full, 0, q0, bh);
       if (has1) tma_load_3d(sm.q[1], &map_qk, &sm.q_full, 0, q0 + kTile, bh);
       int issued = 0;
-      for (; issued < kStages && issued < nkv; ++issued)
+      for (; issued < kStages && issued < ntl; ++issued)
         attn_load_kv(sm, &map_qk, &map_v, issued, issued, BH, bh, vrow);
 
-      constexpr uint32_t idS = idesc_f32acc(128, kTile, AB_F16, false, false);
+      constexpr uint32_t idS = idesc_f32acc(128, kUnit, AB_F16, false, false);
       constexpr uint32_t idO = idesc_f32acc(128, kHD, AB_F16, false, false);
       const int ng = has1 ? 2 : 1;
-      // Descriptors are built once; inside the loop a stage / k-step only moves
-      // the start-address field (bits 0-13, address >> 4), a plain add that
+      // Descriptors are built once; a stage / key half / k-step only moves the
+      // start-address field (bits 0-13, address >> 4) — a plain add that
       // cannot carry out of the field for shared-memory addresses.
       const uint64_t dq0 = sdesc(smem_u32(sm.q[0]), 16, 512, SW_64B);
       const uint64_t dk0 = sdesc(smem_u32(sm.k[0]), 16, 512, SW_64B);
       const uint64_t dv0 = sdesc(smem_u32(sm.v[0][0]), 16, 1024, SW_128B);
-      constexpr uint32_t kQStep = (kTile * 64) >> 4, kKStage = (kTile * 64) >> 4, kVStage = (2 * kVBlk) >> 4;
-      auto issue_s = [&](int g, int stage) {
-        const uint32_t d = tmem + col_s(g);
-        const uint64_t qd = dq0 + (uint64_t)(g * kQStep), kd_ = dk0 + (uint64_t)(stage * kKStage);
+      constexpr uint32_t kQStep = (kTile * 64) >> 4, kKStage = (kTile * 64) >> 4, kKHalf = (kUnit * 64) >> 4;
+      constexpr uint32_t kVStage = (2 * kVBlk) >> 4, kVHalf = kVBlk >> 4;
+      auto issue_s = [&](int g, int u) {  // S_g[u%2] = Q_g · K(unit u)ᵀ
+        const uint32_t d = tmem + col_s(g, u & 1);
+        const uint64_t qd = dq0 + (uint64_t)(g * kQStep);
+        const uint64_t kd_ = dk0 + (uint64_t)(((u >> 1) % kStages) * kKStage + (u & 1) * kKHalf);
 #pragma unroll
         for (int s = 0; s < kKD / 16; ++s) mma_ss(d, qd + (uint64_t)(s * 2), kd_ + (uint64_t)(s * 2), idS, s > 0);
       };
-      auto issue_o = [&](int g, int stage, bool acc) {
-        const uint32_t d = tmem + col_o(g), a = tmem + col_p(g);
-        const uint64_t vd = dv0 + (uint64_t)(stage * kVStage);
+      auto issue_o = [&](int g, int u) {  // O_g += P(u) · V(unit u), P in TMEM
+        const uint32_t d = tmem + col_o(g), a = tmem + col_s(g, u & 1);
+        const uint64_t vd = dv0 + (uint64_t)(((u >> 1) % kStages) * kVStage + (u & 1) * kVHalf);
 #pragma unroll
-        for (int s = 0; s < kTile / 16; ++s)
-          mma_ts(d, a + s * 8, vd + (uint64_t)((((s >> 2) * kVBlk) + (s & 3) * 32) >> 4), idO, (acc || s > 0) ? 1u : 0u);
+        for (int s = 0; s < kUnit / 16; ++s)
+          mma_ts(d, a + s * 8, vd + (uint64_t)(s * 2), idO, (u > 0 || s > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(&sm.q_full, 0, &sm.abort, &g_tc_status, 10) &&
                 mbar_wait(&sm.kv_full[0], 0, &sm.abort, &g_tc_status, 11);
-      int consumed = ok ? 1 : 0;
+      int consumed = ok ? 1 : 0;  // K/V tiles whose full barrier was observed
       if (ok) {
         tc_fence_after();
-        for (int g = 0; g < ng; ++g) {
-          issue_s(g, 0);
-          mma_commit(&sm.s_full[g]);
-        }
-      }
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int st = j % kStages, stn = (j + 1) % kStages;
-        if (j + 1 < nkv) {
-          if (!(ok = mbar_wait(&sm.kv_full[stn], ((j + 1) / kStages) & 1, &sm.abort, &g_tc_status, 12))) break;
-          consumed = j + 2;
-          for (int g = 0; g < ng && ok; ++g) {
-            if (!(ok = mbar_wait(&sm.s_free[g], j & 1, &sm.abort, &g_tc_status, 13))) break;
-            tc_fence_after();
-            issue_s(g, stn);
-            mma_commit(&sm.s_full[g]);
+        for (int u = 0; u < 2 && u < nu; ++u)
+          for (int g = 0; g < ng; ++g) {
+            issue_s(g, u);
+            mma_commit(&sm.s_full[g][u & 1]);
           }
-          if (!ok) break;
+      }
+      for (int u = 0; ok && u < nu; ++u) {
+        const int un = u + 2;  // unit whose scores are issued after this unit's P·V
+        if (un < nu && (un & 1) == 0) {
+          const int t = un >> 1;
+          if (!(ok = mbar_wait(&sm.kv_full[t % kStages], (t / kStages) & 1, &sm.abort, &g_tc_status, 12))) break;
+          consumed = t + 1;
         }
         for (int g = 0; g < ng && ok; ++g) {
-          if (!(ok = mbar_wait(&sm.p_full[g], j & 1, &sm.abort, &g_tc_status, 14))) break;
+          if (!(ok = mbar_wait(&sm.p_full[g], u & 1, &sm.abort, &g_tc_status, 13))) break;
           tc_fence_after();
-          issue_o(g, st, j > 0);
+          issue_o(g, u);
           mma_commit(&sm.o_done[g]);
+          if (un < nu) {
+            issue_s(g, un);
+            mma_commit(&sm.s_full[g][un & 1]);
+          }
         }
         if (!ok) break;
-        mma_commit(&sm.kv_empty[st]);
-        // refill the stage tile j-1 used (its MMAs finished long ago) with tile j+3
-        if (j >= 1 && j + kStages - 1 < nkv) {
-          const int sp = (j - 1) % kStages;
-          if (!(ok = mbar_wait(&sm.kv_empty[sp], ((j - 1) / kStages) & 1, &sm.abort, &g_tc_status, 15))) break;
-          attn_load_kv(sm, &map_qk, &map_v, j + kStages - 1, sp, BH, bh, vrow);
-          ++issued;
+        if ((u & 1) || u == nu - 1) {
+          const int t = u >> 1;
+          mma_commit(&sm.kv_empty[t % kStages]);
+          // refill the stage tile t-1 used (its MMAs finished long ago) with tile t+3
+          if (t >= 1 && t + kStages - 1 < ntl) {
+            const int sp = (t - 1) % kStages;
+            if (!(ok = mbar_wait(&sm.kv_empty[sp], ((t - 1) / kStages) & 1, &sm.abort, &g_tc_status, 14))) break;
+            attn_load_kv(sm, &map_qk, &map_v, t + kStages - 1, sp, BH, bh, vrow);
+            ++issued;
+          }
         }
       }
       // teardown: every issued TMA load has landed and every MMA has completed
@@ -317,80 +324,71 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
     // ── softmax warpgroup g: thread = query row (TMEM lane) ──
     const int g = warp >> 2, row = tid & 127;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t sc = tmem + lane_off + col_s(g), pc = tmem + lane_off + col_p(g), oc = tmem + lane_off + col_o(g);
+    const uint32_t oc = tmem + lane_off + col_o(g);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      if (!(ok = mbar_wait(&sm.s_full[g], j & 1, &sm.abort, &g_tc_status, 20 + g))) break;
+    for (int u = 0; u < nu; ++u) {
+      const uint32_t sc = tmem + lane_off + col_s(g, u & 1);
+      if (!(ok = mbar_wait(&sm.s_full[g][u & 1], (u >> 1) & 1, &sm.abort, &g_tc_status, 20 + g))) break;
       tc_fence_after();
-      float sv[kTile];
+      float sv[kUnit];
       {
-        uint32_t r0[32], r1[32], r2[32], r3[32];
+        uint32_t r0[32], r1[32];
         tmem_ld32(sc + 0, r0);
         tmem_ld32(sc + 32, r1);
-        tmem_ld32(sc + 64, r2);
-        tmem_ld32(sc + 96, r3);
         tmem_ld_wait();
         reg_fence(r0);
         reg_fence(r1);
-        reg_fence(r2);
-        reg_fence(r3);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           sv[i] = __uint_as_float(r0[i]);
           sv[32 + i] = __uint_as_float(r1[i]);
-          sv[64 + i] = __uint_as_float(r2[i]);
-          sv[96 + i] = __uint_as_float(r3[i]);
         }
       }
-      tc_fence_before();
-      mbar_arrive(&sm.s_free[g]);  // S columns may now take the next tile's scores
-      const int kvalid = N - j * kTile;
-      if (kvalid < kTile) {
+      const int kvalid = N - u * kUnit;
+      if (kvalid < kUnit) {
 #pragma unroll
-        for (int i = 0; i < kTile; ++i)
+        for (int i = 0; i < kUnit; ++i)
           if (i >= kvalid) sv[i] = -INFINITY;
       }
-      // row max over all 128 scores: 8 interleaved chains of 3-input max
+      // row max over the 64 scores: 8 interleaved chains of 3-input max
       float mx[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mx[u] = max3(sv[u], sv[8 + u], sv[16 + u]);
+      for (int e = 0; e < 8; ++e) mx[e] = max3(sv[e], sv[8 + e], sv[16 + e]);
 #pragma unroll
-      for (int i = 24; i < kTile - 8; i += 16)
+      for (int i = 24; i < kUnit - 8; i += 16)
 #pragma unroll
-        for (int u = 0; u < 8; ++u) mx[u] = max3(mx[u], sv[i + u], sv[i + 8 + u]);
+        for (int e = 0; e < 8; ++e) mx[e] = max3(mx[e], sv[i + e], sv[i + 8 + e]);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mx[u] = fmaxf(mx[u], sv[kTile - 8 + u]);
+      for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], sv[kUnit - 8 + e]);
       mx[0] = max3(mx[0], mx[1], mx[2]);
       mx[3] = max3(mx[3], mx[4], mx[5]);
       mx[6] = fmaxf(mx[6], mx[7]);
       const float m_new = fmaxf(m, max3(mx[0], mx[3], mx[6]) * scale_log2);
       // Rescale only when the running max grew by more than 2^8 (the stale max
       // keeps P ≤ 256; exact after the final division by the row sum).
-      const bool resc = (j == 0) || (m_new > m + 8.0f);
+      const bool resc = (u == 0) || (m_new > m + 8.0f);
       const float m_use = resc ? m_new : m;
       const float alpha = resc ? ex2(m - m_use) : 1.0f;
-      if (j > 0) {
-        // P·V(j-1) done: the P columns are free and O is stable
-        if (!(ok = mbar_wait(&sm.o_done[g], (j - 1) & 1, &sm.abort, &g_tc_status, 22 + g))) break;
+      if (u > 0 && __any_sync(0xffffffffu, resc)) {
+        // O must be stable: P·V(u-1) complete
+        if (!(ok = mbar_wait(&sm.o_done[g], (u - 1) & 1, &sm.abort, &g_tc_status, 22 + g))) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-          for (int c = 0; c < kHD / 16; ++c) {
-            uint32_t o16[16];
-            tmem_ld16(oc + c * 16, o16);
-            tmem_ld_wait();
-            reg_fence(o16);
+        for (int c = 0; c < kHD / 16; ++c) {
+          uint32_t o16[16];
+          tmem_ld16(oc + c * 16, o16);
+          tmem_ld_wait();
+          reg_fence(o16);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o16[i] = __float_as_uint(__uint_as_float(o16[i]) * alpha);
-            tmem_st16(oc + c * 16, o16);
-          }
+          for (int i = 0; i < 16; ++i) o16[i] = __float_as_uint(__uint_as_float(o16[i]) * alpha);
+          tmem_st16(oc + c * 16, o16);
         }
       }
       const float nm = -m_use;
       float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < kTile / 32; ++c) {
+      for (int c = 0; c < kUnit / 32; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
@@ -400,7 +398,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
           ls1 += p1;
           pk[e] = pack_f16x2(p0, p1);
         }
-        tmem_st16(pc + c * 16, pk);
+        tmem_st16(sc + c * 16, pk);  // P(u) over the scores it came from
       }
       tmem_st_wait();
       l = l * alpha + (ls0 + ls1);
@@ -408,7 +406,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       tc_fence_before();
       mbar_arrive(&sm.p_full[g]);
     }
-    if (ok) ok = mbar_wait(&sm.o_done[g], (nkv - 1) & 1, &sm.abort, &g_tc_status, 24 + g);
+    if (ok) ok = mbar_wait(&sm.o_done[g], (nu - 1) & 1, &sm.abort, &g_tc_status, 24 + g);
     if (ok) {
       tc_fence_after();
       const int n = q0 + g * kTile + row;
