@@ -53,3 +53,22 @@ def cuda():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda:0")
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean(request):
+    """After every GPU test: no bounded device-side wait may have timed out
+    (a timed-out kernel leaves its outputs unwritten rather than faulting)."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import ctypes
+    import torch
+    if not torch.cuda.is_available():
+        return
+    from vision_rs_b200 import _lib
+    st = ctypes.c_int(-1)
+    _lib.call("va_device_status_read", ctypes.byref(st), torch.cuda.current_stream().cuda_stream)
+    if st.value != 0:
+        _lib.call("va_device_status_clear", torch.cuda.current_stream().cuda_stream)
+        pytest.fail(f"device status word {st.value}: a bounded wait in a tensor-core kernel gave up")

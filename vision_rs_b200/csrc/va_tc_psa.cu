@@ -156,25 +156,31 @@ qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
 //   warps 0-3: softmax for query tile 0, warps 4-7: query tile 1 (thread =
 //              query row = TMEM lane); warp 8 lane 0: TMA producer + MMA issuer.
 // Keys are processed in 64-key units u (two per 128-key K/V stage).  TMEM per
-// query tile g (192 columns at 192·g): two score buffers S[u%2] (f32, 64
-// cols) and O (f32, 64 cols).  The softmax writes P(u) as packed f16 over the
-// first 32 columns of the S buffer it just read; the P·V MMA reads it from
-// there (TMEM A operand).  S(u+2) reuses that buffer and is issued right
-// after P(u)·V, so the in-order tensor pipe orders the reuse and the softmax
-// of unit u+1 finds its scores computed a whole unit earlier.
+// query tile g (256 columns at 256·g): score buffers S[u%2] (f32, 64 cols
+// each), probability buffers P[u%2] (packed f16, 32 cols each, the A operand
+// of the P·V MMA) and O (f32, 64 cols).  S(u+2) is issued as soon as the
+// softmax has released unit u, so the softmax of unit u+1 finds its scores
+// computed a whole unit earlier.  P is never written over S: a TMEM
+// A-operand read of one MMA is not ordered against the accumulator writes of
+// a later MMA, so a buffer is reused only after the MMA that reads it has
+// completed (o_done[u%2]).
 constexpr int kStages = 4;
 constexpr int kUnit = 64;                  // keys per softmax step
 constexpr int kVBlk = kHD * 128;           // one 64-key block of V: [64 channel rows × 128 B] SW128 (8 KB)
 constexpr int kAttnThreads = 288;
 
-__device__ __forceinline__ uint32_t col_s(int g, int buf) { return (uint32_t)g * 192u + (uint32_t)buf * 64u; }
-__device__ __forceinline__ uint32_t col_o(int g) { return (uint32_t)g * 192u + 128u; }
+__device__ __forceinline__ uint32_t col_s(int g, int buf) { return (uint32_t)g * 256u + (uint32_t)buf * 64u; }
+__device__ __forceinline__ uint32_t col_p(int g, int buf) { return (uint32_t)g * 256u + 128u + (uint32_t)buf * 32u; }
+__device__ __forceinline__ uint32_t col_o(int g) { return (uint32_t)g * 256u + 192u; }
 
 struct AttnSmem {
   uint8_t q[2][kTile * 64];                // Q tiles [128 rows × 32] f16, K-major SW64 (8 KB each)
   uint8_t k[kStages][kTile * 64];          // K tiles: 128 keys (8 KB each)
   uint8_t v[kStages][2][kVBlk];            // V: stage × 64-key block
-  uint64_t q_full, kv_full[kStages], kv_empty[kStages], s_full[2][2], p_full[2], o_done[2], fin;
+  // per query tile g, all double-buffered by unit parity: a warpgroup can run
+  // up to two units ahead of the issuer, so one barrier per parity keeps every
+  // parity wait within one phase of its barrier
+  uint64_t q_full, kv_full[kStages], kv_empty[kStages], s_full[2][2], p_full[2][2], o_done[2][2], fin;
   uint32_t tmem_base;
   int abort;
 };
@@ -209,8 +215,10 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
     for (int g = 0; g < 2; ++g) {
       mbar_init(&sm.s_full[g][0], 1);
       mbar_init(&sm.s_full[g][1], 1);
-      mbar_init(&sm.p_full[g], 128);
-      mbar_init(&sm.o_done[g], 1);
+      mbar_init(&sm.p_full[g][0], 128);
+      mbar_init(&sm.p_full[g][1], 128);
+      mbar_init(&sm.o_done[g][0], 1);
+      mbar_init(&sm.o_done[g][1], 1);
     }
     mbar_init(&sm.fin, 1);
     sm.abort = 0;
@@ -256,7 +264,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
         for (int s = 0; s < kKD / 16; ++s) mma_ss(d, qd + (uint64_t)(s * 2), kd_ + (uint64_t)(s * 2), idS, s > 0);
       };
       auto issue_o = [&](int g, int u) {  // O_g += P(u) · V(unit u), P in TMEM
-        const uint32_t d = tmem + col_o(g), a = tmem + col_s(g, u & 1);
+        const uint32_t d = tmem + col_o(g), a = tmem + col_p(g, u & 1);
         const uint64_t vd = dv0 + (uint64_t)(((u >> 1) % kStages) * kVStage + (u & 1) * kVHalf);
 #pragma unroll
         for (int s = 0; s < kUnit / 16; ++s)
@@ -281,10 +289,10 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
           consumed = t + 1;
         }
         for (int g = 0; g < ng && ok; ++g) {
-          if (!(ok = mbar_wait(&sm.p_full[g], u & 1, &sm.abort, &g_tc_status, 13))) break;
+          if (!(ok = mbar_wait(&sm.p_full[g][u & 1], (u >> 1) & 1, &sm.abort, &g_tc_status, 13))) break;
           tc_fence_after();
           issue_o(g, u);
-          mma_commit(&sm.o_done[g]);
+          mma_commit(&sm.o_done[g][u & 1]);
           if (un < nu) {
             issue_s(g, un);
             mma_commit(&sm.s_full[g][un & 1]);
@@ -372,7 +380,8 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       const float alpha = resc ? ex2(m - m_use) : 1.0f;
       if (u > 0 && __any_sync(0xffffffffu, resc)) {
         // O must be stable: P·V(u-1) complete
-        if (!(ok = mbar_wait(&sm.o_done[g], (u - 1) & 1, &sm.abort, &g_tc_status, 22 + g))) break;
+        if (!(ok = mbar_wait(&sm.o_done[g][(u - 1) & 1], ((u - 1) >> 1) & 1, &sm.abort, &g_tc_status, 22 + g)))
+          break;
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < kHD / 16; ++c) {
@@ -385,6 +394,12 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
           tmem_st16(oc + c * 16, o16);
         }
       }
+      // P buffer u%2 is free once P·V(u-2) (its last reader) has completed
+      if (u >= 2) {
+        if (!(ok = mbar_wait(&sm.o_done[g][u & 1], ((u - 2) >> 1) & 1, &sm.abort, &g_tc_status, 26 + g))) break;
+        tc_fence_after();
+      }
+      const uint32_t pc = tmem + lane_off + col_p(g, u & 1);
       const float nm = -m_use;
       float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
@@ -398,15 +413,15 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
           ls1 += p1;
           pk[e] = pack_f16x2(p0, p1);
         }
-        tmem_st16(sc + c * 16, pk);  // P(u) over the scores it came from
+        tmem_st16(pc + c * 16, pk);
       }
       tmem_st_wait();
       l = l * alpha + (ls0 + ls1);
       m = m_use;
       tc_fence_before();
-      mbar_arrive(&sm.p_full[g]);
+      mbar_arrive(&sm.p_full[g][u & 1]);
     }
-    if (ok) ok = mbar_wait(&sm.o_done[g], (nu - 1) & 1, &sm.abort, &g_tc_status, 24 + g);
+    if (ok) ok = mbar_wait(&sm.o_done[g][(nu - 1) & 1], ((nu - 1) >> 1) & 1, &sm.abort, &g_tc_status, 24 + g);
     if (ok) {
       tc_fence_after();
       const int n = q0 + g * kTile + row;
