@@ -154,33 +154,31 @@ qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
 // ── Kernel 2: flash attention ───────────────────────────────────────────────
 // One CTA = two 128-query tiles of one (b, h), sharing every K/V tile.
 //   warps 0-3: softmax for query tile 0, warps 4-7: query tile 1 (thread =
-//              query row = TMEM lane); warp 8 lane 0: TMA producer + MMA issuer.
-// Keys are processed in 64-key units u (two per 128-key K/V stage).  TMEM per
-// query tile g (256 columns at 256·g): score buffers S[u%2] (f32, 64 cols
-// each), probability buffers P[u%2] (packed f16, 32 cols each, the A operand
-// of the P·V MMA) and O (f32, 64 cols).  S(u+2) is issued as soon as the
-// softmax has released unit u, so the softmax of unit u+1 finds its scores
-// computed a whole unit earlier.  P is never written over S: a TMEM
-// A-operand read of one MMA is not ordered against the accumulator writes of
-// a later MMA, so a buffer is reused only after the MMA that reads it has
-// completed (o_done[u%2]).
+//              query row = TMEM lane);
+//   warp 8 lane 0: TMA producer + MMA issuer for tile 0;
+//   warp 9 lane 0: MMA issuer for tile 1.
+// Two issuers because a single thread needs ~90 cycles per tcgen05.mma issue,
+// which for these small head dims (S: N=128, K=32; P·V: N=64) is slower than
+// the tensor pipe executes them.
+// TMEM per query tile g (256 columns at 256·g): S (f32, 128 cols), P (packed
+// f16, 64 cols, the A operand of the P·V MMA) and O (f32, 64 cols).  S(j+1) is
+// issued as soon as the softmax has copied S(j) into registers (s_free), so
+// the next tile's scores compute while this tile's exponentials run.  P is
+// written to its own columns: it is reused only after the MMA that read it
+// has completed (o_done).
 constexpr int kStages = 4;
-constexpr int kUnit = 64;                  // keys per softmax step
 constexpr int kVBlk = kHD * 128;           // one 64-key block of V: [64 channel rows × 128 B] SW128 (8 KB)
-constexpr int kAttnThreads = 288;
+constexpr int kAttnThreads = 320;
 
-__device__ __forceinline__ uint32_t col_s(int g, int buf) { return (uint32_t)g * 256u + (uint32_t)buf * 64u; }
-__device__ __forceinline__ uint32_t col_p(int g, int buf) { return (uint32_t)g * 256u + 128u + (uint32_t)buf * 32u; }
+__device__ __forceinline__ uint32_t col_s(int g) { return (uint32_t)g * 256u; }
+__device__ __forceinline__ uint32_t col_p(int g) { return (uint32_t)g * 256u + 128u; }
 __device__ __forceinline__ uint32_t col_o(int g) { return (uint32_t)g * 256u + 192u; }
 
 struct AttnSmem {
   uint8_t q[2][kTile * 64];                // Q tiles [128 rows × 32] f16, K-major SW64 (8 KB each)
-  uint8_t k[kStages][kTile * 64];          // K tiles: 128 keys (8 KB each)
-  uint8_t v[kStages][2][kVBlk];            // V: stage × 64-key block
-  // per query tile g, all double-buffered by unit parity: a warpgroup can run
-  // up to two units ahead of the issuer, so one barrier per parity keeps every
-  // parity wait within one phase of its barrier
-  uint64_t q_full, kv_full[kStages], kv_empty[kStages], s_full[2][2], p_full[2][2], o_done[2][2], fin;
+  uint8_t k[kStages][kTile * 64];          // K tiles (8 KB each)
+  uint8_t v[kStages][2][kVBlk];            // V: stage × key-block
+  uint64_t q_full, kv_full[kStages], kv_empty[kStages], s_full[2], s_free[2], p_full[2], o_done[2], fin[2];
   uint32_t tmem_base;
   int abort;
 };
@@ -201,8 +199,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int q0 = blockIdx.x * 2 * kTile, bh = blockIdx.y;
   const int BH = gridDim.y, b = bh / nh, h = bh % nh;
-  const int ntl = (N + kTile - 1) / kTile;   // 128-key K/V tiles
-  const int nu = (N + kUnit - 1) / kUnit;    // 64-key units
+  const int nkv = (N + kTile - 1) / kTile;
   const bool has1 = q0 + kTile < N;
   const int vrow = b * kC + h * kHD;
 
@@ -210,17 +207,15 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
     mbar_init(&sm.q_full, 1);
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.kv_full[i], 1);
-      mbar_init(&sm.kv_empty[i], 1);
+      mbar_init(&sm.kv_empty[i], has1 ? 2 : 1);  // one commit per issuer
     }
     for (int g = 0; g < 2; ++g) {
-      mbar_init(&sm.s_full[g][0], 1);
-      mbar_init(&sm.s_full[g][1], 1);
-      mbar_init(&sm.p_full[g][0], 128);
-      mbar_init(&sm.p_full[g][1], 128);
-      mbar_init(&sm.o_done[g][0], 1);
-      mbar_init(&sm.o_done[g][1], 1);
+      mbar_init(&sm.s_full[g], 1);
+      mbar_init(&sm.s_free[g], 128);
+      mbar_init(&sm.p_full[g], 128);
+      mbar_init(&sm.o_done[g], 1);
+      mbar_init(&sm.fin[g], 1);
     }
-    mbar_init(&sm.fin, 1);
     sm.abort = 0;
     fence_mbar_init();
   }
@@ -233,98 +228,91 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  if (warp == 8) {
-    if (lane == 0) {
-      // ── control thread: TMA producer and MMA issuer ──
-      tma_prefetch_desc(&map_qk);
-      tma_prefetch_desc(&map_v);
-      mbar_arrive_expect_tx(&sm.q_full, (has1 ? 2 : 1) * kTile * 64);
-      tma_load_3d(sm.q[0], &map_qk, &sm.q_full, 0, q0, bh);
-      if (has1) tma_load_3d(sm.q[1], &map_qk, &sm.q_full, 0, q0 + kTile, bh);
+  if (warp >= 8) {
+    const int g = warp - 8;
+    if (lane == 0 && (g == 0 || has1)) {
+      // ── issuer for query tile g (issuer 0 also drives TMA) ──
+      const bool producer = g == 0;
       int issued = 0;
-      for (; issued < kStages && issued < ntl; ++issued)
-        attn_load_kv(sm, &map_qk, &map_v, issued, issued, BH, bh, vrow);
-
-      constexpr uint32_t idS = idesc_f32acc(128, kUnit, AB_F16, false, false);
+      if (producer) {
+        tma_prefetch_desc(&map_qk);
+        tma_prefetch_desc(&map_v);
+        mbar_arrive_expect_tx(&sm.q_full, (has1 ? 2 : 1) * kTile * 64);
+        tma_load_3d(sm.q[0], &map_qk, &sm.q_full, 0, q0, bh);
+        if (has1) tma_load_3d(sm.q[1], &map_qk, &sm.q_full, 0, q0 + kTile, bh);
+        for (; issued < kStages && issued < nkv; ++issued)
+          attn_load_kv(sm, &map_qk, &map_v, issued, issued, BH, bh, vrow);
+      }
+      constexpr uint32_t idS = idesc_f32acc(128, kTile, AB_F16, false, false);
       constexpr uint32_t idO = idesc_f32acc(128, kHD, AB_F16, false, false);
-      const int ng = has1 ? 2 : 1;
-      // Descriptors are built once; a stage / key half / k-step only moves the
-      // start-address field (bits 0-13, address >> 4) — a plain add that
-      // cannot carry out of the field for shared-memory addresses.
-      const uint64_t dq0 = sdesc(smem_u32(sm.q[0]), 16, 512, SW_64B);
+      // Descriptors are built once; a stage / k-step only moves the start-
+      // address field (bits 0-13, address >> 4) — a plain add that cannot
+      // carry out of the field for shared-memory addresses.
+      const uint64_t dq = sdesc(smem_u32(sm.q[g]), 16, 512, SW_64B);
       const uint64_t dk0 = sdesc(smem_u32(sm.k[0]), 16, 512, SW_64B);
       const uint64_t dv0 = sdesc(smem_u32(sm.v[0][0]), 16, 1024, SW_128B);
-      constexpr uint32_t kQStep = (kTile * 64) >> 4, kKStage = (kTile * 64) >> 4, kKHalf = (kUnit * 64) >> 4;
-      constexpr uint32_t kVStage = (2 * kVBlk) >> 4, kVHalf = kVBlk >> 4;
-      auto issue_s = [&](int g, int u) {  // S_g[u%2] = Q_g · K(unit u)ᵀ
-        const uint32_t d = tmem + col_s(g, u & 1);
-        const uint64_t qd = dq0 + (uint64_t)(g * kQStep);
-        const uint64_t kd_ = dk0 + (uint64_t)(((u >> 1) % kStages) * kKStage + (u & 1) * kKHalf);
-#pragma unroll
-        for (int s = 0; s < kKD / 16; ++s) mma_ss(d, qd + (uint64_t)(s * 2), kd_ + (uint64_t)(s * 2), idS, s > 0);
+      constexpr uint32_t kKStage = (kTile * 64) >> 4, kVStage = (2 * kVBlk) >> 4, kVHalf = kVBlk >> 4;
+      const uint32_t ds = tmem + col_s(g), dp = tmem + col_p(g), dO = tmem + col_o(g);
+      auto issue_s = [&](int stage) {
+        const uint64_t kd_ = dk0 + (uint64_t)(stage * kKStage);
+        mma_ss(ds, dq, kd_, idS, 0u);
+        mma_ss(ds, dq + 2, kd_ + 2, idS, 1u);
       };
-      auto issue_o = [&](int g, int u) {  // O_g += P(u) · V(unit u), P in TMEM
-        const uint32_t d = tmem + col_o(g), a = tmem + col_p(g, u & 1);
-        const uint64_t vd = dv0 + (uint64_t)(((u >> 1) % kStages) * kVStage + (u & 1) * kVHalf);
+      auto issue_o = [&](int stage, uint32_t acc) {
+        const uint64_t vd = dv0 + (uint64_t)(stage * kVStage);
+        mma_ts(dO, dp, vd, idO, acc);
 #pragma unroll
-        for (int s = 0; s < kUnit / 16; ++s)
-          mma_ts(d, a + s * 8, vd + (uint64_t)(s * 2), idO, (u > 0 || s > 0) ? 1u : 0u);
+        for (int s = 1; s < kTile / 16; ++s)
+          mma_ts(dO, dp + s * 8, vd + (uint64_t)((s >> 2) * kVHalf + (s & 3) * 2), idO, 1u);
       };
       bool ok = mbar_wait(&sm.q_full, 0, &sm.abort, &g_tc_status, 10) &&
                 mbar_wait(&sm.kv_full[0], 0, &sm.abort, &g_tc_status, 11);
-      int consumed = ok ? 1 : 0;  // K/V tiles whose full barrier was observed
+      int consumed = ok ? 1 : 0;  // K/V tiles whose full barrier this thread observed
       if (ok) {
         tc_fence_after();
-        for (int u = 0; u < 2 && u < nu; ++u)
-          for (int g = 0; g < ng; ++g) {
-            issue_s(g, u);
-            mma_commit(&sm.s_full[g][u & 1]);
-          }
+        issue_s(0);
+        mma_commit(&sm.s_full[g]);
       }
-      for (int u = 0; ok && u < nu; ++u) {
-        const int un = u + 2;  // unit whose scores are issued after this unit's P·V
-        if (un < nu && (un & 1) == 0) {
-          const int t = un >> 1;
-          if (!(ok = mbar_wait(&sm.kv_full[t % kStages], (t / kStages) & 1, &sm.abort, &g_tc_status, 12))) break;
-          consumed = t + 1;
-        }
-        for (int g = 0; g < ng && ok; ++g) {
-          if (!(ok = mbar_wait(&sm.p_full[g][u & 1], (u >> 1) & 1, &sm.abort, &g_tc_status, 13))) break;
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int st = j % kStages;
+        if (j + 1 < nkv) {
+          const int stn = (j + 1) % kStages;
+          if (!(ok = mbar_wait(&sm.kv_full[stn], ((j + 1) / kStages) & 1, &sm.abort, &g_tc_status, 12))) break;
+          consumed = j + 2;
+          if (!(ok = mbar_wait(&sm.s_free[g], j & 1, &sm.abort, &g_tc_status, 13))) break;
           tc_fence_after();
-          issue_o(g, u);
-          mma_commit(&sm.o_done[g][u & 1]);
-          if (un < nu) {
-            issue_s(g, un);
-            mma_commit(&sm.s_full[g][un & 1]);
+          issue_s(stn);
+          mma_commit(&sm.s_full[g]);
+        }
+        if (!(ok = mbar_wait(&sm.p_full[g], j & 1, &sm.abort, &g_tc_status, 14))) break;
+        tc_fence_after();
+        issue_o(st, j > 0 ? 1u : 0u);
+        mma_commit(&sm.o_done[g]);
+        mma_commit(&sm.kv_empty[st]);
+        // producer: refill the stage tile j-1 used (both issuers done with it) with tile j+3
+        if (producer && j >= 1 && j + kStages - 1 < nkv) {
+          const int sp = (j - 1) % kStages;
+          if (!(ok = mbar_wait(&sm.kv_empty[sp], ((j - 1) / kStages) & 1, &sm.abort, &g_tc_status, 15))) break;
+          attn_load_kv(sm, &map_qk, &map_v, j + kStages - 1, sp, BH, bh, vrow);
+          ++issued;
+        }
+      }
+      // teardown: every TMA load issued here has landed, every MMA issued here completed
+      if (producer) {
+        for (int t = consumed; t < issued; ++t) {
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&sm.kv_full[t % kStages], (t / kStages) & 1) && clock64() - t0 < kSpinCycles) {
           }
         }
-        if (!ok) break;
-        if ((u & 1) || u == nu - 1) {
-          const int t = u >> 1;
-          mma_commit(&sm.kv_empty[t % kStages]);
-          // refill the stage tile t-1 used (its MMAs finished long ago) with tile t+3
-          if (t >= 1 && t + kStages - 1 < ntl) {
-            const int sp = (t - 1) % kStages;
-            if (!(ok = mbar_wait(&sm.kv_empty[sp], ((t - 1) / kStages) & 1, &sm.abort, &g_tc_status, 14))) break;
-            attn_load_kv(sm, &map_qk, &map_v, t + kStages - 1, sp, BH, bh, vrow);
-            ++issued;
+        if (!ok) {
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&sm.q_full, 0) && clock64() - t0 < kSpinCycles) {
           }
         }
       }
-      // teardown: every issued TMA load has landed and every MMA has completed
-      for (int t = consumed; t < issued; ++t) {
-        const long long t0 = clock64();
-        while (!mbar_try_wait(&sm.kv_full[t % kStages], (t / kStages) & 1) && clock64() - t0 < kSpinCycles) {
-        }
-      }
-      if (!ok) {
-        const long long t0 = clock64();
-        while (!mbar_try_wait(&sm.q_full, 0) && clock64() - t0 < kSpinCycles) {
-        }
-      }
-      mma_commit(&sm.fin);
+      mma_commit(&sm.fin[g]);
       const long long t0 = clock64();
-      while (!mbar_try_wait(&sm.fin, 0) && clock64() - t0 < kSpinCycles) {
+      while (!mbar_try_wait(&sm.fin[g], 0) && clock64() - t0 < kSpinCycles) {
       }
     }
     __syncwarp();
@@ -332,78 +320,80 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
     // ── softmax warpgroup g: thread = query row (TMEM lane) ──
     const int g = warp >> 2, row = tid & 127;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t oc = tmem + lane_off + col_o(g);
+    const uint32_t sc = tmem + lane_off + col_s(g), pc = tmem + lane_off + col_p(g), oc = tmem + lane_off + col_o(g);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int u = 0; u < nu; ++u) {
-      const uint32_t sc = tmem + lane_off + col_s(g, u & 1);
-      if (!(ok = mbar_wait(&sm.s_full[g][u & 1], (u >> 1) & 1, &sm.abort, &g_tc_status, 20 + g))) break;
+    for (int j = 0; j < nkv; ++j) {
+      if (!(ok = mbar_wait(&sm.s_full[g], j & 1, &sm.abort, &g_tc_status, 20 + g))) break;
       tc_fence_after();
-      float sv[kUnit];
+      float sv[kTile];
       {
-        uint32_t r0[32], r1[32];
+        uint32_t r0[32], r1[32], r2[32], r3[32];
         tmem_ld32(sc + 0, r0);
         tmem_ld32(sc + 32, r1);
+        tmem_ld32(sc + 64, r2);
+        tmem_ld32(sc + 96, r3);
         tmem_ld_wait();
         reg_fence(r0);
         reg_fence(r1);
+        reg_fence(r2);
+        reg_fence(r3);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           sv[i] = __uint_as_float(r0[i]);
           sv[32 + i] = __uint_as_float(r1[i]);
+          sv[64 + i] = __uint_as_float(r2[i]);
+          sv[96 + i] = __uint_as_float(r3[i]);
         }
       }
-      const int kvalid = N - u * kUnit;
-      if (kvalid < kUnit) {
+      tc_fence_before();
+      mbar_arrive(&sm.s_free[g]);  // S columns may now take the next tile's scores
+      const int kvalid = N - j * kTile;
+      if (kvalid < kTile) {
 #pragma unroll
-        for (int i = 0; i < kUnit; ++i)
+        for (int i = 0; i < kTile; ++i)
           if (i >= kvalid) sv[i] = -INFINITY;
       }
-      // row max over the 64 scores: 8 interleaved chains of 3-input max
+      // row max over all 128 scores: 8 interleaved chains of 3-input max
       float mx[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx[e] = max3(sv[e], sv[8 + e], sv[16 + e]);
 #pragma unroll
-      for (int i = 24; i < kUnit - 8; i += 16)
+      for (int i = 24; i < kTile - 8; i += 16)
 #pragma unroll
         for (int e = 0; e < 8; ++e) mx[e] = max3(mx[e], sv[i + e], sv[i + 8 + e]);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], sv[kUnit - 8 + e]);
+      for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], sv[kTile - 8 + e]);
       mx[0] = max3(mx[0], mx[1], mx[2]);
       mx[3] = max3(mx[3], mx[4], mx[5]);
       mx[6] = fmaxf(mx[6], mx[7]);
       const float m_new = fmaxf(m, max3(mx[0], mx[3], mx[6]) * scale_log2);
       // Rescale only when the running max grew by more than 2^8 (the stale max
       // keeps P ≤ 256; exact after the final division by the row sum).
-      const bool resc = (u == 0) || (m_new > m + 8.0f);
+      const bool resc = (j == 0) || (m_new > m + 8.0f);
       const float m_use = resc ? m_new : m;
       const float alpha = resc ? ex2(m - m_use) : 1.0f;
-      if (u > 0 && __any_sync(0xffffffffu, resc)) {
-        // O must be stable: P·V(u-1) complete
-        if (!(ok = mbar_wait(&sm.o_done[g][(u - 1) & 1], ((u - 1) >> 1) & 1, &sm.abort, &g_tc_status, 22 + g)))
-          break;
+      if (j > 0) {
+        // P·V(j-1) done: the P columns are free and O is stable
+        if (!(ok = mbar_wait(&sm.o_done[g], (j - 1) & 1, &sm.abort, &g_tc_status, 22 + g))) break;
         tc_fence_after();
+        if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-        for (int c = 0; c < kHD / 16; ++c) {
-          uint32_t o16[16];
-          tmem_ld16(oc + c * 16, o16);
-          tmem_ld_wait();
-          reg_fence(o16);
+          for (int c = 0; c < kHD / 16; ++c) {
+            uint32_t o16[16];
+            tmem_ld16(oc + c * 16, o16);
+            tmem_ld_wait();
+            reg_fence(o16);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o16[i] = __float_as_uint(__uint_as_float(o16[i]) * alpha);
-          tmem_st16(oc + c * 16, o16);
+            for (int i = 0; i < 16; ++i) o16[i] = __float_as_uint(__uint_as_float(o16[i]) * alpha);
+            tmem_st16(oc + c * 16, o16);
+          }
         }
       }
-      // P buffer u%2 is free once P·V(u-2) (its last reader) has completed
-      if (u >= 2) {
-        if (!(ok = mbar_wait(&sm.o_done[g][u & 1], ((u - 2) >> 1) & 1, &sm.abort, &g_tc_status, 26 + g))) break;
-        tc_fence_after();
-      }
-      const uint32_t pc = tmem + lane_off + col_p(g, u & 1);
       const float nm = -m_use;
       float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < kUnit / 32; ++c) {
+      for (int c = 0; c < kTile / 32; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
@@ -419,9 +409,9 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       l = l * alpha + (ls0 + ls1);
       m = m_use;
       tc_fence_before();
-      mbar_arrive(&sm.p_full[g][u & 1]);
+      mbar_arrive(&sm.p_full[g]);
     }
-    if (ok) ok = mbar_wait(&sm.o_done[g][(nu - 1) & 1], ((nu - 1) >> 1) & 1, &sm.abort, &g_tc_status, 24 + g);
+    if (ok) ok = mbar_wait(&sm.o_done[g], (nkv - 1) & 1, &sm.abort, &g_tc_status, 24 + g);
     if (ok) {
       tc_fence_after();
       const int n = q0 + g * kTile + row;
