@@ -160,6 +160,10 @@ qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
 // Two issuers because a single thread needs ~90 cycles per tcgen05.mma issue,
 // which for these small head dims (S: N=128, K=32; P·V: N=64) is slower than
 // the tensor pipe executes them.
+// The two softmax groups take turns on the exponentials (a token passed via
+// mufu[]): group 1 runs the exps of tile j while group 0 loads and reduces
+// the scores of tile j+1, and vice versa, so the MUFU is not idle during the
+// row-max / barrier phases.
 // TMEM per query tile g (256 columns at 256·g): S (f32, 128 cols), P (packed
 // f16, 64 cols, the A operand of the P·V MMA) and O (f32, 64 cols).  S(j+1) is
 // issued as soon as the softmax has copied S(j) into registers (s_free), so
@@ -179,6 +183,7 @@ struct AttnSmem {
   uint8_t k[kStages][kTile * 64];          // K tiles (8 KB each)
   uint8_t v[kStages][2][kVBlk];            // V: stage × key-block
   uint64_t q_full, kv_full[kStages], kv_empty[kStages], s_full[2], s_free[2], p_full[2], o_done[2], fin[2];
+  uint64_t mufu[2];  // ping-pong token: group g may run the exponentials of its next tile
   uint32_t tmem_base;
   int abort;
 };
@@ -215,6 +220,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       mbar_init(&sm.p_full[g], 128);
       mbar_init(&sm.o_done[g], 1);
       mbar_init(&sm.fin[g], 1);
+      mbar_init(&sm.mufu[g], 128);
     }
     sm.abort = 0;
     fence_mbar_init();
@@ -390,6 +396,10 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
           }
         }
       }
+      // ping-pong: group 0 runs exps of tile j after group 1 finished tile j-1;
+      // group 1 after group 0 finished tile j
+      const bool pp = has1 && (g == 1 || j > 0);
+      if (pp && !(ok = mbar_wait(&sm.mufu[g], (g == 0 ? j - 1 : j) & 1, &sm.abort, &g_tc_status, 28 + g))) break;
       const float nm = -m_use;
       float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
@@ -405,6 +415,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
         }
         tmem_st16(pc + c * 16, pk);
       }
+      if (has1) mbar_arrive(&sm.mufu[g ^ 1]);  // hand the exponential unit to the other group
       tmem_st_wait();
       l = l * alpha + (ls0 + ls1);
       m = m_use;
