@@ -228,6 +228,26 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   return r;
 }
 
+// 2^x on the FMA pipe, to share the exponential work with the MUFU unit.
+// Cody–Waite range reduction x = n + f (n integer, |f| ≤ 1/2; the rounding
+// uses the 1.5·2^23 magic-number addition), then a degree-4 polynomial for
+// 2^f fitted here on [-1/2, 1/2] by iteratively reweighted least squares on
+// Chebyshev nodes (Lawson's method, max relative error 2.7e-6), and n is
+// added to the exponent field with one integer multiply-add.  Inputs are
+// clamped to [-125, 127]; below -125 the result (≤ 2^-125) is far under
+// anything a probability in f16 can hold.
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fminf(fmaxf(x, -125.0f), 127.0f);
+  const float t = __fadd_rn(x, 12582912.0f);
+  const float n = __fsub_rn(t, 12582912.0f);
+  const float f = __fsub_rn(x, n);
+  float p = fmaf(f, 0.009570101276040077f, 0.05591785907745361f);
+  p = fmaf(p, f, 0.240247443318367f);
+  p = fmaf(p, f, 0.6931217908859253f);
+  p = fmaf(p, f, 0.9999992847442627f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

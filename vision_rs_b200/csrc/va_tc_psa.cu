@@ -173,6 +173,7 @@ qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
 constexpr int kStages = 4;
 constexpr int kVBlk = kHD * 128;           // one 64-key block of V: [64 channel rows × 128 B] SW128 (8 KB)
 constexpr int kAttnThreads = 320;
+constexpr int kPolyEvery = 4;              // 1/4 of the exponentials on the FMA pipe
 
 __device__ __forceinline__ uint32_t col_s(int g) { return (uint32_t)g * 256u; }
 __device__ __forceinline__ uint32_t col_p(int g) { return (uint32_t)g * 256u + 128u; }
@@ -196,7 +197,7 @@ __device__ __forceinline__ void attn_load_kv(AttnSmem& sm, const CUtensorMap* mq
   tma_load_2d(sm.v[stage][1], mv, &sm.kv_full[stage], t * kTile + 64, vrow);
 }
 
-__global__ void __launch_bounds__(kAttnThreads, 1)
+__global__ void __maxnreg__(200)
 attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v,
             __half* __restrict__ obuf, float* __restrict__ lse, int N, int Np, int nh, float scale_log2) {
   extern __shared__ uint8_t smem_raw[];
@@ -407,8 +408,12 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], scale_log2, nm));
-          const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], scale_log2, nm));
+          // every kPolyEvery-th pair on the FMA pipe, the rest on the MUFU
+          const bool poly = (e % kPolyEvery) == kPolyEvery - 1;
+          const float x0 = fmaf(sv[c * 32 + 2 * e], scale_log2, nm);
+          const float x1 = fmaf(sv[c * 32 + 2 * e + 1], scale_log2, nm);
+          const float p0 = poly ? ex2_poly(x0) : ex2(x0);
+          const float p1 = poly ? ex2_poly(x1) : ex2(x1);
           ls0 += p0;
           ls1 += p1;
           pk[e] = pack_f16x2(p0, p1);
