@@ -197,7 +197,7 @@ __device__ __forceinline__ void attn_load_kv(AttnSmem& sm, const CUtensorMap* mq
   tma_load_2d(sm.v[stage][1], mv, &sm.kv_full[stage], t * kTile + 64, vrow);
 }
 
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kAttnThreads, 1)
 attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v,
             __half* __restrict__ obuf, float* __restrict__ lse, int N, int Np, int nh, float scale_log2) {
   extern __shared__ uint8_t smem_raw[];
