@@ -152,28 +152,31 @@ qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
 }
 
 // ── Kernel 2: flash attention ───────────────────────────────────────────────
-// One CTA = two 128-query tiles of one (b, h), sharing every K/V tile.
-//   warps 0-3: softmax for query tile 0, warps 4-7: query tile 1 (thread =
-//              query row = TMEM lane);
-//   warp 8 lane 0: TMA producer + MMA issuer for tile 0;
-//   warp 9 lane 0: MMA issuer for tile 1.
-// Two issuers because a single thread needs ~90 cycles per tcgen05.mma issue,
-// which for these small head dims (S: N=128, K=32; P·V: N=64) is slower than
-// the tensor pipe executes them.
-// The two softmax groups take turns on the exponentials (a token passed via
-// mufu[]): group 1 runs the exps of tile j while group 0 loads and reduces
-// the scores of tile j+1, and vice versa, so the MUFU is not idle during the
-// row-max / barrier phases.
-// TMEM per query tile g (256 columns at 256·g): S (f32, 128 cols), P (packed
-// f16, 64 cols, the A operand of the P·V MMA) and O (f32, 64 cols).  S(j+1) is
-// issued as soon as the softmax has copied S(j) into registers (s_free), so
-// the next tile's scores compute while this tile's exponentials run.  P is
-// written to its own columns: it is reused only after the MMA that read it
-// has completed (o_done).
+// One CTA = two 128-query tiles (groups g = 0, 1) of one (b, h), sharing
+// every K/V tile.  Each query row is split across two warps: warps
+// 8g + 4h + w (h = 0, 1; w = 0..3) handle rows 32w..32w+31 (TMEM lanes) and
+// key columns 64h..64h+63 of group g, so 16 softmax warps (4 per SM
+// sub-partition) feed the exponential unit.  The halves combine their row
+// maxima through shared memory under a per-group named barrier.
+//   warp 16 lane 0: TMA producer + MMA issuer for group 0;
+//   warp 17 lane 0: MMA issuer for group 1 (one thread needs ~90 cycles per
+//   tcgen05.mma issue, slower than the tensor pipe runs these small MMAs).
+// (The exchange uses an mbarrier with a bounded wait rather than bar.sync, so
+// a half that aborts cannot leave its partner blocked.)
+// The two groups take turns on the exponentials (a token passed via mufu[]):
+// one group's exponentials overlap the other's score loads, row maxima and
+// barrier waits.
+// TMEM per group g (256 columns at 256·g): S (f32, 128 cols), P (packed f16,
+// 64 cols; the A operand of the P·V MMA) and O (f32, 64 cols).  S(j+1) is
+// issued as soon as the softmax has copied S(j) into registers (s_free).  P
+// has its own columns: a TMEM A-operand read of one MMA is not ordered
+// against a later MMA's accumulator writes, so P is rewritten only after the
+// MMA that read it completed (o_done).
 constexpr int kStages = 4;
 constexpr int kVBlk = kHD * 128;           // one 64-key block of V: [64 channel rows × 128 B] SW128 (8 KB)
-constexpr int kAttnThreads = 320;
-constexpr int kPolyEvery = 4;              // 1/4 of the exponentials on the FMA pipe
+constexpr int kSoftWarps = 16;
+constexpr int kAttnThreads = (kSoftWarps + 2) * 32;
+constexpr int kHalf = kTile / 2;           // key columns per softmax thread
 
 __device__ __forceinline__ uint32_t col_s(int g) { return (uint32_t)g * 256u; }
 __device__ __forceinline__ uint32_t col_p(int g) { return (uint32_t)g * 256u + 128u; }
@@ -183,8 +186,11 @@ struct AttnSmem {
   uint8_t q[2][kTile * 64];                // Q tiles [128 rows × 32] f16, K-major SW64 (8 KB each)
   uint8_t k[kStages][kTile * 64];          // K tiles (8 KB each)
   uint8_t v[kStages][2][kVBlk];            // V: stage × key-block
+  float xmax[2][2][2][kTile];              // [tile parity][group][half][row] partial row maxima
+  float xsum[2][2][kTile];                 // [group][half][row] partial row sums (end of loop)
   uint64_t q_full, kv_full[kStages], kv_empty[kStages], s_full[2], s_free[2], p_full[2], o_done[2], fin[2];
-  uint64_t mufu[2];  // ping-pong token: group g may run the exponentials of its next tile
+  uint64_t mufu[2];                        // ping-pong token: group g may run the exponentials of its next tile
+  uint64_t xbar[2], fbar[2];               // per group: row-max exchange (per tile), row-sum exchange (end)
   uint32_t tmem_base;
   int abort;
 };
@@ -217,11 +223,13 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
     }
     for (int g = 0; g < 2; ++g) {
       mbar_init(&sm.s_full[g], 1);
-      mbar_init(&sm.s_free[g], 128);
-      mbar_init(&sm.p_full[g], 128);
+      mbar_init(&sm.s_free[g], 256);
+      mbar_init(&sm.p_full[g], 256);
       mbar_init(&sm.o_done[g], 1);
       mbar_init(&sm.fin[g], 1);
-      mbar_init(&sm.mufu[g], 128);
+      mbar_init(&sm.mufu[g], 256);
+      mbar_init(&sm.xbar[g], 256);
+      mbar_init(&sm.fbar[g], 256);
     }
     sm.abort = 0;
     fence_mbar_init();
@@ -235,10 +243,10 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  if (warp >= 8) {
-    const int g = warp - 8;
+  if (warp >= kSoftWarps) {
+    const int g = warp - kSoftWarps;
     if (lane == 0 && (g == 0 || has1)) {
-      // ── issuer for query tile g (issuer 0 also drives TMA) ──
+      // ── issuer for group g (issuer 0 also drives TMA) ──
       const bool producer = g == 0;
       int issued = 0;
       if (producer) {
@@ -323,60 +331,62 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       }
     }
     __syncwarp();
-  } else if (warp < 4 || has1) {
-    // ── softmax warpgroup g: thread = query row (TMEM lane) ──
-    const int g = warp >> 2, row = tid & 127;
+  } else if (warp < 8 || has1) {
+    // ── softmax: group g, key half hf, thread = query row (TMEM lane) ──
+    const int g = warp >> 3, hf = (warp >> 2) & 1, row = (warp & 3) * 32 + lane;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t sc = tmem + lane_off + col_s(g), pc = tmem + lane_off + col_p(g), oc = tmem + lane_off + col_o(g);
+    const uint32_t sc = tmem + lane_off + col_s(g) + hf * kHalf;
+    const uint32_t pc = tmem + lane_off + col_p(g) + hf * (kHalf / 2);
+    const uint32_t oc = tmem + lane_off + col_o(g) + hf * (kHD / 2);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       if (!(ok = mbar_wait(&sm.s_full[g], j & 1, &sm.abort, &g_tc_status, 20 + g))) break;
       tc_fence_after();
-      float sv[kTile];
+      float sv[kHalf];
       {
-        uint32_t r0[32], r1[32], r2[32], r3[32];
+        uint32_t r0[32], r1[32];
         tmem_ld32(sc + 0, r0);
         tmem_ld32(sc + 32, r1);
-        tmem_ld32(sc + 64, r2);
-        tmem_ld32(sc + 96, r3);
         tmem_ld_wait();
         reg_fence(r0);
         reg_fence(r1);
-        reg_fence(r2);
-        reg_fence(r3);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           sv[i] = __uint_as_float(r0[i]);
           sv[32 + i] = __uint_as_float(r1[i]);
-          sv[64 + i] = __uint_as_float(r2[i]);
-          sv[96 + i] = __uint_as_float(r3[i]);
         }
       }
       tc_fence_before();
       mbar_arrive(&sm.s_free[g]);  // S columns may now take the next tile's scores
-      const int kvalid = N - j * kTile;
-      if (kvalid < kTile) {
+      const int kvalid = N - j * kTile - hf * kHalf;
+      if (kvalid < kHalf) {
 #pragma unroll
-        for (int i = 0; i < kTile; ++i)
+        for (int i = 0; i < kHalf; ++i)
           if (i >= kvalid) sv[i] = -INFINITY;
       }
-      // row max over all 128 scores: 8 interleaved chains of 3-input max
+      // partial row max over this thread's 64 scores, then combine the halves
       float mx[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx[e] = max3(sv[e], sv[8 + e], sv[16 + e]);
 #pragma unroll
-      for (int i = 24; i < kTile - 8; i += 16)
+      for (int i = 24; i < kHalf - 8; i += 16)
 #pragma unroll
         for (int e = 0; e < 8; ++e) mx[e] = max3(mx[e], sv[i + e], sv[i + 8 + e]);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], sv[kTile - 8 + e]);
+      for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], sv[kHalf - 8 + e]);
       mx[0] = max3(mx[0], mx[1], mx[2]);
       mx[3] = max3(mx[3], mx[4], mx[5]);
       mx[6] = fmaxf(mx[6], mx[7]);
-      const float m_new = fmaxf(m, max3(mx[0], mx[3], mx[6]) * scale_log2);
+      const float pmax = max3(mx[0], mx[3], mx[6]);
+      sm.xmax[j & 1][g][hf][row] = pmax;
+      mbar_arrive(&sm.xbar[g]);  // release: the partial max is visible to the other half
+      if (!(ok = mbar_wait(&sm.xbar[g], j & 1, &sm.abort, &g_tc_status, 30 + g))) break;
+      const float rmax = fmaxf(pmax, sm.xmax[j & 1][g][hf ^ 1][row]);
+      const float m_new = fmaxf(m, rmax * scale_log2);
       // Rescale only when the running max grew by more than 2^8 (the stale max
-      // keeps P ≤ 256; exact after the final division by the row sum).
+      // keeps P ≤ 256; exact after the final division by the row sum).  Both
+      // halves see the same maxima, so they make the same decision.
       const bool resc = (j == 0) || (m_new > m + 8.0f);
       const float m_use = resc ? m_new : m;
       const float alpha = resc ? ex2(m - m_use) : 1.0f;
@@ -386,7 +396,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
         tc_fence_after();
         if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-          for (int c = 0; c < kHD / 16; ++c) {
+          for (int c = 0; c < kHD / 32; ++c) {  // this half's 32 output columns
             uint32_t o16[16];
             tmem_ld16(oc + c * 16, o16);
             tmem_ld_wait();
@@ -404,16 +414,12 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       const float nm = -m_use;
       float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < kTile / 32; ++c) {
+      for (int c = 0; c < kHalf / 32; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          // every kPolyEvery-th pair on the FMA pipe, the rest on the MUFU
-          const bool poly = (e % kPolyEvery) == kPolyEvery - 1;
-          const float x0 = fmaf(sv[c * 32 + 2 * e], scale_log2, nm);
-          const float x1 = fmaf(sv[c * 32 + 2 * e + 1], scale_log2, nm);
-          const float p0 = poly ? ex2_poly(x0) : ex2(x0);
-          const float p1 = poly ? ex2_poly(x1) : ex2(x1);
+          const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], scale_log2, nm));
+          const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], scale_log2, nm));
           ls0 += p0;
           ls1 += p1;
           pk[e] = pack_f16x2(p0, p1);
@@ -428,23 +434,25 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       mbar_arrive(&sm.p_full[g]);
     }
     if (ok) ok = mbar_wait(&sm.o_done[g], (nkv - 1) & 1, &sm.abort, &g_tc_status, 24 + g);
+    // combine the halves' row sums (every thread of the group reaches this barrier)
+    sm.xsum[g][hf][row] = l;
+    mbar_arrive(&sm.fbar[g]);
+    if (ok) ok = mbar_wait(&sm.fbar[g], 0, &sm.abort, &g_tc_status, 32 + g);
+    const float lt = l + sm.xsum[g][hf ^ 1][row];
     if (ok) {
       tc_fence_after();
       const int n = q0 + g * kTile + row;
-      const float inv = 1.0f / l;
+      const float inv = 1.0f / lt;
+      uint32_t o[32];
+      tmem_ld32(oc, o);
+      tmem_ld_wait();
+      reg_fence(o);
+      if (n < N) {
+        __half* dst = obuf + ((size_t)b * kC + h * kHD + hf * 32) * Np + n;
 #pragma unroll
-      for (int c = 0; c < kHD / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(oc + c * 32, o);
-        tmem_ld_wait();
-        reg_fence(o);
-        if (n < N) {
-          __half* dst = obuf + ((size_t)b * kC + h * kHD + c * 32) * Np + n;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) dst[(size_t)i * Np] = __float2half_rn(__uint_as_float(o[i]) * inv);
-        }
+        for (int i = 0; i < 32; ++i) dst[(size_t)i * Np] = __float2half_rn(__uint_as_float(o[i]) * inv);
       }
-      if (lse && n < N) lse[(size_t)bh * N + n] = (m + __log2f(l)) * 0.6931471805599453f;
+      if (lse && hf == 0 && n < N) lse[(size_t)bh * N + n] = (m + __log2f(lt)) * 0.6931471805599453f;
     }
   }
   tc_fence_before();
