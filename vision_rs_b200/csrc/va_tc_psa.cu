@@ -177,6 +177,7 @@ constexpr int kVBlk = kHD * 128;           // one 64-key block of V: [64 channel
 constexpr int kSoftWarps = 16;
 constexpr int kAttnThreads = (kSoftWarps + 2) * 32;
 constexpr int kHalf = kTile / 2;           // key columns per softmax thread
+constexpr int kTokenEarly = 1;             // 0: release the exponential token after chunk 0 of 2; 1: after the last
 
 __device__ __forceinline__ uint32_t col_s(int g) { return (uint32_t)g * 256u; }
 __device__ __forceinline__ uint32_t col_p(int g) { return (uint32_t)g * 256u + 128u; }
@@ -425,8 +426,11 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
           pk[e] = pack_f16x2(p0, p1);
         }
         tmem_st16(pc + c * 16, pk);
+        // hand the exponential unit over before the last chunk: the other
+        // group's first exponentials overlap this group's last ones instead of
+        // waiting out the hand-off latency
+        if (has1 && c == kHalf / 32 - 2 + kTokenEarly) mbar_arrive(&sm.mufu[g ^ 1]);
       }
-      if (has1) mbar_arrive(&sm.mufu[g ^ 1]);  // hand the exponential unit to the other group
       tmem_st_wait();
       l = l * alpha + (ls0 + ls1);
       m = m_use;
