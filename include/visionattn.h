@@ -179,6 +179,24 @@ VA_API int va_psa_attention_fwd_bf16(const va_bf16 *x, const va_bf16 *w_qkv, con
 VA_API int va_psa_flash_attention_fwd_f16(const void *qk, const void *v, void *o, float *lse, int B,
                                           int num_heads, int H, int W, va_stream_t stream);
 
+/* PSA Attention forward (bf16) that allocates nothing: no counterpart in the
+ * reference.  For callers that cannot hand the op a workspace — a graph
+ * runtime whose device buffers are all planned before it runs, or host code
+ * that must not enter a device allocator mid-run.  Scratch comes from a
+ * VA_NOALLOC_SCRATCH_BYTES array built into the library, held on every GPU
+ * that loads it until the process exits; larger problems return
+ * VA_ERR_WORKSPACE (split the batch, or use the workspace entry above).  The
+ * first call on a device looks up that device's scratch address, so make it
+ * before any stream capture.  Calls share the scratch: calls that overlap on
+ * the GPU race, so serialise them.  Same sizes and results as
+ * va_psa_attention_fwd_bf16. */
+#define VA_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+VA_API int va_psa_attention_fwd_bf16_noalloc(const va_bf16 *x, const va_bf16 *w_qkv, const float *b_qkv,
+                                             const va_bf16 *w_pe, const float *b_pe,
+                                             const va_bf16 *w_proj, const float *b_proj, va_bf16 *y,
+                                             int B, int C, int H, int W, int num_heads, int key_dim,
+                                             va_stream_t stream);
+
 /* Device status word of the tensor-core kernels: 0, or 1000+site of the
  * first bounded wait that gave up.  read: copies it to *status (synchronises
  * `stream`); clear: resets it to 0. */

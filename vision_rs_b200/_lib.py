@@ -51,6 +51,7 @@ SIGNATURES: dict[str, tuple] = {
     "va_psa_attention_fwd_f32": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, SZ, S]),
     "va_psa_attention_fwd_bf16": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, SZ, S]),
     "va_psa_flash_attention_fwd_f16": (I, [P, P, P, P, I, I, I, I, S]),
+    "va_psa_attention_fwd_bf16_noalloc": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, I, S]),
     "va_device_status_read": (I, [C.POINTER(C.c_int), S]),
     "va_device_status_clear": (I, [S]),
 }
