@@ -43,6 +43,9 @@ FLOP_PROJ = 2 * N_TOK * C * C
 FLOP_IMG = FLOP_QKV + FLOP_QK + FLOP_PV + FLOP_PE + FLOP_PROJ
 FLOP_ATTN_IMG = FLOP_QK + FLOP_PV
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+# DRAM bytes (read + write) of one attention-kernel launch at the full workload, from the committed
+# ncu capture in profiles/psa_fwd_kernels_cfg2_ncu_full.md (52.46 MB read + 4.88 MB written)
+ATTN_TRAFFIC_BYTES = 57_345_024
 
 
 def peaks():
@@ -285,7 +288,10 @@ def emit(args, ws, B, ms, e2e_ms, dom, dom_ms, launches, cpu, clk, x, y):
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor", "kernel": dom["name"], "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak, "peak_source": f"{src} bf16_tflops (burst)",
-                     "traffic": None, "flop_per_launch": dom["flop"], "ms_per_launch": dom_ms},
+                     "traffic": ATTN_TRAFFIC_BYTES if B == B_PER_GPU else None,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                                       "(profiles/psa_fwd_kernels_cfg2_ncu_full.md)",
+                     "flop_per_launch": dom["flop"], "ms_per_launch": dom_ms},
         "cpu_baseline": cpu,
         "clocks": clk.summary(),
         "tflops_whole_op": FLOP_IMG * B / (ms * 1e-3) / 1e12,
