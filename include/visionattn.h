@@ -169,6 +169,37 @@ VA_API int va_psa_attention_fwd_bf16(const va_bf16 *x, const va_bf16 *w_qkv, con
                               int num_heads, int key_dim, void *workspace, size_t ws_bytes,
                               va_stream_t stream);
 
+/* ── Multi-scale deformable attention (RF-DETR decoder) ──────────────────────
+ * No counterpart in the reference (it has no deformable attention); the
+ * published MSDeformAttn core with grid_sample(align_corners=False,
+ * padding_mode='zeros') sampling.  Layouts as the PyTorch op: value
+ * [B][S][nh][dh], spatial_shapes [L][2] (H, W) and level_start [L] as int64
+ * device arrays, loc [B][Q][nh][L][P][2] (x, y in [0,1]), attn
+ * [B][Q][nh][L][P] (softmaxed), out [B][Q][nh*dh].  dh ∈ {16, 32}, L ≤ 8.
+ * bf16 variants: value, out, grad_out and grad_value bf16; loc, attn and
+ * their gradients f32.  The backward writes every element of grad_value,
+ * grad_loc and grad_attn (no accumulation, no atomics, deterministic) and
+ * needs a workspace of va_msdeform_attn_bwd_workspace_bytes(); Q*P*4 ≤ 16384. */
+VA_API int va_msdeform_attn_fwd_f32(const float *value, const int64_t *spatial_shapes,
+                                    const int64_t *level_start, const float *loc, const float *attn,
+                                    float *out, int B, int S, int nh, int dh, int L, int Q, int P,
+                                    va_stream_t stream);
+VA_API int va_msdeform_attn_fwd_bf16(const va_bf16 *value, const int64_t *spatial_shapes,
+                                     const int64_t *level_start, const float *loc, const float *attn,
+                                     va_bf16 *out, int B, int S, int nh, int dh, int L, int Q, int P,
+                                     va_stream_t stream);
+VA_API size_t va_msdeform_attn_bwd_workspace_bytes(int B, int nh, int L, int Q, int P);
+VA_API int va_msdeform_attn_bwd_f32(const float *value, const int64_t *spatial_shapes,
+                                    const int64_t *level_start, const float *loc, const float *attn,
+                                    const float *grad_out, float *grad_value, float *grad_loc,
+                                    float *grad_attn, int B, int S, int nh, int dh, int L, int Q, int P,
+                                    void *workspace, size_t ws_bytes, va_stream_t stream);
+VA_API int va_msdeform_attn_bwd_bf16(const va_bf16 *value, const int64_t *spatial_shapes,
+                                     const int64_t *level_start, const float *loc, const float *attn,
+                                     const va_bf16 *grad_out, va_bf16 *grad_value, float *grad_loc,
+                                     float *grad_attn, int B, int S, int nh, int dh, int L, int Q, int P,
+                                     void *workspace, size_t ws_bytes, va_stream_t stream);
+
 /* The attention core of the bf16 path on its own (tcgen05, one launch):
  * O = softmax(Q·Kᵀ/√32)·V per (b, head) with the full 64-wide V — the two
  * reference flash_attention2_forward calls (psa.rs:930-944) in one pass.

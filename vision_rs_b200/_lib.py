@@ -50,6 +50,11 @@ SIGNATURES: dict[str, tuple] = {
     "va_psa_attention_workspace_bytes": (SZ, [I, I, I, I, I, I, I]),
     "va_psa_attention_fwd_f32": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, SZ, S]),
     "va_psa_attention_fwd_bf16": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, SZ, S]),
+    "va_msdeform_attn_fwd_f32": (I, [P, P, P, P, P, P, I, I, I, I, I, I, I, S]),
+    "va_msdeform_attn_fwd_bf16": (I, [P, P, P, P, P, P, I, I, I, I, I, I, I, S]),
+    "va_msdeform_attn_bwd_workspace_bytes": (SZ, [I, I, I, I, I]),
+    "va_msdeform_attn_bwd_f32": (I, [P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, P, SZ, S]),
+    "va_msdeform_attn_bwd_bf16": (I, [P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, P, SZ, S]),
     "va_psa_flash_attention_fwd_f16": (I, [P, P, P, P, I, I, I, I, S]),
     "va_psa_attention_fwd_bf16_noalloc": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, I, S]),
     "va_device_status_read": (I, [C.POINTER(C.c_int), S]),
