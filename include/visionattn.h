@@ -178,8 +178,10 @@ VA_API int va_psa_attention_fwd_bf16(const va_bf16 *x, const va_bf16 *w_qkv, con
  * [B][Q][nh][L][P] (softmaxed), out [B][Q][nh*dh].  dh ∈ {16, 32}, L ≤ 8.
  * bf16 variants: value, out, grad_out and grad_value bf16; loc, attn and
  * their gradients f32.  The backward writes every element of grad_value,
- * grad_loc and grad_attn (no accumulation, no atomics, deterministic) and
- * needs a workspace of va_msdeform_attn_bwd_workspace_bytes(); Q*P*4 ≤ 16384. */
+ * grad_loc and grad_attn (no accumulation, deterministic) and needs a
+ * workspace of va_msdeform_attn_bwd_workspace_bytes(); its per-(b, h, level)
+ * working set, 24·Q·P + 4·Q·dh + 4·(S+1) bytes, must fit in 200 KiB of shared
+ * memory (VA_ERR_SHAPE otherwise). */
 VA_API int va_msdeform_attn_fwd_f32(const float *value, const int64_t *spatial_shapes,
                                     const int64_t *level_start, const float *loc, const float *attn,
                                     float *out, int B, int S, int nh, int dh, int L, int Q, int P,

@@ -14,13 +14,15 @@
 // in shared memory with coalesced loads first.  The op is a gather: its HBM
 // floor is one pass over the value map.
 //
-// Backward, without atomics: pass 1 (same thread groups) recomputes each
-// sample, writes grad_attn and grad_loc, and records every corner's
-// grad_value contribution (destination pixel, weight A·w) in a slot fixed by
-// (b, h, l, q, p, corner).  Pass 2 runs one CTA per (b, h, l): it owns that
-// slice of grad_value exclusively, sorts its contributions by (pixel, slot)
-// in shared memory (bitonic sort of unique 64-bit keys) and each thread sums
-// whole pixel segments in slot order — deterministic results, no atomics.
+// Backward, deterministic: pass 1 (same thread groups) recomputes each
+// sample, writes grad_attn and grad_loc, and records the sample's grad_value
+// contribution (anchor pixel, the four corner weights A·w) in a slot fixed by
+// (b, h, l, q, p).  Pass 2 runs one CTA per (b, h, l): it owns that slice of
+// grad_value exclusively, buckets the samples by anchor pixel in shared
+// memory, and each thread sums one pixel's contributions in a fixed order —
+// deterministic results, no atomics on grad_value.
+#include <algorithm>
+
 #include "va_common.cuh"
 #include "va_psa.h"
 
@@ -30,7 +32,7 @@ namespace {
 
 constexpr int kMsdaThreads = 256;
 constexpr int kMaxLevels = 8;
-constexpr int kMaxContrib = 16384;   // contributions per (b, h, l) sorted in shared memory
+constexpr int kMaxEntries = 65536;   // corner entries 4·Q·P per (b, h, l) bucketed in shared memory (< 2^16)
 
 template <typename T> struct Vec;
 template <> struct Vec<float> {
@@ -43,24 +45,23 @@ template <> struct Vec<float> {
     *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
   }
 };
-template <> struct Vec<__nv_bfloat16> {
+template <> struct Vec<__nv_bfloat16> {  // bf16 ↔ f32 by bit placement (exact widening, RN narrowing)
   static constexpr int N = 8;
   __device__ static void load(const __nv_bfloat16* p, float (&v)[8]) {
     const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    const unsigned w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(h[i]);
-      v[2 * i] = f.x;
-      v[2 * i + 1] = f.y;
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
     }
   }
+  __device__ static unsigned pack(float lo, float hi) {
+    return (unsigned)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
+           ((unsigned)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
+  }
   __device__ static void store(__nv_bfloat16* p, const float (&v)[8]) {
-    uint4 u;
-    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-    *reinterpret_cast<uint4*>(p) = u;
+    *reinterpret_cast<uint4*>(p) = make_uint4(pack(v[0], v[1]), pack(v[2], v[3]), pack(v[4], v[5]), pack(v[6], v[7]));
   }
 };
 
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(kMsdaThreads)
 msda_bwd_sample_kernel(const TV* __restrict__ value, const int64_t* __restrict__ shapes,
                        const int64_t* __restrict__ lstart, const float* __restrict__ loc,
                        const float* __restrict__ attn, const TV* __restrict__ grad_out, float* __restrict__ grad_loc,
-                       float* __restrict__ grad_attn, int* __restrict__ c_pix, float* __restrict__ c_w, int B, int S,
+                       float* __restrict__ grad_attn, int4* __restrict__ c_pix, float4* __restrict__ c_w, int B, int S,
                        int nh, int L, int Q, int P) {
   constexpr int VEC = Vec<TV>::N, G = DH / VEC, ITEMS = kMsdaThreads / G;
   __shared__ Levels lv;
@@ -206,89 +207,185 @@ msda_bwd_sample_kernel(const TV* __restrict__ value, const int64_t* __restrict__
           gy = fmaf((dx ? c.fx : 1.f - c.fx) * (dy ? 1.f : -1.f), gdv[k], gy);
         }
         grad_attn[it * LP + s] = ga;
-        grad_loc[(it * LP + s) * 2] = a * gx * (float)W;
-        grad_loc[(it * LP + s) * 2 + 1] = a * gy * (float)H;
-        // slot of (b, h, l, q, p, corner)
-        const size_t slot = ((((size_t)b * nh + h) * L + l) * Q + q) * (size_t)(P * 4) + p * 4;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          c_pix[slot + k] = c.ok[k] ? c.pix[k] : -1;
-          c_w[slot + k] = a * c.w[k];
-        }
+        *reinterpret_cast<float2*>(grad_loc + (it * LP + s) * 2) = make_float2(a * gx * (float)W, a * gy * (float)H);
+        // the sample's grad_value record at (b, h, l, q·P + p): corner pixels (−1
+        // outside the map) and corner weights
+        const size_t rec = (((size_t)b * nh + h) * L + l) * (size_t)Q * P + (size_t)q * P + p;
+        c_pix[rec] = make_int4(c.ok[0] ? c.pix[0] : -1, c.ok[1] ? c.pix[1] : -1, c.ok[2] ? c.pix[2] : -1,
+                               c.ok[3] ? c.pix[3] : -1);
+        c_w[rec] = make_float4(a * c.w[0], a * c.w[1], a * c.w[2], a * c.w[3]);
       }
     }
   }
 }
 
 // Pass 2: CTA (l, h, b) owns grad_value[b, level l pixels, h, :].
+// Its 4·Q·P corner entries (entry e = 4·sample + corner) are bucketed by
+// pixel with a counting sort in shared memory.  Shared-memory atomics give
+// the counts and a first placement inside each bucket; the final position of
+// an entry is its bucket start plus the number of entries of its bucket with
+// a smaller index, so each bucket ends up in entry order whatever order the
+// atomics ran in.  A group of dh/8 lanes per pixel (8 channels each) sums the
+// pixel's bucket in entry order and writes its grad_value row (zeros when no
+// sample touched it): every sum is taken in a fixed order — deterministic,
+// and no atomics on grad_value.
+constexpr int kValueThreads = 512;
+constexpr int kValueWarps = kValueThreads / 32;
+
+__device__ __forceinline__ void store4(float* p, const float4& v) { *reinterpret_cast<float4*>(p) = v; }
+__device__ __forceinline__ void store4(__nv_bfloat16* p, const float4& v) {
+  *reinterpret_cast<uint2*>(p) = make_uint2(Vec<__nv_bfloat16>::pack(v.x, v.y), Vec<__nv_bfloat16>::pack(v.z, v.w));
+}
+
+// Bucket counters: two 16-bit counters per word (pixel 2k in the low half,
+// 2k + 1 in the high half); counts and positions stay below 2^16 because a
+// bucket set holds fewer than 2^16 entries.
+__device__ __forceinline__ int cnt_get(const unsigned* c, int p) { return (int)((c[p >> 1] >> ((p & 1) * 16)) & 0xffffu); }
+__device__ __forceinline__ int cnt_bump(unsigned* c, int p) {
+  const int sh = (p & 1) * 16;
+  return (int)((atomicAdd(&c[p >> 1], 1u << sh) >> sh) & 0xffffu);
+}
+
 template <typename TV, int DH>
-__global__ void __launch_bounds__(512)
+__global__ void __launch_bounds__(kValueThreads, 2)
 msda_bwd_value_kernel(const int64_t* __restrict__ shapes, const int64_t* __restrict__ lstart,
-                      const TV* __restrict__ grad_out, const int* __restrict__ c_pix, const float* __restrict__ c_w,
-                      TV* __restrict__ grad_value, int S, int nh, int L, int Q, int P, int npad) {
-  extern __shared__ unsigned long long keys[];  // [npad]
+                      const TV* __restrict__ grad_out, const int* __restrict__ c_pix,
+                      const float* __restrict__ c_w, TV* __restrict__ grad_value, int S, int nh, int L, int Q, int P,
+                      unsigned long long q_magic) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int wsum[kValueWarps];
+  constexpr int GS = DH + 4;  // padded grad_out row: rows of nearby queries start in different banks
   const int l = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int H = (int)shapes[2 * l], W = (int)shapes[2 * l + 1], s0 = (int)lstart[l];
-  const int n = Q * P * 4;
-  const size_t base = (((size_t)b * nh + h) * L + l) * (size_t)n;
-  for (int i = threadIdx.x; i < npad; i += blockDim.x) {
-    unsigned long long k = ~0ull;
-    if (i < n) {
-      const int px = c_pix[base + i];
-      if (px >= 0) k = ((unsigned long long)(unsigned)px << 32) | (unsigned)i;
-    }
-    keys[i] = k;
+  const int HW = H * W, n = Q * P * 4;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* gos = reinterpret_cast<float*>(smem);                        // [Q][GS] grad_out rows of (b, h)
+  unsigned short* tmp = reinterpret_cast<unsigned short*>(smem);      // [n] first placement, before gos
+  const int rows_bytes = max(Q * GS * 4, (n * 2 + 15) & ~15);
+  float* bw = reinterpret_cast<float*>(smem + rows_bytes);            // [n] weights in bucket order
+  unsigned short* bq = reinterpret_cast<unsigned short*>(bw + n);     // [n] queries in bucket order
+  unsigned* cnt = reinterpret_cast<unsigned*>(bq + n);                // [(HW + 2) / 2] packed counters
+  const size_t rec0 = (((size_t)b * nh + h) * L + l) * (size_t)n;   // n % 4 == 0
+  const int4* pix4 = reinterpret_cast<const int4*>(c_pix + rec0);
+  const float4* w4p = reinterpret_cast<const float4*>(c_w + rec0);
+  const int nwords = (HW + 2) / 2;
+  for (int i = tid; i < nwords; i += kValueThreads) cnt[i] = 0u;
+  __syncthreads();
+  for (int i = tid; i < n / 4; i += kValueThreads) {
+    const int4 p = __ldg(pix4 + i);
+    if (p.x >= 0) cnt_bump(cnt, p.x);
+    if (p.y >= 0) cnt_bump(cnt, p.y);
+    if (p.z >= 0) cnt_bump(cnt, p.z);
+    if (p.w >= 0) cnt_bump(cnt, p.w);
   }
   __syncthreads();
-  // bitonic sort, ascending
-  for (int size = 2; size <= npad; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < npad / 2; i += blockDim.x) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool up = (lo & size) == 0;
-        const unsigned long long a = keys[lo], c = keys[hi];
-        if ((a > c) == up) {
-          keys[lo] = c;
-          keys[hi] = a;
-        }
+  {  // exclusive scan of the counts: thread t takes a contiguous run of whole words
+    const int per = (nwords + kValueThreads - 1) / kValueThreads;
+    const int lo = min(nwords, tid * per), hi = min(nwords, lo + per);
+    int tot = 0;
+    for (int i = lo; i < hi; ++i) {
+      const unsigned c = cnt[i];
+      tot += (int)(c & 0xffffu) + (int)(c >> 16);
+    }
+    int inc = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += u;
+    }
+    if (lane == 31) wsum[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+      const int own = lane < kValueWarps ? wsum[lane] : 0;
+      int x = own;
+#pragma unroll
+      for (int o = 1; o < kValueWarps; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += u;
       }
-      __syncthreads();
+      if (lane < kValueWarps) wsum[lane] = x - own;
+    }
+    __syncthreads();
+    unsigned run = (unsigned)(wsum[warp] + inc - tot);
+    for (int i = lo; i < hi; ++i) {
+      const unsigned c = cnt[i];
+      const unsigned a = run, bb = run + (c & 0xffffu);
+      cnt[i] = a | (bb << 16);
+      run = bb + (c >> 16);
     }
   }
-  // one thread per destination pixel: sum its segment in slot order
-  const TV* go = grad_out + (size_t)h * DH;
-  for (int px = threadIdx.x; px < H * W; px += blockDim.x) {
-    const unsigned long long key = (unsigned long long)(unsigned)px << 32;
-    int lo = 0, hi = npad;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (keys[mid] < key) lo = mid + 1;
-      else hi = mid;
-    }
-    float acc[DH] = {};
-    for (int i = lo; i < npad && (keys[i] >> 32) == (unsigned long long)(unsigned)px; ++i) {
-      const int slot = (int)(keys[i] & 0xffffffffu);
-      const int q = slot / (P * 4);
-      const float w = c_w[base + slot];
-      const TV* gr = go + ((size_t)b * Q + q) * nh * DH;
+  __syncthreads();
+  for (int i = tid; i < n / 4; i += kValueThreads) {  // first placement
+    const int4 p = __ldg(pix4 + i);
+    if (p.x >= 0) tmp[cnt_bump(cnt, p.x)] = (unsigned short)(4 * i);
+    if (p.y >= 0) tmp[cnt_bump(cnt, p.y)] = (unsigned short)(4 * i + 1);
+    if (p.z >= 0) tmp[cnt_bump(cnt, p.z)] = (unsigned short)(4 * i + 2);
+    if (p.w >= 0) tmp[cnt_bump(cnt, p.w)] = (unsigned short)(4 * i + 3);
+  }
+  __syncthreads();
+  // counter k now holds the end of bucket k (= start of bucket k + 1).  Final
+  // position = bucket start + number of smaller entry ids in the bucket.
+  for (int i = tid; i < n / 4; i += kValueThreads) {
+    const int4 p4 = __ldg(pix4 + i);
+    const float4 w4 = __ldg(w4p + i);
+    const int pc[4] = {p4.x, p4.y, p4.z, p4.w};
+    const float wc[4] = {w4.x, w4.y, w4.z, w4.w};
+    const unsigned short q = (unsigned short)((4u * i * q_magic) >> 32);
 #pragma unroll
-      for (int e0 = 0; e0 < DH; e0 += Vec<TV>::N) {
-        float v[Vec<TV>::N];
-        Vec<TV>::load(gr + e0, v);
-#pragma unroll
-        for (int e = 0; e < Vec<TV>::N; ++e) acc[e0 + e] = fmaf(w, v[e], acc[e0 + e]);
-      }
-    }
-    TV* dst = grad_value + (((size_t)b * S + s0 + px) * nh + h) * DH;
-#pragma unroll
-    for (int e0 = 0; e0 < DH; e0 += Vec<TV>::N) {
-      float v[Vec<TV>::N];
-#pragma unroll
-      for (int e = 0; e < Vec<TV>::N; ++e) v[e] = acc[e0 + e];
-      Vec<TV>::store(dst + e0, v);
+    for (int c = 0; c < 4; ++c) {
+      const int p = pc[c];
+      if (p < 0) continue;
+      const unsigned id = 4u * i + c;
+      const int lo = p ? cnt_get(cnt, p - 1) : 0, hi = cnt_get(cnt, p);
+      int r = 0;
+      for (int j = lo; j < hi; ++j) r += tmp[j] < id;
+      bq[lo + r] = q;
+      bw[lo + r] = wc[c];
     }
   }
+  __syncthreads();
+  constexpr int RV = DH / Vec<TV>::N;  // grad_out rows over the first-placement area
+  for (int i = tid; i < Q * RV; i += kValueThreads) {
+    const int q = i / RV, e0 = (i % RV) * Vec<TV>::N;
+    float v[Vec<TV>::N];
+    Vec<TV>::load(grad_out + (((size_t)b * Q + q) * nh + h) * DH + e0, v);
+#pragma unroll
+    for (int e = 0; e < Vec<TV>::N; ++e) gos[q * GS + e0 + e] = v[e];
+  }
+  __syncthreads();
+  // G lanes per pixel, 8 channels each: a group reads whole grad_out rows
+  constexpr int G = DH / 8, PPW = 32 / G;
+  const int gl = lane % G, pg = lane / G;
+  TV* gvb = grad_value + (((size_t)b * S + s0) * nh + h) * DH + 8 * gl;
+  for (int z = warp * PPW + pg; z - pg < HW; z += kValueWarps * PPW) {
+    if (z >= HW) continue;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    const int hi = cnt_get(cnt, z);
+    for (int j = z ? cnt_get(cnt, z - 1) : 0; j < hi; ++j) {
+      const float w = bw[j];
+      const float* g = gos + (unsigned)bq[j] * GS + 8 * gl;
+#pragma unroll
+      for (int e = 0; e < 8; e += 4) {
+        const float4 g4 = *reinterpret_cast<const float4*>(g + e);
+        acc[e] = fmaf(w, g4.x, acc[e]);
+        acc[e + 1] = fmaf(w, g4.y, acc[e + 1]);
+        acc[e + 2] = fmaf(w, g4.z, acc[e + 2]);
+        acc[e + 3] = fmaf(w, g4.w, acc[e + 3]);
+      }
+    }
+    TV* d = gvb + (size_t)z * nh * DH;
+    store4(d, make_float4(acc[0], acc[1], acc[2], acc[3]));
+    store4(d + 4, make_float4(acc[4], acc[5], acc[6], acc[7]));
+  }
+}
+
+// Dynamic shared memory of the value kernel: the level's pixel count is only
+// known on the device, so the bucket table is sized for S rows (≥ H·W).
+size_t msda_value_smem(int n, int Q, int dh, int S) {
+  const size_t rows = std::max((size_t)Q * (dh + 4) * 4, ((size_t)n * 2 + 15) & ~(size_t)15);  // grad_out rows / first placement
+  return rows + (size_t)n * 6 + (size_t)(S + 2) / 2 * 4;
 }
 
 int check_msda(int B, int S, int nh, int dh, int L, int Q, int P, const void* value, const void* out) {
@@ -318,8 +415,8 @@ int msda_fwd(const TV* value, const int64_t* shapes, const int64_t* lstart, cons
 }
 
 size_t msda_ws_bytes(int B, int nh, int L, int Q, int P) {
-  const size_t n = (size_t)B * nh * L * Q * P * 4;
-  return align256(n * sizeof(int)) + align256(n * sizeof(float));
+  const size_t n = (size_t)B * nh * L * Q * P;  // one record per sample: 4 corner pixels + 4 corner weights
+  return align256(n * sizeof(int4)) + align256(n * sizeof(float4));
 }
 
 template <typename TV>
@@ -327,14 +424,19 @@ int msda_bwd(const TV* value, const int64_t* shapes, const int64_t* lstart, cons
              const TV* grad_out, TV* grad_value, float* grad_loc, float* grad_attn, int B, int S, int nh, int dh,
              int L, int Q, int P, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (int rc = check_msda(B, S, nh, dh, L, Q, P, value, grad_value)) return rc;
-  const int n = Q * P * 4;
-  VA_CHECK_ARG(n <= kMaxContrib, "msdeform_attn backward: Q*P*4 = %d contributions per (b,h,l) > %d", n, kMaxContrib);
+  const long long n_ll = 4LL * Q * P;
+  VA_CHECK_ARG(n_ll < kMaxEntries, "msdeform_attn backward: 4*Q*P = %lld corner entries per (b,h,l) > %d", n_ll,
+               kMaxEntries);
+  const int n = (int)n_ll;
   const size_t need = msda_ws_bytes(B, nh, L, Q, P);
   if (!ws || ws_bytes < need)
     return set_error(VA_ERR_WORKSPACE, "msdeform_attn backward: workspace %zu < %zu bytes", ws_bytes, need);
-  const size_t nall = (size_t)B * nh * L * n;
-  int* c_pix = static_cast<int*>(ws);
-  float* c_w = reinterpret_cast<float*>(static_cast<char*>(ws) + align256(nall * sizeof(int)));
+  const size_t smem = msda_value_smem(n, Q, dh, S);
+  VA_CHECK_ARG(smem <= 200 * 1024, "msdeform_attn backward: per-level working set %zu bytes exceeds shared memory",
+               smem);
+  const size_t nall = (size_t)B * nh * L * Q * P;  // sample records
+  int4* c_pix = static_cast<int4*>(ws);
+  float4* c_w = reinterpret_cast<float4*>(static_cast<char*>(ws) + align256(nall * sizeof(int4)));
   const long long items = (long long)B * Q * nh;
   constexpr int VEC = Vec<TV>::N;
   auto pass1 = [&](auto kernel, int G) {
@@ -346,12 +448,13 @@ int msda_bwd(const TV* value, const int64_t* shapes, const int64_t* lstart, cons
   if (dh == 16) pass1(msda_bwd_sample_kernel<TV, 16>, 16 / VEC);
   else pass1(msda_bwd_sample_kernel<TV, 32>, 32 / VEC);
   if (int rc = check_launch("msdeform_attn backward (samples)")) return rc;
-  int npad = 1;
-  while (npad < n) npad <<= 1;
-  const size_t smem = (size_t)npad * sizeof(unsigned long long);
+  // query of entry e = e / (4P), as a multiply: q_magic = ceil(2^32 / 4P), exact for e, 4P < 2^16
+  const unsigned long long q_magic = ((1ull << 32) + 4ull * P - 1) / (4ull * P);
   auto pass2 = [&](auto kernel) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kMaxContrib * 8));
-    kernel<<<dim3(L, nh, B), 512, smem, st>>>(shapes, lstart, grad_out, c_pix, c_w, grad_value, S, nh, L, Q, P, npad);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    kernel<<<dim3(L, nh, B), kValueThreads, smem, st>>>(shapes, lstart, grad_out, reinterpret_cast<const int*>(c_pix),
+                                                        reinterpret_cast<const float*>(c_w), grad_value, S, nh, L, Q,
+                                                        P, q_magic);
   };
   if (dh == 16) pass2(msda_bwd_value_kernel<TV, 16>);
   else pass2(msda_bwd_value_kernel<TV, 32>);
