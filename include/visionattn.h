@@ -230,6 +230,31 @@ VA_API int va_psa_attention_fwd_bf16_noalloc(const va_bf16 *x, const va_bf16 *w_
                                              int B, int C, int H, int W, int num_heads, int key_dim,
                                              va_stream_t stream);
 
+/* ── DINOv2 backbone attention (bf16, tcgen05) ───────────────────────────
+ * No counterpart in the reference (it has no DINOv2 code): the published
+ * ViT/DINOv2 self-attention.  x [S][n][hidden] bf16 (S sequences of n
+ * tokens), w_qkv [3*hidden][hidden] bf16 (nn.Linear weight: q, k, v sections,
+ * head-major inside each), b_qkv [3*hidden] f32, o [S][n][hidden] bf16 =
+ * concat_heads(softmax(q·kᵀ/8)·v), head dim 64, num_heads*64 == hidden
+ * (DINOv2-S: 384, 6).  Global layers: S = images, n = 1 + H·W (cls first).
+ * Windowed layers: S = images·windows, n = 1 + win² — the cls token joins
+ * every window as token 0 (va_dinov2_window_partition_bf16), and
+ * un-partitioning averages the windows' cls outputs. */
+VA_API size_t va_dinov2_attention_workspace_bytes(int num_seqs, int seq_len, int hidden);
+VA_API int va_dinov2_attention_fwd_bf16(const va_bf16 *x, const va_bf16 *w_qkv, const float *b_qkv,
+                                        va_bf16 *o, int num_seqs, int seq_len, int hidden,
+                                        int num_heads, void *workspace, size_t ws_bytes,
+                                        va_stream_t stream);
+/* The packed QKV Linear alone: qkv [tokens][3*hidden] bf16 = x·w_qkvᵀ + b. */
+VA_API int va_dinov2_qkv_linear_bf16(const va_bf16 *x, const va_bf16 *w_qkv, const float *b_qkv,
+                                     va_bf16 *qkv, int tokens, int hidden, va_stream_t stream);
+/* x [B][1 + gh*gw][hidden] ↔ xw [B*(gh/win)*(gw/win)][1 + win*win][hidden];
+ * window w = wy*(gw/win) + wx, patches row-major inside a window. */
+VA_API int va_dinov2_window_partition_bf16(const va_bf16 *x, va_bf16 *xw, int B, int grid_h,
+                                           int grid_w, int win, int hidden, va_stream_t stream);
+VA_API int va_dinov2_window_unpartition_bf16(const va_bf16 *xw, va_bf16 *x, int B, int grid_h,
+                                             int grid_w, int win, int hidden, va_stream_t stream);
+
 /* Device status word of the tensor-core kernels: 0, or 1000+site of the
  * first bounded wait that gave up.  read: copies it to *status (synchronises
  * `stream`); clear: resets it to 0. */

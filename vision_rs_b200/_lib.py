@@ -57,6 +57,11 @@ SIGNATURES: dict[str, tuple] = {
     "va_msdeform_attn_bwd_bf16": (I, [P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, P, SZ, S]),
     "va_psa_flash_attention_fwd_f16": (I, [P, P, P, P, I, I, I, I, S]),
     "va_psa_attention_fwd_bf16_noalloc": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, I, S]),
+    "va_dinov2_attention_workspace_bytes": (SZ, [I, I, I]),
+    "va_dinov2_attention_fwd_bf16": (I, [P, P, P, P, I, I, I, I, P, SZ, S]),
+    "va_dinov2_qkv_linear_bf16": (I, [P, P, P, P, I, I, S]),
+    "va_dinov2_window_partition_bf16": (I, [P, P, I, I, I, I, I, S]),
+    "va_dinov2_window_unpartition_bf16": (I, [P, P, I, I, I, I, I, S]),
     "va_device_status_read": (I, [C.POINTER(C.c_int), S]),
     "va_device_status_clear": (I, [S]),
 }

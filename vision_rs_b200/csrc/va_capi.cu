@@ -119,11 +119,18 @@ int va_psa_flash_attention_fwd_f16(const void* qk, const void* v, void* o, float
   return psa_attention_core_tc(qk, v, o, lse, B, nh, H, W, (cudaStream_t)s);
 }
 
-int va_device_status_read(int* status, va_stream_t s) {
+int va_device_status_read(int* status, va_stream_t s) {  // first non-zero word of the tensor-core kernels
   if (!status) return set_error(VA_ERR_SHAPE, "device_status_read: null output");
-  return tc_status_read(status, (cudaStream_t)s);
+  int a = 0, b = 0;
+  if (int rc = tc_status_read(&a, (cudaStream_t)s)) return rc;
+  if (int rc = dino_status_read(&b, (cudaStream_t)s)) return rc;
+  *status = a ? a : b;
+  return VA_OK;
 }
 
-int va_device_status_clear(va_stream_t s) { return tc_status_clear((cudaStream_t)s); }
+int va_device_status_clear(va_stream_t s) {
+  if (int rc = tc_status_clear((cudaStream_t)s)) return rc;
+  return dino_status_clear((cudaStream_t)s);
+}
 
 }  // extern "C"

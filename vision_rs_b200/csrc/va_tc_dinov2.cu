@@ -1,0 +1,398 @@
+// DINOv2 backbone attention on the sm_100a tensor cores: the packed QKV
+// Linear (hidden → 3·hidden, tcgen05 GEMM fed by TMA) and softmax(Q·Kᵀ/8)·V
+// over independent token sequences with head dim 64 (the flash-attention
+// kernel shared with the PSA path, tc_flash_attention).
+//
+// The reference (spinorml/vision-rs) has no DINOv2 code; the operator is the
+// published ViT/DINOv2 self-attention (Oquab et al. 2023, Dosovitskiy et al.
+// 2021): qkv = x·W_qkvᵀ + b split as [3][heads][64] along the feature axis
+// (q, k, v sections of `hidden` features each, head-major inside a section),
+// O = softmax(q·kᵀ·64^-½)·v per head, heads concatenated.
+//
+// Global layers attend over a whole image (1 + H·W tokens, cls first).
+// Windowed layers attend inside windows of win×win patches; the cls token
+// joins every window as its first token (window sequences of 1 + win² tokens)
+// and un-partitioning averages the windows' cls outputs.  BASELINE does not
+// fix the cls handling of windowed layers; this is the choice made here.
+//
+// Kernels:
+//  1. dino_qkv_kernel<EPI>  — D[128 tokens × 192 features] per CTA, K streamed
+//     in 64-wide blocks through a 2-stage TMA ring, accumulator in TMEM
+//     (192 columns), 2 CTAs per SM so one CTA's epilogue overlaps the other's
+//     main loop.  EPI kSplitHeads writes Q and K f16 [2][S·heads][n][64] and
+//     V f16 transposed [S·heads·64][n_pad] (the flash-attention operands);
+//     EPI kPackedRows writes bf16 [tokens][3·hidden] (torch Linear layout).
+//  2. window partition / un-partition (bf16 token gathers, 16-byte moves).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "va_common.cuh"
+#include "va_psa.h"
+#include "va_sm100.cuh"
+
+namespace va {
+using namespace sm100;
+
+__device__ int g_dino_status;
+
+namespace {
+
+constexpr int kDM = 128;      // tokens per tile (UMMA M)
+constexpr int kDN = 192;      // features per tile (UMMA N): three heads of 64
+constexpr int kDStages = 2;
+constexpr int kHead = 64;
+constexpr int kSplitHeads = 0, kPackedRows = 1;
+
+struct DinoQkvSmem {
+  uint8_t a[kDStages][kDM * 128];  // x block: 128 tokens × 64 features bf16, K-major SW128 (16 KB)
+  uint8_t b[kDStages][kDN * 128];  // W block: 192 rows × 64 features (24 KB)
+  uint64_t full[kDStages], empty[kDStages], mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(128, 2)
+dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                const float* __restrict__ bias, void* __restrict__ out0, __half* __restrict__ vbuf, int M, int hidden,
+                int n_seq, int n_pad, int heads) {
+  extern __shared__ uint8_t smem_raw[];
+  DinoQkvSmem& sm =
+      *reinterpret_cast<DinoQkvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int m0 = blockIdx.x * kDM, n0 = blockIdx.y * kDN;
+  const int nk = hidden / 64;
+
+  if (tid == 0) {
+    for (int i = 0; i < kDStages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1);
+    }
+    mbar_init(&sm.mma_done, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&sm.tmem_base, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // ── TMA producer ──
+    tma_prefetch_desc(&map_x);
+    tma_prefetch_desc(&map_w);
+    int issued = 0;
+    bool ok = true;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int st = kb % kDStages;
+      if (kb >= kDStages &&
+          !(ok = mbar_wait(&sm.empty[st], ((kb / kDStages) - 1) & 1, &sm.abort, &g_dino_status, 1)))
+        break;
+      mbar_arrive_expect_tx(&sm.full[st], kDM * 128 + kDN * 128);
+      tma_load_2d(sm.a[st], &map_x, &sm.full[st], kb * 64, m0);
+      tma_load_2d(sm.b[st], &map_w, &sm.full[st], kb * 64, n0);
+      ++issued;
+    }
+    if (!ok) {  // let every load issued here land (bounded) before the CTA can exit
+      for (int kb = max(0, issued - kDStages); kb < issued; ++kb) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&sm.full[kb % kDStages], (kb / kDStages) & 1) && clock64() - t0 < kSpinCycles) {
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ── MMA issuer ──
+    constexpr uint32_t idesc = idesc_f32acc(kDM, kDN, AB_BF16, false, false);
+    const uint64_t da0 = sdesc(smem_u32(sm.a[0]), 16, 1024, SW_128B);
+    const uint64_t db0 = sdesc(smem_u32(sm.b[0]), 16, 1024, SW_128B);
+    constexpr uint32_t kAS = (kDM * 128) >> 4, kBS = (kDN * 128) >> 4;
+    bool ok = true;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int st = kb % kDStages;
+      if (!(ok = mbar_wait(&sm.full[st], (kb / kDStages) & 1, &sm.abort, &g_dino_status, 2))) break;
+      tc_fence_after();
+      const uint64_t da = da0 + (uint64_t)(st * kAS), db = db0 + (uint64_t)(st * kBS);
+#pragma unroll
+      for (int s = 0; s < 4; ++s) mma_ss(tmem, da + 2 * s, db + 2 * s, idesc, (kb > 0 || s > 0) ? 1u : 0u);
+      mma_commit(&sm.empty[st]);
+    }
+    mma_commit(&sm.mma_done);  // also after an abort: every MMA issued here has completed when it fires
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(&sm.mma_done, 0, &sm.abort, &g_dino_status, 3) && !sm.abort;
+  tc_fence_after();
+
+  if (ok) {
+    const int r = warp * 32 + lane, m = m0 + r;
+    const bool live = m < M;
+    const int sq = live ? m / n_seq : 0, t = live ? m - sq * n_seq : 0;
+#pragma unroll 1
+    for (int c = 0; c < kDN / 32; ++c) {
+      uint32_t u[32];
+      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, u);
+      tmem_ld_wait();
+      reg_fence(u);
+      const int col = n0 + c * 32;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(u[i]) + __ldg(bias + col + i);
+      if (!live) continue;
+      if constexpr (EPI == kPackedRows) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out0) + (size_t)m * 3 * hidden + col);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                              pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+      } else {
+        const int sec = col / hidden, rem = col - sec * hidden, hd = rem / kHead, d0 = rem - hd * kHead;
+        const size_t bh = (size_t)sq * heads + hd, BH = (size_t)(M / n_seq) * heads;
+        if (sec < 2) {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(out0) +
+                                                (((size_t)sec * BH + bh) * n_seq + t) * kHead + d0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_f16x2_sat(v[8 * q], v[8 * q + 1]), pack_f16x2_sat(v[8 * q + 2], v[8 * q + 3]),
+                                pack_f16x2_sat(v[8 * q + 4], v[8 * q + 5]), pack_f16x2_sat(v[8 * q + 6], v[8 * q + 7]));
+        } else {
+          __half* dst = vbuf + (bh * kHead + d0) * n_pad + t;  // lanes: consecutive tokens
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            dst[(size_t)i * n_pad] = __ushort_as_half((unsigned short)(pack_f16x2_sat(v[i], 0.f) & 0xffffu));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ── window partition / un-partition ─────────────────────────────────────────
+// x [B][1 + gh·gw][C] (cls first, patches row-major) ↔ xw [B·nw][1 + win²][C]
+// (window w = wy·(gw/win) + wx; cls copied to token 0 of every window).
+__global__ void window_partition_kernel(const uint4* __restrict__ x, uint4* __restrict__ xw, int B, int gh, int gw,
+                                        int win, int cv) {
+  const int nwx = gw / win, nw = (gh / win) * nwx, tw = 1 + win * win;
+  const long long total = (long long)B * nw * tw * cv;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % cv);
+    const long long row = i / cv;
+    const int tok = (int)(row % tw);
+    const long long bw = row / tw;
+    const int w = (int)(bw % nw), b = (int)(bw / nw);
+    int src = 0;
+    if (tok > 0) {
+      const int iy = (tok - 1) / win, ix = (tok - 1) - iy * win;
+      const int wy = w / nwx, wx = w - wy * nwx;
+      src = 1 + (wy * win + iy) * gw + wx * win + ix;
+    }
+    xw[i] = x[((long long)b * (1 + gh * gw) + src) * cv + c];
+  }
+}
+
+__global__ void window_unpartition_kernel(const __nv_bfloat16* __restrict__ xw, __nv_bfloat16* __restrict__ x, int B,
+                                          int gh, int gw, int win, int C) {
+  const int nwx = gw / win, nw = (gh / win) * nwx, tw = 1 + win * win, ntok = 1 + gh * gw;
+  const long long total = (long long)B * ntok * (C / 8);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c8 = (int)(i % (C / 8));
+    const long long row = i / (C / 8);
+    const int tok = (int)(row % ntok), b = (int)(row / ntok);
+    uint4 out;
+    if (tok == 0) {  // cls: mean of the windows' cls outputs, summed in window order
+      float acc[8] = {};
+      for (int w = 0; w < nw; ++w) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xw + (((size_t)b * nw + w) * tw) * C + c8 * 8);
+        const unsigned ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc[2 * k] += __uint_as_float(ws[k] << 16);
+          acc[2 * k + 1] += __uint_as_float(ws[k] & 0xffff0000u);
+        }
+      }
+      const float inv = 1.0f / (float)nw;
+      out = make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv),
+                       pack_bf16x2(acc[4] * inv, acc[5] * inv), pack_bf16x2(acc[6] * inv, acc[7] * inv));
+    } else {
+      const int py = (tok - 1) / gw, px = (tok - 1) - py * gw;
+      const int w = (py / win) * nwx + px / win, it = 1 + (py % win) * win + px % win;
+      out = *reinterpret_cast<const uint4*>(xw + (((size_t)b * nw + w) * tw + it) * C + c8 * 8);
+    }
+    *reinterpret_cast<uint4*>(x + ((size_t)b * ntok + tok) * C + c8 * 8) = out;
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 dino_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int dino_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows, const char* what) {
+  auto fn = dino_encode_fn();
+  if (!fn) return set_error(VA_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+  const uint64_t d[2] = {inner, rows}, s[1] = {inner * 2};
+  const uint32_t bx[2] = {64, box_rows}, es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), d, s, bx, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(VA_ERR_ALIGN, "tensor map for %s rejected (CUresult %d)", what, (int)r);
+  return VA_OK;
+}
+
+int check_dino(int tokens, int hidden, const void* x, const void* w) {
+  VA_CHECK_ARG(tokens > 0 && hidden > 0 && hidden % kHead == 0 && (3 * hidden) % kDN == 0,
+               "dinov2 qkv: hidden %d must be a positive multiple of 64", hidden);
+  VA_CHECK_ARG((tokens + kDM - 1) / kDM <= 0x7fffffff && 3 * hidden / kDN <= 65535, "dinov2 qkv: too many tiles");
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
+    return set_error(VA_ERR_ALIGN, "dinov2 qkv: x and w_qkv need 16-byte alignment");
+  return VA_OK;
+}
+
+template <int EPI>
+int launch_qkv(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias, void* out0, __half* vbuf, int M,
+               int hidden, int n_seq, int n_pad, int heads, cudaStream_t st) {
+  CUtensorMap mx, mw;
+  if (int rc = dino_map(&mx, x, (uint64_t)hidden, (uint64_t)M, kDM, "x")) return rc;
+  if (int rc = dino_map(&mw, w, (uint64_t)hidden, (uint64_t)3 * hidden, kDN, "w_qkv")) return rc;
+  const size_t smem = sizeof(DinoQkvSmem) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(dino_qkv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  dino_qkv_kernel<EPI><<<dim3((M + kDM - 1) / kDM, 3 * hidden / kDN), 128, smem, st>>>(mx, mw, bias, out0, vbuf, M,
+                                                                                       hidden, n_seq, n_pad, heads);
+  return check_launch("dinov2 qkv");
+}
+
+struct DinoWs {
+  size_t qk, v, total;
+};
+
+DinoWs dino_layout(int S, int n, int hidden) {
+  const size_t heads = (size_t)hidden / kHead, BH = (size_t)S * heads, np = ((size_t)n + 7) / 8 * 8;
+  DinoWs w;
+  w.qk = 0;
+  w.v = align256(2 * BH * n * kHead * 2);
+  w.total = w.v + align256(BH * kHead * np * 2);
+  return w;
+}
+
+}  // namespace
+
+size_t dino_workspace_bytes(int S, int n, int hidden) {
+  if (S <= 0 || n <= 0 || hidden <= 0 || hidden % kHead) return 0;
+  return dino_layout(S, n, hidden).total;
+}
+
+int dino_qkv_linear(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* b, __nv_bfloat16* qkv, int tokens,
+                    int hidden, cudaStream_t st) {
+  if (int rc = check_dino(tokens, hidden, x, w)) return rc;
+  if (reinterpret_cast<uintptr_t>(qkv) & 15) return set_error(VA_ERR_ALIGN, "dinov2 qkv: output needs 16-byte alignment");
+  return launch_qkv<kPackedRows>(x, w, b, qkv, nullptr, tokens, hidden, tokens, 0, hidden / kHead, st);
+}
+
+int dino_attention_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* b, __nv_bfloat16* o, int S, int n,
+                       int hidden, int heads, void* ws, size_t ws_bytes, cudaStream_t st) {
+  VA_CHECK_ARG(S > 0 && n > 0 && heads > 0 && heads * kHead == hidden, "dinov2 attention: need heads·64 == hidden");
+  VA_CHECK_ARG((long long)S * heads <= 65535, "dinov2 attention: %d sequences × %d heads too many", S, heads);
+  if (int rc = check_dino(S * n, hidden, x, w)) return rc;
+  if (reinterpret_cast<uintptr_t>(o) & 15) return set_error(VA_ERR_ALIGN, "dinov2 attention: o needs 16-byte alignment");
+  const DinoWs L = dino_layout(S, n, hidden);
+  if (!ws || ws_bytes < L.total)
+    return set_error(VA_ERR_WORKSPACE, "dinov2 attention: workspace %zu < %zu bytes", ws_bytes, L.total);
+  if (reinterpret_cast<uintptr_t>(ws) & 255)
+    return set_error(VA_ERR_ALIGN, "dinov2 attention: workspace needs 256-byte alignment");
+  char* base = static_cast<char*>(ws);
+  __half* qk = reinterpret_cast<__half*>(base + L.qk);
+  __half* vb = reinterpret_cast<__half*>(base + L.v);
+  const int np = (n + 7) / 8 * 8;
+  if (int rc = launch_qkv<kSplitHeads>(x, w, b, qk, vb, S * n, hidden, n, np, heads, st)) return rc;
+  return tc_flash_attention(qk, vb, o, nullptr, S * heads, heads, n, kHead, 1, st);
+}
+
+int dino_window_partition(const __nv_bfloat16* x, __nv_bfloat16* xw, int B, int gh, int gw, int win, int C,
+                          cudaStream_t st) {
+  VA_CHECK_ARG(B > 0 && gh > 0 && gw > 0 && win > 0 && gh % win == 0 && gw % win == 0 && C > 0 && C % 8 == 0,
+               "dinov2 window partition: grid %dx%d not divisible by window %d, or C %% 8", gh, gw, win);
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(xw) & 15))
+    return set_error(VA_ERR_ALIGN, "dinov2 window partition: 16-byte alignment needed");
+  const long long total = (long long)B * (gh / win) * (gw / win) * (1 + win * win) * (C / 8);
+  window_partition_kernel<<<(int)std::min<long long>((total + 255) / 256, 148LL * 16), 256, 0, st>>>(
+      reinterpret_cast<const uint4*>(x), reinterpret_cast<uint4*>(xw), B, gh, gw, win, C / 8);
+  return check_launch("dinov2 window partition");
+}
+
+int dino_window_unpartition(const __nv_bfloat16* xw, __nv_bfloat16* x, int B, int gh, int gw, int win, int C,
+                            cudaStream_t st) {
+  VA_CHECK_ARG(B > 0 && gh > 0 && gw > 0 && win > 0 && gh % win == 0 && gw % win == 0 && C > 0 && C % 8 == 0,
+               "dinov2 window unpartition: grid %dx%d not divisible by window %d, or C %% 8", gh, gw, win);
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(xw) & 15))
+    return set_error(VA_ERR_ALIGN, "dinov2 window unpartition: 16-byte alignment needed");
+  const long long total = (long long)B * (1 + gh * gw) * (C / 8);
+  window_unpartition_kernel<<<(int)std::min<long long>((total + 255) / 256, 148LL * 16), 256, 0, st>>>(xw, x, B, gh,
+                                                                                                      gw, win, C);
+  return check_launch("dinov2 window unpartition");
+}
+
+int dino_status_read(int* out, cudaStream_t st) {
+  cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_dino_status, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "device status read: %s", cudaGetErrorString(e));
+  return VA_OK;
+}
+
+int dino_status_clear(cudaStream_t st) {
+  static const int zero = 0;
+  cudaError_t e = cudaMemcpyToSymbolAsync(g_dino_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "device status clear: %s", cudaGetErrorString(e));
+  return VA_OK;
+}
+
+}  // namespace va
+
+using namespace va;
+
+extern "C" {
+
+size_t va_dinov2_attention_workspace_bytes(int num_seqs, int seq_len, int hidden) {
+  return dino_workspace_bytes(num_seqs, seq_len, hidden);
+}
+
+int va_dinov2_attention_fwd_bf16(const va_bf16* x, const va_bf16* w_qkv, const float* b_qkv, va_bf16* o,
+                                 int num_seqs, int seq_len, int hidden, int num_heads, void* workspace,
+                                 size_t ws_bytes, va_stream_t stream) {
+  return dino_attention_fwd((const __nv_bfloat16*)x, (const __nv_bfloat16*)w_qkv, b_qkv, (__nv_bfloat16*)o, num_seqs,
+                            seq_len, hidden, num_heads, workspace, ws_bytes, (cudaStream_t)stream);
+}
+
+int va_dinov2_qkv_linear_bf16(const va_bf16* x, const va_bf16* w_qkv, const float* b_qkv, va_bf16* qkv, int tokens,
+                              int hidden, va_stream_t stream) {
+  return dino_qkv_linear((const __nv_bfloat16*)x, (const __nv_bfloat16*)w_qkv, b_qkv, (__nv_bfloat16*)qkv, tokens,
+                         hidden, (cudaStream_t)stream);
+}
+
+int va_dinov2_window_partition_bf16(const va_bf16* x, va_bf16* xw, int B, int grid_h, int grid_w, int win,
+                                    int hidden, va_stream_t stream) {
+  return dino_window_partition((const __nv_bfloat16*)x, (__nv_bfloat16*)xw, B, grid_h, grid_w, win, hidden,
+                               (cudaStream_t)stream);
+}
+
+int va_dinov2_window_unpartition_bf16(const va_bf16* xw, va_bf16* x, int B, int grid_h, int grid_w, int win,
+                                      int hidden, va_stream_t stream) {
+  return dino_window_unpartition((const __nv_bfloat16*)xw, (__nv_bfloat16*)x, B, grid_h, grid_w, win, hidden,
+                                 (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -183,9 +183,13 @@ __device__ __forceinline__ uint32_t col_s(int g) { return (uint32_t)g * 256u; }
 __device__ __forceinline__ uint32_t col_p(int g) { return (uint32_t)g * 256u + 128u; }
 __device__ __forceinline__ uint32_t col_o(int g) { return (uint32_t)g * 256u + 192u; }
 
+// KD = 32 (PSA key_dim): Q/K rows of 64 bytes, K-major SW64; KD = 64 (DINOv2
+// head dim): rows of 128 bytes, K-major SW128.
+template <int KD>
 struct AttnSmem {
-  uint8_t q[2][kTile * 64];                // Q tiles [128 rows × 32] f16, K-major SW64 (8 KB each)
-  uint8_t k[kStages][kTile * 64];          // K tiles (8 KB each)
+  static constexpr int kQK = kTile * KD * 2;  // bytes of one Q or K tile
+  uint8_t q[2][kQK];                       // Q tiles [128 rows × KD] f16
+  uint8_t k[kStages][kQK];                 // K tiles
   uint8_t v[kStages][2][kVBlk];            // V: stage × key-block
   float xmax[2][2][2][kTile];              // [tile parity][group][half][row] partial row maxima
   float xsum[2][2][kTile];                 // [group][half][row] partial row sums (end of loop)
@@ -196,25 +200,35 @@ struct AttnSmem {
   int abort;
 };
 
-__device__ __forceinline__ void attn_load_kv(AttnSmem& sm, const CUtensorMap* mqk, const CUtensorMap* mv, int t,
+template <int KD>
+__device__ __forceinline__ void attn_load_kv(AttnSmem<KD>& sm, const CUtensorMap* mqk, const CUtensorMap* mv, int t,
                                              int stage, int BH, int bh, int vrow) {
-  mbar_arrive_expect_tx(&sm.kv_full[stage], kTile * 64 + 2 * kVBlk);
+  mbar_arrive_expect_tx(&sm.kv_full[stage], AttnSmem<KD>::kQK + 2 * kVBlk);
   tma_load_3d(sm.k[stage], mqk, &sm.kv_full[stage], 0, t * kTile, BH + bh);
   tma_load_2d(sm.v[stage][0], mv, &sm.kv_full[stage], t * kTile, vrow);
   tma_load_2d(sm.v[stage][1], mv, &sm.kv_full[stage], t * kTile + 64, vrow);
 }
 
+// Output layouts: kOutChannelMajor — f16 [B][nh·64][Np] (PSA: the proj
+// kernel's operand); kOutTokenMajor — bf16 [BH/nh][N][nh·64] (DINOv2: the
+// input of the attention's output Linear).
+constexpr int kOutChannelMajor = 0, kOutTokenMajor = 1;
+
+template <int KD, int OUT>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v,
-            __half* __restrict__ obuf, float* __restrict__ lse, int N, int Np, int nh, float scale_log2) {
+            void* __restrict__ obuf, float* __restrict__ lse, int N, int Np, int nh, float scale_log2) {
+  static_assert(KD == 32 || KD == 64, "key dim 32 or 64");
+  constexpr int kQK = AttnSmem<KD>::kQK;
   extern __shared__ uint8_t smem_raw[];
-  AttnSmem& sm = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  AttnSmem<KD>& sm =
+      *reinterpret_cast<AttnSmem<KD>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int q0 = blockIdx.x * 2 * kTile, bh = blockIdx.y;
   const int BH = gridDim.y, b = bh / nh, h = bh % nh;
   const int nkv = (N + kTile - 1) / kTile;
   const bool has1 = q0 + kTile < N;
-  const int vrow = b * kC + h * kHD;
+  const int vrow = bh * kHD;  // V rows [BH·64][Np]
 
   if (tid == 0) {
     mbar_init(&sm.q_full, 1);
@@ -253,7 +267,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       if (producer) {
         tma_prefetch_desc(&map_qk);
         tma_prefetch_desc(&map_v);
-        mbar_arrive_expect_tx(&sm.q_full, (has1 ? 2 : 1) * kTile * 64);
+        mbar_arrive_expect_tx(&sm.q_full, (has1 ? 2 : 1) * kQK);
         tma_load_3d(sm.q[0], &map_qk, &sm.q_full, 0, q0, bh);
         if (has1) tma_load_3d(sm.q[1], &map_qk, &sm.q_full, 0, q0 + kTile, bh);
         for (; issued < kStages && issued < nkv; ++issued)
@@ -264,15 +278,18 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       // Descriptors are built once; a stage / k-step only moves the start-
       // address field (bits 0-13, address >> 4) — a plain add that cannot
       // carry out of the field for shared-memory addresses.
-      const uint64_t dq = sdesc(smem_u32(sm.q[g]), 16, 512, SW_64B);
-      const uint64_t dk0 = sdesc(smem_u32(sm.k[0]), 16, 512, SW_64B);
+      constexpr uint32_t kSbo = KD == 32 ? 512 : 1024;  // 8 rows of the swizzle atom
+      constexpr uint32_t kSwz = KD == 32 ? SW_64B : SW_128B;
+      const uint64_t dq = sdesc(smem_u32(sm.q[g]), 16, kSbo, kSwz);
+      const uint64_t dk0 = sdesc(smem_u32(sm.k[0]), 16, kSbo, kSwz);
       const uint64_t dv0 = sdesc(smem_u32(sm.v[0][0]), 16, 1024, SW_128B);
-      constexpr uint32_t kKStage = (kTile * 64) >> 4, kVStage = (2 * kVBlk) >> 4, kVHalf = kVBlk >> 4;
+      constexpr uint32_t kKStage = kQK >> 4, kVStage = (2 * kVBlk) >> 4, kVHalf = kVBlk >> 4;
       const uint32_t ds = tmem + col_s(g), dp = tmem + col_p(g), dO = tmem + col_o(g);
       auto issue_s = [&](int stage) {
         const uint64_t kd_ = dk0 + (uint64_t)(stage * kKStage);
         mma_ss(ds, dq, kd_, idS, 0u);
-        mma_ss(ds, dq + 2, kd_ + 2, idS, 1u);
+#pragma unroll
+        for (int s = 1; s < KD / 16; ++s) mma_ss(ds, dq + 2 * s, kd_ + 2 * s, idS, 1u);  // +32 bytes per k-step
       };
       auto issue_o = [&](int stage, uint32_t acc) {
         const uint64_t vd = dv0 + (uint64_t)(stage * kVStage);
@@ -452,9 +469,20 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       tmem_ld_wait();
       reg_fence(o);
       if (n < N) {
-        __half* dst = obuf + ((size_t)b * kC + h * kHD + hf * 32) * Np + n;
+        if constexpr (OUT == kOutChannelMajor) {
+          __half* dst = static_cast<__half*>(obuf) + ((size_t)bh * kHD + hf * 32) * Np + n;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) dst[(size_t)i * Np] = __float2half_rn(__uint_as_float(o[i]) * inv);
+          for (int i = 0; i < 32; ++i) dst[(size_t)i * Np] = __float2half_rn(__uint_as_float(o[i]) * inv);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(obuf) +
+                                                ((size_t)b * N + n) * (nh * kHD) + h * kHD + hf * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                                pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                                pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                                pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+        }
       }
       if (lse && hf == 0 && n < N) lse[(size_t)bh * N + n] = (m + __log2f(lt)) * 0.6931471805599453f;
     }
@@ -782,12 +810,12 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
       return rc;
   }
   const int ntile = (N + kTile - 1) / kTile;
-  const size_t sm1 = sizeof(QkvSmem) + 1024, sm2 = sizeof(AttnSmem) + 1024, sm4 = sizeof(ProjSmem) + 1024;
+  const size_t sm1 = sizeof(QkvSmem) + 1024, sm2 = sizeof(AttnSmem<kKD>) + 1024, sm4 = sizeof(ProjSmem) + 1024;
   const size_t sm3 = (size_t)kPeCh * (H + 2) * ((W + 10) | 1) * sizeof(float);
   static bool attr_done = false;
   if (!attr_done) {
     if (int rc = set_smem(qkv_proj_kernel, sm1)) return rc;
-    if (int rc = set_smem(attn_kernel, sm2)) return rc;
+    if (int rc = set_smem(attn_kernel<kKD, kOutChannelMajor>, sm2)) return rc;
     if (int rc = set_smem(pe_dwconv_kernel, (size_t)kPeCh * kMaxPlane * sizeof(float))) return rc;
     if (int rc = set_smem(proj_kernel, sm4)) return rc;
     attr_done = true;
@@ -813,7 +841,8 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   qkv_proj_kernel<<<dim3(ntile, B), 128, sm1, st>>>(mx, mw, b_qkv, qk, vb, N, Np, nh);
   if (int rc = check_launch("psa qkv_proj")) return rc;
   const float scale_log2 = (1.0f / sqrtf((float)kd)) * 1.4426950408889634f;
-  attn_kernel<<<dim3((ntile + 1) / 2, BH), kAttnThreads, sm2, st>>>(mqk, mv, ob, lse_out, N, Np, nh, scale_log2);
+  attn_kernel<kKD, kOutChannelMajor>
+      <<<dim3((ntile + 1) / 2, BH), kAttnThreads, sm2, st>>>(mqk, mv, ob, lse_out, N, Np, nh, scale_log2);
   if (int rc = check_launch("psa attention")) return rc;
   pe_dwconv_kernel<<<dim3(kC / kPeCh, B), kPeThreads, sm3, st>>>(vb, w_pe, b_pe, peb, w_proj, wp16, H, W, Np);
   if (int rc = check_launch("psa pe")) return rc;
@@ -839,33 +868,47 @@ int tc_status_clear(cudaStream_t st) {
 
 namespace va {
 
-int psa_attention_core_tc(const void* qk, const void* v, void* o, float* lse, int B, int nh, int H, int W,
-                          cudaStream_t st) {
-  VA_CHECK_ARG(nh == 2 && B > 0 && H > 0 && W > 0 && B * nh <= 65535, "psa flash attention: need nh=2, B,H,W > 0");
+int tc_flash_attention(const void* qk, const void* v, void* o, float* lse, int BH, int nh, int N, int kd,
+                       int out_token_major, cudaStream_t st) {
+  VA_CHECK_ARG(kd == 32 || kd == 64, "flash attention: key dim %d (32 or 64)", kd);
+  VA_CHECK_ARG(BH > 0 && nh > 0 && BH % nh == 0 && N > 0 && BH <= 65535, "flash attention: bad sizes");
   if ((reinterpret_cast<uintptr_t>(qk) & 15) || (reinterpret_cast<uintptr_t>(v) & 15) ||
       (reinterpret_cast<uintptr_t>(o) & 15))
-    return set_error(VA_ERR_ALIGN, "psa flash attention: qk/v/o need 16-byte alignment");
-  const int N = H * W, Np = (N + 7) / 8 * 8, BH = B * nh;
+    return set_error(VA_ERR_ALIGN, "flash attention: qk/v/o need 16-byte alignment");
+  const int Np = (N + 7) / 8 * 8;
   CUtensorMap mqk, mv;
   {
-    uint64_t d[3] = {(uint64_t)kKD, (uint64_t)N, (uint64_t)2 * BH}, s[2] = {(uint64_t)kKD * 2, (uint64_t)N * kKD * 2};
-    uint32_t bx[3] = {kKD, kTile, 1};
-    if (int rc = make_map(&mqk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, qk, d, s, bx, CU_TENSOR_MAP_SWIZZLE_64B, "qk"))
+    uint64_t d[3] = {(uint64_t)kd, (uint64_t)N, (uint64_t)2 * BH}, s[2] = {(uint64_t)kd * 2, (uint64_t)N * kd * 2};
+    uint32_t bx[3] = {(uint32_t)kd, kTile, 1};
+    if (int rc = make_map(&mqk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, qk, d, s, bx,
+                          kd == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B, "qk"))
       return rc;
   }
   {
-    uint64_t d[2] = {(uint64_t)N, (uint64_t)B * kC}, s[1] = {(uint64_t)Np * 2};
+    // inner extent N (not Np): the pad columns of a row read as zeros
+    uint64_t d[2] = {(uint64_t)N, (uint64_t)BH * kHD}, s[1] = {(uint64_t)Np * 2};
     uint32_t bx[2] = {64, kHD};
     if (int rc = make_map(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B, "v"))
       return rc;
   }
-  const size_t sm2 = sizeof(AttnSmem) + 1024;
-  if (int rc = set_smem(attn_kernel, sm2)) return rc;
-  const float scale_log2 = (1.0f / sqrtf((float)kKD)) * 1.4426950408889634f;
-  const int ntile = (N + kTile - 1) / kTile;
-  attn_kernel<<<dim3((ntile + 1) / 2, BH), kAttnThreads, sm2, st>>>(mqk, mv, static_cast<__half*>(o), lse, N, Np, nh,
-                                                                    scale_log2);
-  return check_launch("psa flash attention");
+  const float scale_log2 = (1.0f / sqrtf((float)kd)) * 1.4426950408889634f;
+  const dim3 grid(((N + kTile - 1) / kTile + 1) / 2, BH);
+  auto launch = [&](auto kernel, size_t smem) -> int {
+    if (int rc = set_smem(kernel, smem)) return rc;
+    kernel<<<grid, kAttnThreads, smem, st>>>(mqk, mv, o, lse, N, Np, nh, scale_log2);
+    return check_launch("flash attention");
+  };
+  if (kd == 32)
+    return out_token_major ? launch(attn_kernel<32, kOutTokenMajor>, sizeof(AttnSmem<32>) + 1024)
+                           : launch(attn_kernel<32, kOutChannelMajor>, sizeof(AttnSmem<32>) + 1024);
+  return out_token_major ? launch(attn_kernel<64, kOutTokenMajor>, sizeof(AttnSmem<64>) + 1024)
+                         : launch(attn_kernel<64, kOutChannelMajor>, sizeof(AttnSmem<64>) + 1024);
+}
+
+int psa_attention_core_tc(const void* qk, const void* v, void* o, float* lse, int B, int nh, int H, int W,
+                          cudaStream_t st) {
+  VA_CHECK_ARG(nh == 2 && B > 0 && H > 0 && W > 0 && B * nh <= 65535, "psa flash attention: need nh=2, B,H,W > 0");
+  return tc_flash_attention(qk, v, o, lse, B * nh, nh, H * W, kKD, 0, st);
 }
 
 }  // namespace va
