@@ -255,6 +255,48 @@ VA_API int va_dinov2_window_partition_bf16(const va_bf16 *x, va_bf16 *xw, int B,
 VA_API int va_dinov2_window_unpartition_bf16(const va_bf16 *xw, va_bf16 *x, int B, int grid_h,
                                              int grid_w, int win, int hidden, va_stream_t stream);
 
+/* ── PSA Attention training step (data-parallel cfg5) ─────────────────────
+ * One rank's forward + backward on its shard, bf16 activations and weights,
+ * f32 gradients; the caller all-reduces `grads` across ranks and applies
+ * va_psa_sgd_update.  The reference trains the same block through its
+ * backward kernels (psa_fa2_backward psa.rs:650-725, psa_*_backward
+ * psa.rs:201-327, conv BackwardDx/Dw); here BN is folded (conv weight + bias
+ * are the parameters).  Loss = mean((y − target)²) over the shard, written to
+ * *loss (device).  y [B,C,H,W] bf16 output; dx (optional, may be NULL)
+ * bf16; grads f32 [VA_PSA_GRAD_COUNT] in PyTorch parameter layouts at the
+ * offsets below (stored, not accumulated).  Deterministic. */
+#define VA_PSA_GRAD_WQKV 0         /* [256][128] */
+#define VA_PSA_GRAD_WPROJ 32768    /* [128][128] */
+#define VA_PSA_GRAD_WPE 49152      /* [128][1][3][3] */
+#define VA_PSA_GRAD_BQKV 50304     /* [256] */
+#define VA_PSA_GRAD_BPROJ 50560    /* [128] */
+#define VA_PSA_GRAD_BPE 50688      /* [128] */
+#define VA_PSA_GRAD_COUNT 50816
+VA_API size_t va_psa_train_workspace_bytes(int B, int H, int W);
+VA_API int va_psa_train_fwd_bwd_bf16(const va_bf16 *x, const va_bf16 *target, const va_bf16 *w_qkv,
+                                     const float *b_qkv, const va_bf16 *w_pe, const float *b_pe,
+                                     const va_bf16 *w_proj, const float *b_proj, va_bf16 *y,
+                                     va_bf16 *dx, float *grads, float *loss, int B, int C, int H,
+                                     int W, int num_heads, int key_dim, void *workspace,
+                                     size_t ws_bytes, va_stream_t stream);
+/* master (f32, gradient layout) -= lr·grad_scale·grads; then the bf16
+ * weights and f32 biases the forward reads are rewritten from master. */
+VA_API int va_psa_sgd_update(float *master, const float *grads, float lr, float grad_scale,
+                             va_bf16 *w_qkv, float *b_qkv, va_bf16 *w_pe, float *b_pe,
+                             va_bf16 *w_proj, float *b_proj, va_stream_t stream);
+
+/* Batched f16 tensor-core GEMM used by the training step (no counterpart in
+ * the reference): C[z][m][n] = alpha·Σ_k A_z(m,k)·B_z(n,k), f32 accumulation.
+ * An operand is K-major (x_mn = 0: row m holds K elements, row pitch ld) or
+ * MN-major (x_mn = 1: row k holds the M or N elements); x_batch = elements
+ * between batch entries, x_bcast = 1 to use one matrix for all z.  C is f32
+ * (c_bf16 = 0) or bf16, row pitch ldc, batch stride c_batch.  16-byte
+ * aligned bases and pitches. */
+VA_API int va_gemm_f16(const void *a, int a_mn, long long lda, long long a_batch, int a_bcast,
+                       const void *b, int b_mn, long long ldb, long long b_batch, int b_bcast,
+                       void *c, int c_bf16, long long ldc, long long c_batch, int M, int N, int K,
+                       int Z, float alpha, va_stream_t stream);
+
 /* Device status word of the tensor-core kernels: 0, or 1000+site of the
  * first bounded wait that gave up.  read: copies it to *status (synchronises
  * `stream`); clear: resets it to 0. */

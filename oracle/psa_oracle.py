@@ -359,3 +359,30 @@ def psa_attention_torch(x, w_qkv, b_qkv, w_pe, b_pe, w_proj, b_proj, num_heads: 
     o = (v @ attn.transpose(-2, -1)).reshape(B, C, H, W)
     pe = Fn.conv2d(v.reshape(B, C, H, W), w_pe.reshape(C, 1, 3, 3), b_pe, padding=1, groups=C)
     return Fn.conv2d(o + pe, w_proj.reshape(C, C, 1, 1), b_proj)
+
+
+# ── training step (data-parallel cfg5) ───────────────────────────────────────
+
+GRAD_ORDER = ("w_qkv", "w_proj", "w_pe", "b_qkv", "b_proj", "b_pe")  # flat gradient buffer layout
+
+
+def psa_train_step_torch(x, target, params: dict, num_heads: int = 2, key_dim: int = 32):
+    """Forward + autograd backward of the BN-folded PSA Attention block in
+    torch-CPU float64 with loss = mean((y − target)²).  ``params`` holds
+    w_qkv [256,128], b_qkv [256], w_pe [128,1,3,3] (or [128,9]), b_pe [128],
+    w_proj [128,128], b_proj [128].  Returns ``(y, loss, grads, dx)`` with
+    ``grads`` the flat float64 vector in ``GRAD_ORDER`` (PyTorch parameter
+    layouts) — the layout of the device gradient buffer.  This is the same
+    differentiation the reference's backward fixture performs
+    (``c2psa_backward_train_torch``), restricted to the attention block."""
+    import torch
+    t = lambda a: torch.as_tensor(np.asarray(a, F64))
+    p = {k: t(v).requires_grad_(True) for k, v in params.items()}
+    xt = t(x).requires_grad_(True)
+    C = xt.shape[1]
+    y = psa_attention_torch(xt, p["w_qkv"], p["b_qkv"], p["w_pe"].reshape(C, 9), p["b_pe"], p["w_proj"],
+                            p["b_proj"], num_heads, key_dim)
+    loss = ((y - t(target)) ** 2).mean()
+    loss.backward()
+    grads = np.concatenate([p[k].grad.numpy().reshape(-1) for k in GRAD_ORDER])
+    return y.detach().numpy(), float(loss), grads, xt.grad.numpy()

@@ -18,6 +18,7 @@ I = C.c_int
 F = C.c_float
 I64P = C.POINTER(C.c_int64)
 SZ = C.c_size_t
+LL = C.c_longlong
 S = C.c_void_p  # stream
 
 # name -> (restype, argtypes); mirrors include/visionattn.h
@@ -62,6 +63,10 @@ SIGNATURES: dict[str, tuple] = {
     "va_dinov2_qkv_linear_bf16": (I, [P, P, P, P, I, I, S]),
     "va_dinov2_window_partition_bf16": (I, [P, P, I, I, I, I, I, S]),
     "va_dinov2_window_unpartition_bf16": (I, [P, P, I, I, I, I, I, S]),
+    "va_psa_train_workspace_bytes": (SZ, [I, I, I]),
+    "va_psa_train_fwd_bwd_bf16": (I, [P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, SZ, S]),
+    "va_psa_sgd_update": (I, [P, P, F, F, P, P, P, P, P, P, S]),
+    "va_gemm_f16": (I, [P, I, LL, LL, I, P, I, LL, LL, I, P, I, LL, LL, I, I, I, I, F, S]),
     "va_device_status_read": (I, [C.POINTER(C.c_int), S]),
     "va_device_status_clear": (I, [S]),
 }

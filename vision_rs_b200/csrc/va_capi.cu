@@ -121,16 +121,18 @@ int va_psa_flash_attention_fwd_f16(const void* qk, const void* v, void* o, float
 
 int va_device_status_read(int* status, va_stream_t s) {  // first non-zero word of the tensor-core kernels
   if (!status) return set_error(VA_ERR_SHAPE, "device_status_read: null output");
-  int a = 0, b = 0;
+  int a = 0, b = 0, c = 0;
   if (int rc = tc_status_read(&a, (cudaStream_t)s)) return rc;
   if (int rc = dino_status_read(&b, (cudaStream_t)s)) return rc;
-  *status = a ? a : b;
+  if (int rc = gemm_status_read(&c, (cudaStream_t)s)) return rc;
+  *status = a ? a : (b ? b : c);
   return VA_OK;
 }
 
 int va_device_status_clear(va_stream_t s) {
   if (int rc = tc_status_clear((cudaStream_t)s)) return rc;
-  return dino_status_clear((cudaStream_t)s);
+  if (int rc = dino_status_clear((cudaStream_t)s)) return rc;
+  return gemm_status_clear((cudaStream_t)s);
 }
 
 }  // extern "C"

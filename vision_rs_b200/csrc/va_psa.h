@@ -30,6 +30,31 @@ template <typename T, typename TW>
 int dwconv3x3(const T* x, const TW* w, const float* bias, T* y, int B, int C, int H, int W, cudaStream_t st);
 
 size_t psa_tc_workspace_bytes(int B, int H, int W, int nh);
+// Byte offsets of the tensor-core forward's intermediates inside its
+// workspace: Q/K f16 [2][B·nh][N][32], V, O and PE f16 [B][128][Np], W_proj
+// as f16 [128][128].
+struct PsaTcOffsets {
+  size_t qk, v, o, pe, wproj, total;
+};
+PsaTcOffsets psa_tc_offsets(int B, int H, int W, int nh);
+
+// One operand of tc_gemm_f16 (f16 elements): K-major — row r (an M or N
+// index) holds K contiguous elements, `ld` apart; MN-major — row k holds the
+// M (or N) elements contiguously.  batch_stride: elements between batch
+// entries; broadcast: one matrix for every batch entry.
+struct GemmOperand {
+  const void* ptr;
+  bool mn;
+  long long ld;
+  long long batch_stride;
+  bool broadcast;
+};
+// C[z][m][n] = α·Σ_k A_z(m,k)·B_z(n,k), f32 accumulation; C f32 or bf16
+// with row pitch ldc and batch stride c_batch (elements).
+int tc_gemm_f16(const GemmOperand& a, const GemmOperand& b, void* c, bool c_bf16, long long ldc, long long c_batch,
+                int M, int N, int K, int Z, cudaStream_t st, float alpha = 1.0f);
+int gemm_status_read(int* out, cudaStream_t st);
+int gemm_status_clear(cudaStream_t st);
 bool psa_tc_supported(int C, int nh, int kd);
 int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,
                          const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,

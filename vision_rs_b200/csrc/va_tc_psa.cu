@@ -755,6 +755,11 @@ int set_smem(K kernel, size_t bytes) {
 
 size_t psa_tc_workspace_bytes(int B, int H, int W, int nh) { return tc_layout(B, H, W, nh).total; }
 
+PsaTcOffsets psa_tc_offsets(int B, int H, int W, int nh) {
+  const TcWs L = tc_layout(B, H, W, nh);
+  return PsaTcOffsets{L.qk, L.v, L.o, L.pe, L.wproj, L.total};
+}
+
 bool psa_tc_supported(int C, int nh, int kd) { return C == kC && nh * 4 * kd == kQKV && kd == kKD; }
 
 int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,

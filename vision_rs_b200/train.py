@@ -1,0 +1,65 @@
+"""PSA Attention data-parallel training step (cfg5) over the C ABI.
+
+Each rank: ``PsaTrainStep.forward_backward`` (tensor-core forward, backward
+into one f32 gradient buffer), ``torch.distributed.all_reduce`` of that buffer
+over NCCL (sum), then ``sgd`` with ``grad_scale = 1/world`` on f32 master
+weights, which rewrites the bf16 weights the next forward reads.  The
+gradient buffer layout is the header's ``VA_PSA_GRAD_*`` offsets:
+``[w_qkv 256×128 | w_proj 128×128 | w_pe 128×9 | b_qkv | b_proj | b_pe]``.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .psa import _p, _stream
+
+GRAD_COUNT = 50816
+GRAD_SLICES = {"w_qkv": (0, 32768), "w_proj": (32768, 49152), "w_pe": (49152, 50304), "b_qkv": (50304, 50560),
+               "b_proj": (50560, 50688), "b_pe": (50688, 50816)}
+
+
+class PsaTrainStep:
+    """Buffers for one rank's shard of B images of 128×H×W."""
+
+    def __init__(self, B: int, H: int, W: int, device, C: int = 128, num_heads: int = 2, key_dim: int = 32):
+        self.B, self.H, self.W, self.C, self.nh, self.kd = B, H, W, C, num_heads, key_dim
+        need = int(_lib.lib().va_psa_train_workspace_bytes(B, H, W))
+        self.ws = torch.empty(need, dtype=torch.uint8, device=device)
+        self.grads = torch.empty(GRAD_COUNT, dtype=torch.float32, device=device)
+        self.loss = torch.empty(1, dtype=torch.float32, device=device)
+        self.y = torch.empty(B, C, H, W, dtype=torch.bfloat16, device=device)
+        self.dx = torch.empty(B, C, H, W, dtype=torch.bfloat16, device=device)
+
+    def forward_backward(self, x, target, params: dict, want_dx: bool = False, stream=None):
+        """Returns ``(y, loss, grads, dx)`` (device tensors; dx None unless asked)."""
+        _lib.call("va_psa_train_fwd_bwd_bf16", _p(x), _p(target), _p(params["w_qkv"]), _p(params["b_qkv"]),
+                  _p(params["w_pe"]), _p(params["b_pe"]), _p(params["w_proj"]), _p(params["b_proj"]), _p(self.y),
+                  _p(self.dx) if want_dx else None, _p(self.grads), _p(self.loss), self.B, self.C, self.H, self.W,
+                  self.nh, self.kd, _p(self.ws), self.ws.numel(), _stream(stream))
+        return self.y, self.loss, self.grads, (self.dx if want_dx else None)
+
+    @staticmethod
+    def master_from(params: dict) -> torch.Tensor:
+        """f32 master weights in the gradient layout, from the current parameters."""
+        order = ("w_qkv", "w_proj", "w_pe", "b_qkv", "b_proj", "b_pe")
+        return torch.cat([params[k].float().reshape(-1) for k in order]).contiguous()
+
+    @staticmethod
+    def sgd(master, grads, params: dict, lr: float, grad_scale: float = 1.0, stream=None):
+        _lib.call("va_psa_sgd_update", _p(master), _p(grads), float(lr), float(grad_scale), _p(params["w_qkv"]),
+                  _p(params["b_qkv"]), _p(params["w_pe"]), _p(params["b_pe"]), _p(params["w_proj"]),
+                  _p(params["b_proj"]), _stream(stream))
+
+
+def dp_train_step(step: PsaTrainStep, x, target, params: dict, master, lr: float, group=None):
+    """One data-parallel step: local fwd+bwd, NCCL all-reduce (sum) of the f32
+    gradient buffer, SGD with the mean gradient.  Returns the local loss tensor."""
+    import torch.distributed as dist
+    _, loss, grads, _ = step.forward_backward(x, target, params)
+    world = 1
+    if dist.is_available() and dist.is_initialized():
+        dist.all_reduce(grads, op=dist.ReduceOp.SUM, group=group)
+        world = dist.get_world_size(group)
+    step.sgd(master, grads, params, lr, 1.0 / world)
+    return loss
