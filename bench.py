@@ -1,18 +1,28 @@
 #!/usr/bin/env python3
-"""Benchmark of the YOLO26 C2PSA PSA Attention forward (bf16, 1600 tokens).
+"""Benchmarks of the B200 attention hot path of vision-rs.
 
-Workload (configs[1] of the north star): per GPU a batch of 64 seeded N(0,1)
-feature maps 128×40×40, weights N(0,0.02), BN folded; bf16 storage, f32
-accumulation.  One step = one call of the fused op on the whole batch.
-Multi-GPU: one process per GPU (torchrun), image shards with no collective on
-the data path (weak scaling: every rank runs its own 64-image batch); the
-timing is the max over ranks.
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg2|cfg3|cfg4|cfg5]
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Configurations (the north star's configs; synthetic seeded inputs of the
+named shapes and distributions, random-init weights):
 
-``--impl reference`` times the CPU restatement of the reference maths (the
-reference has no CPU path) with all host threads on a bounded sample of the
-same workload; under torchrun only rank 0 runs it.
+* ``cfg2`` (default, the headline): YOLO26 C2PSA PSA Attention forward, bf16,
+  per GPU a batch of 64 feature maps 128×40×40 (1600 tokens).  Step = one
+  call of the fused op on the batch.
+* ``cfg3``: RF-DETR MSDeformAttn forward + backward, batch 8, 300 queries,
+  16 heads × 16, levels 80²/40²/20², 4 points (``--dtype f32|bf16``).
+* ``cfg4``: DINOv2-S attention (packed QKV Linear + attention, bf16), batch 16
+  at 560×560 (1 + 40×40 tokens): one global layer + one 4×4-windowed layer.
+* ``cfg5``: PSA Attention training step, bf16 with f32 master weights, 32
+  images of 128×20×20 per GPU: forward + backward + NCCL all-reduce of the
+  weight gradients + SGD.
+
+Multi-GPU: one process per GPU (torchrun), image shards (weak scaling); cfg2-4
+have no collective, cfg5 all-reduces its gradients.  Timing: CUDA events on
+the launching stream, L2 flushed between timed steps, max over ranks.
+``--impl reference`` times the CPU restatement of the same maths (the
+reference has no CPU path; for cfg3/cfg4 the reference has no such operator at
+all) with all host threads on a bounded sample; under torchrun only rank 0 runs.
 """
 from __future__ import annotations
 
@@ -30,30 +40,44 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-METRIC = "attention images/sec (C2PSA PSA attention fwd, bf16, 1600 tokens)"
-UNIT = "images/s"
-B_PER_GPU, C, H, W, NH, KD = 64, 128, 40, 40, 2, 32
-N_TOK = H * W
-# algorithmic FLOPs per image (qkv + QK^T + PV + PE + proj), per the survey's count
-FLOP_QKV = 2 * N_TOK * C * (NH * 4 * KD)
-FLOP_QK = 2 * NH * N_TOK * N_TOK * KD
-FLOP_PV = 2 * NH * N_TOK * N_TOK * 2 * KD
-FLOP_PE = 2 * 9 * C * N_TOK
-FLOP_PROJ = 2 * N_TOK * C * C
-FLOP_IMG = FLOP_QKV + FLOP_QK + FLOP_PV + FLOP_PE + FLOP_PROJ
-FLOP_ATTN_IMG = FLOP_QK + FLOP_PV
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+# ── cfg2 constants ──────────────────────────────────────────────────────────
+C, NH, KD = 128, 2, 32
+P2_B, P2_H, P2_W = 64, 40, 40
+N2 = P2_H * P2_W
+FLOP_ATTN_IMG2 = 2 * NH * N2 * N2 * KD + 2 * NH * N2 * N2 * 2 * KD
+FLOP_IMG2 = 2 * N2 * C * (NH * 4 * KD) + FLOP_ATTN_IMG2 + 2 * 9 * C * N2 + 2 * N2 * C * C
 # DRAM bytes (read + write) of one attention-kernel launch at the full workload, from the committed
 # ncu capture in profiles/psa_fwd_kernels_cfg2_ncu_full.md (52.46 MB read + 4.88 MB written)
 ATTN_TRAFFIC_BYTES = 57_345_024
+
+# ── cfg3 constants (SURVEY per-unit bytes) ──────────────────────────────────
+MS_B, MS_Q, MS_NH, MS_DH, MS_P = 8, 300, 16, 16, 4
+MS_SHAPES = ((80, 80), (40, 40), (20, 20))
+MS_FWD_BYTES = {"f32": 76_800_000, "bf16": 34_406_400 + 3_686_400 + 1_843_200 + 1_228_800}
+MS_BWD_BYTES_F32 = 151_100_000
+
+# ── cfg4 constants ──────────────────────────────────────────────────────────
+DN_B, DN_HID, DN_HEADS, DN_GRID, DN_WIN = 16, 384, 6, 40, 10
+DN_N = 1 + DN_GRID * DN_GRID
+DN_NW = (DN_GRID // DN_WIN) ** 2
+DN_NWIN = 1 + DN_WIN * DN_WIN
+DN_FLOP_GLOBAL_ATTN_IMG = 2 * 2 * DN_HEADS * DN_N * DN_N * 64
+DN_FLOP_IMG = (2 * DN_N * DN_HID * 3 * DN_HID + DN_FLOP_GLOBAL_ATTN_IMG
+               + 2 * DN_NW * DN_NWIN * DN_HID * 3 * DN_HID + 2 * 2 * DN_HEADS * DN_NW * DN_NWIN * DN_NWIN * 64)
+
+# ── cfg5 constants ──────────────────────────────────────────────────────────
+T5_B, T5_H, T5_W = 32, 20, 20
+N5 = T5_H * T5_W
+FLOP_FWD_IMG5 = 2 * N5 * C * 256 + 2 * NH * N5 * N5 * (KD + 2 * KD) + 2 * 9 * C * N5 + 2 * N5 * C * C
 
 
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
-            d = json.load(f)
-        return d, "measured"
+            return json.load(f), "measured"
     return FALLBACK_PEAKS, "fallback"
 
 
@@ -66,8 +90,9 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
+        self.lines = []
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-lms", "50", "-i", str(self.idx)], stdout=subprocess.PIPE,
@@ -76,8 +101,7 @@ class ClockSampler:
             self.proc = None
         return self
 
-    def __exit__(self, *a):
-        self.lines = []
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -90,7 +114,7 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -107,74 +131,458 @@ class ClockSampler:
 
 
 def dist_env():
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return ws, rank, local
+    return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+            int(os.environ.get("LOCAL_RANK", "0")))
 
 
-def cpu_sample(n_img: int, threads: int, seed: int = 1234):
-    """Times the torch-CPU f32 restatement on ``n_img`` images; returns img/s."""
+def event_time(fn, n, stream, flush=None):
+    """Mean duration (ms) of ``fn`` over n launches, CUDA events on ``stream``,
+    L2 evicted before each (outside the events)."""
     import torch
-    from oracle import psa_oracle as po
-    torch.set_num_threads(threads)
-    p = po.psa_synthetic(n_img, H, W, seed=seed)
-    t = {k: torch.tensor(v) for k, v in p.items()}
-    args = (t["x"], t["w_qkv"], t["b_qkv"], t["w_pe"], t["b_pe"], t["w_proj"], t["b_proj"], NH, KD)
-    po.psa_attention_torch(*args)  # warm
-    t0 = time.perf_counter()
-    po.psa_attention_torch(*args)
-    dt = time.perf_counter() - t0
-    return n_img / dt, dt
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    for i in range(n):
+        if flush is not None:
+            flush.fill_(float(i))
+        evs[i][0].record(stream)
+        fn()
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+
+# ═════════════════════════════ workloads ═════════════════════════════════════
+class Cfg2:
+    metric = "attention images/sec (C2PSA PSA attention fwd, bf16, 1600 tokens)"
+    unit, dtype, batch = "images/s", "bf16", P2_B
+    workload = "cfg2: C2PSA PSA attention fwd, 128x40x40 (1600 tokens), nh=2, kd=32, hd=64"
+
+    def __init__(self, dev, rank, batch, args):
+        import torch
+        from vision_rs_b200 import psa as vp
+        rng = np.random.default_rng(1000 + rank)
+        f = lambda *s, std=1.0: torch.tensor((rng.standard_normal(s) * std).astype(np.float32))
+        self.B = batch
+        self.x = f(batch, C, P2_H, P2_W).to(dev, torch.bfloat16)
+        self.op = vp.PsaAttention(f(NH * 4 * KD, C, std=0.02), f(NH * 4 * KD, std=0.02), f(C, 1, 3, 3, std=0.02),
+                                  f(C, std=0.02), f(C, C, std=0.02), f(C, std=0.02), NH, KD, dtype=torch.bfloat16,
+                                  device=dev)
+        self.y = torch.empty_like(self.x)
+        self.xh = self.x.cpu().pin_memory()
+        self.yh = torch.empty_like(self.xh).pin_memory()
+
+    def step(self):
+        self.op.forward_into(self.x, self.y)
+
+    def e2e_step(self):
+        self.x.copy_(self.xh, non_blocking=True)
+        self.op.forward_into(self.x, self.y)
+        self.yh.copy_(self.y, non_blocking=True)
+
+    def io_bytes(self):
+        return self.x.numel() * 2, self.y.numel() * 2
+
+    def dominant(self, args, stream, flush):
+        """The tcgen05 flash-attention kernel alone on the op's intermediates."""
+        from vision_rs_b200 import _lib
+        B = self.B
+        self.op.forward_into(self.x, self.y)
+        ws = self.op.workspace(B, P2_H, P2_W, self.x.device)
+        Np = (N2 + 7) // 8 * 8
+        al = lambda n: (n + 255) // 256 * 256
+        v_off = al(2 * B * NH * N2 * KD * 2)
+        o_off = v_off + al(B * C * Np * 2)
+        base, st = ws.data_ptr(), stream.cuda_stream
+        call = lambda: _lib.call("va_psa_flash_attention_fwd_f16", base, base + v_off, base + o_off, None, B, NH,
+                                 P2_H, P2_W, st)
+        for _ in range(args.warmup):
+            call()
+        ms = event_time(call, max(5, args.steps), stream, flush)
+        pk, src = peaks()
+        work = B * FLOP_ATTN_IMG2
+        ach = work / (ms * 1e-3) / 1e12
+        return {"bound": "tensor", "kernel": "attn_kernel (tcgen05 flash attention, QK^T + PV, 64-wide V)",
+                "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
+                "peak_source": f"{src} bf16_tflops (burst)",
+                "traffic": ATTN_TRAFFIC_BYTES if B == P2_B else None,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                                  "(profiles/psa_fwd_kernels_cfg2_ncu_full.md)",
+                "flop_per_launch": work, "ms_per_launch": ms}
+
+    def extra(self, ms):
+        return {"tflops_whole_op": FLOP_IMG2 * self.B / (ms * 1e-3) / 1e12}
+
+    config = {"seq_len": N2, "precision": "bf16 I/O and qkv GEMM; f16 attention operands; f32 accumulation"}
+
+    @staticmethod
+    def cpu_sample(threads, n_img=P2_B, seed=1234):
+        import torch
+        from oracle import psa_oracle as po
+        torch.set_num_threads(threads)
+        p = po.psa_synthetic(n_img, P2_H, P2_W, seed=seed)
+        t = {k: torch.tensor(v) for k, v in p.items()}
+        a = (t["x"], t["w_qkv"], t["b_qkv"], t["w_pe"], t["b_pe"], t["w_proj"], t["b_proj"], NH, KD)
+        po.psa_attention_torch(*a)
+        t0 = time.perf_counter()
+        po.psa_attention_torch(*a)
+        return n_img, time.perf_counter() - t0
+
+    sample_desc = "images of 128x40x40, torch-CPU f32 restatement of the reference maths (the reference has no CPU path)"
+
+
+class Cfg3:
+    unit, batch = "images/s", MS_B
+    workload = "cfg3: RF-DETR MSDeformAttn fwd+bwd, Q=300, 16 heads x 16, levels 80x80/40x40/20x20, P=4"
+
+    def __init__(self, dev, rank, batch, args):
+        import torch
+        from oracle import msdeform_oracle as mo
+        from vision_rs_b200 import msdeform as ms
+        self.dtype = args.dtype
+        self.metric = f"attention images/sec (RF-DETR MSDeformAttn fwd+bwd, {self.dtype})"
+        self.ms, self.B = ms, batch
+        p = mo.msdeform_synthetic(B=batch, Q=MS_Q, nh=MS_NH, dh=MS_DH, shapes=MS_SHAPES, P=MS_P, seed=100 + rank)
+        tdt = torch.float32 if self.dtype == "f32" else torch.bfloat16
+        self.d = {k: torch.as_tensor(v).to(dev, tdt if k in ("value", "grad_out") else None) for k, v in p.items()}
+        self.ws = torch.empty(ms.msdeform_attn_workspace_bytes(batch, MS_NH, 3, MS_Q, MS_P), dtype=torch.uint8,
+                              device=dev)
+        self.args = (self.d["value"], self.d["spatial_shapes"], self.d["level_start"], self.d["loc"], self.d["attn"])
+        self.h = {k: self.d[k].cpu().pin_memory() for k in ("value", "loc", "attn", "grad_out")}
+        self.out = None
+        S = sum(h * w for h, w in MS_SHAPES)
+        self.touched = self._touched(p, S)
+
+    @staticmethod
+    def _touched(p, S):
+        """Distinct (b, pixel, head) value rows any sample reads (host count)."""
+        loc, shapes = p["loc"], np.asarray(MS_SHAPES)
+        B, Q, nh, L, P, _ = loc.shape
+        rows = set()
+        for l, (H, W) in enumerate(shapes):
+            s0 = int(sum(h * w for h, w in MS_SHAPES[:l]))
+            x = loc[..., l, :, 0] * W - 0.5
+            y = loc[..., l, :, 1] * H - 0.5
+            x0, y0 = np.floor(x).astype(np.int64), np.floor(y).astype(np.int64)
+            bi = np.broadcast_to(np.arange(B)[:, None, None, None], x0.shape)
+            hi = np.broadcast_to(np.arange(nh)[None, None, :, None], x0.shape)
+            for dy in (0, 1):
+                for dx in (0, 1):
+                    xi, yi = x0 + dx, y0 + dy
+                    ok = (xi >= 0) & (xi < W) & (yi >= 0) & (yi < H)
+                    key = (bi[ok] * S + s0 + yi[ok] * W + xi[ok]) * nh + hi[ok]
+                    rows.update(np.unique(key).tolist())
+        return len(rows)
+
+    def _run(self):
+        self.out = self.ms.msdeform_attn_forward(*self.args)
+        self.g = self.ms.msdeform_attn_backward(*self.args, self.d["grad_out"], workspace=self.ws)
+
+    def step(self):
+        self._run()
+
+    def e2e_step(self):
+        for k, v in self.h.items():
+            self.d[k].copy_(v, non_blocking=True)
+        self._run()
+        outs = (self.out,) + tuple(self.g)
+        if not hasattr(self, "oh"):
+            self.oh = [o.cpu().pin_memory() for o in outs]
+        for o, h in zip(outs, self.oh):
+            h.copy_(o, non_blocking=True)
+
+    def io_bytes(self):
+        h2d = sum(v.numel() * v.element_size() for v in self.h.values())
+        self._run()
+        d2h = sum(o.numel() * o.element_size() for o in (self.out,) + tuple(self.g))
+        return h2d, d2h
+
+    def dominant(self, args, stream, flush):
+        """The forward gather kernel alone (HBM roofline on the full-map bytes)."""
+        call = lambda: self.ms.msdeform_attn_forward(*self.args, out=self.out)
+        self._run()
+        for _ in range(args.warmup):
+            call()
+        ms = event_time(call, max(5, args.steps), stream, flush)
+        bwd = lambda: self.ms.msdeform_attn_backward(*self.args, self.d["grad_out"], workspace=self.ws)
+        ms_b = event_time(bwd, max(5, args.steps), stream, flush)
+        pk, src = peaks()
+        work = MS_FWD_BYTES[self.dtype] * self.B // MS_B
+        ach = work / (ms * 1e-3) / 1e9
+        r = {"bound": "hbm", "kernel": "msda_fwd_kernel (bilinear gather, 16-byte corner loads)", "achieved": ach,
+             "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "peak_source": f"{src} hbm_gbs",
+             "traffic": None, "bytes_per_launch": work, "ms_per_launch": ms,
+             "backward": {"ms": ms_b, "bytes": MS_BWD_BYTES_F32 * self.B // MS_B if self.dtype == "f32" else None,
+                          "frac": (MS_BWD_BYTES_F32 * self.B // MS_B / (ms_b * 1e-3) / 1e9 / pk["hbm_gbs"])
+                          if self.dtype == "f32" else None}}
+        return r
+
+    def extra(self, ms):
+        return {"touched_value_rows": self.touched}
+
+    @property
+    def config(self):
+        return {"seq_len": MS_Q, "precision": f"{self.dtype} value/out/grads, f32 loc/attn, f32 accumulation; "
+                                              "deterministic backward (no atomics)"}
+
+    def cpu_sample(self, threads, n_img=MS_B):
+        import torch
+        from oracle import msdeform_oracle as mo
+        torch.set_num_threads(threads)
+        p = mo.msdeform_synthetic(B=n_img, Q=MS_Q, nh=MS_NH, dh=MS_DH, shapes=MS_SHAPES, P=MS_P, seed=5)
+        t = {k: torch.as_tensor(v) for k, v in p.items()}
+        v = t["value"].requires_grad_(True)
+        loc = t["loc"].requires_grad_(True)
+        at = t["attn"].requires_grad_(True)
+        t0 = time.perf_counter()
+        out = mo.msdeform_attn_torch(v, t["spatial_shapes"], t["level_start"], loc, at)
+        out.backward(t["grad_out"])
+        return n_img, time.perf_counter() - t0
+
+    sample_desc = ("images (8 x 300 queries) fwd+bwd through torch-CPU f32 grid_sample + autograd (the reference "
+                   "has no deformable attention)")
+
+
+class Cfg4:
+    metric = "attention images/sec (DINOv2-S attention, global + 4x4-windowed layer, bf16, 1601 tokens)"
+    unit, dtype, batch = "images/s", "bf16", DN_B
+    workload = ("cfg4: DINOv2-S attention at 560x560 (1601 tokens), hidden 384, 6x64 heads, packed QKV Linear; "
+                "one global layer + one layer over 16 windows of 10x10 patches (+cls per window)")
+
+    def __init__(self, dev, rank, batch, args):
+        import torch
+        from oracle import dinov2_oracle as do
+        from vision_rs_b200 import dinov2
+        self.dn, self.B = dinov2, batch
+        x, w, b = do.dinov2_synthetic(S=batch, n=DN_N, hidden=DN_HID, seed=200 + rank)
+        self.x = torch.as_tensor(x).to(dev, torch.bfloat16)
+        self.op = dinov2.DinoV2Attention(torch.as_tensor(w).to(dev, torch.bfloat16), torch.as_tensor(b).to(dev),
+                                         DN_HEADS)
+        self.opw = dinov2.DinoV2Attention(self.op.w_qkv, self.op.b_qkv, DN_HEADS)
+        self.og = torch.empty_like(self.x)
+        self.xw = dinov2.window_partition(self.x, DN_GRID, DN_GRID, DN_WIN)
+        self.ow = torch.empty_like(self.xw)
+        self.o2 = torch.empty_like(self.x)
+        self.xh = self.x.cpu().pin_memory()
+        self.oh = torch.empty_like(self.xh).pin_memory()
+        self.oh2 = torch.empty_like(self.xh).pin_memory()
+
+    def _run(self):
+        self.op.forward_into(self.x, self.og)
+        self.dn.window_partition(self.x, DN_GRID, DN_GRID, DN_WIN, out=self.xw)
+        self.opw.forward_into(self.xw, self.ow)
+        self.dn.window_unpartition(self.ow, self.B, DN_GRID, DN_GRID, DN_WIN, out=self.o2)
+
+    def step(self):
+        self._run()
+
+    def e2e_step(self):
+        self.x.copy_(self.xh, non_blocking=True)
+        self._run()
+        self.oh.copy_(self.og, non_blocking=True)
+        self.oh2.copy_(self.o2, non_blocking=True)
+
+    def io_bytes(self):
+        return self.x.numel() * 2, 2 * self.x.numel() * 2
+
+    def dominant(self, args, stream, flush):
+        """The global layer's attention kernel alone (head dim 64, 1601 tokens)
+        on the Q/K/V the op's QKV GEMM left in its workspace."""
+        from vision_rs_b200 import _lib
+        self.op.forward_into(self.x, self.og)
+        base, st = self.op._ws.data_ptr(), stream.cuda_stream
+        v_off = (2 * self.B * DN_HEADS * DN_N * 64 * 2 + 255) // 256 * 256
+        call = lambda: _lib.call("va_dinov2_flash_attention_fwd_f16", base, base + v_off, self.og.data_ptr(), self.B,
+                                 DN_N, DN_HEADS, st)
+        for _ in range(args.warmup):
+            call()
+        ms = event_time(call, max(5, args.steps), stream, flush)
+        qkv = torch_empty_like_qkv(self.x)
+        lin = lambda: self.dn.qkv_linear(self.x, self.op.w_qkv, self.op.b_qkv, out=qkv)
+        ms_lin = event_time(lin, max(5, args.steps), stream, flush)
+        pk, src = peaks()
+        work = self.B * DN_FLOP_GLOBAL_ATTN_IMG
+        ach = work / (ms * 1e-3) / 1e12
+        return {"bound": "tensor", "kernel": "attn_kernel<64> (tcgen05 flash attention, global layer, 1601 tokens)",
+                "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
+                "peak_source": f"{src} bf16_tflops (burst)", "traffic": None, "flop_per_launch": work,
+                "ms_per_launch": ms, "qkv_linear_ms": ms_lin,
+                "qkv_linear_tflops": 2 * self.B * DN_N * DN_HID * 3 * DN_HID / (ms_lin * 1e-3) / 1e12}
+
+    def extra(self, ms):
+        return {"tflops_whole_step": DN_FLOP_IMG * self.B / (ms * 1e-3) / 1e12}
+
+    config = {"seq_len": DN_N, "window_seq_len": DN_NWIN,
+              "precision": "bf16 I/O, weights and QKV GEMM; f16 Q/K/V/P; f32 accumulation",
+              "cls_in_windows": "cls token prepended to every window; un-partition averages the windows' cls"}
+
+    @staticmethod
+    def cpu_sample(threads, n_img=2):
+        import torch
+        from oracle import dinov2_oracle as do
+        torch.set_num_threads(threads)
+        x, w, b = do.dinov2_synthetic(S=n_img, n=DN_N, hidden=DN_HID, seed=9)
+        xt, wt, bt = torch.as_tensor(x), torch.as_tensor(w), torch.as_tensor(b)
+        xw = torch.as_tensor(do.window_partition(x, DN_GRID, DN_GRID, DN_WIN))
+        t0 = time.perf_counter()
+        do.dinov2_attention_torch(xt, wt, bt, DN_HEADS)
+        do.dinov2_attention_torch(xw, wt, bt, DN_HEADS)
+        return n_img, time.perf_counter() - t0
+
+    sample_desc = ("images (one global + one windowed layer) through torch-CPU f32 Linear + SDPA (the reference has "
+                   "no DINOv2 code)")
+
+
+def torch_empty_like_qkv(x):
+    import torch
+    return torch.empty(*x.shape[:-1], 3 * x.shape[-1], device=x.device, dtype=x.dtype)
+
+
+class Cfg5:
+    metric = "training images/sec (C2PSA PSA attention fwd+bwd+allreduce+SGD, bf16, 400 tokens)"
+    unit, dtype, batch = "images/s", "bf16", T5_B
+    workload = ("cfg5: C2PSA PSA attention training step, 32 x 128x20x20 per GPU, MSE loss, NCCL all-reduce of "
+                "the 50,816 f32 weight gradients, SGD on f32 master weights")
+
+    def __init__(self, dev, rank, batch, args):
+        import torch
+        from oracle import psa_oracle as po
+        from vision_rs_b200 import train
+        self.train, self.B = train, batch
+        s = po.psa_synthetic(batch, T5_H, T5_W, seed=300 + rank)
+        wseed = po.psa_synthetic(1, T5_H, T5_W, seed=77)  # identical weights on every rank
+        rng = np.random.default_rng(400 + rank)
+        bf = lambda a: torch.as_tensor(np.asarray(a, np.float32)).to(dev, torch.bfloat16)
+        self.x = bf(s["x"])
+        self.t = bf(rng.standard_normal(self.x.shape))
+        self.params = {k: bf(wseed[k]) for k in ("w_qkv", "w_pe", "w_proj")}
+        self.params.update({k: torch.as_tensor(wseed[k]).to(dev) for k in ("b_qkv", "b_pe", "b_proj")})
+        self.step_obj = train.PsaTrainStep(B=batch, H=T5_H, W=T5_W, device=dev)
+        self.master = train.PsaTrainStep.master_from(self.params)
+        self.lr = 1e-3
+        self.xh = self.x.cpu().pin_memory()
+        self.th = self.t.cpu().pin_memory()
+        self.lh = torch.empty(1, dtype=torch.float32).pin_memory()
+
+    def step(self):
+        self.loss = self.train.dp_train_step(self.step_obj, self.x, self.t, self.params, self.master, self.lr)
+
+    def e2e_step(self):
+        self.x.copy_(self.xh, non_blocking=True)
+        self.t.copy_(self.th, non_blocking=True)
+        self.step()
+        self.lh.copy_(self.loss, non_blocking=True)
+
+    def io_bytes(self):
+        return 2 * self.x.numel() * 2, 4
+
+    def dominant(self, args, stream, flush):
+        """The local forward+backward alone (no collective), and the all-reduce alone."""
+        import torch
+        import torch.distributed as dist
+        fb = lambda: self.step_obj.forward_backward(self.x, self.t, self.params)
+        for _ in range(args.warmup):
+            fb()
+        ms = event_time(fb, max(5, args.steps), stream, flush)
+        ar_ms = None
+        if dist.is_initialized():
+            g = self.step_obj.grads
+            ar = lambda: dist.all_reduce(g)
+            for _ in range(3):
+                ar()
+            ar_ms = event_time(ar, max(5, args.steps), stream, None)
+        pk, src = peaks()
+        work = 3 * FLOP_FWD_IMG5 * self.B
+        ach = work / (ms * 1e-3) / 1e12
+        peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+        return {"bound": "tensor", "kernel": "local fwd+bwd (all kernels of one shard's step, no collective)",
+                "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                "peak_source": f"{src} bf16_tflops_sustained", "traffic": None,
+                "flop_per_launch": work, "flop_count": "3 x forward FLOPs (backward ~ 2 x forward)",
+                "ms_per_launch": ms, "allreduce_us": None if ar_ms is None else 1000 * ar_ms,
+                "allreduce_bytes": 4 * self.train.GRAD_COUNT}
+
+    def extra(self, ms):
+        return {}
+
+    config = {"seq_len": N5, "precision": "bf16 activations/weights, f16 GEMM operands, f32 attention backward, "
+                                          "f32 gradients and master weights"}
+
+    @staticmethod
+    def cpu_sample(threads, n_img=T5_B):
+        import torch
+        from oracle import psa_oracle as po
+        torch.set_num_threads(threads)
+        s = po.psa_synthetic(n_img, T5_H, T5_W, seed=3)
+        t = {k: torch.tensor(v).requires_grad_(k.startswith(("w_", "b_"))) for k, v in s.items()}
+        tgt = torch.randn(n_img, C, T5_H, T5_W)
+        t0 = time.perf_counter()
+        y = po.psa_attention_torch(t["x"], t["w_qkv"], t["b_qkv"], t["w_pe"], t["b_pe"], t["w_proj"], t["b_proj"],
+                                   NH, KD)
+        ((y - tgt) ** 2).mean().backward()
+        return n_img, time.perf_counter() - t0
+
+    sample_desc = "images of 128x20x20 fwd+bwd, torch-CPU f32 autograd restatement (the reference has no CPU path)"
+
+
+CONFIGS = {"cfg2": Cfg2, "cfg3": Cfg3, "cfg4": Cfg4, "cfg5": Cfg5}
+
+
+# ═════════════════════════════ arms ══════════════════════════════════════════
+def cpu_baseline(cfg_cls, args, min_s=10.0):
+    """The CPU restatement on this host's cores, repeated until ≥ min_s."""
+    threads = os.cpu_count() or 1
+    inst = cfg_cls.__new__(cfg_cls)
+    inst.dtype = getattr(args, "dtype", "f32")
+    tot_img, tot_s = 0, 0.0
+    while tot_s < min_s:
+        n, dt = inst.cpu_sample(threads)
+        tot_img += n
+        tot_s += dt
+    return {"value": tot_img / tot_s, "unit": "images/s", "cores": threads, "kind": "port",
+            "sample": f"{tot_img} {cfg_cls.sample_desc}; {tot_s:.1f} s"}
 
 
 def run_reference(args, ws, rank):
     """CPU reference arm: rank 0 only."""
     if rank != 0:
         return
+    cls = CONFIGS[args.config]
     threads = os.cpu_count() or 1
-    n_img = B_PER_GPU  # one step = the whole 64-image batch of the workload
-    vals = []
+    inst = cls.__new__(cls)
+    inst.dtype = args.dtype
     for _ in range(args.warmup):
-        cpu_sample(n_img, threads)
+        inst.cpu_sample(threads)
+    vals = []
     for _ in range(args.steps):
-        v, _ = cpu_sample(n_img, threads)
-        vals.append(v)
+        n, dt = inst.cpu_sample(threads)
+        vals.append(n / dt)
     val = statistics.mean(vals)
+    metric = getattr(cls, "metric", None) or f"attention images/sec (RF-DETR MSDeformAttn fwd+bwd, {args.dtype})"
     line = {
-        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * n_img / val,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg2: C2PSA PSA attention fwd, 128x40x40 (1600 tokens), nh=2, kd=32, hd=64",
-                   "global_batch": n_img, "seq_len": N_TOK, "parallelism": "host threads"},
-        "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{n_img} images of 128x40x40 per step, torch-CPU f32 restatement of the "
-                                   "reference maths (the reference has no CPU path)"},
-        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "impl": "reference", "metric": metric, "value": val, "unit": "images/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / val, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cls.workload, "parallelism": "host threads"},
+        "cpu_baseline": {"value": val, "unit": "images/s", "cores": threads, "kind": "port",
+                         "sample": f"per step: {cls.sample_desc}"},
+        "e2e": {"value": val, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 def run_ours(args, ws, rank, local):
+    import datetime
+
     import torch
     import torch.distributed as dist
     from vision_rs_b200 import _lib
-    from vision_rs_b200 import psa as vp
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:
-        import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-
-    rng = np.random.default_rng(1000 + rank)
-    B = args.batch
-    f = lambda *s, std=1.0: torch.tensor((rng.standard_normal(s) * std).astype(np.float32))
-    x = f(B, C, H, W).to(dev, torch.bfloat16)
-    op = vp.PsaAttention(f(NH * 4 * KD, C, std=0.02), f(NH * 4 * KD, std=0.02), f(C, 1, 3, 3, std=0.02),
-                         f(C, std=0.02), f(C, C, std=0.02), f(C, std=0.02), NH, KD, dtype=torch.bfloat16,
-                         device=dev)
-    y = torch.empty_like(x)
+    cls = CONFIGS[args.config]
+    B = args.batch or cls.batch
+    wl = cls(dev, rank, B, args)
     stream = torch.cuda.current_stream()
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # > L2 (126 MB)
 
@@ -183,16 +591,14 @@ def run_ours(args, ws, rank, local):
             dist.barrier()
         torch.cuda.synchronize()
 
-    clk = ClockSampler(local).__enter__()
-    t_w = time.perf_counter()
-    nw = 0
+    clk = ClockSampler(local).start()
+    t_w, nw = time.perf_counter(), 0
     while nw < args.warmup or time.perf_counter() - t_w < args.min_warm_s:
-        op.forward_into(x, y)
+        wl.step()
         nw += 1
         if nw % 50 == 0:
             torch.cuda.synchronize()
     barrier()
-
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     lc0 = _lib.lib().va_launch_count()
@@ -200,140 +606,53 @@ def run_ours(args, ws, rank, local):
     for i in range(args.steps):
         flush.fill_(float(i))  # evict L2 between timed steps (outside the events)
         starts[i].record(stream)
-        op.forward_into(x, y)
+        wl.step()
         ends[i].record(stream)
     barrier()
-    clk.__exit__(None, None, None)
+    clk.stop()
     launches = _lib.lib().va_launch_count() - lc0
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    ms = statistics.mean(step_ms)
+    ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
 
-    # dominant kernel (flash attention) timed alone on the same stream
-    dom = time_dominant(op, x, args, stream)
-
-    if args.no_e2e:
-        e2e_ms = float("nan")
-    else:
-        e2e_ms = time_e2e(op, x, y, args, stream, barrier)
-
-    t = torch.tensor([ms, e2e_ms, dom["ms"]], device=dev, dtype=torch.float64)
+    dom = wl.dominant(args, stream, flush)
+    e2e_ms = float("nan")
+    if not args.no_e2e:
+        h2d, d2h = wl.io_bytes()
+        for _ in range(max(1, args.warmup)):
+            wl.e2e_step()
+        barrier()
+        e2e_ms = event_time(wl.e2e_step, args.steps, stream)
+    t = torch.tensor([ms, e2e_ms, dom["ms_per_launch"]], device=dev, dtype=torch.float64)
     if ws > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms, dom_ms = t.tolist()
+    dom["ms_per_launch_max_over_ranks"] = dom_ms
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_sample()
-
+        cpu = cpu_baseline(cls, args)
     if rank == 0:
-        emit(args, ws, B, ms, e2e_ms, dom, dom_ms, launches, cpu, clk, x, y)
+        metric = wl.metric
+        line = {
+            "metric": metric, "value": B * ws / (ms * 1e-3), "unit": "images/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"), "data": "synthetic",
+            "config": dict({"workload": wl.workload, "global_batch": B * ws, "per_gpu_batch": B,
+                            "parallelism": (f"data parallel x{ws}, NCCL all-reduce of weight gradients"
+                                            if args.config == "cfg5" else f"image shards x{ws}, no collective"),
+                            "l2": "flushed between timed steps (256 MB write)"}, **wl.config),
+            "e2e": None if math.isnan(e2e_ms) else {
+                "value": B * ws / (e2e_ms * 1e-3), "unit": "images/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "roofline": dom,
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+        }
+        line.update(wl.extra(ms))
+        print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
-
-
-def time_e2e(op, x, y, args, stream, barrier):
-    """Same metric through the public API with host buffers: every step copies
-    the batch from pinned host memory, runs the op and copies y back."""
-    import torch
-    xh = x.cpu().pin_memory()
-    yh = torch.empty_like(xh).pin_memory()
-    for _ in range(max(1, args.warmup)):
-        op.forward_into(x.copy_(xh, non_blocking=True), y)
-        yh.copy_(y, non_blocking=True)
-    barrier()
-    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    for i in range(args.steps):
-        e_s[i].record(stream)
-        x.copy_(xh, non_blocking=True)
-        op.forward_into(x, y)
-        yh.copy_(y, non_blocking=True)
-        e_e[i].record(stream)
-    barrier()
-    return statistics.mean(s.elapsed_time(e) for s, e in zip(e_s, e_e))
-
-
-def cpu_baseline_sample():
-    """The torch-CPU f32 restatement on this host's cores: whole 64-image
-    batches, repeated until ≥10 s of CPU time."""
-    threads = os.cpu_count() or 1
-    tot_img, tot_s = 0, 0.0
-    while tot_s < 10.0:
-        v, dt = cpu_sample(B_PER_GPU, threads)
-        tot_img += B_PER_GPU
-        tot_s += dt
-    return {"value": tot_img / tot_s, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{tot_img} images of 128x40x40 in {tot_s:.1f} s (64-image calls), torch-CPU f32 "
-                      "restatement of the reference maths (the reference has no CPU path)"}
-
-
-def emit(args, ws, B, ms, e2e_ms, dom, dom_ms, launches, cpu, clk, x, y):
-    pk, src = peaks()
-    achieved = dom["flop"] / (dom_ms * 1e-3) / 1e12
-    peak = pk["bf16_tflops"]
-    line = {
-        "metric": METRIC, "value": B * ws / (ms * 1e-3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "cfg2: C2PSA PSA attention fwd, 128x40x40 (1600 tokens), nh=2, kd=32, hd=64",
-                   "global_batch": B * ws, "per_gpu_batch": B, "seq_len": N_TOK,
-                   "parallelism": f"image shards x{ws}, no collective",
-                   "l2": "flushed between timed steps (256 MB write)",
-                   "precision": "bf16 I/O and qkv GEMM; f16 attention operands; f32 accumulation"},
-        "e2e": None if math.isnan(e2e_ms) else {
-            "value": B * ws / (e2e_ms * 1e-3), "unit": UNIT,
-            "h2d_bytes_per_step": x.numel() * x.element_size(),
-            "d2h_bytes_per_step": y.numel() * y.element_size()},
-        "gpu_launches": int(launches),
-        "roofline": {"bound": "tensor", "kernel": dom["name"], "achieved": achieved, "peak": peak,
-                     "unit": "TFLOP/s", "frac": achieved / peak, "peak_source": f"{src} bf16_tflops (burst)",
-                     "traffic": ATTN_TRAFFIC_BYTES if B == B_PER_GPU else None,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
-                                       "(profiles/psa_fwd_kernels_cfg2_ncu_full.md)",
-                     "flop_per_launch": dom["flop"], "ms_per_launch": dom_ms},
-        "cpu_baseline": cpu,
-        "clocks": clk.summary(),
-        "tflops_whole_op": FLOP_IMG * B / (ms * 1e-3) / 1e12,
-    }
-    print(json.dumps(line), flush=True)
-
-
-def time_dominant(op, x, args, stream):
-    """Average duration of the dominant kernel — the tcgen05 flash-attention
-    kernel — timed alone with CUDA events on the launching stream, on the
-    op's own intermediates (Q/K/V as the qkv kernel left them in the
-    workspace)."""
-    import torch
-    from vision_rs_b200 import _lib
-    B = x.shape[0]
-    y = torch.empty_like(x)
-    op.forward_into(x, y)  # fills the workspace: qk at offset 0, then v, then o
-    ws = op.workspace(B, H, W, x.device)
-    Np = (N_TOK + 7) // 8 * 8
-    al = lambda n: (n + 255) // 256 * 256
-    qk_off = 0
-    v_off = qk_off + al(2 * B * NH * N_TOK * KD * 2)
-    o_off = v_off + al(B * C * Np * 2)
-    base = ws.data_ptr()
-    st = stream.cuda_stream
-    call = lambda: _lib.call("va_psa_flash_attention_fwd_f16", base + qk_off, base + v_off, base + o_off, None,
-                             B, NH, H, W, st)
-    for _ in range(args.warmup):
-        call()
-    torch.cuda.synchronize()
-    n = max(5, args.steps)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=x.device)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
-    for i in range(n):
-        flush.fill_(float(i))
-        evs[i][0].record(stream)
-        call()
-        evs[i][1].record(stream)
-    torch.cuda.synchronize()
-    ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
-    return {"name": "attn_kernel (tcgen05 flash attention, QK^T + PV, 64-wide V)", "ms": ms,
-            "flop": B * FLOP_ATTN_IMG}
 
 
 def main():
@@ -342,14 +661,15 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"], help="cfg3 value/grad dtype")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--min-warm-s", type=float, default=1.5,
                     help="keep warming up at least this long so the clock sampler sees the load")
-    ap.add_argument("--batch", type=int, default=B_PER_GPU, help="per-GPU batch (profiling of smaller cases)")
+    ap.add_argument("--batch", type=int, default=0, help="per-GPU batch (default: the config's)")
     args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
+    args.warmup = max(args.warmup, 3)
     ws, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, ws, rank)

@@ -245,6 +245,12 @@ VA_API int va_dinov2_attention_fwd_bf16(const va_bf16 *x, const va_bf16 *w_qkv, 
                                         va_bf16 *o, int num_seqs, int seq_len, int hidden,
                                         int num_heads, void *workspace, size_t ws_bytes,
                                         va_stream_t stream);
+/* The attention core alone (one launch), on the operands the fused op keeps
+ * in its workspace: qk f16 [2][S*heads][n][64] (Q then K, sequence-major,
+ * head-minor), v f16 [S*heads*64][roundup(n, 8)] (transposed); o bf16
+ * [S][n][heads*64]. */
+VA_API int va_dinov2_flash_attention_fwd_f16(const void *qk, const void *v, va_bf16 *o, int num_seqs,
+                                             int seq_len, int num_heads, va_stream_t stream);
 /* The packed QKV Linear alone: qkv [tokens][3*hidden] bf16 = x·w_qkvᵀ + b. */
 VA_API int va_dinov2_qkv_linear_bf16(const va_bf16 *x, const va_bf16 *w_qkv, const float *b_qkv,
                                      va_bf16 *qkv, int tokens, int hidden, va_stream_t stream);

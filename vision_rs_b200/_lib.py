@@ -61,6 +61,7 @@ SIGNATURES: dict[str, tuple] = {
     "va_dinov2_attention_workspace_bytes": (SZ, [I, I, I]),
     "va_dinov2_attention_fwd_bf16": (I, [P, P, P, P, I, I, I, I, P, SZ, S]),
     "va_dinov2_qkv_linear_bf16": (I, [P, P, P, P, I, I, S]),
+    "va_dinov2_flash_attention_fwd_f16": (I, [P, P, P, I, I, I, S]),
     "va_dinov2_window_partition_bf16": (I, [P, P, I, I, I, I, I, S]),
     "va_dinov2_window_unpartition_bf16": (I, [P, P, I, I, I, I, I, S]),
     "va_psa_train_workspace_bytes": (SZ, [I, I, I]),

@@ -377,6 +377,12 @@ int va_dinov2_attention_fwd_bf16(const va_bf16* x, const va_bf16* w_qkv, const f
                             seq_len, hidden, num_heads, workspace, ws_bytes, (cudaStream_t)stream);
 }
 
+int va_dinov2_flash_attention_fwd_f16(const void* qk, const void* v, va_bf16* o, int num_seqs, int seq_len,
+                                      int num_heads, va_stream_t stream) {
+  return tc_flash_attention(qk, v, o, nullptr, num_seqs * num_heads, num_heads, seq_len, kHead, 1,
+                            (cudaStream_t)stream);
+}
+
 int va_dinov2_qkv_linear_bf16(const va_bf16* x, const va_bf16* w_qkv, const float* b_qkv, va_bf16* qkv, int tokens,
                               int hidden, va_stream_t stream) {
   return dino_qkv_linear((const __nv_bfloat16*)x, (const __nv_bfloat16*)w_qkv, b_qkv, (__nv_bfloat16*)qkv, tokens,

@@ -38,21 +38,23 @@ def qkv_linear(x, w_qkv, b_qkv, out=None, stream=None):
     return out
 
 
-def window_partition(x, grid_h: int, grid_w: int, win: int, stream=None):
+def window_partition(x, grid_h: int, grid_w: int, win: int, out=None, stream=None):
     """``[B, 1 + gh·gw, C] → [B·nw, 1 + win², C]`` (cls copied into every window)."""
     _check(x, torch.bfloat16, "x")
     B, _, C = x.shape
     nw = (grid_h // win) * (grid_w // win)
-    out = torch.empty(B * nw, 1 + win * win, C, device=x.device, dtype=x.dtype)
+    if out is None:
+        out = torch.empty(B * nw, 1 + win * win, C, device=x.device, dtype=x.dtype)
     _lib.call("va_dinov2_window_partition_bf16", _p(x), _p(out), B, grid_h, grid_w, win, C, _stream(stream))
     return out
 
 
-def window_unpartition(xw, B: int, grid_h: int, grid_w: int, win: int, stream=None):
+def window_unpartition(xw, B: int, grid_h: int, grid_w: int, win: int, out=None, stream=None):
     """Inverse of ``window_partition``; the cls output is the mean over the windows."""
     _check(xw, torch.bfloat16, "xw")
     C = xw.shape[-1]
-    out = torch.empty(B, 1 + grid_h * grid_w, C, device=xw.device, dtype=xw.dtype)
+    if out is None:
+        out = torch.empty(B, 1 + grid_h * grid_w, C, device=xw.device, dtype=xw.dtype)
     _lib.call("va_dinov2_window_unpartition_bf16", _p(xw), _p(out), B, grid_h, grid_w, win, C, _stream(stream))
     return out
 
