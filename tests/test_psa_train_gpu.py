@@ -113,3 +113,17 @@ def test_sgd_update(cuda):
     assert torch.equal(dv["w_qkv"].reshape(-1), master[:32768].to(torch.bfloat16))
     assert torch.equal(dv["b_pe"], master[50688:])
     del wq
+
+
+def test_train_step_long_sequence_fallback(cuda):
+    """N = 24×24 = 576 > 512: the attention backward takes the f32 SIMT path."""
+    from vision_rs_b200 import train
+    dv, h = _case(2, 24, 24, 15, cuda)
+    step = train.PsaTrainStep(B=2, H=24, W=24, device=cuda)
+    y, loss, grads, dx = step.forward_backward(dv["x"], dv["target"], dv, want_dx=True)
+    params = {k: h[k] for k in ("w_qkv", "b_qkv", "w_pe", "b_pe", "w_proj", "b_proj")}
+    ry, rloss, rg, rdx = po.psa_train_step_torch(h["x"], h["target"], params)
+    g = grads.cpu().numpy()
+    for name, (a, b) in SLICES.items():
+        _check(g[a:b], rg[a:b], name)
+    _check(dx.float().cpu().numpy(), rdx, "dx")

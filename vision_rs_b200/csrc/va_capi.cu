@@ -121,18 +121,20 @@ int va_psa_flash_attention_fwd_f16(const void* qk, const void* v, void* o, float
 
 int va_device_status_read(int* status, va_stream_t s) {  // first non-zero word of the tensor-core kernels
   if (!status) return set_error(VA_ERR_SHAPE, "device_status_read: null output");
-  int a = 0, b = 0, c = 0;
-  if (int rc = tc_status_read(&a, (cudaStream_t)s)) return rc;
-  if (int rc = dino_status_read(&b, (cudaStream_t)s)) return rc;
-  if (int rc = gemm_status_read(&c, (cudaStream_t)s)) return rc;
-  *status = a ? a : (b ? b : c);
+  int v[4] = {0, 0, 0, 0};
+  if (int rc = tc_status_read(&v[0], (cudaStream_t)s)) return rc;
+  if (int rc = dino_status_read(&v[1], (cudaStream_t)s)) return rc;
+  if (int rc = gemm_status_read(&v[2], (cudaStream_t)s)) return rc;
+  if (int rc = bwd_status_read(&v[3], (cudaStream_t)s)) return rc;
+  *status = v[0] ? v[0] : (v[1] ? v[1] : (v[2] ? v[2] : v[3]));
   return VA_OK;
 }
 
 int va_device_status_clear(va_stream_t s) {
   if (int rc = tc_status_clear((cudaStream_t)s)) return rc;
   if (int rc = dino_status_clear((cudaStream_t)s)) return rc;
-  return gemm_status_clear((cudaStream_t)s);
+  if (int rc = gemm_status_clear((cudaStream_t)s)) return rc;
+  return bwd_status_clear((cudaStream_t)s);
 }
 
 }  // extern "C"

@@ -54,6 +54,13 @@ struct GemmOperand {
 int tc_gemm_f16(const GemmOperand& a, const GemmOperand& b, void* c, bool c_bf16, long long ldc, long long c_batch,
                 int M, int N, int K, int Z, cudaStream_t st, float alpha = 1.0f);
 int gemm_status_read(int* out, cudaStream_t st);
+// Tensor-core PSA attention backward (nh = 2, kd = 32, N ≤ 512): dk f32
+// [B·nh][N][32], dv f32 [B·nh][N][64], dq_part f32 [ceil(N/128)][B·nh][N][32]
+// (sum over the first index = dQ).  qk, v, o, d_o in the forward's f16 layouts.
+int psa_attn_bwd_tc(const void* qk, const void* v, const void* o, const void* d_o, const float* lse, float* dk,
+                    float* dv, float* dq_part, int B, int nh, int N, cudaStream_t st);
+int bwd_status_read(int* out, cudaStream_t st);
+int bwd_status_clear(cudaStream_t st);
 int gemm_status_clear(cudaStream_t st);
 bool psa_tc_supported(int C, int nh, int kd);
 int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,

@@ -17,7 +17,9 @@
 //   dW_proj = σ Σ_b (r_b·O_bᵀ + r_b·PE_bᵀ), db_proj = σ Σ r (tcgen05 GEMM partials)
 //   dA = W_projᵀ·r  (= dO = dPE, in units of σ)             (tcgen05 GEMM, f32)
 //   dV_pe, dW_pe = dw3×3 backward(V, dA); db_pe = σ Σ dA    (f32 SIMT)
-//   dQ, dK, dV = flash-attention backward for each V half   (f32 SIMT, psa_fa2_backward)
+//   dQ, dK, dV = attention backward: tcgen05 kernel over the full 64-wide V
+//                (N ≤ 512, psa_attn_bwd_tc), else the f32 SIMT kernels once
+//                per 32-wide V half (psa_fa2_backward)
 //   dqkv = [dQ | dK | dV + dV_pe] per head                  (f16 + f32 copies)
 //   dW_qkv = σ Σ_b dqkv_b·x_bᵀ, db_qkv = σ Σ dqkv; dx = σ W_qkvᵀ·dqkv (tcgen05 GEMMs)
 //
@@ -169,6 +171,47 @@ __global__ void assemble_dqkv_kernel(const float* __restrict__ dq, const float* 
   }
 }
 
+// f32 [rows][N] → f16 [rows][Np] (pad zero)
+__global__ void f32_to_f16_pad_kernel(const float* __restrict__ x, __half* __restrict__ y, long long rows, int N,
+                                      int Np) {
+  const long long total = rows * Np;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / Np;
+    const int n = (int)(i - r * Np);
+    y[i] = __float2half_rn(n < N ? x[r * N + n] : 0.f);
+  }
+}
+
+// dqkv from the tensor-core backward: dQ = Σ_j dq_part[j] (j in order), dK
+// [B·nh][N][32], dV [B·nh][N][64] (+ dV_pe); same outputs as assemble_dqkv_kernel.
+__global__ void assemble_dqkv_tc_kernel(const float* __restrict__ dq_part, int nparts, const float* __restrict__ dk,
+                                        const float* __restrict__ dv, const float* __restrict__ dv_pe,
+                                        __half* __restrict__ d16, float* __restrict__ d32, int B, int N, int Np) {
+  const long long total = (long long)B * kQKV * Np;
+  const size_t part = (size_t)B * kNH * N * kKD;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(i % Np);
+    const long long bj = i / Np;
+    const int j = (int)(bj % kQKV), b = (int)(bj / kQKV);
+    float g = 0.f;
+    if (n < N) {
+      const int h = j / 128, r = j % 128, bh = b * kNH + h;
+      if (r < 32) {
+        for (int pj = 0; pj < nparts; ++pj) g += dq_part[pj * part + ((size_t)bh * N + n) * kKD + r];
+      } else if (r < 64) {
+        g = dk[((size_t)bh * N + n) * kKD + r - 32];
+      } else {
+        const int dd = r - 64;
+        g = dv[((size_t)bh * N + n) * kHD + dd] + dv_pe[((size_t)b * kC + h * kHD + dd) * N + n];
+      }
+      d32[((size_t)b * kQKV + j) * N + n] = g;
+    }
+    d16[i] = __float2half_rn(g);
+  }
+}
+
 __global__ void sgd_kernel(float* __restrict__ master, const float* __restrict__ g, int n, float lr, float gscale,
                            __nv_bfloat16* __restrict__ w_qkv, float* __restrict__ b_qkv, __nv_bfloat16* __restrict__ w_pe,
                            float* __restrict__ b_pe, __nv_bfloat16* __restrict__ w_proj, float* __restrict__ b_proj) {
@@ -188,7 +231,7 @@ int grid_for(long long n) { return (int)std::min<long long>(std::max<long long>(
 
 struct TrainWs {
   PsaTcOffsets fwd;
-  size_t lse, dy, loss_part, dA, part, v32, dvpe, wpe32, fa, dqkv16, dqkv32, x16, wqkv16, total;
+  size_t lse, dy, loss_part, dA, part, v32, dvpe, wpe32, fa, dqkv16, dqkv32, x16, wqkv16, do16, total;
 };
 
 TrainWs train_layout(int B, int H, int W) {
@@ -210,6 +253,7 @@ TrainWs train_layout(int B, int H, int W) {
   w.dqkv32 = take((size_t)B * kQKV * N * 4);
   w.x16 = take((size_t)B * kC * Np * 2);
   w.wqkv16 = take((size_t)kQKV * kC * 2);
+  w.do16 = take((size_t)B * kC * Np * 2);
   w.total = off;
   return w;
 }
@@ -281,26 +325,37 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   if (int rc = check_launch("psa train conversions")) return rc;
   if (int rc = va_dwconv3x3_backward_f32(v32, wpe32, dA, dvpe, grads + VA_PSA_GRAD_WPE, B, kC, H, W, st)) return rc;
   scale_kernel<<<grid_for(kC * 9), 256, 0, st>>>(grads + VA_PSA_GRAD_WPE, kC * 9, sigma);
-  // attention backward, one call per V half (dq and dk accumulate)
+  // attention backward
   const size_t fsz = (size_t)BH * N * kKD;
+  VA_CHECK_ARG(2 * fsz < (size_t)INT32_MAX, "psa train: shard too large");
   float* fa = static_cast<float*>(at(L.fa));
-  float *q32 = fa, *k32 = fa + fsz, *vh = fa + 2 * fsz, *oh = fa + 4 * fsz, *doh = fa + 6 * fsz;
-  float *dq = fa + 8 * fsz, *dk = fa + 9 * fsz, *dvh = fa + 10 * fsz;
-  f16_to_f32_kernel<<<grid_for(2 * fsz), 256, 0, st>>>(qk, q32, 1, (int)(2 * fsz), (int)(2 * fsz));
-  to_fa_halves_kernel<__half><<<grid_for(2 * fsz), 256, 0, st>>>(vb, vh, B, N, Np);
-  to_fa_halves_kernel<__half><<<grid_for(2 * fsz), 256, 0, st>>>(ob, oh, B, N, Np);
-  to_fa_halves_kernel<float><<<grid_for(2 * fsz), 256, 0, st>>>(dA, doh, B, N, N);
-  if (int rc = check_launch("psa train layouts")) return rc;
-  cudaMemsetAsync(dq, 0, 2 * fsz * sizeof(float), st);
-  const float scale = 1.0f / sqrtf((float)kd);
-  for (int half = 0; half < 2; ++half)
-    if (int rc = va_psa_fa2_backward_f32(q32, k32, vh + half * fsz, oh + half * fsz, doh + half * fsz, lse, dq, dk,
-                                         dvh + half * fsz, N, scale, BH, kKD, st))
-      return rc;
   __half* dq16 = static_cast<__half*>(at(L.dqkv16));
   float* dq32 = static_cast<float*>(at(L.dqkv32));
-  assemble_dqkv_kernel<<<grid_for((long long)B * kQKV * Np), 256, 0, st>>>(dq, dk, dvh, dvh + fsz, dvpe, dq16, dq32,
-                                                                            B, N, Np);
+  const float scale = 1.0f / sqrtf((float)kd);
+  if (N <= 512) {  // tensor cores: dK, dV and per-key-tile dQ partials, then dqkv
+    __half* do16 = static_cast<__half*>(at(L.do16));
+    f32_to_f16_pad_kernel<<<grid_for(rows * Np), 256, 0, st>>>(dA, do16, rows, N, Np);
+    if (int rc = check_launch("psa train dO")) return rc;
+    float *dk = fa, *dv = fa + fsz, *dqp = fa + 3 * fsz;
+    if (int rc = psa_attn_bwd_tc(qk, vb, ob, do16, lse, dk, dv, dqp, B, nh, N, st)) return rc;
+    assemble_dqkv_tc_kernel<<<grid_for((long long)B * kQKV * Np), 256, 0, st>>>(dqp, (N + 127) / 128, dk, dv, dvpe,
+                                                                               dq16, dq32, B, N, Np);
+  } else {  // f32 SIMT kernels, one call per V half (dq and dk accumulate)
+    float *q32 = fa, *k32 = fa + fsz, *vh = fa + 2 * fsz, *oh = fa + 4 * fsz, *doh = fa + 6 * fsz;
+    float *dq = fa + 8 * fsz, *dk = fa + 9 * fsz, *dvh = fa + 10 * fsz;
+    f16_to_f32_kernel<<<grid_for(2 * fsz), 256, 0, st>>>(qk, q32, 1, (int)(2 * fsz), (int)(2 * fsz));
+    to_fa_halves_kernel<__half><<<grid_for(2 * fsz), 256, 0, st>>>(vb, vh, B, N, Np);
+    to_fa_halves_kernel<__half><<<grid_for(2 * fsz), 256, 0, st>>>(ob, oh, B, N, Np);
+    to_fa_halves_kernel<float><<<grid_for(2 * fsz), 256, 0, st>>>(dA, doh, B, N, N);
+    if (int rc = check_launch("psa train layouts")) return rc;
+    cudaMemsetAsync(dq, 0, 2 * fsz * sizeof(float), st);
+    for (int half = 0; half < 2; ++half)
+      if (int rc = va_psa_fa2_backward_f32(q32, k32, vh + half * fsz, oh + half * fsz, doh + half * fsz, lse, dq, dk,
+                                           dvh + half * fsz, N, scale, BH, kKD, st))
+        return rc;
+    assemble_dqkv_kernel<<<grid_for((long long)B * kQKV * Np), 256, 0, st>>>(dq, dk, dvh, dvh + fsz, dvpe, dq16,
+                                                                              dq32, B, N, Np);
+  }
   rowsum_kernel<float><<<kQKV, 256, 0, st>>>(dq32, grads + VA_PSA_GRAD_BQKV, B, kQKV, N, N, sigma);
   // qkv backward
   __half* x16 = static_cast<__half*>(at(L.x16));
