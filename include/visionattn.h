@@ -296,11 +296,11 @@ VA_API int va_psa_sgd_update(float *master, const float *grads, float lr, float 
  * An operand is K-major (x_mn = 0: row m holds K elements, row pitch ld) or
  * MN-major (x_mn = 1: row k holds the M or N elements); x_batch = elements
  * between batch entries, x_bcast = 1 to use one matrix for all z.  C is f32
- * (c_bf16 = 0) or bf16, row pitch ldc, batch stride c_batch.  16-byte
+ * (c_type = 0), bf16 (1) or f16 (2), row pitch ldc, batch stride c_batch.  16-byte
  * aligned bases and pitches. */
 VA_API int va_gemm_f16(const void *a, int a_mn, long long lda, long long a_batch, int a_bcast,
                        const void *b, int b_mn, long long ldb, long long b_batch, int b_bcast,
-                       void *c, int c_bf16, long long ldc, long long c_batch, int M, int N, int K,
+                       void *c, int c_type, long long ldc, long long c_batch, int M, int N, int K,
                        int Z, float alpha, va_stream_t stream);
 
 /* Device status word of the tensor-core kernels: 0, or 1000+site of the

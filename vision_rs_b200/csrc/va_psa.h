@@ -49,14 +49,16 @@ struct GemmOperand {
   long long batch_stride;
   bool broadcast;
 };
-// C[z][m][n] = α·Σ_k A_z(m,k)·B_z(n,k), f32 accumulation; C f32 or bf16
-// with row pitch ldc and batch stride c_batch (elements).
-int tc_gemm_f16(const GemmOperand& a, const GemmOperand& b, void* c, bool c_bf16, long long ldc, long long c_batch,
-                int M, int N, int K, int Z, cudaStream_t st, float alpha = 1.0f);
+// C[z'][m][n] = α·Σ_{z in fold z'} Σ_k A_z(m,k)·B_z(n,k), f32 accumulation;
+// z' = z / zfold (ceil(Z/zfold) outputs); C is f32 (c_type 0), bf16 (1) or
+// f16 (2) with row pitch ldc and batch stride c_batch (elements).
+int tc_gemm_f16(const GemmOperand& a, const GemmOperand& b, void* c, int c_type, long long ldc, long long c_batch,
+                int M, int N, int K, int Z, cudaStream_t st, float alpha = 1.0f, int zfold = 1);
 int gemm_status_read(int* out, cudaStream_t st);
-// Tensor-core PSA attention backward (nh = 2, kd = 32, N ≤ 512): dk f32
-// [B·nh][N][32], dv f32 [B·nh][N][64], dq_part f32 [ceil(N/128)][B·nh][N][32]
-// (sum over the first index = dQ).  qk, v, o, d_o in the forward's f16 layouts.
+// Tensor-core PSA attention backward (nh = 2, kd = 32, N ≤ 512), channel-major
+// f32 outputs: dk [B·nh][32][N], dv [B·nh][64][N], dq_part
+// [ceil(N/128)][B·nh][32][N] (sum over the first index = dQ).  qk, v, o, d_o
+// in the forward's f16 layouts.
 int psa_attn_bwd_tc(const void* qk, const void* v, const void* o, const void* d_o, const float* lse, float* dk,
                     float* dv, float* dq_part, int B, int nh, int N, cudaStream_t st);
 int bwd_status_read(int* out, cudaStream_t st);

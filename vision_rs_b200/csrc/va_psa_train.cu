@@ -8,20 +8,22 @@
 //   h·128; O_h = V_h·softmax(Q_hᵀK_h/√32)ᵀ; PE = dw3×3(V) + b_pe;
 //   y = W_proj·(O + PE) + b_proj.  Loss = mean((y − t)²) over the shard.
 //
-// Backward, in order (all sums over images run per image and are reduced in
-// a fixed order — deterministic, no atomics).  It runs on the residual
-// r = y − t (O(1) values, well inside the f16 range; dy = 2r/numel would sit
-// in f16's subnormals at these batch sizes) and applies σ = 2/numel once, in
-// f32, to every gradient it stores:
-//   r = y − t                                               (f16, loss_grad_kernel)
-//   dW_proj = σ Σ_b (r_b·O_bᵀ + r_b·PE_bᵀ), db_proj = σ Σ r (tcgen05 GEMM partials)
-//   dA = W_projᵀ·r  (= dO = dPE, in units of σ)             (tcgen05 GEMM, f32)
-//   dV_pe, dW_pe = dw3×3 backward(V, dA); db_pe = σ Σ dA    (f32 SIMT)
-//   dQ, dK, dV = attention backward: tcgen05 kernel over the full 64-wide V
-//                (N ≤ 512, psa_attn_bwd_tc), else the f32 SIMT kernels once
-//                per 32-wide V half (psa_fa2_backward)
-//   dqkv = [dQ | dK | dV + dV_pe] per head                  (f16 + f32 copies)
-//   dW_qkv = σ Σ_b dqkv_b·x_bᵀ, db_qkv = σ Σ dqkv; dx = σ W_qkvᵀ·dqkv (tcgen05 GEMMs)
+// Backward.  It runs on the residual r = y − t (O(1) values, well inside the
+// f16 range; dy = 2r/numel would sit in f16's subnormals at these batch
+// sizes) and applies σ = 2/numel once, in f32, when the gradients are stored.
+// Every sum over images is taken per image (or per group of images inside one
+// GEMM accumulator) and reduced in a fixed order — deterministic, no atomics.
+//   loss_rows_kernel   r (f16), Σr and Σr² per (image, channel)
+//   tcgen05 GEMMs      dW_proj partials = r·Oᵀ + r·PEᵀ; dA = W_projᵀ·r (f16)
+//   attention backward tcgen05 kernel over the full 64-wide V (N ≤ 512,
+//                      psa_attn_bwd_tc), else the f32 SIMT kernels once per
+//                      32-wide V half (psa_fa2_backward) + a transpose
+//   assemble_kernel    per (image, qkv channel): dqkv = [dQ | dK | dV + dV_pe]
+//                      (f16 for the GEMMs), its row sum (db_qkv), and on V
+//                      channels the positional-encoding backward (dV_pe, and
+//                      dW_pe / db_pe partials)
+//   tcgen05 GEMMs      dW_qkv partials = dqkv·xᵀ; dx = σ·W_qkvᵀ·dqkv
+//   finalize_kernel    every gradient = σ · Σ partials (fixed order), loss
 //
 // Gradient buffer (f32, PyTorch parameter layouts):
 //   [dW_qkv 256×128 | dW_proj 128×128 | dW_pe 128×9 | db_qkv 256 | db_proj 128 | db_pe 128]
@@ -35,68 +37,44 @@ namespace va {
 namespace {
 
 constexpr int kC = 128, kQKV = 256, kKD = 32, kHD = 64, kNH = 2;
-constexpr int kLossBlocks = 512;
+constexpr int kRowThreads = 128;
+constexpr int kZFold = 1;  // images per GEMM accumulator in the weight-gradient GEMMs
 
-// scale·(y − t) as f16 [B][C][Np] (pad columns zero); per-block Σ(y − t)².
-__global__ void loss_grad_kernel(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ t,
-                                 __half* __restrict__ dy, float* __restrict__ part, long long rows, int N, int Np,
-                                 float scale) {
-  __shared__ float red[256];
-  float acc = 0.f;
-  const long long total = rows * Np;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / Np;
-    const int n = (int)(i - r * Np);
-    float g = 0.f;
+__device__ __forceinline__ float block_sum(float v, float* red) {  // fixed-order reduction, kRowThreads threads
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < kRowThreads / 32; ++w) s += red[w];
+  return s;
+}
+
+// One CTA per (image, output channel) row: r = y − t as f16 [rows][Np] (pad
+// zero), Σr and Σr² of the row.
+__global__ void __launch_bounds__(kRowThreads)
+loss_rows_kernel(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ t, __half* __restrict__ r16,
+                 float* __restrict__ rsum, float* __restrict__ rsq, int N, int Np) {
+  __shared__ float red[kRowThreads / 32];
+  const size_t row = blockIdx.x;
+  float s = 0.f, q = 0.f;
+  for (int n = threadIdx.x; n < Np; n += kRowThreads) {
+    float d = 0.f;
     if (n < N) {
-      const float d = __bfloat162float(y[r * N + n]) - __bfloat162float(t[r * N + n]);
-      acc = fmaf(d, d, acc);
-      g = d * scale;
+      d = __bfloat162float(y[row * N + n]) - __bfloat162float(t[row * N + n]);
+      s += d;
+      q = fmaf(d, d, q);
     }
-    dy[i] = __float2half_rn(g);
+    r16[row * Np + n] = __float2half_rn(d);
   }
-  red[threadIdx.x] = acc;
-  __syncthreads();
-  for (int s = 128; s > 0; s >>= 1) {
-    if (threadIdx.x < s) red[threadIdx.x] += red[threadIdx.x + s];
-    __syncthreads();
+  s = block_sum(s, red);
+  q = block_sum(q, red);
+  if (threadIdx.x == 0) {
+    rsum[row] = s;
+    rsq[row] = q;
   }
-  if (threadIdx.x == 0) part[blockIdx.x] = red[0];
-}
-
-// out[i] = scale · Σ_z in[z·stride + i], z in order (one thread per i).
-__global__ void reduce_batches_kernel(const float* __restrict__ in, float* __restrict__ out, int count, int Z,
-                                      long long stride, float scale) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
-    float s = 0.f;
-    for (int z = 0; z < Z; ++z) s += in[z * stride + i];
-    out[i] = s * scale;
-  }
-}
-
-// out[c] = scale · Σ_b Σ_{n<N} X[b][c][n]  (X pitch `pitch`), fixed-order tree per channel.
-template <typename T>
-__global__ void rowsum_kernel(const T* __restrict__ x, float* __restrict__ out, int B, int C, int N, int pitch,
-                              float scale) {
-  __shared__ float red[256];
-  const int c = blockIdx.x;
-  float acc = 0.f;
-  for (int b = 0; b < B; ++b) {
-    const T* row = x + ((size_t)b * C + c) * pitch;
-    for (int n = threadIdx.x; n < N; n += blockDim.x) acc += (float)row[n];
-  }
-  red[threadIdx.x] = acc;
-  __syncthreads();
-  for (int s = 128; s > 0; s >>= 1) {
-    if (threadIdx.x < s) red[threadIdx.x] += red[threadIdx.x + s];
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) out[c] = red[0] * scale;
-}
-
-__global__ void scale_kernel(float* __restrict__ x, int n, float s) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) x[i] *= s;
 }
 
 // bf16 [rows][N] → f16 [rows][Np] (pad zero)
@@ -111,25 +89,32 @@ __global__ void bf16_to_f16_pad_kernel(const __nv_bfloat16* __restrict__ x, __ha
   }
 }
 
-// f16 [rows][pitch] → f32 [rows][N]
-__global__ void f16_to_f32_kernel(const __half* __restrict__ x, float* __restrict__ y, long long rows, int N,
-                                  int pitch) {
-  const long long total = rows * N;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / N;
-    y[i] = __half2float(x[r * pitch + (i - r * N)]);
+// bf16 → f16, 8 elements per thread (16-byte loads and stores)
+__global__ void bf16_to_f16_vec_kernel(const uint4* __restrict__ x, uint4* __restrict__ y, long long n8) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const uint4 u = x[i];
+    const unsigned w[4] = {u.x, u.y, u.z, u.w};
+    unsigned o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const __half2 h = __floats2half2_rn(__uint_as_float(w[k] << 16), __uint_as_float(w[k] & 0xffff0000u));
+      o[k] = *reinterpret_cast<const unsigned*>(&h);
+    }
+    y[i] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
-__global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ y, int n) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) y[i] = __bfloat162float(x[i]);
+// f16 [count] → f32 [count]
+__global__ void f16_to_f32_kernel(const __half* __restrict__ x, float* __restrict__ y, long long count) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < count;
+       i += (long long)gridDim.x * blockDim.x)
+    y[i] = __half2float(x[i]);
 }
 
-// channel-major [B][nh·64][pitch] → token-major f32 halves [2][B·nh][N][32]
-// (element (half, b·nh + h, n, d) = src[b][h·64 + half·32 + d][n]).
-template <typename T>
-__global__ void to_fa_halves_kernel(const T* __restrict__ src, float* __restrict__ dst, int B, int N, int pitch) {
+// channel-major f16 [B][nh·64][pitch] → token-major f32 halves [2][B·nh][N][32]
+// (element (half, b·nh + h, n, d) = src[b][h·64 + half·32 + d][n]); the
+// layout of the f32 SIMT attention backward.
+__global__ void to_fa_halves_kernel(const __half* __restrict__ src, float* __restrict__ dst, int B, int N, int pitch) {
   const long long per_half = (long long)B * kNH * N * kKD;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < 2 * per_half;
        i += (long long)gridDim.x * blockDim.x) {
@@ -139,76 +124,149 @@ __global__ void to_fa_halves_kernel(const T* __restrict__ src, float* __restrict
     r /= kKD;
     const int n = (int)(r % N);
     const int bh = (int)(r / N), b = bh / kNH, h = bh % kNH;
-    dst[i] = (float)src[((size_t)b * kC + h * kHD + half * kKD + d) * pitch + n];
+    dst[i] = __half2float(src[((size_t)b * kC + h * kHD + half * kKD + d) * pitch + n]);
   }
 }
 
-// dqkv[b][j][n], j = h·128 + r: r < 32 dQ, r < 64 dK, else dV (+ dV_pe);
-// written f16 [B][256][Np] (pad zero) and f32 [B][256][N].
-__global__ void assemble_dqkv_kernel(const float* __restrict__ dq, const float* __restrict__ dk,
-                                     const float* __restrict__ dv_lo, const float* __restrict__ dv_hi,
-                                     const float* __restrict__ dv_pe, __half* __restrict__ d16, float* __restrict__ d32,
-                                     int B, int N, int Np) {
-  const long long total = (long long)B * kQKV * Np;
+// token-major [mats][N][w] → channel-major [mats][w][N] (f32)
+__global__ void tm_to_cm_kernel(const float* __restrict__ src, float* __restrict__ dst, int mats, int N, int w) {
+  const long long total = (long long)mats * N * w;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
-    const int n = (int)(i % Np);
-    const long long bj = i / Np;
-    const int j = (int)(bj % kQKV), b = (int)(bj / kQKV);
+    const int n = (int)(i % N);
+    const long long mc = i / N;
+    const int c = (int)(mc % w), m = (int)(mc / w);
+    dst[i] = src[((size_t)m * N + n) * w + c];
+  }
+}
+
+// One CTA per (qkv channel j, image b).  dqkv row: dQ = Σ_p dq_part[p] (p in
+// order), dK, or dV + dV_pe, where dV_pe = the depthwise 3×3 backward of dA on
+// channel c = h·64 + (j − h·128 − 64).  Writes the f16 row (pad zero), its
+// sum (db_qkv partial) and, on V channels, the dW_pe (9 taps) and db_pe
+// partials of (b, c).  Shared memory: the dA and V planes of (b, c), f32.
+__global__ void __launch_bounds__(kRowThreads)
+assemble_kernel(const float* __restrict__ dq_part, int nparts, const float* __restrict__ dk, const float* __restrict__ dv,
+                const __half* __restrict__ dA, const __half* __restrict__ vb, const __nv_bfloat16* __restrict__ w_pe,
+                __half* __restrict__ d16, float* __restrict__ part_bqkv, float* __restrict__ part_wpe,
+                float* __restrict__ part_bpe, int B, int H, int W, int Np) {
+  extern __shared__ float planes[];  // [2][N]: dA, V
+  __shared__ float red[kRowThreads / 32];
+  const int j = blockIdx.x, b = blockIdx.y, N = H * W;
+  const int h = j / 128, r = j % 128, bh = b * kNH + h;
+  const size_t part = (size_t)B * kNH * kKD * N;
+  __half* out = d16 + ((size_t)b * kQKV + j) * Np;
+  float rs = 0.f;
+  if (r < 64) {
+    const float* src = r < 32 ? dq_part + ((size_t)bh * kKD + r) * N : dk + ((size_t)bh * kKD + r - 32) * N;
+    for (int n = threadIdx.x; n < Np; n += kRowThreads) {
+      float g = 0.f;
+      if (n < N) {
+        if (r < 32) {
+          for (int p = 0; p < nparts; ++p) g += src[p * part + n];
+        } else {
+          g = src[n];
+        }
+        rs += g;
+      }
+      out[n] = __float2half_rn(g);
+    }
+    rs = block_sum(rs, red);
+    if (threadIdx.x == 0) part_bqkv[(size_t)b * kQKV + j] = rs;
+    return;
+  }
+  const int dd = r - 64, c = h * kHD + dd;
+  float* pa = planes;
+  float* pv = planes + N;
+  const __half* arow = dA + ((size_t)b * kC + c) * Np;
+  const __half* vrow = vb + ((size_t)b * kC + c) * Np;
+  for (int n = threadIdx.x; n < N; n += kRowThreads) {
+    pa[n] = __half2float(arow[n]);
+    pv[n] = __half2float(vrow[n]);
+  }
+  float w[9];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) w[k] = __bfloat162float(w_pe[c * 9 + k]);
+  __syncthreads();
+  const float* dvr = dv + ((size_t)bh * kHD + dd) * N;
+  float tw[9] = {}, ab = 0.f;
+  for (int n = threadIdx.x; n < Np; n += kRowThreads) {
     float g = 0.f;
     if (n < N) {
-      const int h = j / 128, r = j % 128, bh = b * kNH + h;
-      if (r < 32) g = dq[((size_t)bh * N + n) * kKD + r];
-      else if (r < 64) g = dk[((size_t)bh * N + n) * kKD + r - 32];
-      else {
-        const int dd = r - 64;
-        g = (dd < 32 ? dv_lo[((size_t)bh * N + n) * kKD + dd] : dv_hi[((size_t)bh * N + n) * kKD + dd - 32]) +
-            dv_pe[((size_t)b * kC + h * kHD + dd) * N + n];
-      }
-      d32[((size_t)b * kQKV + j) * N + n] = g;
+      const int yy = n / W, xx = n - yy * W;
+      const float a = pa[n];
+      ab += a;
+      float pe = 0.f;
+#pragma unroll
+      for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+          // forward: PE[y][x] += w[ky][kx]·V[y+ky−1][x+kx−1]
+          const int sy = yy - ky + 1, sx = xx - kx + 1;  // dV[y][x] += w·dA[y−ky+1][x−kx+1]
+          if (sy >= 0 && sy < H && sx >= 0 && sx < W) pe = fmaf(w[ky * 3 + kx], pa[sy * W + sx], pe);
+          const int vy = yy + ky - 1, vx = xx + kx - 1;  // dW[ky][kx] += dA[y][x]·V[y+ky−1][x+kx−1]
+          if (vy >= 0 && vy < H && vx >= 0 && vx < W) tw[ky * 3 + kx] = fmaf(a, pv[vy * W + vx], tw[ky * 3 + kx]);
+        }
+      g = dvr[n] + pe;
+      rs += g;
     }
-    d16[i] = __float2half_rn(g);
+    out[n] = __float2half_rn(g);
+  }
+  rs = block_sum(rs, red);
+  ab = block_sum(ab, red);
+  float twr[9];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) twr[k] = block_sum(tw[k], red);
+  if (threadIdx.x == 0) {
+    part_bqkv[(size_t)b * kQKV + j] = rs;
+    part_bpe[(size_t)b * kC + c] = ab;
+#pragma unroll
+    for (int k = 0; k < 9; ++k) part_wpe[((size_t)b * kC + c) * 9 + k] = twr[k];
   }
 }
 
-// f32 [rows][N] → f16 [rows][Np] (pad zero)
-__global__ void f32_to_f16_pad_kernel(const float* __restrict__ x, __half* __restrict__ y, long long rows, int N,
-                                      int Np) {
-  const long long total = rows * Np;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / Np;
-    const int n = (int)(i - r * Np);
-    y[i] = __float2half_rn(n < N ? x[r * N + n] : 0.f);
-  }
-}
+// grads[i] = σ · Σ_p part_i[p] over the partials of each gradient block (p in
+// order); block 0 also writes the loss = Σ rsq / numel.
+struct FinalizeArgs {
+  const float* part_wqkv;  // [Pq][256·128]
+  const float* part_wproj; // [Pp][128·128]
+  const float* part_wpe;   // [B][128·9]
+  const float* part_bqkv;  // [B][256]
+  const float* rsum;       // [B][128]
+  const float* part_bpe;   // [B][128]
+  const float* rsq;        // [B·128]
+  int Pq, Pp, B;
+  float sigma, inv_numel;
+  float* grads;
+  float* loss;
+};
 
-// dqkv from the tensor-core backward: dQ = Σ_j dq_part[j] (j in order), dK
-// [B·nh][N][32], dV [B·nh][N][64] (+ dV_pe); same outputs as assemble_dqkv_kernel.
-__global__ void assemble_dqkv_tc_kernel(const float* __restrict__ dq_part, int nparts, const float* __restrict__ dk,
-                                        const float* __restrict__ dv, const float* __restrict__ dv_pe,
-                                        __half* __restrict__ d16, float* __restrict__ d32, int B, int N, int Np) {
-  const long long total = (long long)B * kQKV * Np;
-  const size_t part = (size_t)B * kNH * N * kKD;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int n = (int)(i % Np);
-    const long long bj = i / Np;
-    const int j = (int)(bj % kQKV), b = (int)(bj / kQKV);
-    float g = 0.f;
-    if (n < N) {
-      const int h = j / 128, r = j % 128, bh = b * kNH + h;
-      if (r < 32) {
-        for (int pj = 0; pj < nparts; ++pj) g += dq_part[pj * part + ((size_t)bh * N + n) * kKD + r];
-      } else if (r < 64) {
-        g = dk[((size_t)bh * N + n) * kKD + r - 32];
-      } else {
-        const int dd = r - 64;
-        g = dv[((size_t)bh * N + n) * kHD + dd] + dv_pe[((size_t)b * kC + h * kHD + dd) * N + n];
-      }
-      d32[((size_t)b * kQKV + j) * N + n] = g;
+__global__ void __launch_bounds__(256) finalize_kernel(FinalizeArgs a) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < VA_PSA_GRAD_COUNT; i += gridDim.x * blockDim.x) {
+    const float* src;
+    int np, off;
+    size_t stride;
+    if (i < VA_PSA_GRAD_WPROJ) { src = a.part_wqkv; np = a.Pq; off = i; stride = (size_t)kQKV * kC; }
+    else if (i < VA_PSA_GRAD_WPE) { src = a.part_wproj; np = a.Pp; off = i - VA_PSA_GRAD_WPROJ; stride = (size_t)kC * kC; }
+    else if (i < VA_PSA_GRAD_BQKV) { src = a.part_wpe; np = a.B; off = i - VA_PSA_GRAD_WPE; stride = (size_t)kC * 9; }
+    else if (i < VA_PSA_GRAD_BPROJ) { src = a.part_bqkv; np = a.B; off = i - VA_PSA_GRAD_BQKV; stride = kQKV; }
+    else if (i < VA_PSA_GRAD_BPE) { src = a.rsum; np = a.B; off = i - VA_PSA_GRAD_BPROJ; stride = kC; }
+    else { src = a.part_bpe; np = a.B; off = i - VA_PSA_GRAD_BPE; stride = kC; }
+    float s = 0.f;
+    for (int p = 0; p < np; ++p) s += src[p * stride + off];
+    a.grads[i] = s * a.sigma;
+  }
+  if (blockIdx.x == 0) {
+    __shared__ float red[256];
+    float s = 0.f;
+    for (int i = threadIdx.x; i < a.B * kC; i += 256) s += a.rsq[i];
+    red[threadIdx.x] = s;
+    __syncthreads();
+    for (int o = 128; o > 0; o >>= 1) {
+      if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+      __syncthreads();
     }
-    d16[i] = __float2half_rn(g);
+    if (threadIdx.x == 0) *a.loss = red[0] * a.inv_numel;
   }
 }
 
@@ -231,29 +289,32 @@ int grid_for(long long n) { return (int)std::min<long long>(std::max<long long>(
 
 struct TrainWs {
   PsaTcOffsets fwd;
-  size_t lse, dy, loss_part, dA, part, v32, dvpe, wpe32, fa, dqkv16, dqkv32, x16, wqkv16, do16, total;
+  size_t lse, r16, rsum, rsq, dA16, part_wproj, part_wqkv, part_wpe, part_bqkv, part_bpe, fa, dqkv16, x16, wqkv16,
+      total;
 };
 
 TrainWs train_layout(int B, int H, int W) {
   const size_t N = (size_t)H * W, Np = (N + 7) / 8 * 8, BH = (size_t)B * kNH;
+  const size_t fsz = BH * N * kKD;
+  const size_t Pz = (size_t)(B + kZFold - 1) / kZFold;
   TrainWs w;
   w.fwd = psa_tc_offsets(B, H, W, kNH);
   size_t off = w.fwd.total;
   auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
   w.lse = take(BH * N * 4);
-  w.dy = take((size_t)B * kC * Np * 2);
-  w.loss_part = take(kLossBlocks * 4);
-  w.dA = take((size_t)B * kC * N * 4);
-  w.part = take((size_t)std::max(2 * B * kC * kC, B * kQKV * kC) * 4);
-  w.v32 = take((size_t)B * kC * N * 4);
-  w.dvpe = take((size_t)B * kC * N * 4);
-  w.wpe32 = take((size_t)kC * 9 * 4);
-  w.fa = take(12 * BH * N * kKD * 4);  // q, k, v lo/hi, o lo/hi, do lo/hi, dq, dk, dv lo/hi
+  w.r16 = take((size_t)B * kC * Np * 2);
+  w.rsum = take((size_t)B * kC * 4);
+  w.rsq = take((size_t)B * kC * 4);
+  w.dA16 = take((size_t)B * kC * Np * 2);
+  w.part_wproj = take(2 * Pz * kC * kC * 4);
+  w.part_wqkv = take(Pz * kQKV * kC * 4);
+  w.part_wpe = take((size_t)B * kC * 9 * 4);
+  w.part_bqkv = take((size_t)B * kQKV * 4);
+  w.part_bpe = take((size_t)B * kC * 4);
+  w.fa = take(16 * fsz * 4);  // tensor-core path: dk, dv (2), dq partials (≤ 4); SIMT path: 12 + 4 (transposes)
   w.dqkv16 = take((size_t)B * kQKV * Np * 2);
-  w.dqkv32 = take((size_t)B * kQKV * N * 4);
   w.x16 = take((size_t)B * kC * Np * 2);
   w.wqkv16 = take((size_t)kQKV * kC * 2);
-  w.do16 = take((size_t)B * kC * Np * 2);
   w.total = off;
   return w;
 }
@@ -270,13 +331,15 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
                       const float* b_proj, __nv_bfloat16* y, __nv_bfloat16* dx, float* grads, float* loss, int B,
                       int C, int H, int W, int nh, int kd, void* ws, size_t ws_bytes, cudaStream_t st) {
   VA_CHECK_ARG(psa_tc_supported(C, nh, kd), "psa train: needs C=128, nh=2, kd=32");
-  VA_CHECK_ARG(B > 0 && H > 0 && W > 0, "psa train: bad sizes");
+  VA_CHECK_ARG(B > 0 && H > 0 && W > 0 && B <= 65535, "psa train: bad sizes");
   VA_CHECK_ARG(target && grads && loss && y, "psa train: null target/grads/loss/y");
+  const int N = H * W, Np = (N + 7) / 8 * 8, BH = B * nh;
+  VA_CHECK_ARG(2 * (size_t)N * sizeof(float) <= 200 * 1024, "psa train: %d tokens per image exceed the staged planes",
+               N);
   const TrainWs L = train_layout(B, H, W);
   if (!ws || ws_bytes < L.total)
     return set_error(VA_ERR_WORKSPACE, "psa train: workspace %zu < %zu bytes", ws_bytes, L.total);
   if (reinterpret_cast<uintptr_t>(ws) & 255) return set_error(VA_ERR_ALIGN, "psa train: workspace needs 256-byte alignment");
-  const int N = H * W, Np = (N + 7) / 8 * 8, BH = B * nh;
   char* base = static_cast<char*>(ws);
   auto at = [&](size_t o) { return static_cast<void*>(base + o); };
   float* lse = static_cast<float*>(at(L.lse));
@@ -289,92 +352,95 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   const __half* ob = static_cast<const __half*>(at(L.fwd.o));
   const __half* peb = static_cast<const __half*>(at(L.fwd.pe));
   const __half* wp16 = static_cast<const __half*>(at(L.fwd.wproj));
-  __half* dy = static_cast<__half*>(at(L.dy));
-  float* lpart = static_cast<float*>(at(L.loss_part));
   const long long rows = (long long)B * kC;
   const double numel = (double)rows * N;
   const float sigma = (float)(2.0 / numel);
-  loss_grad_kernel<<<kLossBlocks, 256, 0, st>>>(y, target, dy, lpart, rows, N, Np, 1.0f);
-  reduce_batches_kernel<<<1, 32, 0, st>>>(lpart, loss, 1, kLossBlocks, 1, (float)(1.0 / numel));
-  if (int rc = check_launch("psa train loss")) return rc;
+  const int Pz = (B + kZFold - 1) / kZFold;
 
-  float* part = static_cast<float*>(at(L.part));
-  // dW_proj partials: z < B from O, z ≥ B from PE
-  const GemmOperand a_dy{dy, false, Np, (long long)kC * Np, false};
-  if (int rc = tc_gemm_f16(a_dy, GemmOperand{ob, false, Np, (long long)kC * Np, false}, part, false, kC,
-                           (long long)kC * kC, kC, kC, N, B, st))
+  __half* r16 = static_cast<__half*>(at(L.r16));
+  float* rsum = static_cast<float*>(at(L.rsum));
+  float* rsq = static_cast<float*>(at(L.rsq));
+  loss_rows_kernel<<<(unsigned)rows, kRowThreads, 0, st>>>(y, target, r16, rsum, rsq, N, Np);
+  if (int rc = check_launch("psa train loss")) return rc;
+  // dW_proj partials: Pz from O, then Pz from PE (kZFold images per accumulator)
+  float* pwp = static_cast<float*>(at(L.part_wproj));
+  const GemmOperand a_r{r16, false, Np, (long long)kC * Np, false};
+  if (int rc = tc_gemm_f16(a_r, GemmOperand{ob, false, Np, (long long)kC * Np, false}, pwp, 0, kC,
+                           (long long)kC * kC, kC, kC, N, B, st, 1.0f, kZFold))
     return rc;
-  if (int rc = tc_gemm_f16(a_dy, GemmOperand{peb, false, Np, (long long)kC * Np, false}, part + (size_t)B * kC * kC,
-                           false, kC, (long long)kC * kC, kC, kC, N, B, st))
+  if (int rc = tc_gemm_f16(a_r, GemmOperand{peb, false, Np, (long long)kC * Np, false}, pwp + (size_t)Pz * kC * kC, 0,
+                           kC, (long long)kC * kC, kC, kC, N, B, st, 1.0f, kZFold))
     return rc;
-  reduce_batches_kernel<<<grid_for(kC * kC), 256, 0, st>>>(part, grads + VA_PSA_GRAD_WPROJ, kC * kC, 2 * B,
-                                                           (long long)kC * kC, sigma);
-  rowsum_kernel<__half><<<kC, 256, 0, st>>>(dy, grads + VA_PSA_GRAD_BPROJ, B, kC, N, Np, sigma);
-  // dA[b][i][n] = Σ_o W_proj[o][i] dy[b][o][n]
-  float* dA = static_cast<float*>(at(L.dA));
-  if (int rc = tc_gemm_f16(GemmOperand{wp16, true, kC, 0, true}, GemmOperand{dy, true, Np, (long long)kC * Np, false},
-                           dA, false, N, (long long)kC * N, kC, N, kC, B, st))
+  // dA[b][i][n] = Σ_o W_proj[o][i]·r[b][o][n]  (f16, dO of the attention and dPE)
+  __half* dA = static_cast<__half*>(at(L.dA16));
+  if (int rc = tc_gemm_f16(GemmOperand{wp16, true, kC, 0, true}, GemmOperand{r16, true, Np, (long long)kC * Np, false},
+                           dA, 2, Np, (long long)kC * Np, kC, N, kC, B, st))
     return rc;
-  rowsum_kernel<float><<<kC, 256, 0, st>>>(dA, grads + VA_PSA_GRAD_BPE, B, kC, N, N, sigma);
-  // positional encoding backward
-  float* v32 = static_cast<float*>(at(L.v32));
-  float* dvpe = static_cast<float*>(at(L.dvpe));
-  float* wpe32 = static_cast<float*>(at(L.wpe32));
-  f16_to_f32_kernel<<<grid_for(rows * N), 256, 0, st>>>(vb, v32, rows, N, Np);
-  bf16_to_f32_kernel<<<1, 256, 0, st>>>(w_pe, wpe32, kC * 9);
-  if (int rc = check_launch("psa train conversions")) return rc;
-  if (int rc = va_dwconv3x3_backward_f32(v32, wpe32, dA, dvpe, grads + VA_PSA_GRAD_WPE, B, kC, H, W, st)) return rc;
-  scale_kernel<<<grid_for(kC * 9), 256, 0, st>>>(grads + VA_PSA_GRAD_WPE, kC * 9, sigma);
-  // attention backward
+  // attention backward → channel-major dK, dV, dQ partials
   const size_t fsz = (size_t)BH * N * kKD;
   VA_CHECK_ARG(2 * fsz < (size_t)INT32_MAX, "psa train: shard too large");
   float* fa = static_cast<float*>(at(L.fa));
-  __half* dq16 = static_cast<__half*>(at(L.dqkv16));
-  float* dq32 = static_cast<float*>(at(L.dqkv32));
-  const float scale = 1.0f / sqrtf((float)kd);
-  if (N <= 512) {  // tensor cores: dK, dV and per-key-tile dQ partials, then dqkv
-    __half* do16 = static_cast<__half*>(at(L.do16));
-    f32_to_f16_pad_kernel<<<grid_for(rows * Np), 256, 0, st>>>(dA, do16, rows, N, Np);
-    if (int rc = check_launch("psa train dO")) return rc;
-    float *dk = fa, *dv = fa + fsz, *dqp = fa + 3 * fsz;
-    if (int rc = psa_attn_bwd_tc(qk, vb, ob, do16, lse, dk, dv, dqp, B, nh, N, st)) return rc;
-    assemble_dqkv_tc_kernel<<<grid_for((long long)B * kQKV * Np), 256, 0, st>>>(dqp, (N + 127) / 128, dk, dv, dvpe,
-                                                                               dq16, dq32, B, N, Np);
-  } else {  // f32 SIMT kernels, one call per V half (dq and dk accumulate)
-    float *q32 = fa, *k32 = fa + fsz, *vh = fa + 2 * fsz, *oh = fa + 4 * fsz, *doh = fa + 6 * fsz;
-    float *dq = fa + 8 * fsz, *dk = fa + 9 * fsz, *dvh = fa + 10 * fsz;
-    f16_to_f32_kernel<<<grid_for(2 * fsz), 256, 0, st>>>(qk, q32, 1, (int)(2 * fsz), (int)(2 * fsz));
-    to_fa_halves_kernel<__half><<<grid_for(2 * fsz), 256, 0, st>>>(vb, vh, B, N, Np);
-    to_fa_halves_kernel<__half><<<grid_for(2 * fsz), 256, 0, st>>>(ob, oh, B, N, Np);
-    to_fa_halves_kernel<float><<<grid_for(2 * fsz), 256, 0, st>>>(dA, doh, B, N, N);
+  float *dk = fa, *dv = fa + fsz, *dqp = fa + 3 * fsz;
+  int nparts = 1;
+  if (N <= 512) {
+    if (int rc = psa_attn_bwd_tc(qk, vb, ob, dA, lse, dk, dv, dqp, B, nh, N, st)) return rc;
+    nparts = (N + 127) / 128;
+  } else {  // f32 SIMT kernels, one call per V half (dq and dk accumulate), then channel-major
+    float *q32 = fa + 4 * fsz, *k32 = fa + 5 * fsz, *vh = fa + 6 * fsz, *oh = fa + 8 * fsz, *doh = fa + 10 * fsz;
+    float *dq = fa + 12 * fsz, *dkt = fa + 13 * fsz, *dvh = fa + 14 * fsz;
+    f16_to_f32_kernel<<<grid_for(2 * fsz), 256, 0, st>>>(qk, q32, (long long)(2 * fsz));
+    to_fa_halves_kernel<<<grid_for(2 * fsz), 256, 0, st>>>(vb, vh, B, N, Np);
+    to_fa_halves_kernel<<<grid_for(2 * fsz), 256, 0, st>>>(ob, oh, B, N, Np);
+    to_fa_halves_kernel<<<grid_for(2 * fsz), 256, 0, st>>>(dA, doh, B, N, Np);
     if (int rc = check_launch("psa train layouts")) return rc;
     cudaMemsetAsync(dq, 0, 2 * fsz * sizeof(float), st);
+    const float scale = 1.0f / sqrtf((float)kd);
     for (int half = 0; half < 2; ++half)
-      if (int rc = va_psa_fa2_backward_f32(q32, k32, vh + half * fsz, oh + half * fsz, doh + half * fsz, lse, dq, dk,
+      if (int rc = va_psa_fa2_backward_f32(q32, k32, vh + half * fsz, oh + half * fsz, doh + half * fsz, lse, dq, dkt,
                                            dvh + half * fsz, N, scale, BH, kKD, st))
         return rc;
-    assemble_dqkv_kernel<<<grid_for((long long)B * kQKV * Np), 256, 0, st>>>(dq, dk, dvh, dvh + fsz, dvpe, dq16,
-                                                                              dq32, B, N, Np);
+    tm_to_cm_kernel<<<grid_for(fsz), 256, 0, st>>>(dq, dqp, BH, N, kKD);
+    tm_to_cm_kernel<<<grid_for(fsz), 256, 0, st>>>(dkt, dk, BH, N, kKD);
+    // dv halves [2][BH][N][32] → [BH][64][N]: channels 0-31 from lo, 32-63 from hi
+    tm_to_cm_kernel<<<grid_for(fsz), 256, 0, st>>>(dvh, q32, BH, N, kKD);            // lo → [BH][32][N]
+    tm_to_cm_kernel<<<grid_for(fsz), 256, 0, st>>>(dvh + fsz, q32 + fsz, BH, N, kKD);  // hi → [BH][32][N]
+    for (int half = 0; half < 2; ++half)
+      cudaMemcpy2DAsync(dv + (size_t)half * kKD * N, (size_t)kHD * N * sizeof(float), q32 + half * fsz,
+                        (size_t)kKD * N * sizeof(float), (size_t)kKD * N * sizeof(float), BH,
+                        cudaMemcpyDeviceToDevice, st);
   }
-  rowsum_kernel<float><<<kQKV, 256, 0, st>>>(dq32, grads + VA_PSA_GRAD_BQKV, B, kQKV, N, N, sigma);
+  // dqkv rows (+ PE backward and the bias partials)
+  __half* dq16 = static_cast<__half*>(at(L.dqkv16));
+  float* pbq = static_cast<float*>(at(L.part_bqkv));
+  float* pwe = static_cast<float*>(at(L.part_wpe));
+  float* pbe = static_cast<float*>(at(L.part_bpe));
+  assemble_kernel<<<dim3(kQKV, B), kRowThreads, 2 * (size_t)N * sizeof(float), st>>>(
+      dqp, nparts, dk, dv, dA, vb, w_pe, dq16, pbq, pwe, pbe, B, H, W, Np);
+  if (int rc = check_launch("psa train assemble")) return rc;
   // qkv backward
   __half* x16 = static_cast<__half*>(at(L.x16));
   __half* wq16 = static_cast<__half*>(at(L.wqkv16));
-  bf16_to_f16_pad_kernel<<<grid_for(rows * Np), 256, 0, st>>>(x, x16, rows, N, Np);
-  bf16_to_f16_pad_kernel<<<grid_for(kQKV * kC), 256, 0, st>>>(w_qkv, wq16, kQKV, kC, kC);
+  if (N == Np && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
+    bf16_to_f16_vec_kernel<<<grid_for(rows * N / 8), 256, 0, st>>>(reinterpret_cast<const uint4*>(x),
+                                                                   reinterpret_cast<uint4*>(x16), rows * N / 8);
+  else
+    bf16_to_f16_pad_kernel<<<grid_for(rows * Np), 256, 0, st>>>(x, x16, rows, N, Np);
+  bf16_to_f16_vec_kernel<<<grid_for(kQKV * kC / 8), 256, 0, st>>>(reinterpret_cast<const uint4*>(w_qkv),
+                                                                  reinterpret_cast<uint4*>(wq16), kQKV * kC / 8);
   if (int rc = check_launch("psa train qkv prep")) return rc;
+  float* pwq = static_cast<float*>(at(L.part_wqkv));
   if (int rc = tc_gemm_f16(GemmOperand{dq16, false, Np, (long long)kQKV * Np, false},
-                           GemmOperand{x16, false, Np, (long long)kC * Np, false}, part, false, kC,
-                           (long long)kQKV * kC, kQKV, kC, N, B, st))
+                           GemmOperand{x16, false, Np, (long long)kC * Np, false}, pwq, 0, kC, (long long)kQKV * kC,
+                           kQKV, kC, N, B, st, 1.0f, kZFold))
     return rc;
-  reduce_batches_kernel<<<grid_for(kQKV * kC), 256, 0, st>>>(part, grads + VA_PSA_GRAD_WQKV, kQKV * kC, B,
-                                                             (long long)kQKV * kC, sigma);
-  if (dx) {  // dx[b][i][n] = Σ_j W_qkv[j][i] dqkv[b][j][n]
+  if (dx) {  // dx[b][i][n] = σ Σ_j W_qkv[j][i] dqkv[b][j][n]
     if (int rc = tc_gemm_f16(GemmOperand{wq16, true, kC, 0, true},
-                             GemmOperand{dq16, true, Np, (long long)kQKV * Np, false}, dx, true, N, (long long)kC * N,
+                             GemmOperand{dq16, true, Np, (long long)kQKV * Np, false}, dx, 1, N, (long long)kC * N,
                              kC, N, kQKV, B, st, sigma))
       return rc;
   }
+  FinalizeArgs fa_args{pwq, pwp, pwe, pbq, rsum, pbe, rsq, Pz, 2 * Pz, B, sigma, (float)(1.0 / numel), grads, loss};
+  finalize_kernel<<<grid_for(VA_PSA_GRAD_COUNT), 256, 0, st>>>(fa_args);
   return check_launch("psa train backward");
 }
 
@@ -411,10 +477,10 @@ int va_psa_sgd_update(float* master, const float* grads, float lr, float grad_sc
 }
 
 int va_gemm_f16(const void* a, int a_mn, long long lda, long long a_batch, int a_bcast, const void* b, int b_mn,
-                long long ldb, long long b_batch, int b_bcast, void* c, int c_bf16, long long ldc, long long c_batch,
+                long long ldb, long long b_batch, int b_bcast, void* c, int c_type, long long ldc, long long c_batch,
                 int M, int N, int K, int Z, float alpha, va_stream_t stream) {
   return tc_gemm_f16(GemmOperand{a, a_mn != 0, lda, a_batch, a_bcast != 0},
-                     GemmOperand{b, b_mn != 0, ldb, b_batch, b_bcast != 0}, c, c_bf16 != 0, ldc, c_batch, M, N, K, Z,
+                     GemmOperand{b, b_mn != 0, ldb, b_batch, b_bcast != 0}, c, c_type, ldc, c_batch, M, N, K, Z,
                      (cudaStream_t)stream, alpha);
 }
 

@@ -8,11 +8,13 @@
 // shared by every batch entry.  One CTA computes a 128×128 tile: a producer
 // thread streams 64-wide K blocks through a 4-stage TMA ring (out-of-range
 // rows and columns read as zeros), one thread issues the MMAs into a TMEM
-// accumulator, and the four warps store it (f32 or bf16).  Batch entries
-// become independent tiles: a weight gradient summed over images is computed
-// as per-image partials and reduced in a fixed order afterwards, so it is
-// deterministic.
+// accumulator, and the four warps store it (f32, bf16 or f16).  A CTA may
+// fold `zfold` consecutive batch entries into its K loop (one accumulator),
+// so a weight gradient summed over images comes out as ceil(Z/zfold)
+// partials that the caller reduces in a fixed order — deterministic.
 #include <cudaTypedefs.h>
+
+#include <type_traits>
 
 #include "va_common.cuh"
 #include "va_psa.h"
@@ -35,16 +37,19 @@ struct GemmSmem {
   int abort;
 };
 
-template <bool A_MN, bool B_MN, bool OUT_BF16>
+constexpr int kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2;
+
+template <bool A_MN, bool B_MN, int OUT>
 __global__ void __launch_bounds__(128, 1)
 gemm_f16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, void* __restrict__ c,
-                int M, int N, int K, long long ldc, long long c_batch, int a_bcast, int b_bcast, float alpha) {
+                int M, int N, int K, long long ldc, long long c_batch, int a_bcast, int b_bcast, float alpha, int Z,
+                int zfold) {
   extern __shared__ uint8_t smem_raw[];
   GemmSmem& sm = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int m0 = blockIdx.x * kGM, n0 = blockIdx.y * kGN, z = blockIdx.z;
-  const int za = a_bcast ? 0 : z, zb = b_bcast ? 0 : z;
-  const int nk = (K + kGK - 1) / kGK;
+  const int zbeg = z * zfold, nz = min(zfold, Z - zbeg);
+  const int nkz = (K + kGK - 1) / kGK, nk = nkz * nz;  // k blocks: batch entries zbeg.. in order
 
   if (tid == 0) {
     for (int i = 0; i < kGStages; ++i) {
@@ -75,17 +80,19 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
           !(ok = mbar_wait(&sm.empty[st], ((kb / kGStages) - 1) & 1, &sm.abort, &g_gemm_status, 1)))
         break;
       mbar_arrive_expect_tx(&sm.full[st], kGM * 128 + kGN * 128);
+      const int ze = zbeg + kb / nkz, kk = kb % nkz;
+      const int za = a_bcast ? 0 : ze, zb = b_bcast ? 0 : ze;
       if (A_MN) {
-        tma_load_3d(sm.a[st], &map_a, &sm.full[st], m0, kb * kGK, za);
-        tma_load_3d(sm.a[st] + 8192, &map_a, &sm.full[st], m0 + 64, kb * kGK, za);
+        tma_load_3d(sm.a[st], &map_a, &sm.full[st], m0, kk * kGK, za);
+        tma_load_3d(sm.a[st] + 8192, &map_a, &sm.full[st], m0 + 64, kk * kGK, za);
       } else {
-        tma_load_3d(sm.a[st], &map_a, &sm.full[st], kb * kGK, m0, za);
+        tma_load_3d(sm.a[st], &map_a, &sm.full[st], kk * kGK, m0, za);
       }
       if (B_MN) {
-        tma_load_3d(sm.b[st], &map_b, &sm.full[st], n0, kb * kGK, zb);
-        tma_load_3d(sm.b[st] + 8192, &map_b, &sm.full[st], n0 + 64, kb * kGK, zb);
+        tma_load_3d(sm.b[st], &map_b, &sm.full[st], n0, kk * kGK, zb);
+        tma_load_3d(sm.b[st] + 8192, &map_b, &sm.full[st], n0 + 64, kk * kGK, zb);
       } else {
-        tma_load_3d(sm.b[st], &map_b, &sm.full[st], kb * kGK, n0, zb);
+        tma_load_3d(sm.b[st], &map_b, &sm.full[st], kk * kGK, n0, zb);
       }
       ++issued;
     }
@@ -133,20 +140,25 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
       for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
       const int nb = n0 + ch * 32;
       if (m >= M || nb >= N) continue;
-      if constexpr (OUT_BF16) {
-        __nv_bfloat16* row = static_cast<__nv_bfloat16*>(c) + z * c_batch + (long long)m * ldc + nb;
+      if constexpr (OUT != kOutF32) {
+        using T = typename std::conditional<OUT == kOutBF16, __nv_bfloat16, __half>::type;
+        auto pk = [](float a, float b) { return OUT == kOutBF16 ? pack_bf16x2(a, b) : pack_f16x2(a, b); };
+        T* row = static_cast<T*>(c) + z * c_batch + (long long)m * ldc + nb;
         if (nb + 32 <= N && ((reinterpret_cast<uintptr_t>(row) & 15) == 0)) {
           uint4* d = reinterpret_cast<uint4*>(row);
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            d[q] = make_uint4(pack_bf16x2(__uint_as_float(u[8 * q]), __uint_as_float(u[8 * q + 1])),
-                              pack_bf16x2(__uint_as_float(u[8 * q + 2]), __uint_as_float(u[8 * q + 3])),
-                              pack_bf16x2(__uint_as_float(u[8 * q + 4]), __uint_as_float(u[8 * q + 5])),
-                              pack_bf16x2(__uint_as_float(u[8 * q + 6]), __uint_as_float(u[8 * q + 7])));
+            d[q] = make_uint4(pk(__uint_as_float(u[8 * q]), __uint_as_float(u[8 * q + 1])),
+                              pk(__uint_as_float(u[8 * q + 2]), __uint_as_float(u[8 * q + 3])),
+                              pk(__uint_as_float(u[8 * q + 4]), __uint_as_float(u[8 * q + 5])),
+                              pk(__uint_as_float(u[8 * q + 6]), __uint_as_float(u[8 * q + 7])));
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (nb + i < N) row[i] = __float2bfloat16_rn(__uint_as_float(u[i]));
+            if (nb + i < N) {
+              const uint32_t h = pk(__uint_as_float(u[i]), 0.f) & 0xffffu;
+              reinterpret_cast<unsigned short*>(row)[i] = (unsigned short)h;
+            }
         }
       } else {
         float* row = static_cast<float*>(c) + z * c_batch + (long long)m * ldc + nb;
@@ -200,33 +212,34 @@ int operand_map(CUtensorMap* m, const GemmOperand& op, uint64_t inner, uint64_t 
 
 }  // namespace
 
-int tc_gemm_f16(const GemmOperand& a, const GemmOperand& b, void* c, bool c_bf16, long long ldc, long long c_batch,
-                int M, int N, int K, int Z, cudaStream_t st, float alpha) {
-  VA_CHECK_ARG(M > 0 && N > 0 && K > 0 && Z > 0 && Z <= 65535 && (N + kGN - 1) / kGN <= 65535, "gemm: bad sizes");
+int tc_gemm_f16(const GemmOperand& a, const GemmOperand& b, void* c, int c_type, long long ldc, long long c_batch,
+                int M, int N, int K, int Z, cudaStream_t st, float alpha, int zfold) {
+  VA_CHECK_ARG(M > 0 && N > 0 && K > 0 && Z > 0 && Z <= 65535 && zfold > 0 && (N + kGN - 1) / kGN <= 65535,
+               "gemm: bad sizes");
+  VA_CHECK_ARG(c_type >= kOutF32 && c_type <= kOutF16, "gemm: output type %d", c_type);
   CUtensorMap ma, mb;
   const uint64_t za = a.broadcast ? 1 : Z, zb = b.broadcast ? 1 : Z;
   if (int rc = a.mn ? operand_map(&ma, a, M, K, za, 64, 64, "A") : operand_map(&ma, a, K, M, za, 64, kGM, "A")) return rc;
   if (int rc = b.mn ? operand_map(&mb, b, N, K, zb, 64, 64, "B") : operand_map(&mb, b, K, N, zb, 64, kGN, "B")) return rc;
   const size_t smem = sizeof(GemmSmem) + 1024;
-  const dim3 grid((M + kGM - 1) / kGM, (N + kGN - 1) / kGN, Z);
+  const dim3 grid((M + kGM - 1) / kGM, (N + kGN - 1) / kGN, (Z + zfold - 1) / zfold);
   auto launch = [&](auto kernel) -> int {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     kernel<<<grid, 128, smem, st>>>(ma, mb, c, M, N, K, ldc, c_batch, a.broadcast ? 1 : 0, b.broadcast ? 1 : 0,
-                                    alpha);
+                                    alpha, Z, zfold);
     return check_launch("gemm");
   };
-  const int sel = (a.mn ? 4 : 0) | (b.mn ? 2 : 0) | (c_bf16 ? 1 : 0);
-  switch (sel) {
-    case 0: return launch(gemm_f16_kernel<false, false, false>);
-    case 1: return launch(gemm_f16_kernel<false, false, true>);
-    case 2: return launch(gemm_f16_kernel<false, true, false>);
-    case 3: return launch(gemm_f16_kernel<false, true, true>);
-    case 4: return launch(gemm_f16_kernel<true, false, false>);
-    case 5: return launch(gemm_f16_kernel<true, false, true>);
-    case 6: return launch(gemm_f16_kernel<true, true, false>);
-    default: return launch(gemm_f16_kernel<true, true, true>);
-  }
+  auto pick = [&](auto amn, auto bmn) -> int {
+    constexpr bool A = decltype(amn)::value, Bm = decltype(bmn)::value;
+    if (c_type == kOutBF16) return launch(gemm_f16_kernel<A, Bm, kOutBF16>);
+    if (c_type == kOutF16) return launch(gemm_f16_kernel<A, Bm, kOutF16>);
+    return launch(gemm_f16_kernel<A, Bm, kOutF32>);
+  };
+  using T_ = std::true_type;
+  using F_ = std::false_type;
+  if (a.mn) return b.mn ? pick(T_{}, T_{}) : pick(T_{}, F_{});
+  return b.mn ? pick(F_{}, T_{}) : pick(F_{}, F_{});
 }
 
 int gemm_status_read(int* out, cudaStream_t st) {

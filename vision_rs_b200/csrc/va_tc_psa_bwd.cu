@@ -17,8 +17,9 @@
 // in registers.  The P and dS tiles are stored once, swizzled (SW128), and
 // read by the MMAs both as M-major operands (Pᵀ, dSᵀ) and as K-major (dS).
 // TMEM (512 columns): S 0-127, dP 128-255, dV 256-319, dK 320-351, dQ_i at
-// 352 + 32i.  dQ is a per-key-tile partial [j][b·h][N][32]; the caller sums
-// the partials in j order (deterministic).
+// 352 + 32i.  Outputs are channel-major f32: dK [b·h][32][N], dV
+// [b·h][64][N], and dQ as per-key-tile partials [j][b·h][32][N] that the
+// caller sums in j order (deterministic).
 //
 // Operands (f16): Q/K [2][B·nh][N][32] (the forward's packed layout), Vᵀ, Oᵀ
 // and dOᵀ channel-major [B][nh·64][Np]; lse [B·nh][N] (natural log).
@@ -251,12 +252,10 @@ psa_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_con
         tmem_ld32(tmem + lane_off + kColDV + hf * 32, r);
         tmem_ld_wait();
         reg_fence(r);
-        if (key < N) {
-          float4* d = reinterpret_cast<float4*>(dv_out + ((size_t)bh * N + key) * kHD + hf * 32);
+        if (key < N) {  // channel-major: lanes store consecutive keys
+          float* d = dv_out + ((size_t)bh * kHD + hf * 32) * N + key;
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
-            d[c] = make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]), __uint_as_float(r[4 * c + 2]),
-                               __uint_as_float(r[4 * c + 3]));
+          for (int c = 0; c < 32; ++c) d[(size_t)c * N] = __uint_as_float(r[c]);
         }
       }
       {
@@ -265,11 +264,9 @@ psa_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_con
         tmem_ld_wait();
         reg_fence(r);
         if (key < N) {
-          float4* d = reinterpret_cast<float4*>(dk_out + ((size_t)bh * N + key) * kKD + hf * 16);
+          float* d = dk_out + ((size_t)bh * kKD + hf * 16) * N + key;
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            d[c] = make_float4(__uint_as_float(r[4 * c]) * sq, __uint_as_float(r[4 * c + 1]) * sq,
-                               __uint_as_float(r[4 * c + 2]) * sq, __uint_as_float(r[4 * c + 3]) * sq);
+          for (int c = 0; c < 16; ++c) d[(size_t)c * N] = __uint_as_float(r[c]) * sq;
         }
       }
       for (int i = 0; i < nt; ++i) {
@@ -279,11 +276,9 @@ psa_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_con
         reg_fence(r);
         const int q = i * kT + row;
         if (q < N) {
-          float4* d = reinterpret_cast<float4*>(dq_part + (((size_t)j * BH + bh) * N + q) * kKD + hf * 16);
+          float* d = dq_part + (((size_t)j * BH + bh) * kKD + hf * 16) * N + q;
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            d[c] = make_float4(__uint_as_float(r[4 * c]) * sq, __uint_as_float(r[4 * c + 1]) * sq,
-                               __uint_as_float(r[4 * c + 2]) * sq, __uint_as_float(r[4 * c + 3]) * sq);
+          for (int c = 0; c < 16; ++c) d[(size_t)c * N] = __uint_as_float(r[c]) * sq;
         }
       }
     }
