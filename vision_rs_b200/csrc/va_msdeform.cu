@@ -103,7 +103,10 @@ __device__ __forceinline__ Corners corners(float lx, float ly, int H, int W) {
   return c;
 }
 
-template <typename TV, int DH>
+// PT > 0: the number of points per level is a compile-time constant; all
+// PT·4 corner loads of a level are issued before any of them is used (more
+// gathers in flight per thread).  PT = 0: any P, one point at a time.
+template <typename TV, int DH, int PT>
 __global__ void __launch_bounds__(kMsdaThreads)
 msda_fwd_kernel(const TV* __restrict__ value, const int64_t* __restrict__ shapes, const int64_t* __restrict__ lstart,
                 const float* __restrict__ loc, const float* __restrict__ attn, TV* __restrict__ out, int B, int S,
@@ -132,18 +135,43 @@ msda_fwd_kernel(const TV* __restrict__ value, const int64_t* __restrict__ shapes
   for (int l = 0; l < L; ++l) {
     const int H = lv.H[l], W = lv.W[l];
     const TV* vbase = value + (((size_t)b * S + lv.s0[l]) * nh + h) * DH + part * VEC;
-    for (int p = 0; p < P; ++p) {
-      const int s = l * P + p;
-      const Corners c = corners(il[2 * s], il[2 * s + 1], H, W);
-      const float a = ia[s];
+    if constexpr (PT > 0) {
+      float v[PT][4][VEC], cw[PT][4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if (!c.ok[k]) continue;
-        float v[VEC];
-        Vec<TV>::load(vbase + (size_t)c.pix[k] * nh * DH, v);
-        const float cw = a * c.w[k];
+      for (int p = 0; p < PT; ++p) {
+        const int s = l * PT + p;
+        const Corners c = corners(il[2 * s], il[2 * s + 1], H, W);
+        const float a = ia[s];
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) acc[e] = fmaf(cw, v[e], acc[e]);
+        for (int k = 0; k < 4; ++k) {  // out-of-map corners load row 0 and contribute exactly 0
+          Vec<TV>::load(vbase + (size_t)c.pix[k] * nh * DH, v[p][k]);
+          cw[p][k] = c.ok[k] ? a * c.w[k] : 0.f;
+          if (!c.ok[k]) {
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) v[p][k][e] = 0.f;
+          }
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < PT; ++p)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[e] = fmaf(cw[p][k], v[p][k][e], acc[e]);
+    } else {
+      for (int p = 0; p < P; ++p) {
+        const int s = l * P + p;
+        const Corners c = corners(il[2 * s], il[2 * s + 1], H, W);
+        const float a = ia[s];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (!c.ok[k]) continue;
+          float vv[VEC];
+          Vec<TV>::load(vbase + (size_t)c.pix[k] * nh * DH, vv);
+          const float w = a * c.w[k];
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[e] = fmaf(w, vv[e], acc[e]);
+        }
       }
     }
   }
@@ -409,8 +437,13 @@ int msda_fwd(const TV* value, const int64_t* shapes, const int64_t* lstart, cons
     kernel<<<(unsigned)blocks, kMsdaThreads, smem, st>>>(value, shapes, lstart, loc, attn, out, B, S, nh, L, Q, P);
   };
   constexpr int VEC = Vec<TV>::N;
-  if (dh == 16) launch(msda_fwd_kernel<TV, 16>, 16 / VEC);
-  else launch(msda_fwd_kernel<TV, 32>, 32 / VEC);
+  if (P == 4) {
+    if (dh == 16) launch(msda_fwd_kernel<TV, 16, 4>, 16 / VEC);
+    else launch(msda_fwd_kernel<TV, 32, 4>, 32 / VEC);
+  } else {
+    if (dh == 16) launch(msda_fwd_kernel<TV, 16, 0>, 16 / VEC);
+    else launch(msda_fwd_kernel<TV, 32, 0>, 32 / VEC);
+  }
   return check_launch("msdeform_attn forward");
 }
 
