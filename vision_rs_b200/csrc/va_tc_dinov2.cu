@@ -55,13 +55,13 @@ struct DinoQkvSmem {
 template <int EPI>
 __global__ void __launch_bounds__(128, 2)
 dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                const float* __restrict__ bias, void* __restrict__ out0, __half* __restrict__ vbuf, int M, int hidden,
-                int n_seq, int n_pad, int heads) {
+                const __grid_constant__ CUtensorMap map_o1, const __grid_constant__ CUtensorMap map_o2,
+                const float* __restrict__ bias, int hidden, int heads, int BH) {
   extern __shared__ uint8_t smem_raw[];
   DinoQkvSmem& sm =
       *reinterpret_cast<DinoQkvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int m0 = blockIdx.x * kDM, n0 = blockIdx.y * kDN;
+  const int t0 = blockIdx.x * kDM, sq = blockIdx.y, n0 = blockIdx.z * kDN;  // tokens of sequence sq
   const int nk = hidden / 64;
 
   if (tid == 0) {
@@ -94,14 +94,14 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
           !(ok = mbar_wait(&sm.empty[st], ((kb / kDStages) - 1) & 1, &sm.abort, &g_dino_status, 1)))
         break;
       mbar_arrive_expect_tx(&sm.full[st], kDM * 128 + kDN * 128);
-      tma_load_2d(sm.a[st], &map_x, &sm.full[st], kb * 64, m0);
+      tma_load_3d(sm.a[st], &map_x, &sm.full[st], kb * 64, t0, sq);
       tma_load_2d(sm.b[st], &map_w, &sm.full[st], kb * 64, n0);
       ++issued;
     }
     if (!ok) {  // let every load issued here land (bounded) before the CTA can exit
       for (int kb = max(0, issued - kDStages); kb < issued; ++kb) {
-        const long long t0 = clock64();
-        while (!mbar_try_wait(&sm.full[kb % kDStages], (kb / kDStages) & 1) && clock64() - t0 < kSpinCycles) {
+        const long long t0c = clock64();
+        while (!mbar_try_wait(&sm.full[kb % kDStages], (kb / kDStages) & 1) && clock64() - t0c < kSpinCycles) {
         }
       }
     }
@@ -127,45 +127,62 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
   const bool ok = mbar_wait(&sm.mma_done, 0, &sm.abort, &g_dino_status, 3) && !sm.abort;
   tc_fence_after();
 
+  // Epilogue: stage the 128 × 192 tile in the (now idle) pipeline buffers as
+  // three 16 KB sub-tiles, one per 64-feature head group, then TMA-store them.
+  //   Q/K (split) and packed rows: [128 tokens][64] SW128 (row = token)
+  //   V (split): [64 d][128 tokens] plain, i.e. transposed
+  uint8_t* stage = sm.a[0];
   if (ok) {
-    const int r = warp * 32 + lane, m = m0 + r;
-    const bool live = m < M;
-    const int sq = live ? m / n_seq : 0, t = live ? m - sq * n_seq : 0;
+    const int row = warp * 32 + lane;
 #pragma unroll 1
     for (int c = 0; c < kDN / 32; ++c) {
       uint32_t u[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, u);
       tmem_ld_wait();
       reg_fence(u);
-      const int col = n0 + c * 32;
+      const int g = c >> 1, half = c & 1, col = n0 + c * 32;
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(u[i]) + __ldg(bias + col + i);
-      if (!live) continue;
-      if constexpr (EPI == kPackedRows) {
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out0) + (size_t)m * 3 * hidden + col);
+      uint8_t* tile = stage + g * 16384;
+      const bool vsec = EPI == kSplitHeads && (n0 + g * kHead) / hidden == 2;
+      if (vsec) {
+        __half* tv = reinterpret_cast<__half*>(tile);
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          dst[q] = make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
-                              pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+        for (int i = 0; i < 32; ++i)
+          tv[(half * 32 + i) * kDM + row] = __ushort_as_half((unsigned short)(pack_f16x2_sat(v[i], 0.f) & 0xffffu));
       } else {
-        const int sec = col / hidden, rem = col - sec * hidden, hd = rem / kHead, d0 = rem - hd * kHead;
-        const size_t bh = (size_t)sq * heads + hd, BH = (size_t)(M / n_seq) * heads;
-        if (sec < 2) {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(out0) +
-                                                (((size_t)sec * BH + bh) * n_seq + t) * kHead + d0);
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            dst[q] = make_uint4(pack_f16x2_sat(v[8 * q], v[8 * q + 1]), pack_f16x2_sat(v[8 * q + 2], v[8 * q + 3]),
-                                pack_f16x2_sat(v[8 * q + 4], v[8 * q + 5]), pack_f16x2_sat(v[8 * q + 6], v[8 * q + 7]));
-        } else {
-          __half* dst = vbuf + (bh * kHead + d0) * n_pad + t;  // lanes: consecutive tokens
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            dst[(size_t)i * n_pad] = __ushort_as_half((unsigned short)(pack_f16x2_sat(v[i], 0.f) & 0xffffu));
+        for (int q = 0; q < 4; ++q) {
+          uint4 w4;
+          if constexpr (EPI == kPackedRows)
+            w4 = make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                            pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+          else
+            w4 = make_uint4(pack_f16x2_sat(v[8 * q], v[8 * q + 1]), pack_f16x2_sat(v[8 * q + 2], v[8 * q + 3]),
+                            pack_f16x2_sat(v[8 * q + 4], v[8 * q + 5]), pack_f16x2_sat(v[8 * q + 6], v[8 * q + 7]));
+          *reinterpret_cast<uint4*>(tile + sw128_off(row, half * 4 + q)) = w4;
         }
       }
     }
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (ok && tid == 0) {
+#pragma unroll 1
+    for (int g = 0; g < kDN / kHead; ++g) {
+      const int gcol = n0 + g * kHead;
+      const uint8_t* tile = stage + g * 16384;
+      if constexpr (EPI == kPackedRows) {
+        tma_store_3d(&map_o1, tile, gcol, t0, sq);
+      } else {
+        const int sec = gcol / hidden, hd = (gcol - sec * hidden) / kHead, bh = sq * heads + hd;
+        if (sec < 2) tma_store_3d(&map_o1, tile, 0, t0, sec * BH + bh);
+        else tma_store_3d(&map_o2, tile, t0, bh * kHead, 0);
+      }
+    }
+    tma_store_commit();
+    tma_store_wait_read();
   }
   tc_fence_before();
   __syncthreads();
@@ -253,26 +270,56 @@ int dino_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, ui
   return VA_OK;
 }
 
-int check_dino(int tokens, int hidden, const void* x, const void* w) {
-  VA_CHECK_ARG(tokens > 0 && hidden > 0 && hidden % kHead == 0 && (3 * hidden) % kDN == 0,
+int check_dino(int S, int n, int hidden, const void* x, const void* w) {
+  VA_CHECK_ARG(S > 0 && n > 0 && hidden > 0 && hidden % kHead == 0 && (3 * hidden) % kDN == 0,
                "dinov2 qkv: hidden %d must be a positive multiple of 64", hidden);
-  VA_CHECK_ARG((tokens + kDM - 1) / kDM <= 0x7fffffff && 3 * hidden / kDN <= 65535, "dinov2 qkv: too many tiles");
+  VA_CHECK_ARG(S <= 65535 && 3 * hidden / kDN <= 65535, "dinov2 qkv: too many sequences");
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
     return set_error(VA_ERR_ALIGN, "dinov2 qkv: x and w_qkv need 16-byte alignment");
   return VA_OK;
 }
 
+int map3(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+         uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz, const char* what) {
+  auto fn = dino_encode_fn();
+  if (!fn) return set_error(VA_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+  const uint64_t d[3] = {d0, d1, d2}, s[2] = {s1, s2};
+  const uint32_t bx[3] = {b0, b1, 1}, es[3] = {1, 1, 1};
+  CUresult r = fn(m, dt, 3, const_cast<void*>(base), d, s, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(VA_ERR_ALIGN, "tensor map for %s rejected (CUresult %d)", what, (int)r);
+  return VA_OK;
+}
+
+// x [S][n][hidden] bf16; EPI kSplitHeads: qk f16 [2][S·heads][n][64], vbuf f16
+// [S·heads·64][n_pad]; EPI kPackedRows: out0 bf16 [S][n][3·hidden].
 template <int EPI>
-int launch_qkv(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias, void* out0, __half* vbuf, int M,
-               int hidden, int n_seq, int n_pad, int heads, cudaStream_t st) {
-  CUtensorMap mx, mw;
-  if (int rc = dino_map(&mx, x, (uint64_t)hidden, (uint64_t)M, kDM, "x")) return rc;
+int launch_qkv(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias, void* out0, __half* vbuf, int S,
+               int n, int hidden, int heads, cudaStream_t st) {
+  const int BH = S * heads, n_pad = (n + 7) / 8 * 8;
+  CUtensorMap mx, mw, mo1, mo2;
+  if (int rc = map3(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, hidden, n, S, (uint64_t)hidden * 2,
+                    (uint64_t)n * hidden * 2, 64, kDM, CU_TENSOR_MAP_SWIZZLE_128B, "x"))
+    return rc;
   if (int rc = dino_map(&mw, w, (uint64_t)hidden, (uint64_t)3 * hidden, kDN, "w_qkv")) return rc;
+  if (EPI == kPackedRows) {
+    if (int rc = map3(&mo1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out0, 3 * hidden, n, S, (uint64_t)3 * hidden * 2,
+                      (uint64_t)n * 3 * hidden * 2, kHead, kDM, CU_TENSOR_MAP_SWIZZLE_128B, "qkv out"))
+      return rc;
+    mo2 = mo1;
+  } else {
+    if (int rc = map3(&mo1, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, out0, kHead, n, 2 * (uint64_t)BH, kHead * 2,
+                      (uint64_t)n * kHead * 2, kHead, kDM, CU_TENSOR_MAP_SWIZZLE_128B, "qk out"))
+      return rc;
+    if (int rc = map3(&mo2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, vbuf, n, (uint64_t)BH * kHead, 1, (uint64_t)n_pad * 2,
+                      (uint64_t)n_pad * 2 * BH * kHead, kDM, kHead, CU_TENSOR_MAP_SWIZZLE_NONE, "v out"))
+      return rc;
+  }
   const size_t smem = sizeof(DinoQkvSmem) + 1024;
   cudaError_t e = cudaFuncSetAttribute(dino_qkv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  dino_qkv_kernel<EPI><<<dim3((M + kDM - 1) / kDM, 3 * hidden / kDN), 128, smem, st>>>(mx, mw, bias, out0, vbuf, M,
-                                                                                       hidden, n_seq, n_pad, heads);
+  dino_qkv_kernel<EPI><<<dim3((n + kDM - 1) / kDM, S, 3 * hidden / kDN), 128, smem, st>>>(mx, mw, mo1, mo2, bias,
+                                                                                          hidden, heads, BH);
   return check_launch("dinov2 qkv");
 }
 
@@ -298,16 +345,17 @@ size_t dino_workspace_bytes(int S, int n, int hidden) {
 
 int dino_qkv_linear(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* b, __nv_bfloat16* qkv, int tokens,
                     int hidden, cudaStream_t st) {
-  if (int rc = check_dino(tokens, hidden, x, w)) return rc;
+  // the packed Linear sees the tokens as one sequence (rows are independent)
+  if (int rc = check_dino(1, tokens, hidden, x, w)) return rc;
   if (reinterpret_cast<uintptr_t>(qkv) & 15) return set_error(VA_ERR_ALIGN, "dinov2 qkv: output needs 16-byte alignment");
-  return launch_qkv<kPackedRows>(x, w, b, qkv, nullptr, tokens, hidden, tokens, 0, hidden / kHead, st);
+  return launch_qkv<kPackedRows>(x, w, b, qkv, nullptr, 1, tokens, hidden, hidden / kHead, st);
 }
 
 int dino_attention_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* b, __nv_bfloat16* o, int S, int n,
                        int hidden, int heads, void* ws, size_t ws_bytes, cudaStream_t st) {
   VA_CHECK_ARG(S > 0 && n > 0 && heads > 0 && heads * kHead == hidden, "dinov2 attention: need heads·64 == hidden");
   VA_CHECK_ARG((long long)S * heads <= 65535, "dinov2 attention: %d sequences × %d heads too many", S, heads);
-  if (int rc = check_dino(S * n, hidden, x, w)) return rc;
+  if (int rc = check_dino(S, n, hidden, x, w)) return rc;
   if (reinterpret_cast<uintptr_t>(o) & 15) return set_error(VA_ERR_ALIGN, "dinov2 attention: o needs 16-byte alignment");
   const DinoWs L = dino_layout(S, n, hidden);
   if (!ws || ws_bytes < L.total)
@@ -317,8 +365,7 @@ int dino_attention_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, const flo
   char* base = static_cast<char*>(ws);
   __half* qk = reinterpret_cast<__half*>(base + L.qk);
   __half* vb = reinterpret_cast<__half*>(base + L.v);
-  const int np = (n + 7) / 8 * 8;
-  if (int rc = launch_qkv<kSplitHeads>(x, w, b, qk, vb, S * n, hidden, n, np, heads, st)) return rc;
+  if (int rc = launch_qkv<kSplitHeads>(x, w, b, qk, vb, S, n, hidden, heads, st)) return rc;
   return tc_flash_attention(qk, vb, o, nullptr, S * heads, heads, n, kHead, 1, st);
 }
 

@@ -492,6 +492,246 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
+// ── Kernel 2s: attention over many short sequences (N ≤ 128) ───────────────
+// A sequence fits one 128-key tile, so there is no online rescale and no K/V
+// ring.  The CTA is persistent: its two groups each walk their own stream of
+// (sequence, head) items, item i of group g being
+// (2·blockIdx.x + g) + i·2·gridDim.x.  Per group, Q/K/V of two consecutive
+// items are double-buffered in shared memory.
+//   warps 0-15 : softmax, 8 per group, two warps per query row (as attn_kernel)
+//   warp 16    : TMA producer
+//   warps 17/18: MMA issuer of group 0 / 1
+// Per item: S = Q·Kᵀ → softmax (row max and row sum exchanged between the two
+// warps of a row) → P (f16, TMEM) → O = P·V → O/l stored.
+constexpr int kShortThreads = 19 * 32;
+
+template <int KD>
+struct ShortSmem {
+  static constexpr int kQK = kTile * KD * 2;
+  uint8_t q[2][2][kQK];         // [group][buffer]
+  uint8_t k[2][2][kQK];
+  uint8_t v[2][2][2][kVBlk];    // [group][buffer][key block]
+  float xmax[2][2][2][kTile];   // [item parity][group][half][row]
+  float xsum[2][2][2][kTile];
+  uint64_t load_full[2][2], buf_free[2][2], s_full[2], p_full[2], o_full[2], o_free[2], xbar[2], sbar[2], fin[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int KD, int OUT>
+__global__ void __launch_bounds__(kShortThreads, 1)
+attn_short_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v,
+                  void* __restrict__ obuf, float* __restrict__ lse, int N, int Np, int nh, int BH, float scale_log2) {
+  constexpr int kQK = ShortSmem<KD>::kQK;
+  extern __shared__ uint8_t smem_raw[];
+  ShortSmem<KD>& sm =
+      *reinterpret_cast<ShortSmem<KD>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  auto item_of = [&](int g, int i) { return (2 * (int)blockIdx.x + g) + i * 2 * (int)gridDim.x; };
+  auto count_of = [&](int g) {
+    const int first = 2 * (int)blockIdx.x + g, step = 2 * (int)gridDim.x;
+    return first < BH ? (BH - first + step - 1) / step : 0;
+  };
+
+  if (tid == 0) {
+    for (int g = 0; g < 2; ++g) {
+      for (int b2 = 0; b2 < 2; ++b2) {
+        mbar_init(&sm.load_full[g][b2], 1);
+        mbar_init(&sm.buf_free[g][b2], 1);
+      }
+      mbar_init(&sm.s_full[g], 1);
+      mbar_init(&sm.p_full[g], 256);
+      mbar_init(&sm.o_full[g], 1);
+      mbar_init(&sm.o_free[g], 256);
+      mbar_init(&sm.xbar[g], 256);
+      mbar_init(&sm.sbar[g], 256);
+      mbar_init(&sm.fin[g], 1);
+    }
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 16) {
+    if (lane == 0) {  // ── TMA producer: both groups, item by item ──
+      tma_prefetch_desc(&map_qk);
+      tma_prefetch_desc(&map_v);
+      const int n0c = count_of(0), n1c = count_of(1), nmax = max(n0c, n1c);
+      int issued[2] = {0, 0};
+      bool ok = true;
+      for (int i = 0; ok && i < nmax; ++i) {
+        for (int g = 0; g < 2; ++g) {
+          if (i >= (g ? n1c : n0c)) continue;
+          const int bf = i & 1;
+          if (i >= 2 && !(ok = mbar_wait(&sm.buf_free[g][bf], ((i >> 1) - 1) & 1, &sm.abort, &g_tc_status, 60)))
+            break;
+          const int bh = item_of(g, i);
+          mbar_arrive_expect_tx(&sm.load_full[g][bf], 2 * kQK + 2 * kVBlk);
+          tma_load_3d(sm.q[g][bf], &map_qk, &sm.load_full[g][bf], 0, 0, bh);
+          tma_load_3d(sm.k[g][bf], &map_qk, &sm.load_full[g][bf], 0, 0, BH + bh);
+          tma_load_2d(sm.v[g][bf][0], &map_v, &sm.load_full[g][bf], 0, bh * kHD);
+          tma_load_2d(sm.v[g][bf][1], &map_v, &sm.load_full[g][bf], 64, bh * kHD);
+          ++issued[g];
+        }
+      }
+      if (!ok) {  // wait (bounded) for the loads of the last two items of each group
+        for (int g = 0; g < 2; ++g)
+          for (int i = max(0, issued[g] - 2); i < issued[g]; ++i) {
+            const long long t0 = clock64();
+            while (!mbar_try_wait(&sm.load_full[g][i & 1], (i >> 1) & 1) && clock64() - t0 < kSpinCycles) {
+            }
+          }
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 17) {
+    const int g = warp - 17;
+    if (lane == 0) {  // ── MMA issuer of group g ──
+      constexpr uint32_t idS = idesc_f32acc(128, kTile, AB_F16, false, false);
+      constexpr uint32_t idO = idesc_f32acc(128, kHD, AB_F16, false, false);
+      constexpr uint32_t kSbo = KD == 32 ? 512 : 1024;
+      constexpr uint32_t kSwz = KD == 32 ? SW_64B : SW_128B;
+      constexpr uint32_t kVHalf = kVBlk >> 4;
+      const uint32_t ds = tmem + col_s(g), dp = tmem + col_p(g), dO = tmem + col_o(g);
+      const int cnt = count_of(g);
+      bool ok = true;
+      for (int i = 0; i < cnt; ++i) {
+        const int bf = i & 1;
+        if (!(ok = mbar_wait(&sm.load_full[g][bf], (i >> 1) & 1, &sm.abort, &g_tc_status, 61))) break;
+        tc_fence_after();
+        const uint64_t dq = sdesc(smem_u32(sm.q[g][bf]), 16, kSbo, kSwz);
+        const uint64_t dk = sdesc(smem_u32(sm.k[g][bf]), 16, kSbo, kSwz);
+        const uint64_t dv = sdesc(smem_u32(sm.v[g][bf][0]), 16, 1024, SW_128B);
+        mma_ss(ds, dq, dk, idS, 0u);
+#pragma unroll
+        for (int s = 1; s < KD / 16; ++s) mma_ss(ds, dq + 2 * s, dk + 2 * s, idS, 1u);
+        mma_commit(&sm.s_full[g]);
+        if (!(ok = mbar_wait(&sm.p_full[g], i & 1, &sm.abort, &g_tc_status, 62))) break;
+        if (i > 0 && !(ok = mbar_wait(&sm.o_free[g], (i - 1) & 1, &sm.abort, &g_tc_status, 63))) break;
+        tc_fence_after();
+        mma_ts(dO, dp, dv, idO, 0u);
+#pragma unroll
+        for (int s = 1; s < kTile / 16; ++s)
+          mma_ts(dO, dp + s * 8, dv + (uint64_t)((s >> 2) * kVHalf + (s & 3) * 2), idO, 1u);
+        mma_commit(&sm.o_full[g]);
+        mma_commit(&sm.buf_free[g][bf]);
+      }
+      mma_commit(&sm.fin[g]);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(&sm.fin[g], 0) && clock64() - t0 < kSpinCycles) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // ── softmax: group g, key half hf, thread = query row (TMEM lane) ──
+    const int g = warp >> 3, hf = (warp >> 2) & 1, row = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t sc = tmem + lane_off + col_s(g) + hf * kHalf;
+    const uint32_t pc = tmem + lane_off + col_p(g) + hf * (kHalf / 2);
+    const uint32_t oc = tmem + lane_off + col_o(g) + hf * (kHD / 2);
+    const int cnt = count_of(g);
+    const int kvalid = N - hf * kHalf;
+    bool ok = true;
+    for (int i = 0; i < cnt; ++i) {
+      const int par = i & 1, bh = item_of(g, i);
+      if (!(ok = mbar_wait(&sm.s_full[g], par, &sm.abort, &g_tc_status, 64))) break;
+      tc_fence_after();
+      float sv[kHalf];
+      {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(sc + 0, r0);
+        tmem_ld32(sc + 32, r1);
+        tmem_ld_wait();
+        reg_fence(r0);
+        reg_fence(r1);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          sv[c] = __uint_as_float(r0[c]);
+          sv[32 + c] = __uint_as_float(r1[c]);
+        }
+      }
+      if (kvalid < kHalf) {
+#pragma unroll
+        for (int c = 0; c < kHalf; ++c)
+          if (c >= kvalid) sv[c] = -INFINITY;
+      }
+      float mx[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx[e] = max3(sv[e], sv[8 + e], sv[16 + e]);
+#pragma unroll
+      for (int c = 24; c < kHalf - 8; c += 16)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx[e] = max3(mx[e], sv[c + e], sv[c + 8 + e]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], sv[kHalf - 8 + e]);
+      const float pmax = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+      sm.xmax[par][g][hf][row] = pmax;
+      mbar_arrive(&sm.xbar[g]);
+      if (!(ok = mbar_wait(&sm.xbar[g], par, &sm.abort, &g_tc_status, 65))) break;
+      const float m = fmaxf(pmax, sm.xmax[par][g][hf ^ 1][row]) * scale_log2;
+      float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < kHalf / 32; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], scale_log2, -m));
+          const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], scale_log2, -m));
+          ls0 += p0;
+          ls1 += p1;
+          pk[e] = pack_f16x2(p0, p1);
+        }
+        tmem_st16(pc + c * 16, pk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&sm.p_full[g]);
+      const float ls = ls0 + ls1;
+      sm.xsum[par][g][hf][row] = ls;
+      mbar_arrive(&sm.sbar[g]);
+      if (!(ok = mbar_wait(&sm.sbar[g], par, &sm.abort, &g_tc_status, 66))) break;
+      const float l = ls + sm.xsum[par][g][hf ^ 1][row];
+      if (!(ok = mbar_wait(&sm.o_full[g], par, &sm.abort, &g_tc_status, 67))) break;
+      tc_fence_after();
+      uint32_t o[32];
+      tmem_ld32(oc, o);
+      tmem_ld_wait();
+      reg_fence(o);
+      tc_fence_before();
+      mbar_arrive(&sm.o_free[g]);
+      const float inv = 1.0f / l;
+      if (row < N) {
+        if constexpr (OUT == kOutChannelMajor) {
+          __half* dst = static_cast<__half*>(obuf) + ((size_t)bh * kHD + hf * 32) * Np + row;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) dst[(size_t)c * Np] = __float2half_rn(__uint_as_float(o[c]) * inv);
+        } else {
+          const int b = bh / nh, h = bh % nh;
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(obuf) + ((size_t)b * N + row) * (nh * kHD) +
+                                                h * kHD + hf * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                                pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                                pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                                pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+        }
+        if (lse && hf == 0) lse[(size_t)bh * N + row] = (m + __log2f(l)) * 0.6931471805599453f;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
 // ── Kernel 3: positional encoding (depthwise 3×3 + bias) ───────────────────
 // One CTA per (image, group of kPeCh channels).  Each channel plane is read
 // with 16-byte loads (all in flight at once), widened to f32 into a zero-
@@ -897,6 +1137,19 @@ int tc_flash_attention(const void* qk, const void* v, void* o, float* lse, int B
       return rc;
   }
   const float scale_log2 = (1.0f / sqrtf((float)kd)) * 1.4426950408889634f;
+  if (N <= kTile) {  // one key tile per sequence: persistent short-sequence kernel
+    const int ctas = std::min((BH + 1) / 2, 148);
+    auto launch_short = [&](auto kernel, size_t smem) -> int {
+      if (int rc = set_smem(kernel, smem)) return rc;
+      kernel<<<ctas, kShortThreads, smem, st>>>(mqk, mv, o, lse, N, Np, nh, BH, scale_log2);
+      return check_launch("short-sequence attention");
+    };
+    if (kd == 32)
+      return out_token_major ? launch_short(attn_short_kernel<32, kOutTokenMajor>, sizeof(ShortSmem<32>) + 1024)
+                             : launch_short(attn_short_kernel<32, kOutChannelMajor>, sizeof(ShortSmem<32>) + 1024);
+    return out_token_major ? launch_short(attn_short_kernel<64, kOutTokenMajor>, sizeof(ShortSmem<64>) + 1024)
+                           : launch_short(attn_short_kernel<64, kOutChannelMajor>, sizeof(ShortSmem<64>) + 1024);
+  }
   const dim3 grid(((N + kTile - 1) / kTile + 1) / 2, BH);
   auto launch = [&](auto kernel, size_t smem) -> int {
     if (int rc = set_smem(kernel, smem)) return rc;
