@@ -16,12 +16,14 @@
 // fix the cls handling of windowed layers; this is the choice made here.
 //
 // Kernels:
-//  1. dino_qkv_kernel<EPI>  — D[128 tokens × 192 features] per CTA, K streamed
-//     in 64-wide blocks through a 2-stage TMA ring, accumulator in TMEM
-//     (192 columns), 2 CTAs per SM so one CTA's epilogue overlaps the other's
-//     main loop.  EPI kSplitHeads writes Q and K f16 [2][S·heads][n][64] and
-//     V f16 transposed [S·heads·64][n_pad] (the flash-attention operands);
-//     EPI kPackedRows writes bf16 [tokens][3·hidden] (torch Linear layout).
+//  1. dino_qkv_kernel<EPI>  — per CTA a 128-token tile of one sequence times
+//     half of W_qkv, 192 features per MMA tile (three heads), x and W k
+//     blocks streamed through a TMA ring, two TMEM
+//     accumulators so the epilogue overlaps the next tile's MMAs, output
+//     staged in shared memory and written by TMA stores.  EPI kSplitHeads
+//     writes Q and K f16 [2][S·heads][n][64] and V f16 transposed
+//     [S·heads·64][n_pad] (the flash-attention operands); EPI kPackedRows
+//     writes bf16 [S][n][3·hidden] (torch Linear layout).
 //  2. window partition / un-partition (bf16 token gathers, 16-byte moves).
 #include <cudaTypedefs.h>
 
@@ -39,21 +41,31 @@ __device__ int g_dino_status;
 namespace {
 
 constexpr int kDM = 128;      // tokens per tile (UMMA M)
-constexpr int kDN = 192;      // features per tile (UMMA N): three heads of 64
-constexpr int kDStages = 2;
+constexpr int kDN = 192;      // features per N tile (UMMA N): three heads of 64
+constexpr int kWStages = 4;   // (x, W) k-block ring
+constexpr int kNSplit = 2;    // CTAs sharing one token tile's N tiles
 constexpr int kHead = 64;
 constexpr int kSplitHeads = 0, kPackedRows = 1;
+constexpr int kQkvThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 
 struct DinoQkvSmem {
-  uint8_t a[kDStages][kDM * 128];  // x block: 128 tokens × 64 features bf16, K-major SW128 (16 KB)
-  uint8_t b[kDStages][kDN * 128];  // W block: 192 rows × 64 features (24 KB)
-  uint64_t full[kDStages], empty[kDStages], mma_done;
+  uint8_t x[kWStages][kDM * 128];     // x block: 128 tokens × 64 features, K-major SW128 (16 KB)
+  uint8_t w[kWStages][kDN * 128];     // W block: 192 rows × 64 features (24 KB)
+  uint8_t stage[3][kDM * 128];        // epilogue staging: three 16 KB head groups
+  uint64_t w_full[kWStages], w_empty[kWStages], acc_full[2], acc_empty[2], fin;
+  uint64_t stage_free, stage_full;  // staging handshakes between the epilogue warps and the storing thread
   uint32_t tmem_base;
   int abort;
 };
 
+// One CTA per (token tile of a sequence, half of the N tiles).  The 64-wide
+// k blocks of x and W stream through a 4-stage TMA ring (x blocks are re-read
+// from L2 for each N tile); two TMEM accumulators (192 columns each) let the
+// epilogue of one N tile overlap the MMAs of the next.  The epilogue stages each 128 × 192
+// tile as three 16 KB head groups and writes them with TMA stores (rows past
+// the sequence end are not written).
 template <int EPI>
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(kQkvThreads, 1)
 dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ CUtensorMap map_o1, const __grid_constant__ CUtensorMap map_o2,
                 const float* __restrict__ bias, int hidden, int heads, int BH) {
@@ -61,20 +73,28 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
   DinoQkvSmem& sm =
       *reinterpret_cast<DinoQkvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t0 = blockIdx.x * kDM, sq = blockIdx.y, n0 = blockIdx.z * kDN;  // tokens of sequence sq
-  const int nk = hidden / 64;
+  const int t0 = blockIdx.x * kDM, sq = blockIdx.y;
+  const int nk = hidden / 64, ntiles = 3 * hidden / kDN;
+  const int nt_lo = blockIdx.z * ntiles / kNSplit, nt_hi = (blockIdx.z + 1) * ntiles / kNSplit;
+  const int my_tiles = nt_hi - nt_lo;
 
   if (tid == 0) {
-    for (int i = 0; i < kDStages; ++i) {
-      mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], 1);
+    for (int i = 0; i < kWStages; ++i) {
+      mbar_init(&sm.w_full[i], 1);
+      mbar_init(&sm.w_empty[i], 1);
     }
-    mbar_init(&sm.mma_done, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sm.acc_full[a], 1);
+      mbar_init(&sm.acc_empty[a], 128);
+    }
+    mbar_init(&sm.fin, 1);
+    mbar_init(&sm.stage_free, 1);
+    mbar_init(&sm.stage_full, 128);
     sm.abort = 0;
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(&sm.tmem_base, 256);
+    tmem_alloc(&sm.tmem_base, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -82,111 +102,132 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  if (warp == 0 && lane == 0) {
-    // ── TMA producer ──
-    tma_prefetch_desc(&map_x);
-    tma_prefetch_desc(&map_w);
-    int issued = 0;
-    bool ok = true;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int st = kb % kDStages;
-      if (kb >= kDStages &&
-          !(ok = mbar_wait(&sm.empty[st], ((kb / kDStages) - 1) & 1, &sm.abort, &g_dino_status, 1)))
-        break;
-      mbar_arrive_expect_tx(&sm.full[st], kDM * 128 + kDN * 128);
-      tma_load_3d(sm.a[st], &map_x, &sm.full[st], kb * 64, t0, sq);
-      tma_load_2d(sm.b[st], &map_w, &sm.full[st], kb * 64, n0);
-      ++issued;
-    }
-    if (!ok) {  // let every load issued here land (bounded) before the CTA can exit
-      for (int kb = max(0, issued - kDStages); kb < issued; ++kb) {
-        const long long t0c = clock64();
-        while (!mbar_try_wait(&sm.full[kb % kDStages], (kb / kDStages) & 1) && clock64() - t0c < kSpinCycles) {
+  if (warp == 0) {
+    if (lane == 0) {  // ── TMA producer ──
+      tma_prefetch_desc(&map_x);
+      tma_prefetch_desc(&map_w);
+      const int total = my_tiles * nk;
+      int issued = 0;
+      bool ok = true;
+      for (int g = 0; g < total; ++g) {
+        const int st = g % kWStages, nt = nt_lo + g / nk, kb = g % nk;
+        if (g >= kWStages &&
+            !(ok = mbar_wait(&sm.w_empty[st], ((g / kWStages) - 1) & 1, &sm.abort, &g_dino_status, 1)))
+          break;
+        mbar_arrive_expect_tx(&sm.w_full[st], kDM * 128 + kDN * 128);
+        tma_load_3d(sm.x[st], &map_x, &sm.w_full[st], kb * 64, t0, sq);
+        tma_load_2d(sm.w[st], &map_w, &sm.w_full[st], kb * 64, nt * kDN);
+        ++issued;
+      }
+      if (!ok) {  // loads issued here land (bounded) before the CTA can exit
+        for (int g = max(0, issued - kWStages); g < issued; ++g) {
+          const long long c0 = clock64();
+          while (!mbar_try_wait(&sm.w_full[g % kWStages], (g / kWStages) & 1) && clock64() - c0 < kSpinCycles) {
+          }
         }
       }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ── MMA issuer ──
-    constexpr uint32_t idesc = idesc_f32acc(kDM, kDN, AB_BF16, false, false);
-    const uint64_t da0 = sdesc(smem_u32(sm.a[0]), 16, 1024, SW_128B);
-    const uint64_t db0 = sdesc(smem_u32(sm.b[0]), 16, 1024, SW_128B);
-    constexpr uint32_t kAS = (kDM * 128) >> 4, kBS = (kDN * 128) >> 4;
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {  // ── MMA issuer ──
+      constexpr uint32_t idesc = idesc_f32acc(kDM, kDN, AB_BF16, false, false);
+      const uint64_t dx0 = sdesc(smem_u32(sm.x[0]), 16, 1024, SW_128B);
+      const uint64_t dw0 = sdesc(smem_u32(sm.w[0]), 16, 1024, SW_128B);
+      constexpr uint32_t kXS = (kDM * 128) >> 4, kWS = (kDN * 128) >> 4;
+      bool ok = true;
+      for (int t = 0; ok && t < my_tiles; ++t) {
+        const int a = t & 1;
+        if (t >= 2 && !(ok = mbar_wait(&sm.acc_empty[a], ((t >> 1) - 1) & 1, &sm.abort, &g_dino_status, 3))) break;
+        for (int kb = 0; kb < nk; ++kb) {
+          const int g = t * nk + kb, st = g % kWStages;
+          if (!(ok = mbar_wait(&sm.w_full[st], (g / kWStages) & 1, &sm.abort, &g_dino_status, 4))) break;
+          tc_fence_after();
+          const uint64_t da = dx0 + (uint64_t)(st * kXS), db = dw0 + (uint64_t)(st * kWS);
+#pragma unroll
+          for (int s = 0; s < 4; ++s)
+            mma_ss(tmem + a * 256, da + 2 * s, db + 2 * s, idesc, (kb > 0 || s > 0) ? 1u : 0u);
+          mma_commit(&sm.w_empty[st]);
+        }
+        if (ok) mma_commit(&sm.acc_full[a]);
+      }
+      mma_commit(&sm.fin);  // every MMA issued here completes before the CTA tears down
+      const long long c0 = clock64();
+      while (!mbar_try_wait(&sm.fin, 0) && clock64() - c0 < kSpinCycles) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // ── epilogue warps 2-5: TMEM lane quarter = warp % 4 ──
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const bool storer = (warp == 2 && lane == 0);
     bool ok = true;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int st = kb % kDStages;
-      if (!(ok = mbar_wait(&sm.full[st], (kb / kDStages) & 1, &sm.abort, &g_dino_status, 2))) break;
+    for (int t = 0; t < my_tiles; ++t) {
+      const int a = t & 1, n0 = (nt_lo + t) * kDN;
+      if (!(ok = mbar_wait(&sm.acc_full[a], (t >> 1) & 1, &sm.abort, &g_dino_status, 5))) break;
       tc_fence_after();
-      const uint64_t da = da0 + (uint64_t)(st * kAS), db = db0 + (uint64_t)(st * kBS);
-#pragma unroll
-      for (int s = 0; s < 4; ++s) mma_ss(tmem, da + 2 * s, db + 2 * s, idesc, (kb > 0 || s > 0) ? 1u : 0u);
-      mma_commit(&sm.empty[st]);
-    }
-    mma_commit(&sm.mma_done);  // also after an abort: every MMA issued here has completed when it fires
-  }
-  __syncwarp();
-  const bool ok = mbar_wait(&sm.mma_done, 0, &sm.abort, &g_dino_status, 3) && !sm.abort;
-  tc_fence_after();
-
-  // Epilogue: stage the 128 × 192 tile in the (now idle) pipeline buffers as
-  // three 16 KB sub-tiles, one per 64-feature head group, then TMA-store them.
-  //   Q/K (split) and packed rows: [128 tokens][64] SW128 (row = token)
-  //   V (split): [64 d][128 tokens] plain, i.e. transposed
-  uint8_t* stage = sm.a[0];
-  if (ok) {
-    const int row = warp * 32 + lane;
+      if (storer) {  // the previous tile's stores have read the staging buffer
+        tma_store_wait_read();
+        mbar_arrive(&sm.stage_free);
+      }
+      if (!(ok = mbar_wait(&sm.stage_free, t & 1, &sm.abort, &g_dino_status, 6))) break;
 #pragma unroll 1
-    for (int c = 0; c < kDN / 32; ++c) {
-      uint32_t u[32];
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, u);
-      tmem_ld_wait();
-      reg_fence(u);
-      const int g = c >> 1, half = c & 1, col = n0 + c * 32;
-      float v[32];
+      for (int c = 0; c < kDN / 32; ++c) {
+        uint32_t u[32];
+        tmem_ld32(tmem + lane_off + a * 256 + c * 32, u);
+        tmem_ld_wait();
+        reg_fence(u);
+        const int g = c >> 1, half = c & 1, col = n0 + c * 32;
+        float v[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(u[i]) + __ldg(bias + col + i);
-      uint8_t* tile = stage + g * 16384;
-      const bool vsec = EPI == kSplitHeads && (n0 + g * kHead) / hidden == 2;
-      if (vsec) {
-        __half* tv = reinterpret_cast<__half*>(tile);
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(u[i]) + __ldg(bias + col + i);
+        uint8_t* tile = sm.stage[g];
+        const bool vsec = EPI == kSplitHeads && (n0 + g * kHead) / hidden == 2;
+        if (vsec) {
+          __half* tv = reinterpret_cast<__half*>(tile);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          tv[(half * 32 + i) * kDM + row] = __ushort_as_half((unsigned short)(pack_f16x2_sat(v[i], 0.f) & 0xffffu));
-      } else {
+          for (int i = 0; i < 32; ++i)
+            tv[(half * 32 + i) * kDM + row] = __ushort_as_half((unsigned short)(pack_f16x2_sat(v[i], 0.f) & 0xffffu));
+        } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 w4;
-          if constexpr (EPI == kPackedRows)
-            w4 = make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
-                            pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
-          else
-            w4 = make_uint4(pack_f16x2_sat(v[8 * q], v[8 * q + 1]), pack_f16x2_sat(v[8 * q + 2], v[8 * q + 3]),
-                            pack_f16x2_sat(v[8 * q + 4], v[8 * q + 5]), pack_f16x2_sat(v[8 * q + 6], v[8 * q + 7]));
-          *reinterpret_cast<uint4*>(tile + sw128_off(row, half * 4 + q)) = w4;
+          for (int q = 0; q < 4; ++q) {
+            uint4 w4;
+            if constexpr (EPI == kPackedRows)
+              w4 = make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                              pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+            else
+              w4 = make_uint4(pack_f16x2_sat(v[8 * q], v[8 * q + 1]), pack_f16x2_sat(v[8 * q + 2], v[8 * q + 3]),
+                              pack_f16x2_sat(v[8 * q + 4], v[8 * q + 5]), pack_f16x2_sat(v[8 * q + 6], v[8 * q + 7]));
+            *reinterpret_cast<uint4*>(tile + sw128_off(row, half * 4 + q)) = w4;
+          }
         }
       }
-    }
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (ok && tid == 0) {
+      tc_fence_before();
+      mbar_arrive(&sm.acc_empty[a]);
+      fence_proxy_async_smem();
+      mbar_arrive(&sm.stage_full);
+      if (storer) {
+        if (!(ok = mbar_wait(&sm.stage_full, t & 1, &sm.abort, &g_dino_status, 7))) break;
 #pragma unroll 1
-    for (int g = 0; g < kDN / kHead; ++g) {
-      const int gcol = n0 + g * kHead;
-      const uint8_t* tile = stage + g * 16384;
-      if constexpr (EPI == kPackedRows) {
-        tma_store_3d(&map_o1, tile, gcol, t0, sq);
-      } else {
-        const int sec = gcol / hidden, hd = (gcol - sec * hidden) / kHead, bh = sq * heads + hd;
-        if (sec < 2) tma_store_3d(&map_o1, tile, 0, t0, sec * BH + bh);
-        else tma_store_3d(&map_o2, tile, t0, bh * kHead, 0);
+        for (int g = 0; g < kDN / kHead; ++g) {
+          const int gcol = n0 + g * kHead;
+          if constexpr (EPI == kPackedRows) {
+            tma_store_3d(&map_o1, sm.stage[g], gcol, t0, sq);
+          } else {
+            const int sec = gcol / hidden, hd = (gcol - sec * hidden) / kHead, bh = sq * heads + hd;
+            if (sec < 2) tma_store_3d(&map_o1, sm.stage[g], 0, t0, sec * BH + bh);
+            else tma_store_3d(&map_o2, sm.stage[g], t0, bh * kHead, 0);
+          }
+        }
+        tma_store_commit();
       }
     }
-    tma_store_commit();
-    tma_store_wait_read();
+    if (storer) tma_store_wait_read();
+    (void)ok;
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 256);
+  if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 // ── window partition / un-partition ─────────────────────────────────────────
@@ -318,8 +359,8 @@ int launch_qkv(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias
   const size_t smem = sizeof(DinoQkvSmem) + 1024;
   cudaError_t e = cudaFuncSetAttribute(dino_qkv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  dino_qkv_kernel<EPI><<<dim3((n + kDM - 1) / kDM, S, 3 * hidden / kDN), 128, smem, st>>>(mx, mw, mo1, mo2, bias,
-                                                                                          hidden, heads, BH);
+  dino_qkv_kernel<EPI><<<dim3((n + kDM - 1) / kDM, S, kNSplit), kQkvThreads, smem, st>>>(mx, mw, mo1, mo2, bias,
+                                                                                            hidden, heads, BH);
   return check_launch("dinov2 qkv");
 }
 
