@@ -336,6 +336,31 @@ class Cfg3:
         for o, h in zip(outs, self.oh):
             h.copy_(o, non_blocking=True)
 
+    def e2e_pipelined(self, steps):
+        import torch
+        keys = ("value", "loc", "attn", "grad_out")
+        dev = [{k: self.d[k] for k in keys}, {k: torch.empty_like(self.d[k]) for k in keys}]
+        self._run()
+        outs = [[torch.empty_like(self.out)] + [torch.empty_like(g) for g in self.g] for _ in range(2)]
+        if not hasattr(self, "oh"):
+            self.oh = [o.cpu().pin_memory() for o in outs[0]]
+
+        def h2d(b, st):
+            for k in keys:
+                dev[b][k].copy_(self.h[k], non_blocking=True)
+
+        def compute(b, st):
+            d = dev[b]
+            a = (d["value"], self.d["spatial_shapes"], self.d["level_start"], d["loc"], d["attn"])
+            self.ms.msdeform_attn_forward(*a, out=outs[b][0], stream=st)
+            self.ms.msdeform_attn_backward(*a, d["grad_out"], workspace=self.ws, stream=st, out=tuple(outs[b][1:]))
+
+        def d2h(b, st):
+            for o, h in zip(outs[b], self.oh):
+                h.copy_(o, non_blocking=True)
+
+        return pipelined_e2e_ms(steps, h2d, compute, d2h)
+
     def io_bytes(self):
         h2d = sum(v.numel() * v.element_size() for v in self.h.values())
         self._run()

@@ -33,15 +33,20 @@ def msdeform_attn_workspace_bytes(B, nh, L, Q, P) -> int:
     return int(_lib.lib().va_msdeform_attn_bwd_workspace_bytes(B, nh, L, Q, P))
 
 
-def msdeform_attn_backward(value, spatial_shapes, level_start, loc, attn, grad_out, workspace=None, stream=None):
-    """Returns ``(grad_value, grad_loc, grad_attn)`` (deterministic, no atomics)."""
+def msdeform_attn_backward(value, spatial_shapes, level_start, loc, attn, grad_out, workspace=None, stream=None,
+                           out=None):
+    """Returns ``(grad_value, grad_loc, grad_attn)`` (deterministic, no atomics);
+    ``out`` may supply those three tensors."""
     B, S, nh, dh, L, Q, P = _dims(value, loc)
     need = msdeform_attn_workspace_bytes(B, nh, L, Q, P)
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(need, dtype=torch.uint8, device=value.device)
-    gv = torch.empty_like(value)
-    gl = torch.empty_like(loc)
-    ga = torch.empty_like(attn)
+    if out is not None:
+        gv, gl, ga = out
+    else:
+        gv = torch.empty_like(value)
+        gl = torch.empty_like(loc)
+        ga = torch.empty_like(attn)
     _lib.call(f"va_msdeform_attn_bwd_{_sfx(value)}", _p(value), _p(spatial_shapes), _p(level_start), _p(loc),
               _p(attn), _p(grad_out), _p(gv), _p(gl), _p(ga), B, S, nh, dh, L, Q, P, _p(workspace),
               workspace.numel(), _stream(stream))
