@@ -385,4 +385,4 @@ def psa_train_step_torch(x, target, params: dict, num_heads: int = 2, key_dim: i
     loss = ((y - t(target)) ** 2).mean()
     loss.backward()
     grads = np.concatenate([p[k].grad.numpy().reshape(-1) for k in GRAD_ORDER])
-    return y.detach().numpy(), float(loss), grads, xt.grad.numpy()
+    return y.detach().numpy(), float(loss.detach()), grads, xt.grad.numpy()

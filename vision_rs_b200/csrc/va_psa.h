@@ -58,9 +58,9 @@ int gemm_status_read(int* out, cudaStream_t st);
 // Tensor-core PSA attention backward (nh = 2, kd = 32, N ≤ 512), channel-major
 // f32 outputs: dk [B·nh][32][N], dv [B·nh][64][N], dq_part
 // [ceil(N/128)][B·nh][32][N] (sum over the first index = dQ).  qk, v, o, d_o
-// in the forward's f16 layouts.
-int psa_attn_bwd_tc(const void* qk, const void* v, const void* o, const void* d_o, const float* lse, float* dk,
-                    float* dv, float* dq_part, int B, int nh, int N, cudaStream_t st);
+// in the forward's f16 layouts; delta: f32 [B·nh][N] scratch.
+int psa_attn_bwd_tc(const void* qk, const void* v, const void* o, const void* d_o, const float* lse, float* delta,
+                    float* dk, float* dv, float* dq_part, int B, int nh, int N, cudaStream_t st);
 int bwd_status_read(int* out, cudaStream_t st);
 int bwd_status_clear(cudaStream_t st);
 int gemm_status_clear(cudaStream_t st);

@@ -383,7 +383,8 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   float *dk = fa, *dv = fa + fsz, *dqp = fa + 3 * fsz;
   int nparts = 1;
   if (N <= 512) {
-    if (int rc = psa_attn_bwd_tc(qk, vb, ob, dA, lse, dk, dv, dqp, B, nh, N, st)) return rc;
+    float* delta = fa + 7 * fsz;  // [B·nh][N] ≤ fsz floats
+    if (int rc = psa_attn_bwd_tc(qk, vb, ob, dA, lse, delta, dk, dv, dqp, B, nh, N, st)) return rc;
     nparts = (N + 127) / 128;
   } else {  // f32 SIMT kernels, one call per V half (dq and dk accumulate), then channel-major
     float *q32 = fa + 4 * fsz, *k32 = fa + 5 * fsz, *vh = fa + 6 * fsz, *oh = fa + 8 * fsz, *doh = fa + 10 * fsz;

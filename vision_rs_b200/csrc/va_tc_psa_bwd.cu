@@ -3,7 +3,7 @@
 // Replaces the reference's psa_fa2_backward pair (psa.rs:650-725: one call
 // per 32-wide V half, dQ/dK accumulated with atomic_add) by one kernel over
 // the full 64-wide V, with no atomics.  Per (b, h) and scale s = 1/√32:
-//   P = exp(s·Q·Kᵀ − lse),  dP = dO·Vᵀ,  Δ = rowsum(dO ⊙ O),
+//   P = exp(s·Q·Kᵀ − lse),  dP = dO·Vᵀ,  Δ = rowsum(dO ⊙ O) (psa_delta_kernel),
 //   dS = P ⊙ (dP − Δ),  dV = Pᵀ·dO,  dK = s·dSᵀ·Q,  dQ = s·dS·K.
 //
 // Work split: one CTA per (key tile j of 128 keys, b·h).  The CTA holds the Q
@@ -49,7 +49,7 @@ struct BwdSmem {
   uint8_t v[2][64 * 128];              // V_jᵀ: 2 blocks [64 d × 64 keys], SW128
   uint8_t p[2][kT * 128];              // P: 2 key blocks [128 q × 64 keys] f16, SW128 (32 KB)
   uint8_t ds[2][kT * 128];             // dS (×256)
-  float dhalf[2][kMaxTiles][kT];       // Δ partial sums (d < 32, d ≥ 32)
+  float delta[kMaxTiles][kT];          // Δ = rowsum(dO ⊙ O)
   float lse2[kMaxTiles][kT];           // lse·log2(e)
   uint64_t load_full, s_full, s_free, p_full, p_free, done;
   uint32_t tmem_base;
@@ -62,9 +62,9 @@ __device__ __forceinline__ void named_sync_compute() { asm volatile("bar.sync 1,
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
 psa_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v,
-                    const __grid_constant__ CUtensorMap map_do, const __half* __restrict__ obuf,
-                    const __half* __restrict__ dobuf, const float* __restrict__ lse, float* __restrict__ dk_out,
-                    float* __restrict__ dv_out, float* __restrict__ dq_part, int N, int Np, float scale) {
+                    const __grid_constant__ CUtensorMap map_do, const float* __restrict__ delta,
+                    const float* __restrict__ lse, float* __restrict__ dk_out, float* __restrict__ dv_out,
+                    float* __restrict__ dq_part, int N, int Np, float scale) {
   extern __shared__ uint8_t smem_raw[];
   BwdSmem& sm = *reinterpret_cast<BwdSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -173,18 +173,11 @@ psa_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_con
     const int row = (warp & 3) * 32 + lane, hf = warp >> 2;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const float scale_log2 = scale * 1.4426950408889634f;
-    // Δ = rowsum(dO ⊙ O) (each half sums 32 channels) and lse·log2(e)
-    for (int i = 0; i < nt; ++i) {
+    // Δ (computed by psa_delta_kernel) and lse·log2(e) of every query row
+    for (int i = hf; i < nt; i += 2) {
       const int q = i * kT + row;
-      float acc = 0.f;
-      if (q < N) {
-        const size_t base = (size_t)(vrow + hf * 32) * Np + q;
-#pragma unroll 8
-        for (int d = 0; d < 32; ++d)
-          acc = fmaf(__half2float(dobuf[base + (size_t)d * Np]), __half2float(obuf[base + (size_t)d * Np]), acc);
-      }
-      sm.dhalf[hf][i][row] = acc;
-      if (hf == 0) sm.lse2[i][row] = q < N ? lse[(size_t)bh * N + q] * 1.4426950408889634f : 0.f;
+      sm.delta[i][row] = q < N ? delta[(size_t)bh * N + q] : 0.f;
+      sm.lse2[i][row] = q < N ? lse[(size_t)bh * N + q] * 1.4426950408889634f : 0.f;
     }
     named_sync_compute();
     const int kvalid = N - j * kT - hf * 64;  // valid keys among this half's 64
@@ -220,7 +213,7 @@ psa_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_con
       mbar_arrive(&sm.s_free);
       const bool qv = i * kT + row < N;
       const float l2 = sm.lse2[i][row];
-      const float dl = sm.dhalf[0][i][row] + sm.dhalf[1][i][row];
+      const float dl = sm.delta[i][row];
       if (i > 0 && !(ok = mbar_wait(&sm.p_free, (i - 1) & 1, &sm.abort, &g_bwd_status, 11))) break;
       uint8_t* prow = sm.p[hf] + row * 128;
       uint8_t* drow = sm.ds[hf] + row * 128;
@@ -288,6 +281,19 @@ psa_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_con
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
+// Δ[b·h][n] = Σ_d dO[b][h·64+d][n] · O[b][h·64+d][n]  (f16 channel-major,
+// pitch Np): one thread per token, coalesced across threads.
+__global__ void psa_delta_kernel(const __half* __restrict__ o, const __half* __restrict__ d_o,
+                                 float* __restrict__ delta, int N, int Np) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x, bh = blockIdx.y;
+  if (n >= N) return;
+  const size_t base = (size_t)bh * kHD * Np + n;
+  float acc = 0.f;
+#pragma unroll 16
+  for (int d = 0; d < kHD; ++d) acc = fmaf(__half2float(d_o[base + (size_t)d * Np]), __half2float(o[base + (size_t)d * Np]), acc);
+  delta[(size_t)bh * N + n] = acc;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 bwd_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -314,8 +320,8 @@ int bwd_map(CUtensorMap* m, int rank, const void* base, const uint64_t* d, const
 
 }  // namespace
 
-int psa_attn_bwd_tc(const void* qk, const void* v, const void* o, const void* d_o, const float* lse, float* dk,
-                    float* dv, float* dq_part, int B, int nh, int N, cudaStream_t st) {
+int psa_attn_bwd_tc(const void* qk, const void* v, const void* o, const void* d_o, const float* lse, float* delta,
+                    float* dk, float* dv, float* dq_part, int B, int nh, int N, cudaStream_t st) {
   VA_CHECK_ARG(nh == 2 && B > 0 && N > 0, "psa attention backward: need nh=2");
   if (N > kMaxTiles * kT) return set_error(VA_ERR_UNSUPPORTED, "psa attention backward: N=%d > %d", N, kMaxTiles * kT);
   const int BH = B * nh, Np = (N + 7) / 8 * 8;
@@ -336,9 +342,11 @@ int psa_attn_bwd_tc(const void* qk, const void* v, const void* o, const void* d_
   cudaError_t e = cudaFuncSetAttribute(psa_attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   const int nt = (N + kT - 1) / kT;
-  psa_attn_bwd_kernel<<<dim3(nt, BH), kBwdThreads, smem, st>>>(mqk, mv, mdo, static_cast<const __half*>(o),
-                                                              static_cast<const __half*>(d_o), lse, dk, dv, dq_part,
-                                                              N, Np, 1.0f / sqrtf((float)kKD));
+  psa_delta_kernel<<<dim3((N + 127) / 128, BH), 128, 0, st>>>(static_cast<const __half*>(o),
+                                                               static_cast<const __half*>(d_o), delta, N, Np);
+  if (int rc = check_launch("psa attention backward (delta)")) return rc;
+  psa_attn_bwd_kernel<<<dim3(nt, BH), kBwdThreads, smem, st>>>(mqk, mv, mdo, delta, lse, dk, dv, dq_part, N, Np,
+                                                              1.0f / sqrtf((float)kKD));
   return check_launch("psa attention backward");
 }
 
