@@ -148,6 +148,30 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Warp-convergent forms: the whole warp executes the call (so descriptor
+// arithmetic stays warp-uniform) and one elected lane issues the instruction.
+__device__ __forceinline__ void mma_ss_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n setp.ne.b32 p, %4, 0;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n setp.ne.b32 p, %4, 0;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit_w(uint64_t* bar) {
+  asm volatile(
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(smem_u32(bar))
+      : "memory");
+}
 // Arrive on `bar` once every previously issued tcgen05.mma of this thread completes.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -256,11 +280,12 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
 // uses the 1.5·2^23 magic-number addition), then a degree-4 polynomial for
 // 2^f fitted here on [-1/2, 1/2] by iteratively reweighted least squares on
 // Chebyshev nodes (Lawson's method, max relative error 2.7e-6), and n is
-// added to the exponent field with one integer multiply-add.  Inputs are
-// clamped to [-125, 127]; below -125 the result (≤ 2^-125) is far under
-// anything a probability in f16 can hold.
+// added to the exponent field with one integer multiply-add.  For x ≤ 127
+// (softmax arguments are ≤ 8); inputs below -125 are clamped there (−∞
+// included): the result, ≤ 2^-125, is far under anything a probability in
+// f16 can hold.
 __device__ __forceinline__ float ex2_poly(float x) {
-  x = fminf(fmaxf(x, -125.0f), 127.0f);
+  x = fmaxf(x, -125.0f);
   const float t = __fadd_rn(x, 12582912.0f);
   const float n = __fsub_rn(t, 12582912.0f);
   const float f = __fsub_rn(x, n);
@@ -269,6 +294,21 @@ __device__ __forceinline__ float ex2_poly(float x) {
   p = fmaf(p, f, 0.6931217908859253f);
   p = fmaf(p, f, 0.9999992847442627f);
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// Packed f32x2 arithmetic (sm_100): two f32 lanes per instruction.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                      float c1) {
+  asm("{\n .reg .b64 a, b, c, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n mov.b64 c, {%6, %7};\n"
+      " fma.rn.f32x2 d, a, b, c;\n mov.b64 {%0, %1}, d;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1) {
+  asm("{\n .reg .b64 a, b;\n mov.b64 a, {%0, %1};\n mov.b64 b, {%2, %3};\n add.f32x2 a, a, b;\n"
+      " mov.b64 {%0, %1}, a;\n}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1));
 }
 
 __device__ __forceinline__ float ex2(float x) {

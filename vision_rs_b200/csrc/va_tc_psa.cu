@@ -156,16 +156,20 @@ qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
 // every K/V tile.  Each query row is split across two warps: warps
 // 8g + 4h + w (h = 0, 1; w = 0..3) handle rows 32w..32w+31 (TMEM lanes) and
 // key columns 64h..64h+63 of group g, so 16 softmax warps (4 per SM
-// sub-partition) feed the exponential unit.  The halves combine their row
-// maxima through shared memory under a per-group named barrier.
-//   warp 16 lane 0: TMA producer + MMA issuer for group 0;
-//   warp 17 lane 0: MMA issuer for group 1 (one thread needs ~90 cycles per
-//   tcgen05.mma issue, slower than the tensor pipe runs these small MMAs).
-// (The exchange uses an mbarrier with a bounded wait rather than bar.sync, so
-// a half that aborts cannot leave its partner blocked.)
-// The two groups take turns on the exponentials (a token passed via mufu[]):
-// one group's exponentials overlap the other's score loads, row maxima and
-// barrier waits.
+// sub-partition) feed the exponential unit.  The two halves of a row sit on
+// the same SM sub-partition and combine their row maxima through shared
+// memory under a barrier of that row quarter (an mbarrier with a bounded
+// wait, so a half that aborts cannot leave its partner blocked).
+//   warp 16: TMA producer + MMA issuer for group 0;
+//   warp 17: MMA issuer for group 1.
+// The issuer warps run their loops converged and one elected lane issues each
+// tcgen05.mma (a lone lane-0 thread issues about 1.5× slower; the issue rate,
+// not the tensor pipe, bounds these small MMAs).
+// The two groups take turns on the exponentials, one token per row quarter
+// (mufu[g][q]): on each sub-partition one group's exponentials overlap the
+// other group's score loads, row maxima and barrier waits.  The token is
+// handed over a few pairs before the end of the last chunk, so the hand-off
+// latency overlaps the tail of the exponentials.
 // TMEM per group g (256 columns at 256·g): S (f32, 128 cols), P (packed f16,
 // 64 cols; the A operand of the P·V MMA) and O (f32, 64 cols).  S(j+1) is
 // issued as soon as the softmax has copied S(j) into registers (s_free).  P
@@ -177,7 +181,11 @@ constexpr int kVBlk = kHD * 128;           // one 64-key block of V: [64 channel
 constexpr int kSoftWarps = 16;
 constexpr int kAttnThreads = (kSoftWarps + 2) * 32;
 constexpr int kHalf = kTile / 2;           // key columns per softmax thread
-constexpr int kTokenEarly = 1;             // 0: release the exponential token after chunk 0 of 2; 1: after the last
+constexpr int kTokenPair = 11;  // release the exponential token after this pair of the last chunk (16: after it)
+// Exponential pairs (bit e of 16 per 32-score chunk) computed by the FMA-pipe
+// polynomial ex2_poly instead of the MUFU unit, which alone would bound the
+// softmax at 16 exponentials per SM clock.
+constexpr uint32_t kPolyMask = 0x8080u;
 
 __device__ __forceinline__ uint32_t col_s(int g) { return (uint32_t)g * 256u; }
 __device__ __forceinline__ uint32_t col_p(int g) { return (uint32_t)g * 256u + 128u; }
@@ -194,8 +202,10 @@ struct AttnSmem {
   float xmax[2][2][2][kTile];              // [tile parity][group][half][row] partial row maxima
   float xsum[2][2][kTile];                 // [group][half][row] partial row sums (end of loop)
   uint64_t q_full, kv_full[kStages], kv_empty[kStages], s_full[2], s_free[2], p_full[2], o_done[2], fin[2];
-  uint64_t mufu[2];                        // ping-pong token: group g may run the exponentials of its next tile
-  uint64_t xbar[2], fbar[2];               // per group: row-max exchange (per tile), row-sum exchange (end)
+  // Per group and row quarter q (the two warps q, q+4 of a group that share SM
+  // sub-partition q with the other group's two warps of that quarter):
+  uint64_t mufu[2][4];  // ping-pong token: group g may run the exponentials of its next tile
+  uint64_t xbar[2][4], fbar[2][4];  // row-max exchange (per tile), row-sum exchange (end)
   uint32_t tmem_base;
   int abort;
 };
@@ -242,9 +252,11 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       mbar_init(&sm.p_full[g], 256);
       mbar_init(&sm.o_done[g], 1);
       mbar_init(&sm.fin[g], 1);
-      mbar_init(&sm.mufu[g], 256);
-      mbar_init(&sm.xbar[g], 256);
-      mbar_init(&sm.fbar[g], 256);
+      for (int q = 0; q < 4; ++q) {
+        mbar_init(&sm.mufu[g][q], 64);
+        mbar_init(&sm.xbar[g][q], 64);
+        mbar_init(&sm.fbar[g][q], 64);
+      }
     }
     sm.abort = 0;
     fence_mbar_init();
@@ -259,19 +271,23 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
   const uint32_t tmem = sm.tmem_base;
 
   if (warp >= kSoftWarps) {
+    // ── issuer for group g (issuer 0 also drives TMA) ──
+    // The whole warp runs this loop (barrier waits and descriptor arithmetic
+    // stay warp-uniform); lane 0 issues TMA, one elected lane issues MMAs.
     const int g = warp - kSoftWarps;
-    if (lane == 0 && (g == 0 || has1)) {
-      // ── issuer for group g (issuer 0 also drives TMA) ──
-      const bool producer = g == 0;
+    if (g == 0 || has1) {
+      const bool producer = g == 0, leader = lane == 0;
       int issued = 0;
       if (producer) {
-        tma_prefetch_desc(&map_qk);
-        tma_prefetch_desc(&map_v);
-        mbar_arrive_expect_tx(&sm.q_full, (has1 ? 2 : 1) * kQK);
-        tma_load_3d(sm.q[0], &map_qk, &sm.q_full, 0, q0, bh);
-        if (has1) tma_load_3d(sm.q[1], &map_qk, &sm.q_full, 0, q0 + kTile, bh);
-        for (; issued < kStages && issued < nkv; ++issued)
-          attn_load_kv(sm, &map_qk, &map_v, issued, issued, BH, bh, vrow);
+        if (leader) {
+          tma_prefetch_desc(&map_qk);
+          tma_prefetch_desc(&map_v);
+          mbar_arrive_expect_tx(&sm.q_full, (has1 ? 2 : 1) * kQK);
+          tma_load_3d(sm.q[0], &map_qk, &sm.q_full, 0, q0, bh);
+          if (has1) tma_load_3d(sm.q[1], &map_qk, &sm.q_full, 0, q0 + kTile, bh);
+          for (int t = 0; t < kStages && t < nkv; ++t) attn_load_kv(sm, &map_qk, &map_v, t, t, BH, bh, vrow);
+        }
+        issued = min(kStages, nkv);
       }
       constexpr uint32_t idS = idesc_f32acc(128, kTile, AB_F16, false, false);
       constexpr uint32_t idO = idesc_f32acc(128, kHD, AB_F16, false, false);
@@ -287,46 +303,53 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       const uint32_t ds = tmem + col_s(g), dp = tmem + col_p(g), dO = tmem + col_o(g);
       auto issue_s = [&](int stage) {
         const uint64_t kd_ = dk0 + (uint64_t)(stage * kKStage);
-        mma_ss(ds, dq, kd_, idS, 0u);
+        mma_ss_w(ds, dq, kd_, idS, 0u);
 #pragma unroll
-        for (int s = 1; s < KD / 16; ++s) mma_ss(ds, dq + 2 * s, kd_ + 2 * s, idS, 1u);  // +32 bytes per k-step
+        for (int s = 1; s < KD / 16; ++s) mma_ss_w(ds, dq + 2 * s, kd_ + 2 * s, idS, 1u);  // +32 bytes per k-step
       };
       auto issue_o = [&](int stage, uint32_t acc) {
         const uint64_t vd = dv0 + (uint64_t)(stage * kVStage);
-        mma_ts(dO, dp, vd, idO, acc);
+        mma_ts_w(dO, dp, vd, idO, acc);
 #pragma unroll
         for (int s = 1; s < kTile / 16; ++s)
-          mma_ts(dO, dp + s * 8, vd + (uint64_t)((s >> 2) * kVHalf + (s & 3) * 2), idO, 1u);
+          mma_ts_w(dO, dp + s * 8, vd + (uint64_t)((s >> 2) * kVHalf + (s & 3) * 2), idO, 1u);
       };
       bool ok = mbar_wait(&sm.q_full, 0, &sm.abort, &g_tc_status, 10) &&
                 mbar_wait(&sm.kv_full[0], 0, &sm.abort, &g_tc_status, 11);
-      int consumed = ok ? 1 : 0;  // K/V tiles whose full barrier this thread observed
+      ok = __all_sync(0xffffffffu, ok);
+      int consumed = ok ? 1 : 0;  // K/V tiles whose full barrier this warp observed
       if (ok) {
         tc_fence_after();
         issue_s(0);
-        mma_commit(&sm.s_full[g]);
+        mma_commit_w(&sm.s_full[g]);
       }
       for (int j = 0; ok && j < nkv; ++j) {
         const int st = j % kStages;
         if (j + 1 < nkv) {
           const int stn = (j + 1) % kStages;
-          if (!(ok = mbar_wait(&sm.kv_full[stn], ((j + 1) / kStages) & 1, &sm.abort, &g_tc_status, 12))) break;
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(&sm.kv_full[stn], ((j + 1) / kStages) & 1, &sm.abort, &g_tc_status, 12));
+          if (!ok) break;
           consumed = j + 2;
-          if (!(ok = mbar_wait(&sm.s_free[g], j & 1, &sm.abort, &g_tc_status, 13))) break;
+          ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_free[g], j & 1, &sm.abort, &g_tc_status, 13));
+          if (!ok) break;
           tc_fence_after();
           issue_s(stn);
-          mma_commit(&sm.s_full[g]);
+          mma_commit_w(&sm.s_full[g]);
         }
-        if (!(ok = mbar_wait(&sm.p_full[g], j & 1, &sm.abort, &g_tc_status, 14))) break;
+        ok = __all_sync(0xffffffffu, mbar_wait(&sm.p_full[g], j & 1, &sm.abort, &g_tc_status, 14));
+        if (!ok) break;
         tc_fence_after();
         issue_o(st, j > 0 ? 1u : 0u);
-        mma_commit(&sm.o_done[g]);
-        mma_commit(&sm.kv_empty[st]);
+        mma_commit_w(&sm.o_done[g]);
+        mma_commit_w(&sm.kv_empty[st]);
         // producer: refill the stage tile j-1 used (both issuers done with it) with tile j+3
         if (producer && j >= 1 && j + kStages - 1 < nkv) {
           const int sp = (j - 1) % kStages;
-          if (!(ok = mbar_wait(&sm.kv_empty[sp], ((j - 1) / kStages) & 1, &sm.abort, &g_tc_status, 15))) break;
-          attn_load_kv(sm, &map_qk, &map_v, j + kStages - 1, sp, BH, bh, vrow);
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(&sm.kv_empty[sp], ((j - 1) / kStages) & 1, &sm.abort, &g_tc_status, 15));
+          if (!ok) break;
+          if (leader) attn_load_kv(sm, &map_qk, &map_v, j + kStages - 1, sp, BH, bh, vrow);
           ++issued;
         }
       }
@@ -343,7 +366,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
           }
         }
       }
-      mma_commit(&sm.fin[g]);
+      mma_commit_w(&sm.fin[g]);
       const long long t0 = clock64();
       while (!mbar_try_wait(&sm.fin[g], 0) && clock64() - t0 < kSpinCycles) {
       }
@@ -351,7 +374,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
     __syncwarp();
   } else if (warp < 8 || has1) {
     // ── softmax: group g, key half hf, thread = query row (TMEM lane) ──
-    const int g = warp >> 3, hf = (warp >> 2) & 1, row = (warp & 3) * 32 + lane;
+    const int g = warp >> 3, hf = (warp >> 2) & 1, qr = warp & 3, row = qr * 32 + lane;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t sc = tmem + lane_off + col_s(g) + hf * kHalf;
     const uint32_t pc = tmem + lane_off + col_p(g) + hf * (kHalf / 2);
@@ -398,8 +421,8 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       mx[6] = fmaxf(mx[6], mx[7]);
       const float pmax = max3(mx[0], mx[3], mx[6]);
       sm.xmax[j & 1][g][hf][row] = pmax;
-      mbar_arrive(&sm.xbar[g]);  // release: the partial max is visible to the other half
-      if (!(ok = mbar_wait(&sm.xbar[g], j & 1, &sm.abort, &g_tc_status, 30 + g))) break;
+      mbar_arrive(&sm.xbar[g][qr]);  // release: the partial max is visible to the other half
+      if (!(ok = mbar_wait(&sm.xbar[g][qr], j & 1, &sm.abort, &g_tc_status, 30 + g))) break;
       const float rmax = fmaxf(pmax, sm.xmax[j & 1][g][hf ^ 1][row]);
       const float m_new = fmaxf(m, rmax * scale_log2);
       // Rescale only when the running max grew by more than 2^8 (the stale max
@@ -428,7 +451,7 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
       // ping-pong: group 0 runs exps of tile j after group 1 finished tile j-1;
       // group 1 after group 0 finished tile j
       const bool pp = has1 && (g == 1 || j > 0);
-      if (pp && !(ok = mbar_wait(&sm.mufu[g], (g == 0 ? j - 1 : j) & 1, &sm.abort, &g_tc_status, 28 + g))) break;
+      if (pp && !(ok = mbar_wait(&sm.mufu[g][qr], (g == 0 ? j - 1 : j) & 1, &sm.abort, &g_tc_status, 28 + g))) break;
       const float nm = -m_use;
       float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
@@ -436,17 +459,20 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], scale_log2, nm));
-          const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], scale_log2, nm));
-          ls0 += p0;
-          ls1 += p1;
+          float x0, x1;
+          ffma2(x0, x1, sv[c * 32 + 2 * e], sv[c * 32 + 2 * e + 1], scale_log2, scale_log2, nm, nm);
+          const bool poly = (kPolyMask >> e) & 1u;
+          const float p0 = poly ? ex2_poly(x0) : ex2(x0);
+          const float p1 = poly ? ex2_poly(x1) : ex2(x1);
+          fadd2(ls0, ls1, p0, p1);
           pk[e] = pack_f16x2(p0, p1);
+          // hand the exponential unit over shortly before the end: the other
+          // group's first exponentials overlap this group's last ones instead
+          // of waiting out the hand-off latency
+          if (has1 && c == kHalf / 32 - 1 && e == kTokenPair) mbar_arrive(&sm.mufu[g ^ 1][qr]);
         }
         tmem_st16(pc + c * 16, pk);
-        // hand the exponential unit over before the last chunk: the other
-        // group's first exponentials overlap this group's last ones instead of
-        // waiting out the hand-off latency
-        if (has1 && c == kHalf / 32 - 2 + kTokenEarly) mbar_arrive(&sm.mufu[g ^ 1]);
+        if (has1 && c == kHalf / 32 - 1 && kTokenPair >= 16) mbar_arrive(&sm.mufu[g ^ 1][qr]);
       }
       tmem_st_wait();
       l = l * alpha + (ls0 + ls1);
@@ -457,8 +483,8 @@ attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ 
     if (ok) ok = mbar_wait(&sm.o_done[g], (nkv - 1) & 1, &sm.abort, &g_tc_status, 24 + g);
     // combine the halves' row sums (every thread of the group reaches this barrier)
     sm.xsum[g][hf][row] = l;
-    mbar_arrive(&sm.fbar[g]);
-    if (ok) ok = mbar_wait(&sm.fbar[g], 0, &sm.abort, &g_tc_status, 32 + g);
+    mbar_arrive(&sm.fbar[g][qr]);
+    if (ok) ok = mbar_wait(&sm.fbar[g][qr], 0, &sm.abort, &g_tc_status, 32 + g);
     const float lt = l + sm.xsum[g][hf ^ 1][row];
     if (ok) {
       tc_fence_after();
