@@ -101,6 +101,10 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, const void* s
 }
 __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// All but the most recently committed bulk-store group have read their source.
+__device__ __forceinline__ void tma_store_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+// Every committed bulk store has completed (its global writes are done).
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Offset of 16-byte chunk `chunk` of row `row` in a SW128 tile of 128-byte rows.
 __device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
   return (uint32_t)row * 128u + ((uint32_t)(chunk ^ (row & 7)) << 4);

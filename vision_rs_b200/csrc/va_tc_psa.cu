@@ -3,20 +3,22 @@
 // The reference graph (src/models/yolo/yolo26/blocks/c2psa.rs:61-116) runs
 // 7 nodes: qkv conv+BN, psa_pack_qkv, flash attention ×2 (V split into two
 // 32-wide halves, psa.rs:930-944), psa_merge_attn_nchw, psa_extract_v_nchw,
-// pe dw-conv+BN, add, proj conv+BN.  Here it is three kernels:
+// pe dw-conv+BN, add, proj conv+BN.  Here it is four kernels:
 //
-//  1. qkv_proj_kernel  — D[128 tok × 256 ch] = xᵀ·W_qkvᵀ on tcgen05 (x tile is
-//     the MN-major A operand read straight from NCHW by TMA).  The epilogue
-//     adds the folded-BN bias and writes exactly the layouts the next kernel
-//     reads: Q and K token-major [2][B·nh][N][32] (psa_pack_qkv sections 0/1)
-//     and V channel-major [B][C][Np] (psa_extract_v_nchw's output), f16.
-//  2. attn_kernel      — flash attention per (b, h, 128-query tile):
-//     S = Q·Kᵀ (TMEM), online softmax in registers (one thread per query
-//     row), P → smem (f16), O += P·V with the full 64-wide V in one MMA (no
-//     lo/hi split).  O is written channel-major [B][C][Np] — the layout
+//  1. qkv_proj_kernel  — persistent GEMM D[128 tok × 256 ch] = xᵀ·W_qkvᵀ on
+//     tcgen05 (x tile is the MN-major A operand read straight from NCHW by
+//     TMA, W_qkv resident).  The epilogue adds the folded-BN bias and writes
+//     exactly the layouts the next kernels read: Q and K token-major
+//     [2][B·nh][N][32] (psa_pack_qkv sections 0/1) and V channel-major
+//     [B][C][Np] (psa_extract_v_nchw's output), f16.
+//  2. attn_kernel      — flash attention per (b, h, pair of 128-query tiles):
+//     S = Q·Kᵀ (TMEM), online softmax in registers (two threads per query
+//     row), P → TMEM (f16), O += P·V with the full 64-wide V (no lo/hi
+//     split).  O is written channel-major [B][C][Np] — the layout
 //     psa_merge_attn_nchw produces.
-//  3. pe_proj_kernel   — A = O + dw3×3(V) + b_pe built in smem as the MN-major
-//     operand, D = A·W_projᵀ on tcgen05, + b_proj, y stored NCHW bf16.
+//  3. pe_dwconv(_vec)_kernel — PE = dw3×3(V) + b_pe, f16 [B][C][Np].
+//  4. proj_kernel      — D = (O + PE)ᵀ·W_projᵀ on tcgen05 (the sum formed by
+//     accumulating both MMAs into one TMEM tile), + b_proj, y stored NCHW bf16.
 //
 // Precision: x, weights and y are bf16; the qkv GEMM runs bf16×bf16; the
 // attention operands Q, K, V, P, O and the proj A operand are f16 (3 more
@@ -45,32 +47,67 @@ constexpr int kHD = 64;      // head_dim (V width)
 constexpr int kTile = 128;   // tokens per tile (UMMA M)
 
 // ── Kernel 1: qkv projection ────────────────────────────────────────────────
+// Persistent: a CTA keeps W_qkv (64 KB) resident and walks the (image, 128-
+// token tile) items blockIdx.x, blockIdx.x + gridDim.x, …  Warp 0 streams xᵀ
+// tiles (two 64-token boxes of the NCHW input per tile) through a TMA ring.
+// Warp 1 issues two GEMMs per tile into one of two TMEM accumulator pairs:
+//   Q/K:  D1[128 tokens][128] = xᵀ·W_qkᵀ   (x tile as the MN-major A operand)
+//   V:    D2[128 channels][128 tokens] = W_v·x  (x tile as the MN-major B operand)
+// so V comes out of the tensor core already channel-major.  Eight epilogue
+// warps drain the other pair meanwhile: warps 2-5 write Q and K rows (thread =
+// token, 64 contiguous bytes per row); warps 6-9 (thread = channel) stage the
+// V tile in shared memory as two SW128 [128 channels][64 tokens] boxes
+// (16-byte stores, conflict-free) that one thread writes with TMA stores
+// (double-buffered).  W_qkv's rows are regrouped on load: the Q/K rows of both
+// heads form one 128-row operand, the V rows the other.
+constexpr int kQpStages = 2;
+constexpr int kQpEpiWarps = 8;
+constexpr int kQpThreads = (2 + kQpEpiWarps) * 32;
+
 struct QkvSmem {
-  uint8_t a[2][kC * 128];      // xᵀ tile, MN-major SW128: 2 blocks of 64 tokens × 128 channel rows (16 KB each)
-  uint8_t w[2][kQKV * 128];    // W_qkv K-major SW128: 2 blocks of 64 in-channels × 256 rows (32 KB each)
-  uint64_t full_bar;
-  uint64_t mma_bar;
+  uint8_t wqk[2][128 * 128];          // K-major SW128: 2 k-blocks × 128 rows (head 0 q,k; head 1 q,k)
+  uint8_t wv[2][128 * 128];           // K-major SW128: 2 k-blocks × 128 rows (head 0 v; head 1 v)
+  uint8_t a[kQpStages][2][kC * 128];  // x tile: 2 blocks of 64 tokens × 128 channel rows, SW128
+  uint8_t vst[2][2][kC * 128];        // V staging [buffer][token half]: 128 channel rows × 64 tokens, SW128
+  float bias[kQKV];
+  uint64_t w_full, a_full[kQpStages], a_empty[kQpStages], acc_full[2], acc_empty[2], fin;
+  uint64_t stage_free[2], stage_full[2];
   uint32_t tmem_base;
   int abort;
 };
 
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kQpThreads, 1)
 qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                const float* __restrict__ bias, __half* __restrict__ qk, __half* __restrict__ vbuf, int N, int Np,
-                int nh) {
+                const __grid_constant__ CUtensorMap map_vst, const float* __restrict__ bias,
+                __half* __restrict__ qk, int N, int nh, int B, int ntile) {
   extern __shared__ uint8_t smem_raw[];
   QkvSmem& sm = *reinterpret_cast<QkvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * kTile, b = blockIdx.y;
+  const int total = B * ntile;
+  const int cnt = (int)blockIdx.x < total ? (total - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+  auto tile_of = [&](int i) { return (int)blockIdx.x + i * (int)gridDim.x; };
 
   if (tid == 0) {
-    mbar_init(&sm.full_bar, 1);
-    mbar_init(&sm.mma_bar, 1);
+    mbar_init(&sm.w_full, 1);
+    for (int s = 0; s < kQpStages; ++s) {
+      mbar_init(&sm.a_full[s], 1);
+      mbar_init(&sm.a_empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sm.acc_full[a], 1);
+      mbar_init(&sm.acc_empty[a], kQpEpiWarps * 32);
+    }
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(&sm.stage_free[k], 1);
+      mbar_init(&sm.stage_full[k], 4 * 32);
+    }
+    mbar_init(&sm.fin, 1);
     sm.abort = 0;
     fence_mbar_init();
   }
+  for (int i = tid; i < kQKV; i += kQpThreads) sm.bias[i] = bias[i];
   if (warp == 0) {
-    tmem_alloc(&sm.tmem_base, 256);
+    tmem_alloc(&sm.tmem_base, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -78,77 +115,159 @@ qkv_proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  if (tid == 0) {
-    tma_prefetch_desc(&map_x);
-    tma_prefetch_desc(&map_w);
-    mbar_arrive_expect_tx(&sm.full_bar, 2 * kC * 128 + 2 * kQKV * 128);
-    tma_load_2d(sm.a[0], &map_x, &sm.full_bar, n0, b * kC);
-    tma_load_2d(sm.a[1], &map_x, &sm.full_bar, n0 + 64, b * kC);
-    tma_load_2d(sm.w[0], &map_w, &sm.full_bar, 0, 0);
-    tma_load_2d(sm.w[1], &map_w, &sm.full_bar, 64, 0);
-    if (mbar_wait(&sm.full_bar, 0, &sm.abort, &g_tc_status, 1)) {
-      tc_fence_after();
-      constexpr uint32_t idesc = idesc_f32acc(128, kQKV, AB_BF16, /*a_mn=*/true, /*b_mn=*/false);
-      const uint32_t a0 = smem_u32(sm.a[0]), w0 = smem_u32(sm.w[0]);
-#pragma unroll
-      for (int s = 0; s < kC / 16; ++s) {
-        uint64_t ad = sdesc(a0 + s * 16 * 128, /*lbo=*/kC * 128, /*sbo=*/1024, SW_128B);
-        uint64_t bd = sdesc(w0 + (s >> 2) * (kQKV * 128) + (s & 3) * 32, 16, 1024, SW_128B);
-        mma_ss(tmem, ad, bd, idesc, s > 0);
+  if (warp == 0) {
+    if (lane == 0) {  // ── TMA producer ──
+      tma_prefetch_desc(&map_x);
+      tma_prefetch_desc(&map_w);
+      mbar_arrive_expect_tx(&sm.w_full, 4 * 128 * 128);
+      for (int kb = 0; kb < 2; ++kb)
+        for (int h = 0; h < 2; ++h) {  // 64-row boxes: W rows h·128 + [0,64) → q,k; h·128 + [64,128) → v
+          tma_load_2d(sm.wqk[kb] + h * 64 * 128, &map_w, &sm.w_full, kb * 64, h * 128);
+          tma_load_2d(sm.wv[kb] + h * 64 * 128, &map_w, &sm.w_full, kb * 64, h * 128 + 64);
+        }
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < cnt; ++i) {
+        const int s = i % kQpStages, t = tile_of(i), b = t / ntile, n0 = (t - b * ntile) * kTile;
+        if (i >= kQpStages &&
+            !(ok = mbar_wait(&sm.a_empty[s], ((i / kQpStages) - 1) & 1, &sm.abort, &g_tc_status, 1)))
+          break;
+        mbar_arrive_expect_tx(&sm.a_full[s], 2 * kC * 128);
+        tma_load_2d(sm.a[s][0], &map_x, &sm.a_full[s], n0, b * kC);
+        tma_load_2d(sm.a[s][1], &map_x, &sm.a_full[s], n0 + 64, b * kC);
+        ++issued;
       }
-    } else {
-      // the TMA loads may still land: wait for them (bounded) before leaving
-      const long long t0 = clock64();
-      while (!mbar_try_wait(&sm.full_bar, 0) && clock64() - t0 < kSpinCycles) {
+      // every load issued here lands (bounded) before the CTA can exit
+      const long long c0 = clock64();
+      while (!mbar_try_wait(&sm.w_full, 0) && clock64() - c0 < kSpinCycles) {
       }
-    }
-    mma_commit(&sm.mma_bar);
-  }
-  __syncwarp();
-  const bool ok = mbar_wait(&sm.mma_bar, 0, &sm.abort, &g_tc_status, 2) && !sm.abort;
-  tc_fence_after();
-
-  if (ok) {
-    const int n = n0 + warp * 32 + lane;
-    const int BH = gridDim.y * nh;
-#pragma unroll 1
-    for (int c = 0; c < kQKV / 32; ++c) {
-      uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
-      tmem_ld_wait();
-      reg_fence(r);
-      const int h = c >> 2, sec = c & 3;
-      float v[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + __ldg(bias + c * 32 + i);
-      if (n < N) {
-        if (sec < 2) {
-          // Q / K row: 32 contiguous f16 in [sec][b*nh+h][n][:]
-          uint4* dst = reinterpret_cast<uint4*>(qk + (((size_t)sec * BH + (size_t)b * nh + h) * N + n) * kKD);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 u;
-            u.x = pack_f16x2_sat(v[q * 8 + 0], v[q * 8 + 1]);
-            u.y = pack_f16x2_sat(v[q * 8 + 2], v[q * 8 + 3]);
-            u.z = pack_f16x2_sat(v[q * 8 + 4], v[q * 8 + 5]);
-            u.w = pack_f16x2_sat(v[q * 8 + 6], v[q * 8 + 7]);
-            dst[q] = u;
-          }
-        } else {
-          // V channels h*64 + (sec-2)*32 + i, channel-major
-          __half* dst = vbuf + ((size_t)b * kC + h * kHD + (sec - 2) * 32) * Np + n;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            uint32_t p = pack_f16x2_sat(v[i], 0.f);
-            dst[(size_t)i * Np] = __ushort_as_half((unsigned short)(p & 0xFFFF));
+      if (!ok) {
+        for (int i = max(0, issued - kQpStages); i < issued; ++i) {
+          const long long c1 = clock64();
+          while (!mbar_try_wait(&sm.a_full[i % kQpStages], (i / kQpStages) & 1) && clock64() - c1 < kSpinCycles) {
           }
         }
       }
     }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ── MMA issuer: the warp waits converged, one elected lane issues ──
+    constexpr uint32_t id_qk = idesc_f32acc(128, 128, AB_BF16, /*a_mn=*/true, /*b_mn=*/false);
+    constexpr uint32_t id_v = idesc_f32acc(128, 128, AB_BF16, /*a_mn=*/false, /*b_mn=*/true);
+    const uint32_t wqk0 = smem_u32(sm.wqk[0]), wv0 = smem_u32(sm.wv[0]);
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.w_full, 0, &sm.abort, &g_tc_status, 2));
+    for (int i = 0; ok && i < cnt; ++i) {
+      const int s = i % kQpStages, a = i & 1;
+      if (i >= 2) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&sm.acc_empty[a], ((i >> 1) - 1) & 1, &sm.abort, &g_tc_status, 3));
+        if (!ok) break;
+      }
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.a_full[s], (i / kQpStages) & 1, &sm.abort, &g_tc_status, 4));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t x0 = smem_u32(sm.a[s][0]);
+#pragma unroll
+      for (int k = 0; k < kC / 16; ++k) {
+        // x tile, MN-major: 16 channel rows per k-step, the two 64-token blocks 16 KB apart
+        const uint64_t xd = sdesc(x0 + k * 16 * 128, /*lbo=*/kC * 128, /*sbo=*/1024, SW_128B);
+        const uint32_t wk = (k >> 2) * (128 * 128) + (k & 3) * 32;
+        mma_ss_w(tmem + a * 256, xd, sdesc(wqk0 + wk, 16, 1024, SW_128B), id_qk, k > 0 ? 1u : 0u);
+        mma_ss_w(tmem + a * 256 + 128, sdesc(wv0 + wk, 16, 1024, SW_128B), xd, id_v, k > 0 ? 1u : 0u);
+      }
+      mma_commit_w(&sm.a_empty[s]);
+      mma_commit_w(&sm.acc_full[a]);
+    }
+    mma_commit_w(&sm.fin);  // every MMA issued here completes before the CTA tears down
+    const long long c0 = clock64();
+    while (!mbar_try_wait(&sm.fin, 0) && clock64() - c0 < kSpinCycles) {
+    }
+    __syncwarp();
+  } else {
+    // ── epilogue warps 2-9 (TMEM lane quarter = warp % 4) ──
+    const int q4 = warp & 3, row = q4 * 32 + lane;
+    const bool vwarp = warp >= 6;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const int BH = B * nh;
+    for (int i = 0; i < cnt; ++i) {
+      const int a = i & 1, t = tile_of(i), b = t / ntile, n0 = (t - b * ntile) * kTile;
+      if (!mbar_wait(&sm.acc_full[a], (i >> 1) & 1, &sm.abort, &g_tc_status, 5)) break;
+      tc_fence_after();
+      if (!vwarp) {
+        // Q/K: thread = token n0 + row; chunk c = (head c/2, section c%2)
+        const int n = n0 + row;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          const int h = c >> 1, sec = c & 1, bcol = h * 128 + sec * 32;
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_off + a * 256 + c * 32, r);
+          tmem_ld_wait();
+          reg_fence(r);
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            v[e] = __uint_as_float(r[e]);
+            v[e + 1] = __uint_as_float(r[e + 1]);
+            fadd2(v[e], v[e + 1], sm.bias[bcol + e], sm.bias[bcol + e + 1]);
+          }
+          if (n < N) {  // 32 contiguous f16 in [sec][b*nh+h][n][:]
+            uint4* dst = reinterpret_cast<uint4*>(qk + (((size_t)sec * BH + (size_t)b * nh + h) * N + n) * kKD);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              dst[q] = make_uint4(pack_f16x2_sat(v[q * 8 + 0], v[q * 8 + 1]), pack_f16x2_sat(v[q * 8 + 2], v[q * 8 + 3]),
+                                  pack_f16x2_sat(v[q * 8 + 4], v[q * 8 + 5]), pack_f16x2_sat(v[q * 8 + 6], v[q * 8 + 7]));
+          }
+        }
+      } else {
+        // V: thread = channel row (h·64 + cv, the MMA's M index); chunk c = tokens 32c .. 32c+31 of the tile
+        const int k = i & 1, h = row >> 6, cv = row & 63;
+        const bool storer = warp == 6 && lane == 0;
+        const float bv = sm.bias[h * 128 + 64 + cv];
+        if (storer) {  // the V store of tile i-2 has read staging buffer k (tile i-1's may be in flight)
+          tma_store_wait_read_1();
+          mbar_arrive(&sm.stage_free[k]);
+        }
+        if (!mbar_wait(&sm.stage_free[k], (i >> 1) & 1, &sm.abort, &g_tc_status, 6)) break;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_off + a * 256 + 128 + c * 32, r);
+          tmem_ld_wait();
+          reg_fence(r);
+          uint8_t* box = sm.vst[k][c >> 1];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+              v[e] = __uint_as_float(r[q * 8 + e]);
+              v[e + 1] = __uint_as_float(r[q * 8 + e + 1]);
+              fadd2(v[e], v[e + 1], bv, bv);
+            }
+            *reinterpret_cast<uint4*>(box + sw128_off(row, (c & 1) * 4 + q)) =
+                make_uint4(pack_f16x2_sat(v[0], v[1]), pack_f16x2_sat(v[2], v[3]), pack_f16x2_sat(v[4], v[5]),
+                           pack_f16x2_sat(v[6], v[7]));
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&sm.acc_empty[a]);
+        fence_proxy_async_smem();
+        mbar_arrive(&sm.stage_full[k]);
+        if (storer) {
+          if (!mbar_wait(&sm.stage_full[k], (i >> 1) & 1, &sm.abort, &g_tc_status, 7)) break;
+          tma_store_2d(&map_vst, sm.vst[k][0], n0, b * kC);  // columns past N are clipped
+          tma_store_2d(&map_vst, sm.vst[k][1], n0 + 64, b * kC);
+          tma_store_commit();
+        }
+        continue;
+      }
+      tc_fence_before();
+      mbar_arrive(&sm.acc_empty[a]);
+    }
+    if (warp == 6 && lane == 0) tma_store_wait_all();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 256);
+  if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 // ── Kernel 2: flash attention ───────────────────────────────────────────────
@@ -761,21 +880,24 @@ attn_short_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_const
 // ── Kernel 3: positional encoding (depthwise 3×3 + bias) ───────────────────
 // One CTA per (image, group of kPeCh channels).  Each channel plane is read
 // with 16-byte loads (all in flight at once), widened to f32 into a zero-
-// bordered [H+2][W+2] shared-memory plane, and every thread then produces
-// consecutive outputs (conflict-free shared reads, coalesced stores).  PE is
-// stored f16 [B][C][Np], the layout the projection kernel reads with TMA.
-// CTA 0 also converts W_proj (bf16) to the f16 operand the projection uses.
+// bordered [H+2][W2] shared-memory plane (odd pitch W2 ≥ W+10).  A thread then
+// produces an 8-column × kPeRows-row block of one channel, sliding a 3-row
+// window of 10 values down the rows (1.5 shared loads and 9 FMAs per output;
+// the item index is decomposed once per block).  PE is stored f16 [B][C][Np],
+// the layout the projection kernel reads with TMA.  CTA 0 also converts
+// W_proj (bf16) to the f16 operand the projection uses.
 constexpr int kPeCh = 4;
 constexpr int kPeThreads = 256;
+constexpr int kPeRows = 4;
 constexpr int kMaxPlane = 12288;   // (H+2)·pitch floats per staged channel
 
 __global__ void __launch_bounds__(kPeThreads)
 pe_dwconv_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __restrict__ w_pe,
                  const float* __restrict__ b_pe, __half* __restrict__ pebuf,
                  const __nv_bfloat16* __restrict__ w_proj, __half* __restrict__ wproj16, int H, int W, int Np) {
-  extern __shared__ float plane[];   // [kPeCh][(H+2)*(W+2)]
+  extern __shared__ float plane[];   // [kPeCh][(H+2)*W2]
   const int tid = threadIdx.x;
-  const int N = H * W, W2 = (W + 10) | 1, P2 = (H + 2) * W2;   // odd pitch; 8 zero columns of slack
+  const int N = H * W, W2 = (W + 10) | 1, P2 = (H + 2) * W2;
   const int cg = blockIdx.x, b = blockIdx.y;
   if (cg == 0 && b == 0) {
     for (int i = tid; i < kC * kC / 8; i += kPeThreads) {
@@ -791,9 +913,20 @@ pe_dwconv_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __restric
       reinterpret_cast<uint4*>(wproj16)[i] = u;
     }
   }
-  // zero border, then the interior from global (16-byte loads, batched)
-  for (int i = tid; i < kPeCh * P2; i += kPeThreads) plane[i] = 0.f;
-  __syncthreads();
+  // border cells (rows 0 and H+1, column 0 and columns W+1.. of the pitch) are
+  // zero; they are disjoint from the interior, so one barrier covers both
+  for (int c = 0; c < kPeCh; ++c) {
+    float* pl = plane + c * P2;
+    for (int i = tid; i < W2; i += kPeThreads) {
+      pl[i] = 0.f;
+      pl[(H + 1) * W2 + i] = 0.f;
+    }
+    const int nb = W2 - W;  // column 0 plus the W2-W-1 columns right of the image
+    for (int i = tid; i < H * nb; i += kPeThreads) {
+      const int r = i / nb, k = i - r * nb;
+      pl[(r + 1) * W2 + (k == 0 ? 0 : W + k)] = 0.f;
+    }
+  }
   const int nchunk = Np >> 3;
   const __half* vb = vbuf + ((size_t)b * kC + (size_t)cg * kPeCh) * Np;
   constexpr int kBatch = 4;
@@ -813,55 +946,166 @@ pe_dwconv_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __restric
       if (i < kPeCh * nchunk) {
         const int c = i / nchunk, k = i - c * nchunk;
         const __half* h = reinterpret_cast<const __half*>(&u[q]);
-        int n = k * 8, r = n / W, j = n - r * W;
+        const int n = k * 8;
+        int r = n / W, j = n - r * W;
+        if ((W & 7) == 0) {  // the 8 tokens lie in one image row
+          float* dst = plane + c * P2 + (r + 1) * W2 + j + 1;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          if (n + e < N) plane[c * P2 + (r + 1) * W2 + j + 1] = __half2float(h[e]);
-          if (++j == W) { j = 0; ++r; }
+          for (int e = 0; e < 8; ++e) dst[e] = __half2float(h[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (n + e < N) plane[c * P2 + (r + 1) * W2 + j + 1] = __half2float(h[e]);
+            if (++j == W) { j = 0; ++r; }
+          }
         }
       }
     }
   }
   __syncthreads();
-  // items: (channel, 8-column group, row) with the row fastest across threads
-  // (odd plane pitch → conflict-free shared reads); 8 outputs per item from a
-  // 3×10 register window
-  const int ngrp = (W + 7) >> 3;
+  const int ngrp = (W + 7) >> 3, nrb = (H + kPeRows - 1) / kPeRows;
   const bool vec_store = (W & 7) == 0;
-  for (int it = tid; it < kPeCh * ngrp * H; it += kPeThreads) {
-    const int r = it % H, rest = it / H;
+  for (int it = tid; it < kPeCh * ngrp * nrb; it += kPeThreads) {
+    const int rb = it % nrb, rest = it / nrb;
     const int g = rest % ngrp, c = rest / ngrp;
-    const int ch = cg * kPeCh + c, j0 = g * 8;
-    const float* p = plane + c * P2 + r * W2 + j0;   // window top-left: image (r-1, j0-1)
+    const int ch = cg * kPeCh + c, j0 = g * 8, r0 = rb * kPeRows;
     float w[9];
 #pragma unroll
     for (int t = 0; t < 9; ++t) w[t] = __bfloat162float(w_pe[ch * 9 + t]);
-    float acc[8];
     const float bias = b_pe[ch];
+    const float* p = plane + c * P2 + r0 * W2 + j0;   // window top-left: image (r0-1, j0-1)
+    float xa[10], xb[10];
+#pragma unroll
+    for (int q = 0; q < 10; ++q) {
+      xa[q] = p[q];
+      xb[q] = p[W2 + q];
+    }
+    __half* out = pebuf + ((size_t)b * kC + ch) * Np + (size_t)r0 * W + j0;
+#pragma unroll
+    for (int rr = 0; rr < kPeRows; ++rr) {
+      if (r0 + rr >= H) break;
+      float xc[10];
+#pragma unroll
+      for (int q = 0; q < 10; ++q) xc[q] = p[(rr + 2) * W2 + q];
+      float acc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float a = fmaf(w[0], xa[e], fmaf(w[1], xa[e + 1], fmaf(w[2], xa[e + 2], bias)));
+        a = fmaf(w[3], xb[e], fmaf(w[4], xb[e + 1], fmaf(w[5], xb[e + 2], a)));
+        acc[e] = fmaf(w[6], xc[e], fmaf(w[7], xc[e + 1], fmaf(w[8], xc[e + 2], a)));
+      }
+      if (vec_store) {
+        uint4 u;
+        u.x = pack_f16x2(acc[0], acc[1]);
+        u.y = pack_f16x2(acc[2], acc[3]);
+        u.z = pack_f16x2(acc[4], acc[5]);
+        u.w = pack_f16x2(acc[6], acc[7]);
+        *reinterpret_cast<uint4*>(out) = u;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (j0 + e < W) out[e] = __float2half_rn(acc[e]);
+      }
+#pragma unroll
+      for (int q = 0; q < 10; ++q) {
+        xa[q] = xb[q];
+        xb[q] = xc[q];
+      }
+      out += W;
+    }
+  }
+}
+
+// Kernel 3v: the same positional encoding for W % 8 == 0 without shared
+// memory: a thread produces an 8-column × kPevRows-row block of one channel
+// (columns j0..j0+7 of rows r0..r0+kPevRows-1) from kPevRows+2 sixteen-byte
+// row loads plus the two edge values of each row (L1 hits: neighbouring
+// threads read the same lines), all issued before any arithmetic, with packed
+// f32x2 FMAs.  Blocks are numbered over all B·C planes, so a launch has no
+// idle tail per plane.  CTA 0 also converts W_proj, as above.
+constexpr int kPevThreads = 256;
+constexpr int kPevRows = 4;
+
+__global__ void __launch_bounds__(kPevThreads)
+pe_dwconv_vec_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __restrict__ w_pe,
+                     const float* __restrict__ b_pe, __half* __restrict__ pebuf,
+                     const __nv_bfloat16* __restrict__ w_proj, __half* __restrict__ wproj16, int B, int H, int W,
+                     int Np) {
+  const int tid = threadIdx.x;
+  if (blockIdx.x == 0) {
+    for (int i = tid; i < kC * kC / 8; i += kPevThreads) {
+      const uint4 src = __ldg(reinterpret_cast<const uint4*>(w_proj) + i);
+      const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&src);
+      uint4 u;
+      uint32_t* uu = &u.x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(s2[e]);
+        uu[e] = pack_f16x2_sat(f.x, f.y);
+      }
+      reinterpret_cast<uint4*>(wproj16)[i] = u;
+    }
+  }
+  constexpr int R = kPevRows;
+  const unsigned cpr = W >> 3, nrb = (H + R - 1) / R, nblk = nrb * cpr;  // per plane
+  const unsigned q = blockIdx.x * kPevThreads + tid;  // < 2^31 (checked by the launcher)
+  if (q >= (unsigned)B * kC * nblk) return;
+  const unsigned plane = q / nblk, k = q - plane * nblk;
+  const int rb = (int)(k / cpr), j0 = (int)(k - rb * cpr) * 8, r0 = rb * R, ch = (int)(plane % kC);
+  const __half* src = vbuf + (size_t)plane * Np + j0;
+  // rows r0-1 .. r0+R, clamped into the image (masked below)
+  uint4 u[R + 2];
+  __half2 edge[R + 2];
+#pragma unroll
+  for (int i = 0; i < R + 2; ++i) {
+    const int rr = min(max(r0 + i - 1, 0), H - 1);
+    const __half* row = src + (size_t)rr * W;
+    u[i] = __ldg(reinterpret_cast<const uint4*>(row));
+    edge[i] = __halves2half2(__ldg(row + (j0 > 0 ? -1 : 0)), __ldg(row + (j0 + 8 < W ? 8 : 7)));
+  }
+  float w[9];
+#pragma unroll
+  for (int t = 0; t < 9; ++t) w[t] = __bfloat162float(w_pe[ch * 9 + t]);
+  const float bias = b_pe[ch];
+  float x[R + 2][10];
+#pragma unroll
+  for (int i = 0; i < R + 2; ++i) {
+    const int rr = r0 + i - 1;
+    const bool in = rr >= 0 && rr < H;
+    const __half2* h2 = reinterpret_cast<const __half2*>(&u[i]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h2[e]);
+      x[i][1 + 2 * e] = in ? f.x : 0.f;
+      x[i][2 + 2 * e] = in ? f.y : 0.f;
+    }
+    const float2 ed = __half22float2(edge[i]);
+    x[i][0] = in && j0 > 0 ? ed.x : 0.f;
+    x[i][9] = in && j0 + 8 < W ? ed.y : 0.f;
+  }
+  __half* dst = pebuf + (size_t)plane * Np + (size_t)r0 * W + j0;
+#pragma unroll
+  for (int o = 0; o < R; ++o) {
+    if (r0 + o >= H) break;
+    float acc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = bias;
 #pragma unroll
     for (int di = 0; di < 3; ++di) {
-      float x[10];
+      const float* xr = x[o + di];
 #pragma unroll
-      for (int q = 0; q < 10; ++q) x[q] = p[di * W2 + q];
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        acc[e] = fmaf(w[di * 3], x[e], fmaf(w[di * 3 + 1], x[e + 1], fmaf(w[di * 3 + 2], x[e + 2], acc[e])));
+      for (int e = 0; e < 8; e += 2) {
+        ffma2(acc[e], acc[e + 1], w[di * 3 + 2], w[di * 3 + 2], xr[e + 2], xr[e + 3], acc[e], acc[e + 1]);
+        ffma2(acc[e], acc[e + 1], w[di * 3 + 1], w[di * 3 + 1], xr[e + 1], xr[e + 2], acc[e], acc[e + 1]);
+        ffma2(acc[e], acc[e + 1], w[di * 3], w[di * 3], xr[e], xr[e + 1], acc[e], acc[e + 1]);
+      }
     }
-    __half* out = pebuf + ((size_t)b * kC + ch) * Np + (size_t)r * W + j0;
-    if (vec_store) {
-      uint4 u;
-      u.x = pack_f16x2(acc[0], acc[1]);
-      u.y = pack_f16x2(acc[2], acc[3]);
-      u.z = pack_f16x2(acc[4], acc[5]);
-      u.w = pack_f16x2(acc[6], acc[7]);
-      *reinterpret_cast<uint4*>(out) = u;
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (j0 + e < W) out[e] = __float2half_rn(acc[e]);
-    }
+    uint4 ov;
+    ov.x = pack_f16x2(acc[0], acc[1]);
+    ov.y = pack_f16x2(acc[2], acc[3]);
+    ov.z = pack_f16x2(acc[4], acc[5]);
+    ov.w = pack_f16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(dst + (size_t)o * W) = ov;
   }
 }
 
@@ -953,6 +1197,186 @@ proj_kernel(const __grid_constant__ CUtensorMap map_o, const __grid_constant__ C
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
+// Kernel 4p: the projection for N % 8 == 0 (y rows TMA-addressable),
+// persistent and transposed: D[128 out-channels][128 tokens] = W_proj·O +
+// W_proj·PE (W_proj resident as the K-major A operand, the O and PE tiles as
+// MN-major B operands straight from their channel-major buffers), so y comes
+// out of the tensor core channel-major.  Warp 0 streams (O, PE) tiles through
+// a two-stage TMA ring, warp 1 issues the 16 MMAs of a tile into one of two
+// TMEM accumulators, warps 2-5 (thread = output channel) add b_proj, stage
+// the bf16 tile as two SW128 [128 channels][64 tokens] boxes and one thread
+// writes them with TMA stores.
+constexpr int kPpStages = 2;
+constexpr int kPpThreads = 6 * 32;
+
+struct ProjPSmem {
+  uint8_t w[2][kC * 128];                // W_proj f16, K-major SW128: 2 k-blocks × 128 rows
+  uint8_t x[kPpStages][2][2][kC * 128];  // [stage][O, PE][token half]: 128 channel rows × 64 tokens, SW128
+  uint8_t yst[2][kC * 128];              // y staging [token half]: 128 channel rows × 64 tokens bf16, SW128
+  float bias[kC];
+  uint64_t w_full, x_full[kPpStages], x_empty[kPpStages], acc_full[2], acc_empty[2], stage_free, stage_full, fin;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __launch_bounds__(kPpThreads, 1)
+proj_pers_kernel(const __grid_constant__ CUtensorMap map_o, const __grid_constant__ CUtensorMap map_pe,
+                 const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_y,
+                 const float* __restrict__ b_proj, int B, int ntile) {
+  extern __shared__ uint8_t smem_raw[];
+  ProjPSmem& sm =
+      *reinterpret_cast<ProjPSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int total = B * ntile;
+  const int cnt = (int)blockIdx.x < total ? (total - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+  auto tile_of = [&](int i) { return (int)blockIdx.x + i * (int)gridDim.x; };
+
+  if (tid == 0) {
+    mbar_init(&sm.w_full, 1);
+    for (int s = 0; s < kPpStages; ++s) {
+      mbar_init(&sm.x_full[s], 1);
+      mbar_init(&sm.x_empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sm.acc_full[a], 1);
+      mbar_init(&sm.acc_empty[a], 128);
+    }
+    mbar_init(&sm.stage_free, 1);
+    mbar_init(&sm.stage_full, 128);
+    mbar_init(&sm.fin, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  for (int i = tid; i < kC; i += kPpThreads) sm.bias[i] = b_proj[i];
+  if (warp == 0) {
+    tmem_alloc(&sm.tmem_base, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ── TMA producer ──
+      tma_prefetch_desc(&map_o);
+      tma_prefetch_desc(&map_pe);
+      tma_prefetch_desc(&map_w);
+      mbar_arrive_expect_tx(&sm.w_full, 2 * kC * 128);
+      tma_load_2d(sm.w[0], &map_w, &sm.w_full, 0, 0);
+      tma_load_2d(sm.w[1], &map_w, &sm.w_full, 64, 0);
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < cnt; ++i) {
+        const int s = i % kPpStages, t = tile_of(i), b = t / ntile, n0 = (t - b * ntile) * kTile;
+        if (i >= kPpStages &&
+            !(ok = mbar_wait(&sm.x_empty[s], ((i / kPpStages) - 1) & 1, &sm.abort, &g_tc_status, 40)))
+          break;
+        mbar_arrive_expect_tx(&sm.x_full[s], 4 * kC * 128);
+        tma_load_2d(sm.x[s][0][0], &map_o, &sm.x_full[s], n0, b * kC);
+        tma_load_2d(sm.x[s][0][1], &map_o, &sm.x_full[s], n0 + 64, b * kC);
+        tma_load_2d(sm.x[s][1][0], &map_pe, &sm.x_full[s], n0, b * kC);
+        tma_load_2d(sm.x[s][1][1], &map_pe, &sm.x_full[s], n0 + 64, b * kC);
+        ++issued;
+      }
+      const long long c0 = clock64();
+      while (!mbar_try_wait(&sm.w_full, 0) && clock64() - c0 < kSpinCycles) {
+      }
+      if (!ok) {
+        for (int i = max(0, issued - kPpStages); i < issued; ++i) {
+          const long long c1 = clock64();
+          while (!mbar_try_wait(&sm.x_full[i % kPpStages], (i / kPpStages) & 1) && clock64() - c1 < kSpinCycles) {
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ── MMA issuer (converged warp, elected lane) ──
+    constexpr uint32_t idesc = idesc_f32acc(128, kTile, AB_F16, /*a_mn=*/false, /*b_mn=*/true);
+    const uint32_t w0 = smem_u32(sm.w[0]);
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.w_full, 0, &sm.abort, &g_tc_status, 41));
+    for (int i = 0; ok && i < cnt; ++i) {
+      const int s = i % kPpStages, a = i & 1;
+      if (i >= 2) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&sm.acc_empty[a], ((i >> 1) - 1) & 1, &sm.abort, &g_tc_status, 42));
+        if (!ok) break;
+      }
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.x_full[s], (i / kPpStages) & 1, &sm.abort, &g_tc_status, 43));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int src = 0; src < 2; ++src) {  // O, then PE into the same accumulator
+        const uint32_t x0 = smem_u32(sm.x[s][src][0]);
+#pragma unroll
+        for (int k = 0; k < kC / 16; ++k) {
+          const uint64_t ad = sdesc(w0 + (k >> 2) * (kC * 128) + (k & 3) * 32, 16, 1024, SW_128B);
+          const uint64_t bd = sdesc(x0 + k * 16 * 128, /*lbo=*/kC * 128, /*sbo=*/1024, SW_128B);
+          mma_ss_w(tmem + a * 128, ad, bd, idesc, (src | k) ? 1u : 0u);
+        }
+      }
+      mma_commit_w(&sm.x_empty[s]);
+      mma_commit_w(&sm.acc_full[a]);
+    }
+    mma_commit_w(&sm.fin);
+    const long long c0 = clock64();
+    while (!mbar_try_wait(&sm.fin, 0) && clock64() - c0 < kSpinCycles) {
+    }
+    __syncwarp();
+  } else {
+    // ── epilogue warps 2-5: thread = output channel (TMEM lane) ──
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const bool storer = warp == 2 && lane == 0;
+    const float bv = sm.bias[row];
+    for (int i = 0; i < cnt; ++i) {
+      const int a = i & 1, t = tile_of(i), b = t / ntile, n0 = (t - b * ntile) * kTile;
+      if (!mbar_wait(&sm.acc_full[a], (i >> 1) & 1, &sm.abort, &g_tc_status, 44)) break;
+      tc_fence_after();
+      if (storer) {  // the previous tile's y store has read the staging tile
+        tma_store_wait_read();
+        mbar_arrive(&sm.stage_free);
+      }
+      if (!mbar_wait(&sm.stage_free, i & 1, &sm.abort, &g_tc_status, 45)) break;
+#pragma unroll 1
+      for (int c = 0; c < kTile / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + a * 128 + c * 32, r);
+        tmem_ld_wait();
+        reg_fence(r);
+        uint8_t* box = sm.yst[c >> 1];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            v[e] = __uint_as_float(r[q * 8 + e]);
+            v[e + 1] = __uint_as_float(r[q * 8 + e + 1]);
+            fadd2(v[e], v[e + 1], bv, bv);
+          }
+          *reinterpret_cast<uint4*>(box + sw128_off(row, (c & 1) * 4 + q)) =
+              make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                         pack_bf16x2(v[6], v[7]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sm.acc_empty[a]);
+      fence_proxy_async_smem();
+      mbar_arrive(&sm.stage_full);
+      if (storer) {
+        if (!mbar_wait(&sm.stage_full, i & 1, &sm.abort, &g_tc_status, 46)) break;
+        tma_store_2d(&map_y, sm.yst[0], n0, b * kC);  // columns past N are clipped
+        tma_store_2d(&map_y, sm.yst[1], n0 + 64, b * kC);
+        tma_store_commit();
+      }
+    }
+    if (storer) tma_store_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
 // x with a row pitch that TMA cannot address (N*2 bytes not a multiple of 16)
@@ -1054,7 +1478,7 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
     if (int rc = check_launch("psa pad")) return rc;
     xs = xp;
   }
-  CUtensorMap mx, mw, mqk, mv;
+  CUtensorMap mx, mw, mqk, mv, mvst;
   {
     uint64_t d[2] = {(uint64_t)N, (uint64_t)B * kC}, s[1] = {(uint64_t)Np * 2};
     uint32_t bx[2] = {64, kC};
@@ -1063,7 +1487,7 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   }
   {
     uint64_t d[2] = {(uint64_t)kC, (uint64_t)kQKV}, s[1] = {(uint64_t)kC * 2};
-    uint32_t bx[2] = {64, kQKV};
+    uint32_t bx[2] = {64, 64};  // 64-row boxes: the kernel regroups W_qkv's rows on load
     if (int rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_qkv, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B,
                           "w_qkv"))
       return rc;
@@ -1080,6 +1504,14 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
     if (int rc = make_map(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, vb, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B, "v"))
       return rc;
   }
+  {
+    // V store: [B·C rows][Np] f16 in SW128 boxes of 64 tokens × 128 channels; inner
+    // extent N, so a tile's columns past N are not written
+    uint64_t d[2] = {(uint64_t)N, (uint64_t)B * kC}, s[1] = {(uint64_t)Np * 2};
+    uint32_t bx[2] = {64, kC};
+    if (int rc = make_map(&mvst, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, vb, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B, "v store"))
+      return rc;
+  }
   const int ntile = (N + kTile - 1) / kTile;
   const size_t sm1 = sizeof(QkvSmem) + 1024, sm2 = sizeof(AttnSmem<kKD>) + 1024, sm4 = sizeof(ProjSmem) + 1024;
   const size_t sm3 = (size_t)kPeCh * (H + 2) * ((W + 10) | 1) * sizeof(float);
@@ -1089,6 +1521,7 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
     if (int rc = set_smem(attn_kernel<kKD, kOutChannelMajor>, sm2)) return rc;
     if (int rc = set_smem(pe_dwconv_kernel, (size_t)kPeCh * kMaxPlane * sizeof(float))) return rc;
     if (int rc = set_smem(proj_kernel, sm4)) return rc;
+    if (int rc = set_smem(proj_pers_kernel, sizeof(ProjPSmem) + 1024)) return rc;
     attr_done = true;
   }
   __half* peb = reinterpret_cast<__half*>(base + L.pe);
@@ -1109,15 +1542,32 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
                           "w_proj"))
       return rc;
   }
-  qkv_proj_kernel<<<dim3(ntile, B), 128, sm1, st>>>(mx, mw, b_qkv, qk, vb, N, Np, nh);
+  qkv_proj_kernel<<<std::min(B * ntile, 148), kQpThreads, sm1, st>>>(mx, mw, mvst, b_qkv, qk, N, nh, B, ntile);
   if (int rc = check_launch("psa qkv_proj")) return rc;
   const float scale_log2 = (1.0f / sqrtf((float)kd)) * 1.4426950408889634f;
   attn_kernel<kKD, kOutChannelMajor>
       <<<dim3((ntile + 1) / 2, BH), kAttnThreads, sm2, st>>>(mqk, mv, ob, lse_out, N, Np, nh, scale_log2);
   if (int rc = check_launch("psa attention")) return rc;
-  pe_dwconv_kernel<<<dim3(kC / kPeCh, B), kPeThreads, sm3, st>>>(vb, w_pe, b_pe, peb, w_proj, wp16, H, W, Np);
+  const long long pe_blocks = (long long)B * kC * ((H + kPevRows - 1) / kPevRows) * (W >> 3);
+  if ((W & 7) == 0 && pe_blocks < (1LL << 31)) {
+    const long long chunks = pe_blocks;
+    pe_dwconv_vec_kernel<<<(unsigned)((chunks + kPevThreads - 1) / kPevThreads), kPevThreads, 0, st>>>(
+        vb, w_pe, b_pe, peb, w_proj, wp16, B, H, W, Np);
+  } else {
+    pe_dwconv_kernel<<<dim3(kC / kPeCh, B), kPeThreads, sm3, st>>>(vb, w_pe, b_pe, peb, w_proj, wp16, H, W, Np);
+  }
   if (int rc = check_launch("psa pe")) return rc;
-  proj_kernel<<<dim3(ntile, B), 128, sm4, st>>>(mo, mpe, mwp, b_proj, y, N);
+  if (N % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    CUtensorMap my;
+    uint64_t d[2] = {(uint64_t)N, (uint64_t)B * kC}, s[1] = {(uint64_t)N * 2};
+    uint32_t bx[2] = {64, kC};
+    if (int rc = make_map(&my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B, "y"))
+      return rc;
+    proj_pers_kernel<<<std::min(B * ntile, 148), kPpThreads, sizeof(ProjPSmem) + 1024, st>>>(mo, mpe, mwp, my,
+                                                                                              b_proj, B, ntile);
+  } else {
+    proj_kernel<<<dim3(ntile, B), 128, sm4, st>>>(mo, mpe, mwp, b_proj, y, N);
+  }
   return check_launch("psa proj");
 }
 
