@@ -1016,21 +1016,54 @@ pe_dwconv_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __restric
   }
 }
 
-// Kernel 3v: the same positional encoding for W % 8 == 0 without shared
-// memory: a thread produces an 8-column × kPevRows-row block of one channel
-// (columns j0..j0+7 of rows r0..r0+kPevRows-1) from kPevRows+2 sixteen-byte
-// row loads plus the two edge values of each row (L1 hits: neighbouring
-// threads read the same lines), all issued before any arithmetic, with packed
-// f32x2 FMAs.  Blocks are numbered over all B·C planes, so a launch has no
-// idle tail per plane.  CTA 0 also converts W_proj, as above.
+// Kernel 3v: the same positional encoding for W % CW == 0 (CW = 8 or 4)
+// without shared memory: a thread produces a CW-column × kPevRows-row block of
+// one channel (columns j0..j0+CW-1 of rows r0..r0+kPevRows-1) from kPevRows+2
+// row loads of 2·CW bytes plus the two edge values of each row (L1 hits:
+// neighbouring threads read the same lines), all issued before any
+// arithmetic, with packed f32x2 FMAs.  Blocks are numbered over all B·C
+// planes, so a launch has no idle tail per plane.  CTA 0 also converts
+// W_proj, as above.
 constexpr int kPevThreads = 256;
 constexpr int kPevRows = 4;
 
+template <int CW> struct PeRow;
+template <> struct PeRow<8> {
+  using T = uint4;
+  __device__ static void unpack(const T& u, float* x) {
+    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h2[e]);
+      x[2 * e] = f.x;
+      x[2 * e + 1] = f.y;
+    }
+  }
+  __device__ static T pack(const float* a) {
+    return make_uint4(pack_f16x2(a[0], a[1]), pack_f16x2(a[2], a[3]), pack_f16x2(a[4], a[5]), pack_f16x2(a[6], a[7]));
+  }
+};
+template <> struct PeRow<4> {
+  using T = uint2;
+  __device__ static void unpack(const T& u, float* x) {
+    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float2 f = __half22float2(h2[e]);
+      x[2 * e] = f.x;
+      x[2 * e + 1] = f.y;
+    }
+  }
+  __device__ static T pack(const float* a) { return make_uint2(pack_f16x2(a[0], a[1]), pack_f16x2(a[2], a[3])); }
+};
+
+template <int CW>
 __global__ void __launch_bounds__(kPevThreads)
 pe_dwconv_vec_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __restrict__ w_pe,
                      const float* __restrict__ b_pe, __half* __restrict__ pebuf,
                      const __nv_bfloat16* __restrict__ w_proj, __half* __restrict__ wproj16, int B, int H, int W,
                      int Np) {
+  using Row = PeRow<CW>;
   const int tid = threadIdx.x;
   if (blockIdx.x == 0) {
     for (int i = tid; i < kC * kC / 8; i += kPevThreads) {
@@ -1047,65 +1080,57 @@ pe_dwconv_vec_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __res
     }
   }
   constexpr int R = kPevRows;
-  const unsigned cpr = W >> 3, nrb = (H + R - 1) / R, nblk = nrb * cpr;  // per plane
+  const unsigned cpr = W / CW, nrb = (H + R - 1) / R, nblk = nrb * cpr;  // per plane
   const unsigned q = blockIdx.x * kPevThreads + tid;  // < 2^31 (checked by the launcher)
   if (q >= (unsigned)B * kC * nblk) return;
   const unsigned plane = q / nblk, k = q - plane * nblk;
-  const int rb = (int)(k / cpr), j0 = (int)(k - rb * cpr) * 8, r0 = rb * R, ch = (int)(plane % kC);
+  const int rb = (int)(k / cpr), j0 = (int)(k - rb * cpr) * CW, r0 = rb * R, ch = (int)(plane % kC);
   const __half* src = vbuf + (size_t)plane * Np + j0;
   // rows r0-1 .. r0+R, clamped into the image (masked below)
-  uint4 u[R + 2];
+  typename Row::T u[R + 2];
   __half2 edge[R + 2];
 #pragma unroll
   for (int i = 0; i < R + 2; ++i) {
     const int rr = min(max(r0 + i - 1, 0), H - 1);
     const __half* row = src + (size_t)rr * W;
-    u[i] = __ldg(reinterpret_cast<const uint4*>(row));
-    edge[i] = __halves2half2(__ldg(row + (j0 > 0 ? -1 : 0)), __ldg(row + (j0 + 8 < W ? 8 : 7)));
+    u[i] = __ldg(reinterpret_cast<const typename Row::T*>(row));
+    edge[i] = __halves2half2(__ldg(row + (j0 > 0 ? -1 : 0)), __ldg(row + (j0 + CW < W ? CW : CW - 1)));
   }
   float w[9];
 #pragma unroll
   for (int t = 0; t < 9; ++t) w[t] = __bfloat162float(w_pe[ch * 9 + t]);
   const float bias = b_pe[ch];
-  float x[R + 2][10];
+  float x[R + 2][CW + 2];
 #pragma unroll
   for (int i = 0; i < R + 2; ++i) {
     const int rr = r0 + i - 1;
     const bool in = rr >= 0 && rr < H;
-    const __half2* h2 = reinterpret_cast<const __half2*>(&u[i]);
+    float xv[CW];
+    Row::unpack(u[i], xv);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __half22float2(h2[e]);
-      x[i][1 + 2 * e] = in ? f.x : 0.f;
-      x[i][2 + 2 * e] = in ? f.y : 0.f;
-    }
+    for (int e = 0; e < CW; ++e) x[i][1 + e] = in ? xv[e] : 0.f;
     const float2 ed = __half22float2(edge[i]);
     x[i][0] = in && j0 > 0 ? ed.x : 0.f;
-    x[i][9] = in && j0 + 8 < W ? ed.y : 0.f;
+    x[i][CW + 1] = in && j0 + CW < W ? ed.y : 0.f;
   }
   __half* dst = pebuf + (size_t)plane * Np + (size_t)r0 * W + j0;
 #pragma unroll
   for (int o = 0; o < R; ++o) {
     if (r0 + o >= H) break;
-    float acc[8];
+    float acc[CW];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = bias;
+    for (int e = 0; e < CW; ++e) acc[e] = bias;
 #pragma unroll
     for (int di = 0; di < 3; ++di) {
       const float* xr = x[o + di];
 #pragma unroll
-      for (int e = 0; e < 8; e += 2) {
+      for (int e = 0; e < CW; e += 2) {
         ffma2(acc[e], acc[e + 1], w[di * 3 + 2], w[di * 3 + 2], xr[e + 2], xr[e + 3], acc[e], acc[e + 1]);
         ffma2(acc[e], acc[e + 1], w[di * 3 + 1], w[di * 3 + 1], xr[e + 1], xr[e + 2], acc[e], acc[e + 1]);
         ffma2(acc[e], acc[e + 1], w[di * 3], w[di * 3], xr[e], xr[e + 1], acc[e], acc[e + 1]);
       }
     }
-    uint4 ov;
-    ov.x = pack_f16x2(acc[0], acc[1]);
-    ov.y = pack_f16x2(acc[2], acc[3]);
-    ov.z = pack_f16x2(acc[4], acc[5]);
-    ov.w = pack_f16x2(acc[6], acc[7]);
-    *reinterpret_cast<uint4*>(dst + (size_t)o * W) = ov;
+    *reinterpret_cast<typename Row::T*>(dst + (size_t)o * W) = Row::pack(acc);
   }
 }
 
@@ -1548,11 +1573,14 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   attn_kernel<kKD, kOutChannelMajor>
       <<<dim3((ntile + 1) / 2, BH), kAttnThreads, sm2, st>>>(mqk, mv, ob, lse_out, N, Np, nh, scale_log2);
   if (int rc = check_launch("psa attention")) return rc;
-  const long long pe_blocks = (long long)B * kC * ((H + kPevRows - 1) / kPevRows) * (W >> 3);
-  if ((W & 7) == 0 && pe_blocks < (1LL << 31)) {
-    const long long chunks = pe_blocks;
-    pe_dwconv_vec_kernel<<<(unsigned)((chunks + kPevThreads - 1) / kPevThreads), kPevThreads, 0, st>>>(
-        vb, w_pe, b_pe, peb, w_proj, wp16, B, H, W, Np);
+  const int pe_cw = (W & 7) == 0 ? 8 : (W & 3) == 0 ? 4 : 0;
+  const long long pe_blocks = pe_cw ? (long long)B * kC * ((H + kPevRows - 1) / kPevRows) * (W / pe_cw) : 0;
+  if (pe_cw && pe_blocks < (1LL << 31)) {
+    const unsigned grid = (unsigned)((pe_blocks + kPevThreads - 1) / kPevThreads);
+    if (pe_cw == 8)
+      pe_dwconv_vec_kernel<8><<<grid, kPevThreads, 0, st>>>(vb, w_pe, b_pe, peb, w_proj, wp16, B, H, W, Np);
+    else
+      pe_dwconv_vec_kernel<4><<<grid, kPevThreads, 0, st>>>(vb, w_pe, b_pe, peb, w_proj, wp16, B, H, W, Np);
   } else {
     pe_dwconv_kernel<<<dim3(kC / kPeCh, B), kPeThreads, sm3, st>>>(vb, w_pe, b_pe, peb, w_proj, wp16, H, W, Np);
   }
