@@ -695,12 +695,21 @@ def run_ours(args, ws, rank, local):
         torch.cuda.synchronize()
 
     clk = ClockSampler(local).start()
+    # Warm up in chunks of `warmup` steps until both the step count and the
+    # minimum duration are reached; with several ranks they agree (MAX) after
+    # every chunk, so all run the same number of steps — a step may hold a
+    # collective (cfg5), and ranks that disagreed on the count would hang.
     t_w, nw = time.perf_counter(), 0
-    while nw < args.warmup or time.perf_counter() - t_w < args.min_warm_s:
-        wl.step()
-        nw += 1
-        if nw % 50 == 0:
-            torch.cuda.synchronize()
+    while True:
+        for _ in range(args.warmup):
+            wl.step()
+            nw += 1
+        torch.cuda.synchronize()
+        more = torch.tensor([1.0 if time.perf_counter() - t_w < args.min_warm_s else 0.0], device=dev)
+        if ws > 1:
+            dist.all_reduce(more, op=dist.ReduceOp.MAX)
+        if more.item() == 0.0:
+            break
     barrier()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
