@@ -20,10 +20,21 @@ GRAD_SLICES = {"w_qkv": (0, 32768), "w_proj": (32768, 49152), "w_pe": (49152, 50
 
 
 class PsaTrainStep:
-    """Buffers for one rank's shard of B images of 128×H×W."""
+    """Buffers for one rank's shard of B images of 128×H×W.
 
-    def __init__(self, B: int, H: int, W: int, device, C: int = 128, num_heads: int = 2, key_dim: int = 32):
+    ``graph=True`` replays ``forward_backward`` from a CUDA graph once it has
+    run eagerly for a given set of input / parameter tensors: the ≈15 kernel
+    launches of a step then cost one graph launch on the host (an eager step
+    spends ≈105 µs of host time on ≈160 µs of GPU work at cfg5, which lets
+    the host, not the GPU, pace a multi-rank step).  The graph is re-captured
+    whenever the tensors' addresses change; it runs on the current stream."""
+
+    def __init__(self, B: int, H: int, W: int, device, C: int = 128, num_heads: int = 2, key_dim: int = 32,
+                 graph: bool = False):
         self.B, self.H, self.W, self.C, self.nh, self.kd = B, H, W, C, num_heads, key_dim
+        self.use_graph, self._graph, self._graph_key = graph, None, None
+        self.graph_kernels = 0     # kernels one replay launches (the library's launch counter skips replays)
+        self.replayed_kernels = 0  # kernels launched by replays so far
         need = int(_lib.lib().va_psa_train_workspace_bytes(B, H, W))
         self.ws = torch.empty(need, dtype=torch.uint8, device=device)
         self.grads = torch.empty(GRAD_COUNT, dtype=torch.float32, device=device)
@@ -33,11 +44,28 @@ class PsaTrainStep:
 
     def forward_backward(self, x, target, params: dict, want_dx: bool = False, stream=None):
         """Returns ``(y, loss, grads, dx)`` (device tensors; dx None unless asked)."""
+        if self.use_graph and stream is None and not want_dx:
+            key = (x.data_ptr(), target.data_ptr()) + tuple(params[k].data_ptr() for k in sorted(params))
+            if self._graph is None or self._graph_key != key:
+                self._launch(x, target, params, False, None)  # eager first: one-time set-up stays out of the graph
+                torch.cuda.current_stream().synchronize()
+                g = torch.cuda.CUDAGraph()
+                n0 = int(_lib.lib().va_launch_count())
+                with torch.cuda.graph(g, capture_error_mode="relaxed"):
+                    self._launch(x, target, params, False, None)
+                self.graph_kernels = int(_lib.lib().va_launch_count()) - n0
+                self._graph, self._graph_key = g, key
+            self._graph.replay()
+            self.replayed_kernels += self.graph_kernels
+        else:
+            self._launch(x, target, params, want_dx, stream)
+        return self.y, self.loss, self.grads, (self.dx if want_dx else None)
+
+    def _launch(self, x, target, params: dict, want_dx: bool, stream):
         _lib.call("va_psa_train_fwd_bwd_bf16", _p(x), _p(target), _p(params["w_qkv"]), _p(params["b_qkv"]),
                   _p(params["w_pe"]), _p(params["b_pe"]), _p(params["w_proj"]), _p(params["b_proj"]), _p(self.y),
                   _p(self.dx) if want_dx else None, _p(self.grads), _p(self.loss), self.B, self.C, self.H, self.W,
                   self.nh, self.kd, _p(self.ws), self.ws.numel(), _stream(stream))
-        return self.y, self.loss, self.grads, (self.dx if want_dx else None)
 
     @staticmethod
     def master_from(params: dict) -> torch.Tensor:
