@@ -140,26 +140,37 @@ __global__ void tm_to_cm_kernel(const float* __restrict__ src, float* __restrict
   }
 }
 
-// One CTA per (qkv channel j, image b).  dqkv row: dQ = Σ_p dq_part[p] (p in
-// order), dK, or dV + dV_pe, where dV_pe = the depthwise 3×3 backward of dA on
-// channel c = h·64 + (j − h·128 − 64).  Writes the f16 row (pad zero), its
-// sum (db_qkv partial) and, on V channels, the dW_pe (9 taps) and db_pe
-// partials of (b, c).  Shared memory: the dA and V planes of (b, c), f32.
-__global__ void __launch_bounds__(kRowThreads)
+// One warp per (qkv channel j, image b) row, blockDim.x / 32 rows per CTA
+// (kAsmRows, or fewer for large images).  dqkv row:
+// dQ = Σ_p dq_part[p] (p in order), dK, or dV + dV_pe, where dV_pe = the
+// depthwise 3×3 backward of dA on channel c = h·64 + (j − h·128 − 64).
+// Writes the f16 row (pad zero), its sum (db_qkv partial) and, on V channels,
+// the dW_pe (9 taps) and db_pe partials of (b, c).  Every sum is a fixed-order
+// warp reduction (no block barrier).  Shared memory: per warp the dA and V
+// planes of (b, c), f32.
+constexpr int kAsmRows = 4;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__global__ void __launch_bounds__(kAsmRows * 32)
 assemble_kernel(const float* __restrict__ dq_part, int nparts, const float* __restrict__ dk, const float* __restrict__ dv,
                 const __half* __restrict__ dA, const __half* __restrict__ vb, const __nv_bfloat16* __restrict__ w_pe,
                 __half* __restrict__ d16, float* __restrict__ part_bqkv, float* __restrict__ part_wpe,
                 float* __restrict__ part_bpe, int B, int H, int W, int Np) {
-  extern __shared__ float planes[];  // [2][N]: dA, V
-  __shared__ float red[kRowThreads / 32];
-  const int j = blockIdx.x, b = blockIdx.y, N = H * W;
+  extern __shared__ float planes[];  // [rows][2][N]: dA, V
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x * (blockDim.x >> 5) + warp, b = blockIdx.y, N = H * W;
   const int h = j / 128, r = j % 128, bh = b * kNH + h;
   const size_t part = (size_t)B * kNH * kKD * N;
   __half* out = d16 + ((size_t)b * kQKV + j) * Np;
   float rs = 0.f;
   if (r < 64) {
     const float* src = r < 32 ? dq_part + ((size_t)bh * kKD + r) * N : dk + ((size_t)bh * kKD + r - 32) * N;
-    for (int n = threadIdx.x; n < Np; n += kRowThreads) {
+    for (int n = lane; n < Np; n += 32) {
       float g = 0.f;
       if (n < N) {
         if (r < 32) {
@@ -171,29 +182,30 @@ assemble_kernel(const float* __restrict__ dq_part, int nparts, const float* __re
       }
       out[n] = __float2half_rn(g);
     }
-    rs = block_sum(rs, red);
-    if (threadIdx.x == 0) part_bqkv[(size_t)b * kQKV + j] = rs;
+    rs = warp_sum(rs);
+    if (lane == 0) part_bqkv[(size_t)b * kQKV + j] = rs;
     return;
   }
   const int dd = r - 64, c = h * kHD + dd;
-  float* pa = planes;
-  float* pv = planes + N;
+  float* pa = planes + (size_t)warp * 2 * N;
+  float* pv = pa + N;
   const __half* arow = dA + ((size_t)b * kC + c) * Np;
   const __half* vrow = vb + ((size_t)b * kC + c) * Np;
-  for (int n = threadIdx.x; n < N; n += kRowThreads) {
+  for (int n = lane; n < N; n += 32) {
     pa[n] = __half2float(arow[n]);
     pv[n] = __half2float(vrow[n]);
   }
   float w[9];
 #pragma unroll
   for (int k = 0; k < 9; ++k) w[k] = __bfloat162float(w_pe[c * 9 + k]);
-  __syncthreads();
+  __syncwarp();
   const float* dvr = dv + ((size_t)bh * kHD + dd) * N;
   float tw[9] = {}, ab = 0.f;
-  for (int n = threadIdx.x; n < Np; n += kRowThreads) {
+  int yy = lane / W, xx = lane - yy * W;  // (y, x) of n, advanced by 32 per iteration
+  const int dy = 32 / W, dx = 32 - dy * W;
+  for (int n = lane; n < Np; n += 32) {
     float g = 0.f;
     if (n < N) {
-      const int yy = n / W, xx = n - yy * W;
       const float a = pa[n];
       ab += a;
       float pe = 0.f;
@@ -211,17 +223,22 @@ assemble_kernel(const float* __restrict__ dq_part, int nparts, const float* __re
       rs += g;
     }
     out[n] = __float2half_rn(g);
+    yy += dy;
+    xx += dx;
+    if (xx >= W) {
+      xx -= W;
+      ++yy;
+    }
   }
-  rs = block_sum(rs, red);
-  ab = block_sum(ab, red);
-  float twr[9];
+  rs = warp_sum(rs);
+  ab = warp_sum(ab);
 #pragma unroll
-  for (int k = 0; k < 9; ++k) twr[k] = block_sum(tw[k], red);
-  if (threadIdx.x == 0) {
+  for (int k = 0; k < 9; ++k) tw[k] = warp_sum(tw[k]);
+  if (lane == 0) {
     part_bqkv[(size_t)b * kQKV + j] = rs;
     part_bpe[(size_t)b * kC + c] = ab;
 #pragma unroll
-    for (int k = 0; k < 9; ++k) part_wpe[((size_t)b * kC + c) * 9 + k] = twr[k];
+    for (int k = 0; k < 9; ++k) part_wpe[((size_t)b * kC + c) * 9 + k] = tw[k];
   }
 }
 
@@ -415,7 +432,15 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   float* pbq = static_cast<float*>(at(L.part_bqkv));
   float* pwe = static_cast<float*>(at(L.part_wpe));
   float* pbe = static_cast<float*>(at(L.part_bpe));
-  assemble_kernel<<<dim3(kQKV, B), kRowThreads, 2 * (size_t)N * sizeof(float), st>>>(
+  static bool asm_attr = false;  // the planes of a large image need more than the default 48 KB
+  if (!asm_attr) {
+    cudaError_t e = cudaFuncSetAttribute(assemble_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    asm_attr = true;
+  }
+  int asm_rows = kAsmRows;  // rows (warps) per CTA: a power of two dividing kQKV whose planes fit
+  while (asm_rows > 1 && (size_t)asm_rows * 2 * N * sizeof(float) > 200 * 1024) asm_rows >>= 1;
+  assemble_kernel<<<dim3(kQKV / asm_rows, B), asm_rows * 32, (size_t)asm_rows * 2 * N * sizeof(float), st>>>(
       dqp, nparts, dk, dv, dA, vb, w_pe, dq16, pbq, pwe, pbe, B, H, W, Np);
   if (int rc = check_launch("psa train assemble")) return rc;
   // qkv backward
