@@ -9,8 +9,8 @@
 // attn [B][Q][nh][L][P] (already softmaxed), out [B][Q][nh·dh].
 //
 // Forward: a group of G = dh / VEC threads serves one (b, q, h); each thread
-// owns VEC channels and reads every bilinear corner as one 16-byte load
-// (f32: 4 channels, bf16: 8).  The block's locations and weights are staged
+// owns VEC channels and reads every bilinear corner as one vector load
+// (f32: 4 channels in 16 bytes, bf16: 4 channels in 8 bytes).  The block's locations and weights are staged
 // in shared memory with coalesced loads first.  The op is a gather: its HBM
 // floor is one pass over the value map.
 //
@@ -65,6 +65,25 @@ template <> struct Vec<__nv_bfloat16> {  // bf16 ↔ f32 by bit placement (exact
   }
 };
 
+// The forward gathers bf16 maps 4 channels (8 bytes) per thread: twice the
+// threads of 16-byte loads over the same rows, which the gather's latency
+// needs (with 8-channel loads the bf16 forward ran slower than the f32 one).
+struct VecBf4 {
+  static constexpr int N = 4;
+  __device__ static void load(const __nv_bfloat16* p, float (&v)[4]) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+    v[0] = __uint_as_float(u.x << 16);
+    v[1] = __uint_as_float(u.x & 0xffff0000u);
+    v[2] = __uint_as_float(u.y << 16);
+    v[3] = __uint_as_float(u.y & 0xffff0000u);
+  }
+  __device__ static void store(__nv_bfloat16* p, const float (&v)[4]) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(Vec<__nv_bfloat16>::pack(v[0], v[1]), Vec<__nv_bfloat16>::pack(v[2], v[3]));
+  }
+};
+template <typename TV> struct FwdVec { using type = Vec<TV>; };
+template <> struct FwdVec<__nv_bfloat16> { using type = VecBf4; };
+
 struct Levels {
   int H[kMaxLevels], W[kMaxLevels], s0[kMaxLevels];
 };
@@ -111,7 +130,7 @@ __global__ void __launch_bounds__(kMsdaThreads)
 msda_fwd_kernel(const TV* __restrict__ value, const int64_t* __restrict__ shapes, const int64_t* __restrict__ lstart,
                 const float* __restrict__ loc, const float* __restrict__ attn, TV* __restrict__ out, int B, int S,
                 int nh, int L, int Q, int P) {
-  constexpr int VEC = Vec<TV>::N, G = DH / VEC, ITEMS = kMsdaThreads / G;
+  constexpr int VEC = FwdVec<TV>::type::N, G = DH / VEC, ITEMS = kMsdaThreads / G;
   extern __shared__ float sm_f[];
   __shared__ Levels lv;
   const int LP = L * P;
@@ -144,7 +163,7 @@ msda_fwd_kernel(const TV* __restrict__ value, const int64_t* __restrict__ shapes
         const float a = ia[s];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {  // out-of-map corners load row 0 and contribute exactly 0
-          Vec<TV>::load(vbase + (size_t)c.pix[k] * nh * DH, v[p][k]);
+          FwdVec<TV>::type::load(vbase + (size_t)c.pix[k] * nh * DH, v[p][k]);
           cw[p][k] = c.ok[k] ? a * c.w[k] : 0.f;
           if (!c.ok[k]) {
 #pragma unroll
@@ -167,7 +186,7 @@ msda_fwd_kernel(const TV* __restrict__ value, const int64_t* __restrict__ shapes
         for (int k = 0; k < 4; ++k) {
           if (!c.ok[k]) continue;
           float vv[VEC];
-          Vec<TV>::load(vbase + (size_t)c.pix[k] * nh * DH, vv);
+          FwdVec<TV>::type::load(vbase + (size_t)c.pix[k] * nh * DH, vv);
           const float w = a * c.w[k];
 #pragma unroll
           for (int e = 0; e < VEC; ++e) acc[e] = fmaf(w, vv[e], acc[e]);
@@ -175,7 +194,7 @@ msda_fwd_kernel(const TV* __restrict__ value, const int64_t* __restrict__ shapes
       }
     }
   }
-  Vec<TV>::store(out + item * DH + part * VEC, acc);
+  FwdVec<TV>::type::store(out + item * DH + part * VEC, acc);
 }
 
 // Pass 1 of the backward: grad_attn, grad_loc, and the grad_value
@@ -187,7 +206,7 @@ msda_bwd_sample_kernel(const TV* __restrict__ value, const int64_t* __restrict__
                        const float* __restrict__ attn, const TV* __restrict__ grad_out, float* __restrict__ grad_loc,
                        float* __restrict__ grad_attn, int4* __restrict__ c_pix, float4* __restrict__ c_w, int B, int S,
                        int nh, int L, int Q, int P) {
-  constexpr int VEC = Vec<TV>::N, G = DH / VEC, ITEMS = kMsdaThreads / G;
+  constexpr int VEC = FwdVec<TV>::type::N, G = DH / VEC, ITEMS = kMsdaThreads / G;
   __shared__ Levels lv;
   load_levels(lv, shapes, lstart, L);
   __syncthreads();
@@ -200,7 +219,7 @@ msda_bwd_sample_kernel(const TV* __restrict__ value, const int64_t* __restrict__
   const int b = (int)(it / ((long long)Q * nh));
   const int LP = L * P;
   float g[VEC];
-  Vec<TV>::load(grad_out + it * DH + part * VEC, g);
+  FwdVec<TV>::type::load(grad_out + it * DH + part * VEC, g);
   for (int l = 0; l < L; ++l) {
     const int H = lv.H[l], W = lv.W[l];
     const TV* vbase = value + (((size_t)b * S + lv.s0[l]) * nh + h) * DH + part * VEC;
@@ -215,7 +234,7 @@ msda_bwd_sample_kernel(const TV* __restrict__ value, const int64_t* __restrict__
         float d = 0.f;
         if (c.ok[k]) {
           float v[VEC];
-          Vec<TV>::load(vbase + (size_t)c.pix[k] * nh * DH, v);
+          FwdVec<TV>::type::load(vbase + (size_t)c.pix[k] * nh * DH, v);
 #pragma unroll
           for (int e = 0; e < VEC; ++e) d = fmaf(g[e], v[e], d);
         }
@@ -436,7 +455,7 @@ int msda_fwd(const TV* value, const int64_t* shapes, const int64_t* lstart, cons
     const long long blocks = (items + per - 1) / per;
     kernel<<<(unsigned)blocks, kMsdaThreads, smem, st>>>(value, shapes, lstart, loc, attn, out, B, S, nh, L, Q, P);
   };
-  constexpr int VEC = Vec<TV>::N;
+  constexpr int VEC = FwdVec<TV>::type::N;
   if (P == 4) {
     if (dh == 16) launch(msda_fwd_kernel<TV, 16, 4>, 16 / VEC);
     else launch(msda_fwd_kernel<TV, 32, 4>, 32 / VEC);
@@ -471,7 +490,7 @@ int msda_bwd(const TV* value, const int64_t* shapes, const int64_t* lstart, cons
   int4* c_pix = static_cast<int4*>(ws);
   float4* c_w = reinterpret_cast<float4*>(static_cast<char*>(ws) + align256(nall * sizeof(int4)));
   const long long items = (long long)B * Q * nh;
-  constexpr int VEC = Vec<TV>::N;
+  constexpr int VEC = FwdVec<TV>::type::N;  // channels per thread in the sample pass, as in the forward
   auto pass1 = [&](auto kernel, int G) {
     const int per = kMsdaThreads / G;
     kernel<<<(unsigned)((items + per - 1) / per), kMsdaThreads, 0, st>>>(value, shapes, lstart, loc, attn, grad_out,
