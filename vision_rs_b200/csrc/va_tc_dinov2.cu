@@ -233,36 +233,33 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
 // ── window partition / un-partition ─────────────────────────────────────────
 // x [B][1 + gh·gw][C] (cls first, patches row-major) ↔ xw [B·nw][1 + win²][C]
 // (window w = wy·(gw/win) + wx; cls copied to token 0 of every window).
+// One thread per 16-byte chunk (32-bit index arithmetic: the element counts
+// are checked < 2^31 by the launchers; 64-bit divisions made these copies
+// instruction-bound).
 __global__ void window_partition_kernel(const uint4* __restrict__ x, uint4* __restrict__ xw, int B, int gh, int gw,
                                         int win, int cv) {
-  const int nwx = gw / win, nw = (gh / win) * nwx, tw = 1 + win * win;
-  const long long total = (long long)B * nw * tw * cv;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % cv);
-    const long long row = i / cv;
-    const int tok = (int)(row % tw);
-    const long long bw = row / tw;
-    const int w = (int)(bw % nw), b = (int)(bw / nw);
-    int src = 0;
-    if (tok > 0) {
-      const int iy = (tok - 1) / win, ix = (tok - 1) - iy * win;
-      const int wy = w / nwx, wx = w - wy * nwx;
-      src = 1 + (wy * win + iy) * gw + wx * win + ix;
-    }
-    xw[i] = x[((long long)b * (1 + gh * gw) + src) * cv + c];
+  const unsigned nwx = gw / win, nw = (gh / win) * nwx, tw = 1 + win * win;
+  const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (unsigned)B * nw * tw * cv) return;
+  const unsigned row = i / cv, c = i - row * cv;
+  const unsigned bw = row / tw, tok = row - bw * tw;
+  const unsigned b = bw / nw, w = bw - b * nw;
+  unsigned src = 0;
+  if (tok > 0) {
+    const unsigned iy = (tok - 1) / win, ix = (tok - 1) - iy * win;
+    const unsigned wy = w / nwx, wx = w - wy * nwx;
+    src = 1 + (wy * win + iy) * gw + wx * win + ix;
   }
+  xw[i] = x[((size_t)b * (1 + gh * gw) + src) * cv + c];
 }
 
 __global__ void window_unpartition_kernel(const __nv_bfloat16* __restrict__ xw, __nv_bfloat16* __restrict__ x, int B,
                                           int gh, int gw, int win, int C) {
   const int nwx = gw / win, nw = (gh / win) * nwx, tw = 1 + win * win, ntok = 1 + gh * gw;
-  const long long total = (long long)B * ntok * (C / 8);
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int c8 = (int)(i % (C / 8));
-    const long long row = i / (C / 8);
-    const int tok = (int)(row % ntok), b = (int)(row / ntok);
+  const unsigned cv = C / 8, i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < (unsigned)B * ntok * cv) {
+    const unsigned row = i / cv, c8 = i - row * cv;
+    const unsigned b = row / ntok, tok = row - b * ntok;
     uint4 out;
     if (tok == 0) {  // cls: mean of the windows' cls outputs, summed in window order
       float acc[8] = {};
@@ -417,7 +414,8 @@ int dino_window_partition(const __nv_bfloat16* x, __nv_bfloat16* xw, int B, int 
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(xw) & 15))
     return set_error(VA_ERR_ALIGN, "dinov2 window partition: 16-byte alignment needed");
   const long long total = (long long)B * (gh / win) * (gw / win) * (1 + win * win) * (C / 8);
-  window_partition_kernel<<<(int)std::min<long long>((total + 255) / 256, 148LL * 16), 256, 0, st>>>(
+  VA_CHECK_ARG(total < (1LL << 31), "dinov2 window partition: too many elements");
+  window_partition_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
       reinterpret_cast<const uint4*>(x), reinterpret_cast<uint4*>(xw), B, gh, gw, win, C / 8);
   return check_launch("dinov2 window partition");
 }
@@ -429,8 +427,8 @@ int dino_window_unpartition(const __nv_bfloat16* xw, __nv_bfloat16* x, int B, in
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(xw) & 15))
     return set_error(VA_ERR_ALIGN, "dinov2 window unpartition: 16-byte alignment needed");
   const long long total = (long long)B * (1 + gh * gw) * (C / 8);
-  window_unpartition_kernel<<<(int)std::min<long long>((total + 255) / 256, 148LL * 16), 256, 0, st>>>(xw, x, B, gh,
-                                                                                                      gw, win, C);
+  VA_CHECK_ARG(total < (1LL << 31), "dinov2 window unpartition: too many elements");
+  window_unpartition_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(xw, x, B, gh, gw, win, C);
   return check_launch("dinov2 window unpartition");
 }
 
