@@ -542,7 +542,7 @@ def torch_empty_like_qkv(x):
 class Cfg5:
     metric = "training images/sec (C2PSA PSA attention fwd+bwd+allreduce+SGD, bf16, 400 tokens)"
     unit, dtype, batch = "images/s", "bf16", T5_B
-    workload = ("cfg5: C2PSA PSA attention training step, 32 x 128x20x20 per GPU, MSE loss, NCCL all-reduce of "
+    workload = ("cfg5: C2PSA PSA attention training step, 32 x 128x20x20 per GPU, MSE loss, all-reduce of "
                 "the 50,816 f32 weight gradients, SGD on f32 master weights")
 
     def __init__(self, dev, rank, batch, args):
@@ -565,9 +565,21 @@ class Cfg5:
         self.xh = self.x.cpu().pin_memory()
         self.th = self.t.cpu().pin_memory()
         self.lh = torch.empty(1, dtype=torch.float32).pin_memory()
+        # several ranks: the all-reduce + SGD is one peer-memory kernel per rank
+        # (PeerGradComm), or NCCL all-reduce + the SGD kernel with --allreduce nccl
+        import torch.distributed as dist
+        multi = dist.is_initialized() and dist.get_world_size() > 1
+        self.comm = train.PeerGradComm() if multi and args.allreduce == "peer" else None
+        self.allreduce = ("none (one rank)" if not multi else
+                          "peer-memory all-reduce fused with SGD (one kernel)" if self.comm else "NCCL all-reduce")
 
     def step(self):
-        self.loss = self.train.dp_train_step(self.step_obj, self.x, self.t, self.params, self.master, self.lr)
+        self.loss = self.train.dp_train_step(self.step_obj, self.x, self.t, self.params, self.master, self.lr,
+                                             comm=self.comm)
+
+    def close(self):
+        if self.comm is not None:
+            self.comm.close()
 
     def e2e_step(self):
         self.x.copy_(self.xh, non_blocking=True)
@@ -586,13 +598,20 @@ class Cfg5:
         for _ in range(args.warmup):
             fb()
         ms = event_time(fb, max(5, args.steps), stream, flush)
-        ar_ms = None
+        ar_ms = nccl_ms = None
         if dist.is_initialized():
             g = self.step_obj.grads
-            ar = lambda: dist.all_reduce(g)
+            nccl = lambda: dist.all_reduce(g)
             for _ in range(3):
-                ar()
-            ar_ms = event_time(ar, max(5, args.steps), stream, None)
+                nccl()
+            nccl_ms = event_time(nccl, max(5, args.steps), stream, None)
+            ar_ms = nccl_ms
+            if self.comm is not None:
+                g.zero_()  # repeated in-place sums stay finite; lr 0 leaves the weights as they are
+                peer = lambda: self.comm.allreduce_sgd(g, self.master, self.params, 0.0)
+                for _ in range(3):
+                    peer()
+                ar_ms = event_time(peer, max(5, args.steps), stream, None)
         pk, src = peaks()
         work = 3 * FLOP_FWD_IMG5 * self.B
         ach = work / (ms * 1e-3) / 1e12
@@ -601,10 +620,14 @@ class Cfg5:
                 "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
                 "peak_source": f"{src} bf16_tflops_sustained", "traffic": None,
                 "flop_per_launch": work, "flop_count": "3 x forward FLOPs (backward ~ 2 x forward)",
-                "ms_per_launch": ms, "allreduce_us": None if ar_ms is None else 1000 * ar_ms,
+                "ms_per_launch": ms, "allreduce": self.allreduce,
+                "allreduce_us": None if ar_ms is None else 1000 * ar_ms,
+                "nccl_allreduce_us": None if nccl_ms is None else 1000 * nccl_ms,
                 "allreduce_bytes": 4 * self.train.GRAD_COUNT}
 
     def extra(self, ms):
+        if self.comm is not None and self.comm.status() != 0:
+            raise RuntimeError(f"peer all-reduce: a device-side wait gave up (status {self.comm.status()})")
         return {}
 
     config = {"seq_len": N5, "precision": "bf16 activations/weights, f16 GEMM operands, f32 attention backward, "
@@ -759,7 +782,7 @@ def run_ours(args, ws, rank, local):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"), "data": "synthetic",
             "config": dict({"workload": wl.workload, "global_batch": B * ws, "per_gpu_batch": B,
-                            "parallelism": (f"data parallel x{ws}, NCCL all-reduce of weight gradients"
+                            "parallelism": (f"data parallel x{ws}, {wl.allreduce} of the weight gradients"
                                             if args.config == "cfg5" else f"image shards x{ws}, no collective"),
                             "l2": "evicted between timed steps (256 MB buffer written, then read back)"}, **wl.config),
             "e2e": None if math.isnan(e2e_ms) else {
@@ -772,6 +795,8 @@ def run_ours(args, ws, rank, local):
         }
         line.update(wl.extra(ms))
         print(json.dumps(line), flush=True)
+    if hasattr(wl, "close"):
+        wl.close()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -785,6 +810,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"], help="cfg3 value/grad dtype")
+    ap.add_argument("--allreduce", default="nccl", choices=["peer", "nccl"],
+                    help="cfg5 with several GPUs: peer-memory all-reduce + SGD kernel, or NCCL all-reduce + SGD")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--min-warm-s", type=float, default=1.5,

@@ -1,9 +1,11 @@
 """PSA Attention data-parallel training step (cfg5) over the C ABI.
 
 Each rank: ``PsaTrainStep.forward_backward`` (tensor-core forward, backward
-into one f32 gradient buffer), ``torch.distributed.all_reduce`` of that buffer
-over NCCL (sum), then ``sgd`` with ``grad_scale = 1/world`` on f32 master
-weights, which rewrites the bf16 weights the next forward reads.  The
+into one f32 gradient buffer), then either ``torch.distributed.all_reduce`` of
+that buffer (sum) and ``sgd`` with ``grad_scale = 1/world`` on f32 master
+weights, or — with a ``PeerGradComm`` — one kernel that sums the ranks'
+buffers over NVLink peer memory and applies the same SGD update.  The update
+rewrites the bf16 weights the next forward reads.  The
 gradient buffer layout is the header's ``VA_PSA_GRAD_*`` offsets:
 ``[w_qkv 256×128 | w_proj 128×128 | w_pe 128×9 | b_qkv | b_proj | b_pe]``.
 """
@@ -80,11 +82,67 @@ class PsaTrainStep:
                   _p(params["b_proj"]), _stream(stream))
 
 
-def dp_train_step(step: PsaTrainStep, x, target, params: dict, master, lr: float, group=None):
-    """One data-parallel step: local fwd+bwd, NCCL all-reduce (sum) of the f32
-    gradient buffer, SGD with the mean gradient.  Returns the local loss tensor."""
+class PeerGradComm:
+    """All-reduce of the gradient buffer over NVLink peer memory, fused with
+    the SGD update (``va_psa_dp_allreduce_sgd``): every rank exports one
+    device buffer through CUDA IPC, the handles are exchanged once with an
+    ``all_gather`` of the process group, and each step is one kernel launch
+    per rank with no NCCL call.  One process per GPU, all on one node.  The
+    summed gradients are bit-identical on every rank (summed in rank order).
+    ``close()`` on every rank (it begins with a barrier) before the process
+    group is destroyed."""
+
+    def __init__(self, group=None):
+        import ctypes as C
+        import torch.distributed as dist
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self._h = C.c_void_p()
+        buf = C.create_string_buffer(64)
+        _lib.call("va_dp_comm_create", self.rank, self.world, GRAD_COUNT, C.byref(self._h), buf)
+        mine = torch.frombuffer(bytearray(buf.raw), dtype=torch.uint8)
+        if dist.get_backend(group) == "nccl":
+            mine = mine.to(torch.device("cuda", torch.cuda.current_device()))
+        parts = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(parts, mine, group=group)
+        handles = b"".join(t.cpu().numpy().tobytes() for t in parts)
+        _lib.call("va_dp_comm_connect", self._h, C.create_string_buffer(handles, len(handles)))
+
+    def allreduce_sgd(self, grads, master, params: dict, lr: float, stream=None):
+        """grads (in place) = Σ over ranks; master -= lr·grads/world; bf16/f32
+        parameters rewritten from master."""
+        _lib.call("va_psa_dp_allreduce_sgd", self._h, _p(grads), _p(master), float(lr), _p(params["w_qkv"]),
+                  _p(params["b_qkv"]), _p(params["w_pe"]), _p(params["b_pe"]), _p(params["w_proj"]),
+                  _p(params["b_proj"]), _stream(stream))
+
+    def status(self) -> int:
+        """0, or 100 + the rank whose flag a device-side wait gave up on (synchronises)."""
+        import ctypes as C
+        st = C.c_int(0)
+        _lib.call("va_dp_comm_status", self._h, C.byref(st))
+        return st.value
+
+    def close(self):
+        import torch.distributed as dist
+        if self._h is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        _lib.call("va_dp_comm_destroy", self._h)
+        self._h = None
+
+
+def dp_train_step(step: PsaTrainStep, x, target, params: dict, master, lr: float, group=None,
+                  comm: PeerGradComm | None = None):
+    """One data-parallel step: local fwd+bwd, all-reduce (sum) of the f32
+    gradient buffer, SGD with the mean gradient — through ``comm`` (one fused
+    peer-memory kernel) when given, else NCCL all-reduce + ``sgd``.  Returns
+    the local loss tensor."""
     import torch.distributed as dist
     _, loss, grads, _ = step.forward_backward(x, target, params)
+    if comm is not None:
+        comm.allreduce_sgd(grads, master, params, lr)
+        return loss
     world = 1
     if dist.is_available() and dist.is_initialized():
         dist.all_reduce(grads, op=dist.ReduceOp.SUM, group=group)
