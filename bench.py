@@ -810,7 +810,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"], help="cfg3 value/grad dtype")
-    ap.add_argument("--allreduce", default="nccl", choices=["peer", "nccl"],
+    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
                     help="cfg5 with several GPUs: peer-memory all-reduce + SGD kernel, or NCCL all-reduce + SGD")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
