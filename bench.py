@@ -1,11 +1,13 @@
 #!/usr/bin/env python3
 """Benchmarks of the B200 attention hot path of vision-rs.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg2|cfg3|cfg4|cfg5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg1|...|cfg5]
 
 Configurations (the north star's configs; synthetic seeded inputs of the
 named shapes and distributions, random-init weights):
 
+* ``cfg1``: the same op in f32 on one 128×20×20 feature map (batch 1, 400
+  tokens): the latency of the f32 path.
 * ``cfg2`` (default, the headline): YOLO26 C2PSA PSA Attention forward, bf16,
   per GPU a batch of 64 feature maps 128×40×40 (1600 tokens).  Step = one
   call of the fused op on the batch.
@@ -42,14 +44,22 @@ sys.path.insert(0, ROOT)
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
-# ── cfg2 constants ──────────────────────────────────────────────────────────
+# ── cfg1 constants ──────────────────────────────────────────────────────────
 C, NH, KD = 128, 2, 32
+P1_B, P1_H, P1_W = 1, 20, 20
+N1 = P1_H * P1_W
+# one flash_attention2_forward call (one V half, 32 wide): QK^T + PV FLOPs and q/k/v/o + LSE bytes
+FLOP_FA_CALL1 = 2 * NH * N1 * N1 * KD * 2
+BYTES_FA_CALL1 = 4 * NH * N1 * KD * 4 + NH * N1 * 4
+FLOP_IMG1 = 2 * N1 * C * (NH * 4 * KD) + 2 * FLOP_FA_CALL1 + 2 * 9 * C * N1 + 2 * N1 * C * C
+
+# ── cfg2 constants ──────────────────────────────────────────────────────────
 P2_B, P2_H, P2_W = 64, 40, 40
 N2 = P2_H * P2_W
 FLOP_ATTN_IMG2 = 2 * NH * N2 * N2 * KD + 2 * NH * N2 * N2 * 2 * KD
 FLOP_IMG2 = 2 * N2 * C * (NH * 4 * KD) + FLOP_ATTN_IMG2 + 2 * 9 * C * N2 + 2 * N2 * C * C
-# DRAM bytes (read + write) of one attention-kernel launch at the full workload, from the committed
-# ncu capture in profiles/psa_fwd_kernels_cfg2_ncu_full.md (52.46 MB read + 4.88 MB written)
+# DRAM bytes (read + write) of one attention-kernel launch at the full cfg2 workload, measured by ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum of attn_kernel, one launch: 52.46 MB read + 4.88 MB written)
 ATTN_TRAFFIC_BYTES = 57_345_024
 
 # ── cfg3 constants (SURVEY per-unit bytes) ──────────────────────────────────
@@ -199,6 +209,84 @@ def pipelined_e2e_ms(steps, h2d, compute, d2h, nbuf=2):
 
 
 # ═════════════════════════════ workloads ═════════════════════════════════════
+class Cfg1:
+    metric = "attention images/sec (C2PSA PSA attention fwd, f32, 400 tokens, batch 1)"
+    unit, dtype, batch = "images/s", "f32", P1_B
+    workload = "cfg1: C2PSA PSA attention fwd, f32, 1x128x20x20 (400 tokens), nh=2, kd=32, hd=64"
+
+    def __init__(self, dev, rank, batch, args):
+        import torch
+        from vision_rs_b200 import psa as vp
+        rng = np.random.default_rng(900 + rank)
+        f = lambda *s, std=1.0: torch.tensor((rng.standard_normal(s) * std).astype(np.float32))
+        self.B = batch
+        self.x = f(batch, C, P1_H, P1_W).to(dev)
+        self.op = vp.PsaAttention(f(NH * 4 * KD, C, std=0.02), f(NH * 4 * KD, std=0.02), f(C, 1, 3, 3, std=0.02),
+                                  f(C, std=0.02), f(C, C, std=0.02), f(C, std=0.02), NH, KD, dtype=torch.float32,
+                                  device=dev)
+        self.y = torch.empty_like(self.x)
+        self.xh = self.x.cpu().pin_memory()
+        self.yh = torch.empty_like(self.xh).pin_memory()
+        self.packed = f(4, batch * NH, N1, KD).to(dev)  # a packed Q|K|V_lo|V_hi buffer for the kernel alone
+
+    def step(self):
+        self.op.forward_into(self.x, self.y)
+
+    def e2e_step(self):
+        self.x.copy_(self.xh, non_blocking=True)
+        self.op.forward_into(self.x, self.y)
+        self.yh.copy_(self.y, non_blocking=True)
+
+    def io_bytes(self):
+        return self.x.numel() * 4, self.y.numel() * 4
+
+    def dominant(self, args, stream, flush):
+        """One flash_attention2_forward call (the FFMA flash attention, one
+        32-wide V half; the op makes two) on a packed buffer of cfg1's size."""
+        import torch
+        from vision_rs_b200 import _lib
+        BH = self.B * NH
+        sec = BH * N1 * KD * 4
+        base, st = self.packed.data_ptr(), stream.cuda_stream
+        o = torch.empty(BH, N1, KD, device=self.x.device)
+        lse = torch.empty(BH * N1, device=self.x.device)
+        call = lambda: _lib.call("va_flash_attention2_forward_f32", base, base + sec, base + 2 * sec, o.data_ptr(),
+                                 lse.data_ptr(), N1, N1, 1.0 / math.sqrt(KD), float("-inf"), BH, KD, st)
+        for _ in range(args.warmup):
+            call()
+        ms = event_time(call, max(5, args.steps), stream, flush)
+        pk, src = peaks()
+        work = BYTES_FA_CALL1 * self.B
+        ach = work / (ms * 1e-3) / 1e9
+        return {"bound": "hbm", "kernel": "fa_fwd_simt_kernel (f32 FFMA flash attention, one V half)",
+                "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
+                "peak_source": f"{src} hbm_gbs", "traffic": None, "bytes_per_launch": work,
+                "flop_per_launch": FLOP_FA_CALL1 * self.B, "ms_per_launch": ms,
+                "note": "latency-bound: one image is 800 query rows; neither HBM nor the FFMA pipe is the limit"}
+
+    def extra(self, ms):
+        return {"us_per_image": 1000.0 * ms / self.B, "gflops_whole_op": FLOP_IMG1 * self.B / (ms * 1e-3) / 1e9}
+
+    config = {"seq_len": N1, "precision": "f32 throughout (FFMA kernels; the f32 bound max-abs 1e-5 rules out TF32)"}
+
+    @staticmethod
+    def cpu_sample(threads, n_img=1, seed=1234):
+        import torch
+        from oracle import psa_oracle as po
+        torch.set_num_threads(threads)
+        p = po.psa_synthetic(1, P1_H, P1_W, seed=seed)
+        t = {k: torch.tensor(v) for k, v in p.items()}
+        a = (t["x"], t["w_qkv"], t["b_qkv"], t["w_pe"], t["b_pe"], t["w_proj"], t["b_proj"], NH, KD)
+        po.psa_attention_torch(*a)
+        t0 = time.perf_counter()
+        for _ in range(n_img):
+            po.psa_attention_torch(*a)
+        return n_img, time.perf_counter() - t0
+
+    sample_desc = ("single images of 128x20x20 (batch 1), torch-CPU f32 restatement of the reference maths (the "
+                   "reference has no CPU path)")
+
+
 class Cfg2:
     metric = "attention images/sec (C2PSA PSA attention fwd, bf16, 1600 tokens)"
     unit, dtype, batch = "images/s", "bf16", P2_B
@@ -260,8 +348,7 @@ class Cfg2:
                 "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
                 "peak_source": f"{src} bf16_tflops (burst)",
                 "traffic": ATTN_TRAFFIC_BYTES if B == P2_B else None,
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
-                                  "(profiles/psa_fwd_kernels_cfg2_ncu_full.md)",
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at this workload",
                 "flop_per_launch": work, "ms_per_launch": ms}
 
     def extra(self, ms):
@@ -611,6 +698,8 @@ class Cfg5:
                 peer = lambda: self.comm.allreduce_sgd(g, self.master, self.params, 0.0)
                 for _ in range(3):
                     peer()
+                torch.cuda.synchronize()
+                dist.barrier()  # ranks start the timed launches together
                 ar_ms = event_time(peer, max(5, args.steps), stream, None)
         pk, src = peaks()
         work = 3 * FLOP_FWD_IMG5 * self.B
@@ -622,6 +711,8 @@ class Cfg5:
                 "flop_per_launch": work, "flop_count": "3 x forward FLOPs (backward ~ 2 x forward)",
                 "ms_per_launch": ms, "allreduce": self.allreduce,
                 "allreduce_us": None if ar_ms is None else 1000 * ar_ms,
+                "allreduce_us_note": "back-to-back launches per rank after a barrier; includes the ranks' "
+                                     "timeline skew (each launch waits for every peer's flag)",
                 "nccl_allreduce_us": None if nccl_ms is None else 1000 * nccl_ms,
                 "allreduce_bytes": 4 * self.train.GRAD_COUNT}
 
@@ -650,7 +741,7 @@ class Cfg5:
     sample_desc = "images of 128x20x20 fwd+bwd, torch-CPU f32 autograd restatement (the reference has no CPU path)"
 
 
-CONFIGS = {"cfg2": Cfg2, "cfg3": Cfg3, "cfg4": Cfg4, "cfg5": Cfg5}
+CONFIGS = {"cfg1": Cfg1, "cfg2": Cfg2, "cfg3": Cfg3, "cfg4": Cfg4, "cfg5": Cfg5}
 
 
 # ═════════════════════════════ arms ══════════════════════════════════════════
@@ -678,17 +769,19 @@ def run_reference(args, ws, rank):
     inst.dtype = args.dtype
     for _ in range(args.warmup):
         inst.cpu_sample(threads)
-    vals = []
+    n_tot, t_tot, ns = 0, 0.0, []
     for _ in range(args.steps):
         n, dt = inst.cpu_sample(threads)
-        vals.append(n / dt)
-    val = statistics.mean(vals)
+        n_tot, t_tot = n_tot + n, t_tot + dt
+        ns.append(n)
+    val = n_tot / t_tot
     metric = getattr(cls, "metric", None) or f"attention images/sec (RF-DETR MSDeformAttn fwd+bwd, {args.dtype})"
     line = {
         "impl": "reference", "metric": metric, "value": val, "unit": "images/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / val, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": cls.workload, "parallelism": "host threads"},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * t_tot / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cls.workload, "global_batch": cls.batch * args.gpus, "per_gpu_batch": cls.batch,
+                   "parallelism": "host threads", "sample_images_per_step": ns[0]},
         "cpu_baseline": {"value": val, "unit": "images/s", "cores": threads, "kind": "port",
                          "sample": f"per step: {cls.sample_desc}"},
         "e2e": {"value": val, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

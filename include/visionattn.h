@@ -298,24 +298,38 @@ VA_API int va_psa_sgd_update(float *master, const float *grads, float lr, float 
  * process per GPU on one node:
  *   va_dp_comm_create   allocates and zeroes this rank's exported buffer and
  *                       writes its CUDA IPC handle (VA_DP_HANDLE_BYTES) to
- *                       *handle; count must be VA_PSA_GRAD_COUNT; 1..8 ranks.
+ *                       *handle; count must be VA_PSA_GRAD_COUNT; 1..8 ranks;
+ *                       timeout_ms bounds each device-side wait for a peer
+ *                       (0 = the default, 10 s).
  *   va_dp_comm_connect  opens every peer's buffer from the rank-ordered array
  *                       of all ranks' handles (world × VA_DP_HANDLE_BYTES);
  *                       call on every rank after all have created theirs.
- *   va_dp_comm_destroy  closes and frees; call after a barrier that follows
- *                       every rank's last all-reduce.
+ *   Teardown, in this order on every rank:
+ *   va_dp_comm_disconnect  closes this rank's mappings of the peers' buffers;
+ *                       call after a barrier that follows every rank's last
+ *                       all-reduce;
+ *   va_dp_comm_destroy  frees this rank's buffer; call after a second barrier,
+ *                       once every peer has disconnected (it also closes any
+ *                       mapping still open).
  * va_psa_dp_allreduce_sgd: grads (f32 [VA_PSA_GRAD_COUNT], in place) becomes
  * the sum over ranks, taken in rank order (the same bits on every rank), and
  * master -= lr · sum / world, then the bf16 weights and f32 biases are
  * rewritten from master as in va_psa_sgd_update.  Every rank must call it once
- * per step, in the same order.  A device-side wait that gives up after about a
- * second records 100 + the peer's rank in the comm's status word, which
- * va_dp_comm_status reads (synchronising); 0 = no failure. */
+ * per step, in the same order.  A device-side wait that passes timeout_ms
+ * records 100 + the peer's rank in the comm's status word, which
+ * va_dp_comm_status reads (synchronising); 0 = no failure.  The status word is
+ * sticky: once it is set, every later call returns at once without publishing
+ * or updating anything.  Blocks whose waits had passed before the failure
+ * have already updated their part of master and the weights, so after a
+ * non-zero status the weights must be restored on every rank and the comm
+ * destroyed and created anew on every rank. */
 #define VA_DP_HANDLE_BYTES 64
 typedef struct va_dp_comm va_dp_comm;
-VA_API int va_dp_comm_create(int rank, int world, int count, va_dp_comm **comm, void *handle);
+VA_API int va_dp_comm_create(int rank, int world, int count, int timeout_ms, va_dp_comm **comm,
+                             void *handle);
 VA_API int va_dp_comm_connect(va_dp_comm *comm, const void *handles);
 VA_API int va_dp_comm_status(va_dp_comm *comm, int *status);
+VA_API int va_dp_comm_disconnect(va_dp_comm *comm);
 VA_API int va_dp_comm_destroy(va_dp_comm *comm);
 VA_API int va_psa_dp_allreduce_sgd(va_dp_comm *comm, float *grads, float *master, float lr, va_bf16 *w_qkv,
                                    float *b_qkv, va_bf16 *w_pe, float *b_pe, va_bf16 *w_proj, float *b_proj,

@@ -97,10 +97,12 @@ def test_argument_validation_fails_before_launch():
         _lib.call("va_psa_merge_attn_nchw_f32", None, None, None, 127, 4, 4, 2, 2, None)
     # peer all-reduce set-up: rank/world and the buffer size are checked before any CUDA call
     h, buf = C.c_void_p(), C.create_string_buffer(64)
-    assert lib.va_dp_comm_create(0, 9, 50816, C.byref(h), buf) == 1 and b"world" in lib.va_get_last_error_string()
-    assert lib.va_dp_comm_create(2, 2, 50816, C.byref(h), buf) == 1
-    assert lib.va_dp_comm_create(0, 2, 1000, C.byref(h), buf) == 1 and b"count" in lib.va_get_last_error_string()
+    assert lib.va_dp_comm_create(0, 9, 50816, 0, C.byref(h), buf) == 1 and b"world" in lib.va_get_last_error_string()
+    assert lib.va_dp_comm_create(2, 2, 50816, 0, C.byref(h), buf) == 1
+    assert lib.va_dp_comm_create(0, 2, 1000, 0, C.byref(h), buf) == 1 and b"count" in lib.va_get_last_error_string()
+    assert lib.va_dp_comm_create(0, 2, 50816, -1, C.byref(h), buf) == 1 and b"timeout" in lib.va_get_last_error_string()
     assert lib.va_psa_dp_allreduce_sgd(None, *([None] * 2), 0.1, *([None] * 6), None) == 1
+    assert lib.va_dp_comm_disconnect(None) == 1
     assert lib.va_dp_comm_destroy(None) == 0
 
 

@@ -75,6 +75,40 @@ def test_windowed_layer_cfg4(cuda):
     _check(o, do.window_unpartition(ow_ref, B, gh, gw, win))
 
 
+def test_global_layer_full_cfg4_batch(cuda):
+    """cfg4's global layer at full size (16 images × 1601 tokens): images 0, 7
+    and 15 against the oracle, and batch independence (an image's output does
+    not depend on its batch neighbours: image 5 alone gives the same bits)."""
+    from vision_rs_b200 import dinov2
+    xt, wt, bt, x, w, b = _inputs(16, 1601, 384, 5, cuda)
+    op = dinov2.DinoV2Attention(wt, bt, 6)
+    o = op(xt)
+    for i in (0, 7, 15):
+        _check(o[i:i + 1], do.dinov2_attention(x[i:i + 1], w, b, 6))
+    assert torch.equal(op(xt[5:6].contiguous()), o[5:6])
+
+
+def test_windowed_layer_full_cfg4_batch(cuda):
+    """cfg4's windowed layer at full size (16 images → 256 windows of 1 + 100
+    tokens): the windows of images 0 and 15 against the oracle, the whole
+    un-partitioned output of image 15, and batch independence."""
+    from vision_rs_b200 import dinov2
+    B, gh, gw, win = 16, 40, 40, 10
+    xt, wt, bt, x, w, b = _inputs(B, 1 + gh * gw, 384, 6, cuda)
+    xw = dinov2.window_partition(xt, gh, gw, win)
+    op = dinov2.DinoV2Attention(wt, bt, 6)
+    ow = op(xw)
+    nw = (gh // win) * (gw // win)
+    for i in (0, 15):
+        xw_ref = do.window_partition(x[i:i + 1], gh, gw, win)
+        ow_ref = do.dinov2_attention(xw_ref, w, b, 6)
+        _check(ow[i * nw:(i + 1) * nw], ow_ref)
+        if i == 15:
+            o = dinov2.window_unpartition(ow, B, gh, gw, win)
+            _check(o[15:16], do.window_unpartition(ow_ref, 1, gh, gw, win))
+    assert torch.equal(op(xw[3 * nw:4 * nw].contiguous()), ow[3 * nw:4 * nw])
+
+
 def test_deterministic(cuda):
     from vision_rs_b200 import dinov2
     xt, wt, bt, *_ = _inputs(2, 1601, 384, 3, cuda)

@@ -22,7 +22,7 @@ pytestmark = pytest.mark.gpu
 
 CASES = [
     dict(B=2, Q=7, nh=3, dh=16, shapes=((9, 11), (5, 4), (2, 3)), P=3, seed=1),
-    dict(B=2, Q=300, nh=16, dh=16, shapes=((80, 80), (40, 40), (20, 20)), P=4, seed=2),
+    dict(B=8, Q=300, nh=16, dh=16, shapes=((80, 80), (40, 40), (20, 20)), P=4, seed=2),  # cfg3, full size
     dict(B=1, Q=33, nh=4, dh=32, shapes=((17, 13), (1, 1)), P=5, seed=3),
 ]
 

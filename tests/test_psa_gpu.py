@@ -94,7 +94,7 @@ def test_fa_forward_f32_vs_oracle(cuda, bh, nq, nk, d):
     o, l = vp.flash_attention2_forward(dev(q), dev(k), dev(v), 1 / math.sqrt(d))
     ro, rl = po.flash_attention2_forward(q, k, v, 1 / math.sqrt(d))
     assert max_abs(host(o), ro) < F32_MAX_ABS
-    assert max_abs(host(l), rl) < 1e-4  # LSE magnitude ~log(N)+|s|
+    assert max_abs(host(l), rl) < F32_MAX_ABS  # LSE magnitude ~log(N)+|s| ≈ 8: measured ≤ 2.9e-6
 
 
 def test_fa_forward_bf16_vs_oracle(cuda):
@@ -119,14 +119,16 @@ def test_psa_fa2_backward_f32(cuda, bh, n, d):
     args = [dev(a) for a in (q, k, v, o, do, l)]
     _lib.call("va_psa_fa2_backward_f32", *map(sp, args), sp(dq), sp(dk), sp(dv), n, 1 / math.sqrt(d), bh, d, st)
     rq, rk, rv = po.psa_fa2_backward(q, k, v, o, do, l, 1 / math.sqrt(d), dq_acc=dq0, dk_acc=dk0)
-    assert max_abs(host(dq), rq) < 1e-4 and max_abs(host(dk), rk) < 1e-4 and max_abs(host(dv), rv) < 1e-4
+    # the north star's f32 bound (measured ≤ 7.5e-7 with |dq|, |dk| up to ≈5)
+    assert max_abs(host(dq), rq) < F32_MAX_ABS and max_abs(host(dk), rk) < F32_MAX_ABS
+    assert max_abs(host(dv), rv) < F32_MAX_ABS
     # split kernels (flash_attn2.rs:129-260) store instead of accumulating
     dq2, dk2, dv2 = (torch.empty(bh, n, d, device="cuda") for _ in range(3))
     _lib.call("va_flash_attention2_backward_dq_f32", *map(sp, args), sp(dq2), n, n, 1 / math.sqrt(d), bh, d, st)
     _lib.call("va_flash_attention2_backward_dkv_f32", *map(sp, args), sp(dk2), sp(dv2), n, n, 1 / math.sqrt(d),
               bh, d, st)
-    assert max_abs(host(dq2), rq - dq0) < 1e-4 and max_abs(host(dk2), rk - dk0) < 1e-4
-    assert max_abs(host(dv2), rv) < 1e-4
+    assert max_abs(host(dq2), rq - dq0) < F32_MAX_ABS and max_abs(host(dk2), rk - dk0) < F32_MAX_ABS
+    assert max_abs(host(dv2), rv) < F32_MAX_ABS
 
 
 def test_dwconv_golden_fixture(cuda):

@@ -68,9 +68,10 @@ SIGNATURES: dict[str, tuple] = {
     "va_psa_train_fwd_bwd_bf16": (I, [P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, SZ, S]),
     "va_psa_sgd_update": (I, [P, P, F, F, P, P, P, P, P, P, S]),
     "va_gemm_f16": (I, [P, I, LL, LL, I, P, I, LL, LL, I, P, I, LL, LL, I, I, I, I, F, S]),
-    "va_dp_comm_create": (I, [I, I, I, C.POINTER(P), P]),
+    "va_dp_comm_create": (I, [I, I, I, I, C.POINTER(P), P]),
     "va_dp_comm_connect": (I, [P, P]),
     "va_dp_comm_status": (I, [P, C.POINTER(C.c_int)]),
+    "va_dp_comm_disconnect": (I, [P]),
     "va_dp_comm_destroy": (I, [P]),
     "va_psa_dp_allreduce_sgd": (I, [P, P, P, F, P, P, P, P, P, P, S]),
     "va_device_status_read": (I, [C.POINTER(C.c_int), S]),

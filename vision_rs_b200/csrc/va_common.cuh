@@ -8,6 +8,8 @@
 #include <stdio.h>
 
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 
 #include "../../include/visionattn.h"
 
@@ -28,6 +30,33 @@ inline int check_launch(const char* what) {
   if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
   return VA_OK;
 }
+
+// One-time set-up that must run once on every device, such as
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize), which applies to the
+// current device only.  run(f) calls f() with the calling thread's current
+// device unless it already succeeded there; safe from several host threads.
+// Devices with an index ≥ 64 run f() on every call.
+class PerDeviceOnce {
+ public:
+  template <typename F>
+  int run(F&& f) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return f();
+    const uint64_t bit = 1ull << dev;
+    if (done_.load(std::memory_order_acquire) & bit) return VA_OK;
+    std::lock_guard<std::mutex> lock(mu_);
+    if (done_.load(std::memory_order_relaxed) & bit) return VA_OK;
+    const int rc = f();
+    if (rc == VA_OK) done_.fetch_or(bit, std::memory_order_release);
+    return rc;
+  }
+
+ private:
+  std::atomic<uint64_t> done_{0};
+  std::mutex mu_;
+};
 
 inline int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 

@@ -28,8 +28,14 @@
 //
 // The grid is fixed (kDpBlocks, one block per SM at most) so that every rank
 // runs the same slices and all blocks are resident together.  A wait that
-// passes kDpSpinCycles records 100 + the peer rank in the comm's status word
-// and the block returns without updating; va_dp_comm_status reads it.
+// passes the comm's time limit (va_dp_comm_create) records 100 + the peer rank
+// in the comm's status word and the block returns without updating; blocks
+// that got through have already updated their slices, so the rank's weights
+// are then partly stepped.  The status word is sticky: every later launch
+// reads it first and returns at once, publishing and updating nothing, so a
+// failed comm never sums stale peer data; the caller reads it
+// (va_dp_comm_status), and a comm whose status is not 0 must be destroyed and
+// created anew on every rank, with the weights restored on every rank.
 #include <string.h>
 
 #include "va_common.cuh"
@@ -40,7 +46,13 @@ namespace {
 constexpr int kDpBlocks = 128;
 constexpr int kDpThreads = 256;
 constexpr int kDpMaxWorld = 8;
-constexpr long long kDpSpinCycles = 2000000000LL;  // SM clocks (≈1 s at 1.9 GHz) before a wait gives up
+constexpr long long kDpDefaultTimeoutNs = 10000000000LL;  // 10 s: room for host-side skew between ranks
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -63,6 +75,7 @@ struct DpArgs {
   __nv_bfloat16 *w_qkv, *w_pe, *w_proj;
   float *b_qkv, *b_pe, *b_proj;
   float lr, gscale;
+  long long timeout_ns;
   int rank, world, count, slice;
 };
 
@@ -72,16 +85,19 @@ __global__ void __launch_bounds__(kDpThreads) dp_allreduce_sgd_kernel(DpArgs a) 
   const int lo = b * a.slice, hi = min(lo + a.slice, a.count);
   const unsigned e = a.epoch[b] + 1u;
   const size_t par = (size_t)(e & 1u) * (size_t)a.count;
-  if (tid == 0) s_fail = 0;
+  // a comm that failed once stays failed: publish nothing, update nothing
+  if (tid == 0) s_fail = *static_cast<volatile int*>(a.status) != 0;
+  __syncthreads();
+  if (s_fail) return;
   for (int i = lo + tid; i < hi; i += kDpThreads) a.data_self[par + i] = a.grads[i];
   __syncthreads();
   const bool peer = tid < a.world && tid != a.rank;
   if (peer) st_release_sys(a.flags_peer[tid] + b * kDpMaxWorld + a.rank, e);
   if (peer) {
     const unsigned* f = a.flags_self + b * kDpMaxWorld + tid;
-    const long long t0 = clock64();
+    const unsigned long long t0 = globaltimer_ns();
     while ((int)(ld_acquire_sys(f) - e) < 0) {
-      if (clock64() - t0 > kDpSpinCycles) {
+      if ((long long)(globaltimer_ns() - t0) > a.timeout_ns) {
         atomicCAS(a.status, 0, 100 + tid);
         s_fail = 1;
         break;
@@ -118,6 +134,7 @@ size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
 struct va_dp_comm {
   int rank, world, count, device, connected;
+  long long timeout_ns;
   void* base;           // exported allocation: data [2][count] f32, then flags
   unsigned* epoch;      // [kDpBlocks]
   int* status;
@@ -129,9 +146,10 @@ using namespace va;
 
 extern "C" {
 
-int va_dp_comm_create(int rank, int world, int count, va_dp_comm** out, void* handle) {
+int va_dp_comm_create(int rank, int world, int count, int timeout_ms, va_dp_comm** out, void* handle) {
   clear_error();
   VA_CHECK_ARG(out && handle, "dp comm: null output");
+  VA_CHECK_ARG(timeout_ms >= 0, "dp comm: timeout %d ms", timeout_ms);
   VA_CHECK_ARG(world >= 1 && world <= kDpMaxWorld && rank >= 0 && rank < world,
                "dp comm: rank %d / world %d (1..%d ranks)", rank, world, kDpMaxWorld);
   VA_CHECK_ARG(count == VA_PSA_GRAD_COUNT, "dp comm: count %d (the PSA gradient buffer has %d)", count,
@@ -141,6 +159,7 @@ int va_dp_comm_create(int rank, int world, int count, va_dp_comm** out, void* ha
   c->rank = rank;
   c->world = world;
   c->count = count;
+  c->timeout_ns = timeout_ms > 0 ? (long long)timeout_ms * 1000000LL : kDpDefaultTimeoutNs;
   c->flags_off = align256((size_t)2 * count * sizeof(float));
   const size_t bytes = c->flags_off + align256((size_t)kDpBlocks * kDpMaxWorld * sizeof(unsigned));
   cudaError_t e = cudaGetDevice(&c->device);
@@ -198,14 +217,31 @@ int va_dp_comm_status(va_dp_comm* c, int* status) {
   return VA_OK;
 }
 
+int va_dp_comm_disconnect(va_dp_comm* c) {
+  clear_error();
+  VA_CHECK_ARG(c, "dp comm disconnect: null comm");
+  cudaError_t first = cudaSuccess;
+  for (int p = 0; p < c->world; ++p)
+    if (c->peer_base[p]) {
+      cudaError_t e = cudaIpcCloseMemHandle(c->peer_base[p]);
+      if (first == cudaSuccess) first = e;
+      c->peer_base[p] = nullptr;
+    }
+  c->connected = c->world == 1;
+  if (first != cudaSuccess) return set_error(VA_ERR_LAUNCH, "dp comm disconnect: %s", cudaGetErrorString(first));
+  return VA_OK;
+}
+
 int va_dp_comm_destroy(va_dp_comm* c) {
   clear_error();
   if (!c) return VA_OK;
   for (int p = 0; p < c->world; ++p)
     if (c->peer_base[p]) cudaIpcCloseMemHandle(c->peer_base[p]);
-  cudaFree(c->base);
-  cudaFree(c->epoch);
+  cudaError_t e = cudaFree(c->base);
+  cudaError_t e2 = cudaFree(c->epoch);
   delete c;
+  if (e == cudaSuccess) e = e2;
+  if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "dp comm destroy: %s", cudaGetErrorString(e));
   return VA_OK;
 }
 
@@ -234,6 +270,7 @@ int va_psa_dp_allreduce_sgd(va_dp_comm* c, float* grads, float* master, float lr
   a.b_pe = b_pe;
   a.b_proj = b_proj;
   a.lr = lr;
+  a.timeout_ns = c->timeout_ns;
   a.gscale = 1.f / (float)c->world;
   a.rank = c->rank;
   a.world = c->world;

@@ -4,7 +4,7 @@
 // _backward_dq / _backward_dkv (src/models/yolo/kernels/attention/flash_attn2.rs)
 // and psa_fa2_backward (psa.rs:650-725), which the f32 configuration
 // (max-abs 1e-5 against the f32 reference) needs: tensor-core TF32 would not
-// meet that bound.  The bf16 tensor-core path lives in va_fa_tc.cu.
+// meet that bound.  The bf16 tensor-core attention lives in va_tc_psa.cu.
 //
 // Work split: the reference runs one CTA per (bh, query row) and re-reads all
 // K/V rows for every row.  Here a 128-thread CTA owns 128 query rows (one per

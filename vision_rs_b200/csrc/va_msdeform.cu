@@ -502,15 +502,15 @@ int msda_bwd(const TV* value, const int64_t* shapes, const int64_t* lstart, cons
   if (int rc = check_launch("msdeform_attn backward (samples)")) return rc;
   // query of entry e = e / (4P), as a multiply: q_magic = ceil(2^32 / 4P), exact for e, 4P < 2^16
   const unsigned long long q_magic = ((1ull << 32) + 4ull * P - 1) / (4ull * P);
-  auto pass2 = [&](auto kernel) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  auto pass2 = [&](auto kernel) -> int {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     kernel<<<dim3(L, nh, B), kValueThreads, smem, st>>>(shapes, lstart, grad_out, reinterpret_cast<const int*>(c_pix),
                                                         reinterpret_cast<const float*>(c_w), grad_value, S, nh, L, Q,
                                                         P, q_magic);
+    return check_launch("msdeform_attn backward (value)");
   };
-  if (dh == 16) pass2(msda_bwd_value_kernel<TV, 16>);
-  else pass2(msda_bwd_value_kernel<TV, 32>);
-  return check_launch("msdeform_attn backward (value)");
+  return dh == 16 ? pass2(msda_bwd_value_kernel<TV, 16>) : pass2(msda_bwd_value_kernel<TV, 32>);
 }
 
 }  // namespace

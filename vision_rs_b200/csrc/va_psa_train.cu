@@ -432,12 +432,12 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   float* pbq = static_cast<float*>(at(L.part_bqkv));
   float* pwe = static_cast<float*>(at(L.part_wpe));
   float* pbe = static_cast<float*>(at(L.part_bpe));
-  static bool asm_attr = false;  // the planes of a large image need more than the default 48 KB
-  if (!asm_attr) {
-    cudaError_t e = cudaFuncSetAttribute(assemble_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    asm_attr = true;
-  }
+  static PerDeviceOnce asm_attr;  // the planes of a large image need more than the default 48 KB (per device)
+  if (int rc = asm_attr.run([] {
+        cudaError_t e = cudaFuncSetAttribute(assemble_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        return e == cudaSuccess ? VA_OK : set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      }))
+    return rc;
   int asm_rows = kAsmRows;  // rows (warps) per CTA: a power of two dividing kQKV whose planes fit
   while (asm_rows > 1 && (size_t)asm_rows * 2 * N * sizeof(float) > 200 * 1024) asm_rows >>= 1;
   assemble_kernel<<<dim3(kQKV / asm_rows, B), asm_rows * 32, (size_t)asm_rows * 2 * N * sizeof(float), st>>>(

@@ -1540,15 +1540,15 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   const int ntile = (N + kTile - 1) / kTile;
   const size_t sm1 = sizeof(QkvSmem) + 1024, sm2 = sizeof(AttnSmem<kKD>) + 1024, sm4 = sizeof(ProjSmem) + 1024;
   const size_t sm3 = (size_t)kPeCh * (H + 2) * ((W + 10) | 1) * sizeof(float);
-  static bool attr_done = false;
-  if (!attr_done) {
-    if (int rc = set_smem(qkv_proj_kernel, sm1)) return rc;
-    if (int rc = set_smem(attn_kernel<kKD, kOutChannelMajor>, sm2)) return rc;
-    if (int rc = set_smem(pe_dwconv_kernel, (size_t)kPeCh * kMaxPlane * sizeof(float))) return rc;
-    if (int rc = set_smem(proj_kernel, sm4)) return rc;
-    if (int rc = set_smem(proj_pers_kernel, sizeof(ProjPSmem) + 1024)) return rc;
-    attr_done = true;
-  }
+  static PerDeviceOnce attrs;  // the shared-memory limits are per device
+  if (int rc = attrs.run([&] {
+        if (int r = set_smem(qkv_proj_kernel, sm1)) return r;
+        if (int r = set_smem(attn_kernel<kKD, kOutChannelMajor>, sm2)) return r;
+        if (int r = set_smem(pe_dwconv_kernel, (size_t)kPeCh * kMaxPlane * sizeof(float))) return r;
+        if (int r = set_smem(proj_kernel, sm4)) return r;
+        return set_smem(proj_pers_kernel, sizeof(ProjPSmem) + 1024);
+      }))
+    return rc;
   __half* peb = reinterpret_cast<__half*>(base + L.pe);
   __half* wp16 = reinterpret_cast<__half*>(base + L.wproj);
   CUtensorMap mo, mpe, mwp;

@@ -90,16 +90,23 @@ class PeerGradComm:
     per rank with no NCCL call.  One process per GPU, all on one node.  The
     summed gradients are bit-identical on every rank (summed in rank order).
     ``close()`` on every rank (it begins with a barrier) before the process
-    group is destroyed."""
+    group is destroyed.
 
-    def __init__(self, group=None):
+    ``timeout_ms`` bounds every device-side wait for a peer (0: the library's
+    default, 10 s).  A wait that gives up makes the comm's status non-zero;
+    from then on its kernel updates nothing, and ``allreduce_sgd`` raises on
+    the next status check (every ``check_every`` calls, and in ``close``):
+    the weights must then be restored on every rank and the comm recreated."""
+
+    def __init__(self, group=None, timeout_ms: int = 0, check_every: int = 64):
         import ctypes as C
         import torch.distributed as dist
         self.group = group
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.check_every, self._calls = check_every, 0
         self._h = C.c_void_p()
         buf = C.create_string_buffer(64)
-        _lib.call("va_dp_comm_create", self.rank, self.world, GRAD_COUNT, C.byref(self._h), buf)
+        _lib.call("va_dp_comm_create", self.rank, self.world, GRAD_COUNT, int(timeout_ms), C.byref(self._h), buf)
         mine = torch.frombuffer(bytearray(buf.raw), dtype=torch.uint8)
         if dist.get_backend(group) == "nccl":
             mine = mine.to(torch.device("cuda", torch.cuda.current_device()))
@@ -111,6 +118,9 @@ class PeerGradComm:
     def allreduce_sgd(self, grads, master, params: dict, lr: float, stream=None):
         """grads (in place) = Σ over ranks; master -= lr·grads/world; bf16/f32
         parameters rewritten from master."""
+        self._calls += 1
+        if self.check_every and self._calls % self.check_every == 0:
+            self.raise_on_failure()
         _lib.call("va_psa_dp_allreduce_sgd", self._h, _p(grads), _p(master), float(lr), _p(params["w_qkv"]),
                   _p(params["b_qkv"]), _p(params["w_pe"]), _p(params["b_pe"]), _p(params["w_proj"]),
                   _p(params["b_proj"]), _stream(stream))
@@ -122,14 +132,28 @@ class PeerGradComm:
         _lib.call("va_dp_comm_status", self._h, C.byref(st))
         return st.value
 
-    def close(self):
+    def raise_on_failure(self):
+        st = self.status()
+        if st != 0:
+            raise RuntimeError(f"peer all-reduce on rank {self.rank}: a device-side wait for rank {st - 100} gave "
+                               f"up (status {st}); restore the weights and recreate the comm on every rank")
+
+    def close(self, check: bool = True):
+        """Two-phase teardown: every rank closes its mappings of the peers'
+        buffers, then (after a barrier) frees its own.  Raises afterwards if
+        the status is non-zero and ``check`` is set."""
         import torch.distributed as dist
         if self._h is None:
             return
         torch.cuda.synchronize()
-        dist.barrier(group=self.group)
+        st = self.status()
+        dist.barrier(group=self.group)      # every rank's last all-reduce has finished
+        _lib.call("va_dp_comm_disconnect", self._h)
+        dist.barrier(group=self.group)      # no rank maps this rank's buffer any more
         _lib.call("va_dp_comm_destroy", self._h)
         self._h = None
+        if check and st != 0:
+            raise RuntimeError(f"peer all-reduce on rank {self.rank}: status {st} at close")
 
 
 def dp_train_step(step: PsaTrainStep, x, target, params: dict, master, lr: float, group=None,
