@@ -287,21 +287,37 @@ class Cfg1:
                    "reference has no CPU path)")
 
 
+# YOLO26 widths of the C2PSA block (c2psa sets num_heads = c/64): n → 128, s/m/l → 256, x → 384
+WIDTHS = {"n": 128, "s": 256, "x": 384}
+
+
 class Cfg2:
-    metric = "attention images/sec (C2PSA PSA attention fwd, bf16, 1600 tokens)"
     unit, dtype, batch = "images/s", "bf16", P2_B
-    workload = "cfg2: C2PSA PSA attention fwd, 128x40x40 (1600 tokens), nh=2, kd=32, hd=64"
+
+    @staticmethod
+    def names(width):
+        """(metric, workload) of the config at a YOLO26 width."""
+        Cw = WIDTHS[width]
+        wtag = "" if width == "n" else f", width {width} (C={Cw})"
+        return (f"attention images/sec (C2PSA PSA attention fwd, bf16, 1600 tokens{wtag})",
+                f"cfg2: C2PSA PSA attention fwd, {Cw}x40x40 (1600 tokens), nh={Cw // 64}, kd=32, hd=64")
 
     def __init__(self, dev, rank, batch, args):
         import torch
         from vision_rs_b200 import psa as vp
+        self.C = WIDTHS[args.width]
+        self.nh = self.C // 64
+        Cw, nh = self.C, self.nh
+        self.metric, self.workload = self.names(args.width)
+        self.flop_attn_img = FLOP_ATTN_IMG2 * nh // NH
+        self.flop_img = 2 * N2 * Cw * (nh * 4 * KD) + self.flop_attn_img + 2 * 9 * Cw * N2 + 2 * N2 * Cw * Cw
         rng = np.random.default_rng(1000 + rank)
         f = lambda *s, std=1.0: torch.tensor((rng.standard_normal(s) * std).astype(np.float32))
         self.B = batch
-        self.x = f(batch, C, P2_H, P2_W).to(dev, torch.bfloat16)
-        self.op = vp.PsaAttention(f(NH * 4 * KD, C, std=0.02), f(NH * 4 * KD, std=0.02), f(C, 1, 3, 3, std=0.02),
-                                  f(C, std=0.02), f(C, C, std=0.02), f(C, std=0.02), NH, KD, dtype=torch.bfloat16,
-                                  device=dev)
+        self.x = f(batch, Cw, P2_H, P2_W).to(dev, torch.bfloat16)
+        self.op = vp.PsaAttention(f(nh * 4 * KD, Cw, std=0.02), f(nh * 4 * KD, std=0.02), f(Cw, 1, 3, 3, std=0.02),
+                                  f(Cw, std=0.02), f(Cw, Cw, std=0.02), f(Cw, std=0.02), nh, KD,
+                                  dtype=torch.bfloat16, device=dev)
         self.y = torch.empty_like(self.x)
         self.xh = self.x.cpu().pin_memory()
         self.yh = torch.empty_like(self.xh).pin_memory()
@@ -333,43 +349,49 @@ class Cfg2:
         ws = self.op.workspace(B, P2_H, P2_W, self.x.device)
         Np = (N2 + 7) // 8 * 8
         al = lambda n: (n + 255) // 256 * 256
-        v_off = al(2 * B * NH * N2 * KD * 2)
-        o_off = v_off + al(B * C * Np * 2)
+        Cw, nh = self.C, self.nh
+        # workspace offsets of Q/K, V and O: the C = 128 kernels' layout, or the general one (after qkv)
+        qk_off = 0 if Cw == C else al(B * 2 * Cw * Np * 2)
+        v_off = qk_off + al(2 * B * nh * N2 * KD * 2)
+        o_off = v_off + al(B * Cw * Np * 2)
         base, st = ws.data_ptr(), stream.cuda_stream
-        call = lambda: _lib.call("va_psa_flash_attention_fwd_f16", base, base + v_off, base + o_off, None, B, NH,
-                                 P2_H, P2_W, st)
+        call = lambda: _lib.call("va_psa_flash_attention_fwd_f16", base + qk_off, base + v_off, base + o_off, None,
+                                 B, nh, P2_H, P2_W, st)
         for _ in range(args.warmup):
             call()
         ms = event_time(call, max(5, args.steps), stream, flush)
         pk, src = peaks()
-        work = B * FLOP_ATTN_IMG2
+        work = B * self.flop_attn_img
         ach = work / (ms * 1e-3) / 1e12
         return {"bound": "tensor", "kernel": "attn_kernel (tcgen05 flash attention, QK^T + PV, 64-wide V)",
                 "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
                 "peak_source": f"{src} bf16_tflops (burst)",
-                "traffic": ATTN_TRAFFIC_BYTES if B == P2_B else None,
+                "traffic": ATTN_TRAFFIC_BYTES if (B == P2_B and Cw == C) else None,
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at this workload",
                 "flop_per_launch": work, "ms_per_launch": ms}
 
     def extra(self, ms):
-        return {"tflops_whole_op": FLOP_IMG2 * self.B / (ms * 1e-3) / 1e12}
+        return {"tflops_whole_op": self.flop_img * self.B / (ms * 1e-3) / 1e12}
 
-    config = {"seq_len": N2, "precision": "bf16 I/O and qkv GEMM; f16 attention operands; f32 accumulation"}
+    @property
+    def config(self):
+        return {"seq_len": N2, "channels": self.C, "heads": self.nh,
+                "precision": "bf16 I/O and qkv GEMM; f16 attention operands; f32 accumulation"}
 
-    @staticmethod
-    def cpu_sample(threads, n_img=P2_B, seed=1234):
+    def cpu_sample(self, threads, n_img=P2_B, seed=1234):
         import torch
         from oracle import psa_oracle as po
         torch.set_num_threads(threads)
-        p = po.psa_synthetic(n_img, P2_H, P2_W, seed=seed)
+        Cw = WIDTHS[getattr(self, "width", "n")]
+        p = po.psa_synthetic(n_img, P2_H, P2_W, C=Cw, num_heads=Cw // 64, seed=seed)
         t = {k: torch.tensor(v) for k, v in p.items()}
-        a = (t["x"], t["w_qkv"], t["b_qkv"], t["w_pe"], t["b_pe"], t["w_proj"], t["b_proj"], NH, KD)
+        a = (t["x"], t["w_qkv"], t["b_qkv"], t["w_pe"], t["b_pe"], t["w_proj"], t["b_proj"], Cw // 64, KD)
         po.psa_attention_torch(*a)
         t0 = time.perf_counter()
         po.psa_attention_torch(*a)
         return n_img, time.perf_counter() - t0
 
-    sample_desc = "images of 128x40x40, torch-CPU f32 restatement of the reference maths (the reference has no CPU path)"
+    sample_desc = "images of Cx40x40, torch-CPU f32 restatement of the reference maths (the reference has no CPU path)"
 
 
 class Cfg3:
@@ -750,6 +772,7 @@ def cpu_baseline(cfg_cls, args, min_s=10.0):
     threads = os.cpu_count() or 1
     inst = cfg_cls.__new__(cfg_cls)
     inst.dtype = getattr(args, "dtype", "f32")
+    inst.width = getattr(args, "width", "n")
     tot_img, tot_s = 0, 0.0
     while tot_s < min_s:
         n, dt = inst.cpu_sample(threads)
@@ -767,6 +790,7 @@ def run_reference(args, ws, rank):
     threads = os.cpu_count() or 1
     inst = cls.__new__(cls)
     inst.dtype = args.dtype
+    inst.width = args.width
     for _ in range(args.warmup):
         inst.cpu_sample(threads)
     n_tot, t_tot, ns = 0, 0.0, []
@@ -775,12 +799,14 @@ def run_reference(args, ws, rank):
         n_tot, t_tot = n_tot + n, t_tot + dt
         ns.append(n)
     val = n_tot / t_tot
-    metric = getattr(cls, "metric", None) or f"attention images/sec (RF-DETR MSDeformAttn fwd+bwd, {args.dtype})"
+    metric, workload = (cls.names(args.width) if hasattr(cls, "names")
+                        else (getattr(cls, "metric", None)
+                              or f"attention images/sec (RF-DETR MSDeformAttn fwd+bwd, {args.dtype})", cls.workload))
     line = {
         "impl": "reference", "metric": metric, "value": val, "unit": "images/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * t_tot / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": cls.workload, "global_batch": cls.batch * args.gpus, "per_gpu_batch": cls.batch,
+        "config": {"workload": workload, "global_batch": cls.batch * args.gpus, "per_gpu_batch": cls.batch,
                    "parallelism": "host threads", "sample_images_per_step": ns[0]},
         "cpu_baseline": {"value": val, "unit": "images/s", "cores": threads, "kind": "port",
                          "sample": f"per step: {cls.sample_desc}"},
@@ -903,6 +929,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"], help="cfg3 value/grad dtype")
+    ap.add_argument("--width", default="n", choices=sorted(WIDTHS),
+                    help="cfg2: YOLO26 width of the C2PSA block (n: C=128, s/m/l: 256, x: 384)")
     ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
                     help="cfg5 with several GPUs: peer-memory all-reduce + SGD kernel, or NCCL all-reduce + SGD")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -208,7 +208,7 @@ VA_API int va_msdeform_attn_bwd_bf16(const va_bf16 *value, const int64_t *spatia
  * Layouts (f16): qk = [2][B*nh][N][32] (psa_pack_qkv sections 0 and 1),
  * v and o = [B][nh*64][Np] channel-major with row pitch Np = roundup(N, 8)
  * (psa_extract_v_nchw / psa_merge_attn_nchw layouts, padded); lse optional
- * [B*nh][N] f32.  nh = 2 only. */
+ * [B*nh][N] f32.  Any number of heads (C = 64·nh). */
 VA_API int va_psa_flash_attention_fwd_f16(const void *qk, const void *v, void *o, float *lse, int B,
                                           int num_heads, int H, int W, va_stream_t stream);
 

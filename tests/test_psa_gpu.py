@@ -86,8 +86,10 @@ def test_fa_forward_golden_fixture(cuda):
         assert max_abs(host(l), g["attn_l"]) < F32_MAX_ABS
 
 
+# small problems run the split-row kernel (several threads per query row); (300, 130, 130, 32)
+# has enough rows for the row-per-thread kernel
 @pytest.mark.parametrize("bh,nq,nk,d", [(2, 400, 400, 32), (4, 37, 129, 32), (1, 1601, 1601, 64),
-                                        (3, 100, 100, 64), (2, 1, 5, 16)])
+                                        (3, 100, 100, 64), (2, 1, 5, 16), (5, 70, 333, 16), (300, 130, 130, 32)])
 def test_fa_forward_f32_vs_oracle(cuda, bh, nq, nk, d):
     rng = np.random.default_rng(nq + nk)
     q, k, v = (rng.standard_normal((bh, n, d)).astype(np.float32) for n in (nq, nk, nk))
@@ -200,6 +202,20 @@ def test_fused_bf16_full_cfg2_batch(cuda):
         assert rel_l2(y[i:i + 1], ref) < BF16_REL_L2 and max_abs(y[i:i + 1], ref) < BF16_MAX_ABS
     y_single = host(op(x[5:6].contiguous()))
     assert np.array_equal(y_single, y[5:6])
+
+
+@pytest.mark.parametrize("C,B,H,W", [(256, 2, 20, 20), (384, 2, 40, 40), (256, 3, 13, 11), (64, 2, 9, 7)])
+def test_fused_bf16_other_widths_vs_oracle(cuda, C, B, H, W):
+    """The tensor-core forward at the other c2psa widths (num_heads = C/64,
+    c2psa.rs:158): YOLO26 s/m/l (C = 256, 4 heads) and x (C = 384, 6 heads),
+    plus one head and a ragged image, bf16 tolerance against the oracle."""
+    nh = C // 64
+    p = _bf16_inputs(po.psa_synthetic(B, H, W, C=C, num_heads=nh, seed=C + H))
+    op = vp.PsaAttention(p["w_qkv"], p["b_qkv"], p["w_pe"], p["b_pe"], p["w_proj"], p["b_proj"], num_heads=nh,
+                         key_dim=32, dtype=torch.bfloat16)
+    y = host(op(dev(p["x"], torch.bfloat16)))
+    ref = po.psa_attention(p["x"], p["w_qkv"], p["b_qkv"], p["w_pe"], p["b_pe"], p["w_proj"], p["b_proj"], nh, 32)
+    assert rel_l2(y, ref) < BF16_REL_L2 and max_abs(y, ref) < BF16_MAX_ABS
 
 
 def test_reference_node_sequence_matches_fused(cuda):

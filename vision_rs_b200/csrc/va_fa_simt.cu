@@ -89,6 +89,129 @@ __global__ void __launch_bounds__(128) fa_fwd_simt_kernel(const T* __restrict__ 
   }
 }
 
+constexpr int kSplitKeys = 256;
+
+// Forward for small problems (few rows per head, few heads): R threads share
+// a query row, each taking every R-th key of a shared-memory K/V tile with its
+// own running max, sum and accumulator; the R partial states are merged at
+// the end with warp shuffles (rescaled to the common max, then summed).  One
+// image of cfg1 (2 heads × 400 rows) fills only 7 CTAs of the row-per-thread
+// kernel; here it fills 100.  K/V rows are padded to D+4 floats, so the R
+// lanes of a row group read R consecutive rows as 16-byte vectors without
+// bank conflicts.
+// 4 consecutive elements as f32 (one 16-byte load for f32, 8 bytes for bf16).
+__device__ __forceinline__ float4 ld4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 ld4(const __nv_bfloat16* p) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&u.x), b = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+  return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
+}
+
+template <typename T, int D, int DV, int R>
+__global__ void __launch_bounds__(256) fa_fwd_split_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                           const T* __restrict__ v, T* __restrict__ o,
+                                                           float* __restrict__ lse, int nq, int nk, float scale) {
+  static_assert(D % 4 == 0 && DV % 4 == 0 && DV % R == 0 && 32 % R == 0, "shape");
+  // BK keys per shared-memory chunk (all of a cfg1 head's keys in two chunks),
+  // KPT of them per thread
+  constexpr int BK = kSplitKeys, KPT = BK / R, ROWS = 256 / R, PD = D + 4, PV = DV + 4;
+  extern __shared__ float4 split_smem[];
+  float* ks = reinterpret_cast<float*>(split_smem);
+  float* vs = ks + BK * PD;
+  const int bh = blockIdx.y, t = threadIdx.x % R;
+  const int row = blockIdx.x * ROWS + threadIdx.x / R;
+  const bool valid = row < nq;
+  const float sl2 = scale * kLog2e;
+  float qr[D];
+  const T* qp = q + ((long long)bh * nq + (valid ? row : 0)) * D;
+#pragma unroll
+  for (int d = 0; d < D; ++d) qr[d] = ldg(qp + d) * sl2;
+  float acc[DV];
+#pragma unroll
+  for (int d = 0; d < DV; ++d) acc[d] = 0.f;
+  float m = -INFINITY, lsum = 0.f;
+  const T* kb = k + (long long)bh * nk * D;
+  const T* vb = v + (long long)bh * nk * DV;
+  for (int k0 = 0; k0 < nk; k0 += BK) {
+    __syncthreads();
+    // the chunk's K and V rows, 4 elements per load, all loads of a thread in flight together
+    for (int i = threadIdx.x; i < BK * (D / 4); i += 256) {
+      const int r = i / (D / 4), c = 4 * (i % (D / 4));
+      const float4 x = k0 + r < nk ? ld4(kb + (long long)(k0 + r) * D + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(ks + r * PD + c) = x;
+    }
+    for (int i = threadIdx.x; i < BK * (DV / 4); i += 256) {
+      const int r = i / (DV / 4), c = 4 * (i % (DV / 4));
+      const float4 x = k0 + r < nk ? ld4(vb + (long long)(k0 + r) * DV + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(vs + r * PV + c) = x;
+    }
+    __syncthreads();
+  const int kn = min(BK, nk - k0);
+    float s[KPT];
+    float cmax = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < KPT; ++i) {
+      const int j = t + R * i;
+      const float4* kr = reinterpret_cast<const float4*>(ks + j * PD);
+      float dot = 0.f;
+#pragma unroll
+      for (int d4 = 0; d4 < D / 4; ++d4) {
+        const float4 kk = kr[d4];
+        dot = fmaf(qr[4 * d4], kk.x, dot);
+        dot = fmaf(qr[4 * d4 + 1], kk.y, dot);
+        dot = fmaf(qr[4 * d4 + 2], kk.z, dot);
+        dot = fmaf(qr[4 * d4 + 3], kk.w, dot);
+      }
+      s[i] = j < kn ? dot : -INFINITY;
+      cmax = fmaxf(cmax, s[i]);
+    }
+    const float mnew = fmaxf(m, cmax);
+    if (mnew == -INFINITY) continue;  // every key of this thread's share lies past nk
+    const float alpha = exp2f(m - mnew);
+    lsum *= alpha;
+#pragma unroll
+    for (int d = 0; d < DV; ++d) acc[d] *= alpha;
+#pragma unroll
+    for (int i = 0; i < KPT; ++i) {
+      const float p = exp2f(s[i] - mnew);
+      lsum += p;
+      const float4* vr = reinterpret_cast<const float4*>(vs + (t + R * i) * PV);
+#pragma unroll
+      for (int d4 = 0; d4 < DV / 4; ++d4) {
+        const float4 vv = vr[d4];
+        acc[4 * d4] = fmaf(p, vv.x, acc[4 * d4]);
+        acc[4 * d4 + 1] = fmaf(p, vv.y, acc[4 * d4 + 1]);
+        acc[4 * d4 + 2] = fmaf(p, vv.z, acc[4 * d4 + 2]);
+        acc[4 * d4 + 3] = fmaf(p, vv.w, acc[4 * d4 + 3]);
+      }
+    }
+    m = mnew;
+  }
+  // merge the R partial states of the row (lanes t = 0..R-1 of one row group)
+  float mrow = m;
+#pragma unroll
+  for (int off = R / 2; off > 0; off >>= 1) mrow = fmaxf(mrow, __shfl_xor_sync(0xffffffffu, mrow, off));
+  const float f = m == -INFINITY ? 0.f : exp2f(m - mrow);
+  lsum *= f;
+#pragma unroll
+  for (int d = 0; d < DV; ++d) acc[d] *= f;
+#pragma unroll
+  for (int off = R / 2; off > 0; off >>= 1) {
+    lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+#pragma unroll
+    for (int d = 0; d < DV; ++d) acc[d] += __shfl_xor_sync(0xffffffffu, acc[d], off);
+  }
+  if (valid) {
+    const float inv = 1.f / lsum;
+    T* op = o + ((long long)bh * nq + row) * DV;
+    // lane t writes outputs t·DV/R .. +DV/R (constant indices into acc: a predicated unrolled loop)
+#pragma unroll
+    for (int d = 0; d < DV; ++d)
+      if (d / (DV / R) == t) st(op + d, acc[d] * inv);
+    if (t == 0) lse[(long long)bh * nq + row] = (mrow + log2f(lsum)) * kLn2;
+  }
+}
+
 // dQ: one thread per query row (flash_attn2.rs:129-187).  ACC → dq += result.
 template <int D, int DV, bool ACC>
 __global__ void __launch_bounds__(128) fa_bwd_dq_kernel(const float* __restrict__ q, const float* __restrict__ k,
@@ -219,6 +342,39 @@ static int fa_fwd(const T* q, const T* k, const T* v, T* o, float* l, int nq, in
   VA_CHECK_ARG(nq > 0 && nk > 0 && bh > 0, "flash_attention2_forward: non-positive size");
   VA_CHECK_ARG(bh <= 65535, "flash_attention2_forward: bh=%d exceeds 65535", bh);
   dim3 grid(ceil_div(nq, 128), bh);
+  const uintptr_t vec = sizeof(T) * 4 - 1;  // the split kernel reads 4 elements per load
+  const bool aligned = !((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & vec);
+  if ((long long)grid.x * bh < 2 * 148 && aligned) {
+    // few rows in flight: several threads per row (R), chosen so the grid covers the SMs
+    int R = 8;
+    const int rmax = hd == 16 ? 16 : 32;  // R divides the head dim (each lane writes DV/R outputs)
+    while (R < rmax && (long long)ceil_div(nq, 256 / R) * bh < 148) R *= 2;
+    const dim3 gs(ceil_div(nq, 256 / R), bh);
+    const size_t smem = (size_t)kSplitKeys * (hd + 4) * 2 * sizeof(float);
+    int rc = VA_OK;
+    auto launch = [&](auto kernel) {
+      // the dynamic shared-memory limit is a per-device, per-kernel attribute: set it at every launch
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) {
+        rc = set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        return;
+      }
+      kernel<<<gs, 256, smem, st>>>(q, k, v, o, l, nq, nk, scale);
+    };
+    switch (hd * 100 + R) {
+      case 1608: launch(fa_fwd_split_kernel<T, 16, 16, 8>); break;
+      case 1616: launch(fa_fwd_split_kernel<T, 16, 16, 16>); break;
+      case 3208: launch(fa_fwd_split_kernel<T, 32, 32, 8>); break;
+      case 3216: launch(fa_fwd_split_kernel<T, 32, 32, 16>); break;
+      case 3232: launch(fa_fwd_split_kernel<T, 32, 32, 32>); break;
+      case 6408: launch(fa_fwd_split_kernel<T, 64, 64, 8>); break;
+      case 6416: launch(fa_fwd_split_kernel<T, 64, 64, 16>); break;
+      case 6432: launch(fa_fwd_split_kernel<T, 64, 64, 32>); break;
+      default: return set_error(VA_ERR_SHAPE, "flash_attention2_forward: head_dim %d unsupported (16/32/64)", hd);
+    }
+    if (rc) return rc;
+    return check_launch("flash_attention2_forward (split rows)");
+  }
   switch (hd) {
     case 16: fa_fwd_simt_kernel<T, 16, 16><<<grid, 128, 0, st>>>(q, k, v, o, l, nq, nk, scale); break;
     case 32: fa_fwd_simt_kernel<T, 32, 32><<<grid, 128, 0, st>>>(q, k, v, o, l, nq, nk, scale); break;

@@ -62,8 +62,9 @@ extern "C" int va_psa_attention_fwd_bf16_noalloc(const va_bf16* x, const va_bf16
                                                  int num_heads, int key_dim, va_stream_t stream) {
   VA_CHECK_ARG(B > 0 && C > 0 && H > 0 && W > 0 && num_heads > 0 && key_dim > 0,
                "psa_attention noalloc: non-positive size");
-  VA_CHECK_ARG(psa_tc_supported(C, num_heads, key_dim), "psa_attention noalloc: needs C=128, nh=2, kd=32");
-  const size_t need = psa_tc_workspace_bytes(B, H, W, num_heads);
+  VA_CHECK_ARG(psa_tc_supported(C, num_heads, key_dim),
+               "psa_attention noalloc: needs key_dim 32 and C = 64·num_heads");
+  const size_t need = psa_tc_workspace_bytes(B, C, H, W, num_heads);
   if (need > kScratchBytes)
     return set_error(VA_ERR_WORKSPACE,
                      "psa_attention noalloc: B=%d at %dx%d needs %zu bytes of scratch, more than the %zu bytes "

@@ -29,7 +29,14 @@ int conv1x1(const T* x, const T* x2, const TW* w, const float* bias, T* y, int B
 template <typename T, typename TW>
 int dwconv3x3(const T* x, const TW* w, const float* bias, T* y, int B, int C, int H, int W, cudaStream_t st);
 
-size_t psa_tc_workspace_bytes(int B, int H, int W, int nh);
+// Workspace of the tensor-core forward (bf16): the specialised C = 128 path
+// or, for other widths C = 64·nh, the general one (va_tc_psa_wide.cu).
+size_t psa_tc_workspace_bytes(int B, int C, int H, int W, int nh);
+size_t psa_tc_wide_workspace_bytes(int B, int C, int H, int W);
+int psa_attention_fwd_tc_wide(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,
+                              const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
+                              const float* b_proj, __nv_bfloat16* y, int B, int C, int H, int W, int nh, void* ws,
+                              size_t ws_bytes, cudaStream_t st);
 // Byte offsets of the tensor-core forward's intermediates inside its
 // workspace: Q/K f16 [2][B·nh][N][32], V, O and PE f16 [B][128][Np], W_proj
 // as f16 [128][128].
@@ -38,7 +45,7 @@ struct PsaTcOffsets {
 };
 PsaTcOffsets psa_tc_offsets(int B, int H, int W, int nh);
 
-// One operand of tc_gemm_f16 (f16 elements): K-major — row r (an M or N
+// One operand of tc_gemm_f16 (f16 or bf16 elements): K-major — row r (an M or N
 // index) holds K contiguous elements, `ld` apart; MN-major — row k holds the
 // M (or N) elements contiguously.  batch_stride: elements between batch
 // entries; broadcast: one matrix for every batch entry.
@@ -49,11 +56,13 @@ struct GemmOperand {
   long long batch_stride;
   bool broadcast;
 };
-// C[z'][m][n] = α·Σ_{z in fold z'} Σ_k A_z(m,k)·B_z(n,k), f32 accumulation;
-// z' = z / zfold (ceil(Z/zfold) outputs); C is f32 (c_type 0), bf16 (1) or
-// f16 (2) with row pitch ldc and batch stride c_batch (elements).
+// C[z'][m][n] = α·Σ_{z in fold z'} Σ_k A_z(m,k)·B_z(n,k) + bias[m], f32
+// accumulation; z' = z / zfold (ceil(Z/zfold) outputs); C is f32 (c_type 0),
+// bf16 (1) or f16 (2) with row pitch ldc and batch stride c_batch (elements).
+// Operands are f16, or bf16 with ab_bf16; bias (f32 [M]) is optional.
 int tc_gemm_f16(const GemmOperand& a, const GemmOperand& b, void* c, int c_type, long long ldc, long long c_batch,
-                int M, int N, int K, int Z, cudaStream_t st, float alpha = 1.0f, int zfold = 1);
+                int M, int N, int K, int Z, cudaStream_t st, float alpha = 1.0f, int zfold = 1,
+                const float* bias = nullptr, bool ab_bf16 = false);
 int gemm_status_read(int* out, cudaStream_t st);
 // Tensor-core PSA attention backward (nh = 2, kd = 32, N ≤ 512), channel-major
 // f32 outputs: dk [B·nh][32][N], dv [B·nh][64][N], dq_part
@@ -64,7 +73,10 @@ int psa_attn_bwd_tc(const void* qk, const void* v, const void* o, const void* d_
 int bwd_status_read(int* out, cudaStream_t st);
 int bwd_status_clear(cudaStream_t st);
 int gemm_status_clear(cudaStream_t st);
+// Tensor-core forward: any C = 64·nh with key dim 32 (the c2psa widths);
+// the C = 128 kernels of the training step: psa_tc_is_n.
 bool psa_tc_supported(int C, int nh, int kd);
+inline bool psa_tc_is_n(int C, int nh, int kd) { return C == 128 && nh == 2 && kd == 32; }
 int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,
                          const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
                          const float* b_proj, __nv_bfloat16* y, int B, int C, int H, int W, int nh, int kd,

@@ -52,7 +52,7 @@ int check_common(int B, int C, int H, int W, int nh, int kd, void* ws, size_t ws
 
 size_t psa_workspace_bytes(int B, int C, int H, int W, int nh, int kd, int dtype) {
   if (dtype == 0) return layout(B, C, H, W, nh, kd, 4).total;
-  return psa_tc_supported(C, nh, kd) ? psa_tc_workspace_bytes(B, H, W, nh) : 0;
+  return psa_tc_supported(C, nh, kd) ? psa_tc_workspace_bytes(B, C, H, W, nh) : 0;
 }
 
 #define VA_TRY(expr)          \

@@ -347,7 +347,7 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
                       const float* b_qkv, const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
                       const float* b_proj, __nv_bfloat16* y, __nv_bfloat16* dx, float* grads, float* loss, int B,
                       int C, int H, int W, int nh, int kd, void* ws, size_t ws_bytes, cudaStream_t st) {
-  VA_CHECK_ARG(psa_tc_supported(C, nh, kd), "psa train: needs C=128, nh=2, kd=32");
+  VA_CHECK_ARG(psa_tc_is_n(C, nh, kd), "psa train: needs C=128, nh=2, kd=32");
   VA_CHECK_ARG(B > 0 && H > 0 && W > 0 && B <= 65535, "psa train: bad sizes");
   VA_CHECK_ARG(target && grads && loss && y, "psa train: null target/grads/loss/y");
   const int N = H * W, Np = (N + 7) / 8 * 8, BH = B * nh;

@@ -1,7 +1,9 @@
-// Batched f16 GEMM on tcgen05 for the training path (weight and input
-// gradients of the 1×1 convolutions):
+// Batched GEMM on tcgen05 for the training path (weight and input gradients
+// of the 1×1 convolutions) and the 1×1 convolutions of the PSA forward at
+// widths other than 128:
 //
-//   C[z][m][n] = α · Σ_k A_z(m, k) · B_z(n, k)    f16 operands, f32 accumulate
+//   C[z][m][n] = α · Σ_k A_z(m, k) · B_z(n, k) (+ bias[m])
+//                f16 or bf16 operands (both the same), f32 accumulate
 //
 // Each operand is K-major (row m holds its K elements contiguously) or
 // MN-major (row k holds its M — or N — elements contiguously), optionally
@@ -43,7 +45,7 @@ template <bool A_MN, bool B_MN, int OUT>
 __global__ void __launch_bounds__(128, 1)
 gemm_f16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, void* __restrict__ c,
                 int M, int N, int K, long long ldc, long long c_batch, int a_bcast, int b_bcast, float alpha, int Z,
-                int zfold) {
+                int zfold, uint32_t ab_fmt, const float* __restrict__ bias) {
   extern __shared__ uint8_t smem_raw[];
   GemmSmem& sm = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -104,7 +106,7 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
       }
     }
   } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc = idesc_f32acc(kGM, kGN, AB_F16, A_MN, B_MN);
+    const uint32_t idesc = idesc_f32acc(kGM, kGN, ab_fmt, A_MN, B_MN);
     // K-major SW128: 8-row groups 1024 B apart, a 16-wide k step = +32 B.
     // MN-major SW128: two 64-element blocks 8 KB apart (LBO), 8 k-rows per
     // 1024 B (SBO), a 16-row k step = +2048 B.
@@ -136,8 +138,9 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + ch * 32, u);
       tmem_ld_wait();
       reg_fence(u);
+      const float bm = (bias && m < M) ? bias[m] : 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
+      for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(fmaf(__uint_as_float(u[i]), alpha, bm));
       const int nb = n0 + ch * 32;
       if (m >= M || nb >= N) continue;
       if constexpr (OUT != kOutF32) {
@@ -195,7 +198,7 @@ PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn() {
 
 // 3D map over an operand: inner = contiguous extent, outer = rows, z = batch.
 int operand_map(CUtensorMap* m, const GemmOperand& op, uint64_t inner, uint64_t outer, uint64_t zdim, uint32_t box_inner,
-                uint32_t box_outer, const char* what) {
+                uint32_t box_outer, bool bf16, const char* what) {
   auto fn = gemm_encode_fn();
   if (!fn) return set_error(VA_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(op.ptr) & 15) || ((op.ld * 2) % 16) || (zdim > 1 && (op.batch_stride * 2) % 16))
@@ -203,7 +206,8 @@ int operand_map(CUtensorMap* m, const GemmOperand& op, uint64_t inner, uint64_t 
   const uint64_t d[3] = {inner, outer, zdim};
   const uint64_t s[2] = {(uint64_t)op.ld * 2, (uint64_t)(zdim > 1 ? op.batch_stride : op.ld * outer) * 2};
   const uint32_t bx[3] = {box_inner, box_outer, 1}, es[3] = {1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(op.ptr), d, s, bx, es,
+  CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(op.ptr), d, s, bx, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(VA_ERR_ALIGN, "tensor map for gemm %s rejected (CUresult %d)", what, (int)r);
@@ -213,21 +217,25 @@ int operand_map(CUtensorMap* m, const GemmOperand& op, uint64_t inner, uint64_t 
 }  // namespace
 
 int tc_gemm_f16(const GemmOperand& a, const GemmOperand& b, void* c, int c_type, long long ldc, long long c_batch,
-                int M, int N, int K, int Z, cudaStream_t st, float alpha, int zfold) {
+                int M, int N, int K, int Z, cudaStream_t st, float alpha, int zfold, const float* bias, bool ab_bf16) {
   VA_CHECK_ARG(M > 0 && N > 0 && K > 0 && Z > 0 && Z <= 65535 && zfold > 0 && (N + kGN - 1) / kGN <= 65535,
                "gemm: bad sizes");
   VA_CHECK_ARG(c_type >= kOutF32 && c_type <= kOutF16, "gemm: output type %d", c_type);
   CUtensorMap ma, mb;
   const uint64_t za = a.broadcast ? 1 : Z, zb = b.broadcast ? 1 : Z;
-  if (int rc = a.mn ? operand_map(&ma, a, M, K, za, 64, 64, "A") : operand_map(&ma, a, K, M, za, 64, kGM, "A")) return rc;
-  if (int rc = b.mn ? operand_map(&mb, b, N, K, zb, 64, 64, "B") : operand_map(&mb, b, K, N, zb, 64, kGN, "B")) return rc;
+  if (int rc = a.mn ? operand_map(&ma, a, M, K, za, 64, 64, ab_bf16, "A")
+                    : operand_map(&ma, a, K, M, za, 64, kGM, ab_bf16, "A"))
+    return rc;
+  if (int rc = b.mn ? operand_map(&mb, b, N, K, zb, 64, 64, ab_bf16, "B")
+                    : operand_map(&mb, b, K, N, zb, 64, kGN, ab_bf16, "B"))
+    return rc;
   const size_t smem = sizeof(GemmSmem) + 1024;
   const dim3 grid((M + kGM - 1) / kGM, (N + kGN - 1) / kGN, (Z + zfold - 1) / zfold);
   auto launch = [&](auto kernel) -> int {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     kernel<<<grid, 128, smem, st>>>(ma, mb, c, M, N, K, ldc, c_batch, a.broadcast ? 1 : 0, b.broadcast ? 1 : 0,
-                                    alpha, Z, zfold);
+                                    alpha, Z, zfold, ab_bf16 ? (uint32_t)AB_BF16 : (uint32_t)AB_F16, bias);
     return check_launch("gemm");
   };
   auto pick = [&](auto amn, auto bmn) -> int {

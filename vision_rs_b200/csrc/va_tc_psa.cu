@@ -1468,20 +1468,24 @@ int set_smem(K kernel, size_t bytes) {
 
 }  // namespace
 
-size_t psa_tc_workspace_bytes(int B, int H, int W, int nh) { return tc_layout(B, H, W, nh).total; }
+size_t psa_tc_workspace_bytes(int B, int C, int H, int W, int nh) {
+  return psa_tc_is_n(C, nh, kKD) ? tc_layout(B, H, W, nh).total : psa_tc_wide_workspace_bytes(B, C, H, W);
+}
 
 PsaTcOffsets psa_tc_offsets(int B, int H, int W, int nh) {
   const TcWs L = tc_layout(B, H, W, nh);
   return PsaTcOffsets{L.qk, L.v, L.o, L.pe, L.wproj, L.total};
 }
 
-bool psa_tc_supported(int C, int nh, int kd) { return C == kC && nh * 4 * kd == kQKV && kd == kKD; }
+bool psa_tc_supported(int C, int nh, int kd) { return kd == kKD && nh >= 1 && C == nh * kHD; }
 
 int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,
                          const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
                          const float* b_proj, __nv_bfloat16* y, int B, int C, int H, int W, int nh, int kd,
                          void* ws, size_t ws_bytes, cudaStream_t st, float* lse_out) {
-  VA_CHECK_ARG(psa_tc_supported(C, nh, kd), "psa_attention bf16: tensor-core path needs C=128, nh=2, kd=32");
+  VA_CHECK_ARG(psa_tc_supported(C, nh, kd), "psa_attention bf16: tensor-core path needs key_dim 32 and C = 64·num_heads");
+  if (!psa_tc_is_n(C, nh, kd))
+    return psa_attention_fwd_tc_wide(x, w_qkv, b_qkv, w_pe, b_pe, w_proj, b_proj, y, B, C, H, W, nh, ws, ws_bytes, st);
   VA_CHECK_ARG(B > 0 && H > 0 && W > 0 && B <= 65535, "psa_attention bf16: bad sizes");
   VA_CHECK_ARG((H + 2) * ((W + 10) | 1) <= kMaxPlane, "psa_attention bf16: image %dx%d larger than supported", H, W);
   const TcWs L = tc_layout(B, H, W, nh);
@@ -1669,7 +1673,7 @@ int tc_flash_attention(const void* qk, const void* v, void* o, float* lse, int B
 
 int psa_attention_core_tc(const void* qk, const void* v, void* o, float* lse, int B, int nh, int H, int W,
                           cudaStream_t st) {
-  VA_CHECK_ARG(nh == 2 && B > 0 && H > 0 && W > 0 && B * nh <= 65535, "psa flash attention: need nh=2, B,H,W > 0");
+  VA_CHECK_ARG(nh >= 1 && B > 0 && H > 0 && W > 0 && (long long)B * nh <= 65535, "psa flash attention: bad sizes");
   return tc_flash_attention(qk, v, o, lse, B * nh, nh, H * W, kKD, 0, st);
 }
 
