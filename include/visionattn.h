@@ -151,9 +151,10 @@ VA_API int va_dwconv3x3_backward_f32(const float *x, const float *w, const float
  * f32 variant: f32 everything (SIMT FFMA path, max-abs 1e-5 class).
  * bf16 variant: x, y and weights bf16, biases f32 (tcgen05/TMEM tensor-core
  * path: bf16 qkv GEMM, f16 attention operands, f32 accumulation); it
- * supports the YOLO26 PSA shape C = 128, nh = 2, kd = 32 and any H, W
- * (returns VA_ERR_SHAPE otherwise); x, w_qkv, w_proj 16-byte aligned,
- * workspace 256-byte aligned.  f32 variant: any C = nh*2*kd.
+ * supports every c2psa width, kd = 32 and C = 64*nh (YOLO26 n: 128, s/m/l:
+ * 256, x: 384; c2psa.rs:158) and any H, W (returns VA_ERR_SHAPE otherwise);
+ * x, w_qkv, w_proj 16-byte aligned, workspace 256-byte aligned.  f32
+ * variant: any C = nh*2*kd.
  * `workspace` holds the qkv/attention intermediates; size from
  * va_psa_attention_workspace_bytes().  dtype: 0 = f32, 1 = bf16. */
 VA_API size_t va_psa_attention_workspace_bytes(int B, int C, int H, int W, int num_heads, int key_dim,
@@ -168,6 +169,36 @@ VA_API int va_psa_attention_fwd_bf16(const va_bf16 *x, const va_bf16 *w_qkv, con
                               const float *b_proj, va_bf16 *y, int B, int C, int H, int W,
                               int num_heads, int key_dim, void *workspace, size_t ws_bytes,
                               va_stream_t stream);
+
+/* ── PSABlock and C2PSA forward (c2psa.rs:123-179, BN folded, bf16) ─────────
+ * PSABlock (psa_block, c2psa.rs:123-137): y1 = x + attn(x);
+ * y = y1 + ffn1(SiLU(ffn0(y1))) with ffn0 a 1×1 conv C→2C + BN + SiLU and
+ * ffn1 a 1×1 conv 2C→C + BN (conv.rs:31-69).  C2PSA (c2psa.rs:150-179):
+ * h = SiLU(cv1(x)) (C1→C1, split into a = h[:C1/2], b = h[C1/2:]);
+ * b = PSABlock(b) n_blocks times; y = SiLU(cv2(cat(a, b))); C = C1/2,
+ * num_heads = C/64, key_dim 32.  Weights bf16 with BN folded ([out][in] for
+ * 1×1 convs), biases f32; x, y bf16 NCHW; H*W % 8 == 0; 16-byte aligned
+ * pointers, 256-byte aligned workspace.  Tensor-core GEMMs with bias, SiLU
+ * and residual in their epilogues around the tensor-core PSA Attention;
+ * intermediates f16 except the attention op's bf16 input and output.  No
+ * counterpart entry in the reference (its graph records these as separate
+ * conv / elem_add nodes); the maths is the reference graph's. */
+typedef struct va_psa_block_weights {
+  const va_bf16 *w_qkv;  const float *b_qkv;   /* [2C][C], [2C]  qkv conv + BN */
+  const va_bf16 *w_pe;   const float *b_pe;    /* [C][1][3][3], [C]  pe dw-conv + BN */
+  const va_bf16 *w_proj; const float *b_proj;  /* [C][C], [C]  proj conv + BN */
+  const va_bf16 *w_ffn0; const float *b_ffn0;  /* [2C][C], [2C]  ffn.0 conv + BN (SiLU) */
+  const va_bf16 *w_ffn1; const float *b_ffn1;  /* [C][2C], [C]  ffn.1 conv + BN */
+} va_psa_block_weights;
+VA_API size_t va_psa_block_workspace_bytes(int B, int C, int H, int W);
+VA_API int va_psa_block_fwd_bf16(const va_bf16 *x, const va_psa_block_weights *w, va_bf16 *y, int B,
+                                 int C, int H, int W, void *workspace, size_t ws_bytes,
+                                 va_stream_t stream);
+VA_API size_t va_c2psa_workspace_bytes(int B, int C1, int H, int W, int n_blocks);
+VA_API int va_c2psa_fwd_bf16(const va_bf16 *x, const va_bf16 *w_cv1, const float *b_cv1, int n_blocks,
+                             const va_psa_block_weights *blocks, const va_bf16 *w_cv2,
+                             const float *b_cv2, va_bf16 *y, int B, int C1, int H, int W,
+                             void *workspace, size_t ws_bytes, va_stream_t stream);
 
 /* ── Multi-scale deformable attention (RF-DETR decoder) ──────────────────────
  * No counterpart in the reference (it has no deformable attention); the

@@ -24,8 +24,11 @@ returning float32 unless noted:
   proj conv+BN), with BN folded into conv weight + bias as ``graph.optimise()``
   does (``examples/yolo26.rs:3021``).
 * ``c2psa_forward_eval``  — ``c2psa.rs:150-179`` + ``psa_block`` ``c2psa.rs:123-137``,
-  used only to pin this oracle against the reference's golden fixtures
+  used to pin this oracle against the reference's golden fixtures
   (``tests/fixtures/c2psa_yolo26/generate.py``).
+* ``psa_block_forward`` / ``c2psa_forward_folded`` — the same block and
+  C2PSA with BN folded (the form the fused bf16 ops take), checked against
+  ``c2psa_forward_eval`` in ``tests/test_oracle_golden.py``.
 
 Parity pin: ``tests/test_oracle_golden.py`` checks these functions against
 the reference's committed PyTorch-generated fixtures (copied into
@@ -247,6 +250,29 @@ def psa_attention(x, w_qkv, b_qkv, w_pe, b_pe, w_proj, b_proj, num_heads: int, k
         return y, dict(qkv=qkv, packed=packed, o_lo=o_lo, o_hi=o_hi, lse=lse,
                        merged=merged, v=v, pe=pe)
     return y
+
+
+def psa_block_forward(x, w: dict, num_heads: int, key_dim: int = 32):
+    """PSABlock with BN folded (``psa_block``, c2psa.rs:123-137):
+    b = x + attn(x); out = b + ffn1(SiLU(ffn0(b))), ffn0 = conv1x1 C→2C (+ bias,
+    SiLU: ``conv``, conv.rs:31-45), ffn1 = conv1x1 2C→C (+ bias: ``conv_bn``,
+    conv.rs:53-69).  ``w`` holds w_qkv … b_proj (as psa_attention takes them)
+    and w_ffn0, b_ffn0, w_ffn1, b_ffn1."""
+    x = _f64(x)
+    b = x + psa_attention(x, w["w_qkv"], w["b_qkv"], w["w_pe"], w["b_pe"], w["w_proj"], w["b_proj"], num_heads,
+                          key_dim)
+    return b + conv1x1(silu(conv1x1(b, w["w_ffn0"], w["b_ffn0"])), w["w_ffn1"], w["b_ffn1"])
+
+
+def c2psa_forward_folded(x, w_cv1, b_cv1, blocks: list, w_cv2, b_cv2, key_dim: int = 32):
+    """C2PSA with BN folded (c2psa.rs:150-179): h = SiLU(cv1(x)); a, b = split;
+    b = PSABlock(b) per entry of ``blocks``; SiLU(cv2(cat(a, b)))."""
+    h = silu(conv1x1(_f64(x), w_cv1, b_cv1))
+    c = h.shape[1] // 2
+    a, b = h[:, :c], h[:, c:]
+    for w in blocks:
+        b = psa_block_forward(b, w, c // 64, key_dim)
+    return silu(conv1x1(np.concatenate([a, b], axis=1), w_cv2, b_cv2))
 
 
 def c2psa_forward_eval(x, prm: dict, eps: float = 1e-5, num_heads: int = 2, key_dim: int = 32):

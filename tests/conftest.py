@@ -30,6 +30,21 @@ def stage_params(g):
     return {s: tuple(g[f"{s}_{p}"] for p in ("conv_w", "bn_w", "bn_b", "bn_rm", "bn_rv")) for s in STAGES}
 
 
+def folded_c2psa(g, eps=1e-5):
+    """The golden C2PSA fixture's parameters with BN folded into conv weight +
+    bias (1×1 weights as [out][in]): (w_cv1, b_cv1, [block dict], w_cv2, b_cv2)."""
+    from oracle import psa_oracle as po
+    prm = stage_params(g)
+    f = {k: po.fold_bn(*prm[k], eps) for k in prm}
+    mat = lambda w: np.asarray(w, np.float64).reshape(w.shape[0], -1)
+    blk = {"w_qkv": mat(f["m0_attn_qkv"][0]), "b_qkv": f["m0_attn_qkv"][1],
+           "w_pe": np.asarray(f["m0_attn_pe"][0], np.float64), "b_pe": f["m0_attn_pe"][1],
+           "w_proj": mat(f["m0_attn_proj"][0]), "b_proj": f["m0_attn_proj"][1],
+           "w_ffn0": mat(f["m0_ffn0"][0]), "b_ffn0": f["m0_ffn0"][1],
+           "w_ffn1": mat(f["m0_ffn1"][0]), "b_ffn1": f["m0_ffn1"][1]}
+    return mat(f["cv1"][0]), f["cv1"][1], [blk], mat(f["cv2"][0]), f["cv2"][1]
+
+
 def rel_l2(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)

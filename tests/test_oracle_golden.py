@@ -6,7 +6,7 @@ the reference's ultralytics/PyTorch-generated fixtures for the PSA block
 depthwise conv (tests/fixtures/conv_grouped/depthwise)."""
 import numpy as np
 
-from conftest import load_golden, max_abs, stage_params
+from conftest import folded_c2psa, load_golden, max_abs, stage_params
 from oracle import psa_oracle as po
 
 SCALE = 1.0 / np.sqrt(np.float32(32))
@@ -16,6 +16,14 @@ def test_c2psa_eval_forward_matches_reference_fixture():
     g = load_golden("c2psa_fwd.npz")
     y = po.c2psa_forward_eval(g["x"], stage_params(g))
     # reference tolerance 1e-3 (test_c2psa_cuda.rs:673); the oracle is far inside it
+    assert max_abs(y, g["expected_output"]) < 1e-5
+
+
+def test_c2psa_folded_forward_matches_reference_fixture():
+    """The BN-folded PSABlock / C2PSA restatement (the form the fused ops take)."""
+    g = load_golden("c2psa_fwd.npz")
+    w_cv1, b_cv1, blocks, w_cv2, b_cv2 = folded_c2psa(g)
+    y = po.c2psa_forward_folded(g["x"], w_cv1, b_cv1, blocks, w_cv2, b_cv2)
     assert max_abs(y, g["expected_output"]) < 1e-5
 
 

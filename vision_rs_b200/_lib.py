@@ -68,6 +68,10 @@ SIGNATURES: dict[str, tuple] = {
     "va_psa_train_fwd_bwd_bf16": (I, [P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, SZ, S]),
     "va_psa_sgd_update": (I, [P, P, F, F, P, P, P, P, P, P, S]),
     "va_gemm_f16": (I, [P, I, LL, LL, I, P, I, LL, LL, I, P, I, LL, LL, I, I, I, I, F, S]),
+    "va_psa_block_workspace_bytes": (SZ, [I, I, I, I]),
+    "va_psa_block_fwd_bf16": (I, [P, P, P, I, I, I, I, P, SZ, S]),
+    "va_c2psa_workspace_bytes": (SZ, [I, I, I, I, I]),
+    "va_c2psa_fwd_bf16": (I, [P, P, P, I, P, P, P, P, I, I, I, I, P, SZ, S]),
     "va_dp_comm_create": (I, [I, I, I, I, C.POINTER(P), P]),
     "va_dp_comm_connect": (I, [P, P]),
     "va_dp_comm_status": (I, [P, C.POINTER(C.c_int)]),
@@ -101,6 +105,12 @@ def lib() -> C.CDLL:
             fn.argtypes = args
         _lib = lb
     return _lib
+
+
+class PsaBlockWeights(C.Structure):
+    """``va_psa_block_weights``: device pointers of one PSABlock's folded weights."""
+    _fields_ = [(n, P) for n in ("w_qkv", "b_qkv", "w_pe", "b_pe", "w_proj", "b_proj", "w_ffn0", "b_ffn0",
+                                 "w_ffn1", "b_ffn1")]
 
 
 def call(name: str, *args) -> int:

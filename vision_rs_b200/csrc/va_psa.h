@@ -33,6 +33,12 @@ int dwconv3x3(const T* x, const TW* w, const float* bias, T* y, int B, int C, in
 // or, for other widths C = 64·nh, the general one (va_tc_psa_wide.cu).
 size_t psa_tc_workspace_bytes(int B, int C, int H, int W, int nh);
 size_t psa_tc_wide_workspace_bytes(int B, int C, int H, int W);
+// PE = dw3×3(V) + b_pe (+ add, when given) for V f16 [B·C][Np] with rows of W
+// (W % 4 == 0; VA_ERR_UNSUPPORTED otherwise, nothing launched), and W_proj
+// [C][C] to f16 on the side.
+int pe_dwconv_vec(const __half* v, const __nv_bfloat16* w_pe, const float* b_pe, __half* pe,
+                  const __nv_bfloat16* w_proj, __half* wproj16, int B, int C, int H, int W, int Np,
+                  const __half* add, cudaStream_t st);
 int psa_attention_fwd_tc_wide(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,
                               const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
                               const float* b_proj, __nv_bfloat16* y, int B, int C, int H, int W, int nh, void* ws,
@@ -59,10 +65,19 @@ struct GemmOperand {
 // C[z'][m][n] = α·Σ_{z in fold z'} Σ_k A_z(m,k)·B_z(n,k) + bias[m], f32
 // accumulation; z' = z / zfold (ceil(Z/zfold) outputs); C is f32 (c_type 0),
 // bf16 (1) or f16 (2) with row pitch ldc and batch stride c_batch (elements).
-// Operands are f16, or bf16 with ab_bf16; bias (f32 [M]) is optional.
+// Operands are f16, or bf16 with ab_bf16; bias (f32 [M]) is optional;
+// epi adds SiLU and a residual.
+// Optional epilogue of tc_gemm_f16: SiLU after the bias, then + res[z][m][n]
+// (res_type 0 f32, 1 bf16, 2 f16; row pitch ldr, batch stride r_batch).
+struct GemmEpilogue {
+  bool silu = false;
+  const void* res = nullptr;
+  int res_type = 0;
+  long long ldr = 0, r_batch = 0;
+};
 int tc_gemm_f16(const GemmOperand& a, const GemmOperand& b, void* c, int c_type, long long ldc, long long c_batch,
                 int M, int N, int K, int Z, cudaStream_t st, float alpha = 1.0f, int zfold = 1,
-                const float* bias = nullptr, bool ab_bf16 = false);
+                const float* bias = nullptr, bool ab_bf16 = false, const GemmEpilogue& epi = GemmEpilogue());
 int gemm_status_read(int* out, cudaStream_t st);
 // Tensor-core PSA attention backward (nh = 2, kd = 32, N ≤ 512), channel-major
 // f32 outputs: dk [B·nh][32][N], dv [B·nh][64][N], dq_part

@@ -2,13 +2,14 @@
 // of the 1×1 convolutions) and the 1×1 convolutions of the PSA forward at
 // widths other than 128:
 //
-//   C[z][m][n] = α · Σ_k A_z(m, k) · B_z(n, k) (+ bias[m])
-//                f16 or bf16 operands (both the same), f32 accumulate
+//   C[z][m][n] = act(α · Σ_k A_z(m, k) · B_z(n, k) + bias[m]) (+ R[z][m][n])
+//                f16 or bf16 operands (both the same), f32 accumulate, act = SiLU
+//                or none, R an optional residual (f32, bf16 or f16)
 //
 // Each operand is K-major (row m holds its K elements contiguously) or
 // MN-major (row k holds its M — or N — elements contiguously), optionally
 // shared by every batch entry.  One CTA computes a 128×128 tile: a producer
-// thread streams 64-wide K blocks through a 4-stage TMA ring (out-of-range
+// thread streams 64-wide K blocks through a 3-stage TMA ring (out-of-range
 // rows and columns read as zeros), one thread issues the MMAs into a TMEM
 // accumulator, and the four warps store it (f32, bf16 or f16).  A CTA may
 // fold `zfold` consecutive batch entries into its K loop (one accumulator),
@@ -29,7 +30,9 @@ __device__ int g_gemm_status;
 
 namespace {
 
-constexpr int kGM = 128, kGN = 128, kGK = 64, kGStages = 4;
+// Three ring stages (96 KB of shared memory) let two CTAs share an SM, so one
+// CTA's set-up, pipeline fill and epilogue overlap the other's MMAs.
+constexpr int kGM = 128, kGN = 128, kGK = 64, kGStages = 3;
 
 struct GemmSmem {
   uint8_t a[kGStages][kGM * 128];  // 16 KB per stage
@@ -42,10 +45,11 @@ struct GemmSmem {
 constexpr int kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2;
 
 template <bool A_MN, bool B_MN, int OUT>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(128, 2)
 gemm_f16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, void* __restrict__ c,
                 int M, int N, int K, long long ldc, long long c_batch, int a_bcast, int b_bcast, float alpha, int Z,
-                int zfold, uint32_t ab_fmt, const float* __restrict__ bias) {
+                int zfold, uint32_t ab_fmt, const float* __restrict__ bias, int act, const void* __restrict__ res,
+                int res_type, long long ldr, long long r_batch) {
   extern __shared__ uint8_t smem_raw[];
   GemmSmem& sm = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -143,6 +147,24 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
       for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(fmaf(__uint_as_float(u[i]), alpha, bm));
       const int nb = n0 + ch * 32;
       if (m >= M || nb >= N) continue;
+      if (act) {  // SiLU: v·σ(v)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float v = __uint_as_float(u[i]);
+          u[i] = __float_as_uint(v / (1.0f + __expf(-v)));
+        }
+      }
+      if (res) {  // + residual (f32, bf16 or f16 by res_type), columns < N
+        const long long ro = z * r_batch + (long long)m * ldr + nb;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (nb + i >= N) continue;
+          const float r = res_type == kOutF32 ? static_cast<const float*>(res)[ro + i]
+                          : res_type == kOutBF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(res)[ro + i])
+                                                 : __half2float(static_cast<const __half*>(res)[ro + i]);
+          u[i] = __float_as_uint(__uint_as_float(u[i]) + r);
+        }
+      }
       if constexpr (OUT != kOutF32) {
         using T = typename std::conditional<OUT == kOutBF16, __nv_bfloat16, __half>::type;
         auto pk = [](float a, float b) { return OUT == kOutBF16 ? pack_bf16x2(a, b) : pack_f16x2(a, b); };
@@ -217,7 +239,8 @@ int operand_map(CUtensorMap* m, const GemmOperand& op, uint64_t inner, uint64_t 
 }  // namespace
 
 int tc_gemm_f16(const GemmOperand& a, const GemmOperand& b, void* c, int c_type, long long ldc, long long c_batch,
-                int M, int N, int K, int Z, cudaStream_t st, float alpha, int zfold, const float* bias, bool ab_bf16) {
+                int M, int N, int K, int Z, cudaStream_t st, float alpha, int zfold, const float* bias, bool ab_bf16,
+                const GemmEpilogue& epi) {
   VA_CHECK_ARG(M > 0 && N > 0 && K > 0 && Z > 0 && Z <= 65535 && zfold > 0 && (N + kGN - 1) / kGN <= 65535,
                "gemm: bad sizes");
   VA_CHECK_ARG(c_type >= kOutF32 && c_type <= kOutF16, "gemm: output type %d", c_type);
@@ -235,7 +258,8 @@ int tc_gemm_f16(const GemmOperand& a, const GemmOperand& b, void* c, int c_type,
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     kernel<<<grid, 128, smem, st>>>(ma, mb, c, M, N, K, ldc, c_batch, a.broadcast ? 1 : 0, b.broadcast ? 1 : 0,
-                                    alpha, Z, zfold, ab_bf16 ? (uint32_t)AB_BF16 : (uint32_t)AB_F16, bias);
+                                    alpha, Z, zfold, ab_bf16 ? (uint32_t)AB_BF16 : (uint32_t)AB_F16, bias, epi.silu ? 1 : 0,
+                                    epi.res, epi.res_type, epi.ldr, epi.r_batch);
     return check_launch("gemm");
   };
   auto pick = [&](auto amn, auto bmn) -> int {

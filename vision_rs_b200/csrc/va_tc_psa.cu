@@ -1057,16 +1057,19 @@ template <> struct PeRow<4> {
   __device__ static T pack(const float* a) { return make_uint2(pack_f16x2(a[0], a[1]), pack_f16x2(a[2], a[3])); }
 };
 
+// Also used by the other widths (va_tc_psa_wide.cu) with C channels per image
+// and `add` (O): then pebuf receives O + PE.  Block 0 converts W_proj
+// [C][C] to f16 on the side.
 template <int CW>
 __global__ void __launch_bounds__(kPevThreads)
 pe_dwconv_vec_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __restrict__ w_pe,
                      const float* __restrict__ b_pe, __half* __restrict__ pebuf,
                      const __nv_bfloat16* __restrict__ w_proj, __half* __restrict__ wproj16, int B, int H, int W,
-                     int Np) {
+                     int Np, int C, const __half* __restrict__ add) {
   using Row = PeRow<CW>;
   const int tid = threadIdx.x;
   if (blockIdx.x == 0) {
-    for (int i = tid; i < kC * kC / 8; i += kPevThreads) {
+    for (int i = tid; i < C * C / 8; i += kPevThreads) {
       const uint4 src = __ldg(reinterpret_cast<const uint4*>(w_proj) + i);
       const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&src);
       uint4 u;
@@ -1082,9 +1085,9 @@ pe_dwconv_vec_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __res
   constexpr int R = kPevRows;
   const unsigned cpr = W / CW, nrb = (H + R - 1) / R, nblk = nrb * cpr;  // per plane
   const unsigned q = blockIdx.x * kPevThreads + tid;  // < 2^31 (checked by the launcher)
-  if (q >= (unsigned)B * kC * nblk) return;
+  if (q >= (unsigned)B * C * nblk) return;
   const unsigned plane = q / nblk, k = q - plane * nblk;
-  const int rb = (int)(k / cpr), j0 = (int)(k - rb * cpr) * CW, r0 = rb * R, ch = (int)(plane % kC);
+  const int rb = (int)(k / cpr), j0 = (int)(k - rb * cpr) * CW, r0 = rb * R, ch = (int)(plane % (unsigned)C);
   const __half* src = vbuf + (size_t)plane * Np + j0;
   // rows r0-1 .. r0+R, clamped into the image (masked below)
   typename Row::T u[R + 2];
@@ -1130,9 +1133,17 @@ pe_dwconv_vec_kernel(const __half* __restrict__ vbuf, const __nv_bfloat16* __res
         ffma2(acc[e], acc[e + 1], w[di * 3], w[di * 3], xr[e], xr[e + 1], acc[e], acc[e + 1]);
       }
     }
+    if (add) {
+      float ov[CW];
+      Row::unpack(__ldg(reinterpret_cast<const typename Row::T*>(add + (size_t)plane * Np + (size_t)(r0 + o) * W + j0)),
+                  ov);
+#pragma unroll
+      for (int e = 0; e < CW; ++e) acc[e] += ov[e];
+    }
     *reinterpret_cast<typename Row::T*>(dst + (size_t)o * W) = Row::pack(acc);
   }
 }
+
 
 // ── Kernel 4: output projection y = W_proj·(O + PE) + b_proj ───────────────
 // Both O and PE tiles arrive by TMA as MN-major operands; the sum O + PE is
@@ -1468,6 +1479,20 @@ int set_smem(K kernel, size_t bytes) {
 
 }  // namespace
 
+int pe_dwconv_vec(const __half* v, const __nv_bfloat16* w_pe, const float* b_pe, __half* pe,
+                  const __nv_bfloat16* w_proj, __half* wproj16, int B, int C, int H, int W, int Np,
+                  const __half* add, cudaStream_t st) {
+  const int cw = (W & 7) == 0 ? 8 : (W & 3) == 0 ? 4 : 0;
+  const long long blocks = cw ? (long long)B * C * ((H + kPevRows - 1) / kPevRows) * (W / cw) : 0;
+  if (!cw || blocks >= (1LL << 31)) return VA_ERR_UNSUPPORTED;
+  const unsigned grid = (unsigned)((blocks + kPevThreads - 1) / kPevThreads);
+  if (cw == 8)
+    pe_dwconv_vec_kernel<8><<<grid, kPevThreads, 0, st>>>(v, w_pe, b_pe, pe, w_proj, wproj16, B, H, W, Np, C, add);
+  else
+    pe_dwconv_vec_kernel<4><<<grid, kPevThreads, 0, st>>>(v, w_pe, b_pe, pe, w_proj, wproj16, B, H, W, Np, C, add);
+  return check_launch("psa pe");
+}
+
 size_t psa_tc_workspace_bytes(int B, int C, int H, int W, int nh) {
   return psa_tc_is_n(C, nh, kKD) ? tc_layout(B, H, W, nh).total : psa_tc_wide_workspace_bytes(B, C, H, W);
 }
@@ -1577,18 +1602,13 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   attn_kernel<kKD, kOutChannelMajor>
       <<<dim3((ntile + 1) / 2, BH), kAttnThreads, sm2, st>>>(mqk, mv, ob, lse_out, N, Np, nh, scale_log2);
   if (int rc = check_launch("psa attention")) return rc;
-  const int pe_cw = (W & 7) == 0 ? 8 : (W & 3) == 0 ? 4 : 0;
-  const long long pe_blocks = pe_cw ? (long long)B * kC * ((H + kPevRows - 1) / kPevRows) * (W / pe_cw) : 0;
-  if (pe_cw && pe_blocks < (1LL << 31)) {
-    const unsigned grid = (unsigned)((pe_blocks + kPevThreads - 1) / kPevThreads);
-    if (pe_cw == 8)
-      pe_dwconv_vec_kernel<8><<<grid, kPevThreads, 0, st>>>(vb, w_pe, b_pe, peb, w_proj, wp16, B, H, W, Np);
-    else
-      pe_dwconv_vec_kernel<4><<<grid, kPevThreads, 0, st>>>(vb, w_pe, b_pe, peb, w_proj, wp16, B, H, W, Np);
-  } else {
+  const int pe_rc = pe_dwconv_vec(vb, w_pe, b_pe, peb, w_proj, wp16, B, kC, H, W, Np, nullptr, st);
+  if (pe_rc == VA_ERR_UNSUPPORTED) {
     pe_dwconv_kernel<<<dim3(kC / kPeCh, B), kPeThreads, sm3, st>>>(vb, w_pe, b_pe, peb, w_proj, wp16, H, W, Np);
+    if (int rc = check_launch("psa pe")) return rc;
+  } else if (pe_rc) {
+    return pe_rc;
   }
-  if (int rc = check_launch("psa pe")) return rc;
   if (N % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
     CUtensorMap my;
     uint64_t d[2] = {(uint64_t)N, (uint64_t)B * kC}, s[1] = {(uint64_t)N * 2};

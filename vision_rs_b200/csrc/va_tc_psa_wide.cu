@@ -47,28 +47,52 @@ WideWs wide_layout(int B, int C, int H, int W) {
 
 // Block (b·nh + h, 64-token block): the head's 128 qkv rows (q 32 | k 32 | v 64)
 // → Q, K token-major rows of 32 channels and V rows of the [B·C][Np] buffer.
+// 16-byte loads and stores; Q and K pass through a shared-memory transpose.
 __global__ void __launch_bounds__(256) split_qkv_kernel(const __half* __restrict__ qkv, __half* __restrict__ qk,
                                                         __half* __restrict__ v, int N, int Np, int nh, int BH) {
-  __shared__ __half t[64][64 + 2];  // [channel (q then k)][token]
+  __shared__ __align__(16) __half t[64][72];  // [q, k channel][token], 144-byte rows
   const int bh = blockIdx.y, n0 = blockIdx.x * 64, tid = threadIdx.x;
   const int b = bh / nh, h = bh % nh, C = nh * kWHD;
   const __half* src = qkv + ((size_t)b * 2 * C + (size_t)h * 128) * Np;
-  for (int i = tid; i < 64 * 64; i += 256) {  // q, k rows: coalesced along tokens
-    const int c = i >> 6, n = n0 + (i & 63);
-    t[c][i & 63] = n < N ? src[(size_t)c * Np + n] : __float2half_rn(0.f);
-  }
-  for (int i = tid; i < 64 * 64; i += 256) {  // v rows: plain copies
-    const int c = i >> 6, n = n0 + (i & 63);
-    if (n < N) v[((size_t)bh * kWHD + c) * Np + n] = src[(size_t)(64 + c) * Np + n];
+  for (int i = tid; i < 128 * 8; i += 256) {  // 128 rows × 8 chunks of 8 tokens
+    const int r = i >> 3, c8 = (i & 7) * 8, n = n0 + c8;
+    const __half* sp = src + (size_t)r * Np + n;
+    uint4 u = make_uint4(0u, 0u, 0u, 0u);
+    if (n + 8 <= N) {
+      u = __ldg(reinterpret_cast<const uint4*>(sp));
+    } else {
+      __half* e = reinterpret_cast<__half*>(&u);
+      for (int k = 0; k < 8 && n + k < N; ++k) e[k] = sp[k];
+    }
+    if (r < 64) {
+      *reinterpret_cast<uint4*>(&t[r][c8]) = u;
+    } else {
+      __half* dp = v + ((size_t)bh * kWHD + r - 64) * Np + n;
+      if (n + 8 <= N) {
+        *reinterpret_cast<uint4*>(dp) = u;
+      } else {
+        const __half* e = reinterpret_cast<const __half*>(&u);
+        for (int k = 0; k < 8 && n + k < N; ++k) dp[k] = e[k];
+      }
+    }
   }
   __syncthreads();
-  for (int i = tid; i < 2 * 64 * kWKD; i += 256) {  // token-major: 32 channels of one token are contiguous
-    const int sec = i / (64 * kWKD), r = i % (64 * kWKD), n = r / kWKD, c = r % kWKD;
-    if (n0 + n < N) qk[(((size_t)sec * BH + bh) * N + n0 + n) * kWKD + c] = t[sec * kWKD + c][n];
+  for (int i = tid; i < 64 * 2 * 4; i += 256) {  // token × section × 8-channel chunk
+    const int n = i >> 3, sec = (i >> 2) & 1, c8 = (i & 3) * 8;
+    if (n0 + n >= N) continue;
+    uint4 u;
+    uint32_t* w = &u.x;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __half2 hh = __halves2half2(t[sec * kWKD + c8 + 2 * e][n], t[sec * kWKD + c8 + 2 * e + 1][n]);
+      w[e] = *reinterpret_cast<const uint32_t*>(&hh);
+    }
+    *reinterpret_cast<uint4*>(qk + (((size_t)sec * BH + bh) * N + n0 + n) * kWKD + c8) = u;
   }
 }
 
-// S = O + dw3×3(V) + b_pe, one thread per output; plane p = b·C + c.
+// S = O + dw3×3(V) + b_pe, one thread per output; plane p = b·C + c (images
+// whose width is not a multiple of 4).
 __global__ void __launch_bounds__(256) pe_add_kernel(const __half* __restrict__ v, const __half* __restrict__ o,
                                                      const __nv_bfloat16* __restrict__ w_pe,
                                                      const float* __restrict__ b_pe, __half* __restrict__ s, int C,
@@ -154,12 +178,17 @@ int psa_attention_fwd_tc_wide(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv
   if (int rc = check_launch("psa wide split")) return rc;
   // 3. attention (O channel-major [B·C][Np])
   if (int rc = tc_flash_attention(qk, v, o, nullptr, BH, nh, N, kWKD, 0, st)) return rc;
-  // 4. S = O + PE, W_proj as f16
-  pe_add_kernel<<<grid_for((long long)B * C * N), 256, 0, st>>>(v, o, w_pe, b_pe, s, C, H, W, Np,
-                                                                 (long long)B * C * N);
-  if (int rc = check_launch("psa wide pe")) return rc;
-  bf16_to_f16_kernel<<<grid_for((long long)C * C), 256, 0, st>>>(w_proj, w16, C * C);
-  if (int rc = check_launch("psa wide w_proj")) return rc;
+  // 4. S = O + PE, W_proj as f16 (register-window kernel when W % 4 == 0)
+  const int pe_rc = pe_dwconv_vec(v, w_pe, b_pe, s, w_proj, w16, B, C, H, W, Np, o, st);
+  if (pe_rc == VA_ERR_UNSUPPORTED) {
+    pe_add_kernel<<<grid_for((long long)B * C * N), 256, 0, st>>>(v, o, w_pe, b_pe, s, C, H, W, Np,
+                                                                   (long long)B * C * N);
+    if (int rc = check_launch("psa wide pe")) return rc;
+    bf16_to_f16_kernel<<<grid_for((long long)C * C), 256, 0, st>>>(w_proj, w16, C * C);
+    if (int rc = check_launch("psa wide w_proj")) return rc;
+  } else if (pe_rc) {
+    return pe_rc;
+  }
   // 5. y[b] = W_proj · S[b] + b_proj   (M = C, N tokens, K = C), bf16 NCHW
   return tc_gemm_f16(GemmOperand{w16, false, C, 0, true}, GemmOperand{s, true, Np, (long long)C * Np, false}, y, 1,
                      N, (long long)C * N, C, N, C, B, st, 1.0f, 1, b_proj, false);
