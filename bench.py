@@ -825,7 +825,11 @@ def run_ours(args, ws, rank, local):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:
+        # NCCL reports each rank's communicator set-up (stderr), which shows every rank joined
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        dist.barrier()  # communicator created on every rank before any work
     cls = CONFIGS[args.config]
     B = args.batch or cls.batch
     wl = cls(dev, rank, B, args)
