@@ -200,6 +200,30 @@ VA_API int va_c2psa_fwd_bf16(const va_bf16 *x, const va_bf16 *w_cv1, const float
                              const float *b_cv2, va_bf16 *y, int B, int C1, int H, int W,
                              void *workspace, size_t ws_bytes, va_stream_t stream);
 
+/* ── safetensors weights with BN folding (examples/yolo26.rs:3403-3470) ──────
+ * Host-side reader of a safetensors checkpoint (u64 header size, JSON header
+ * of name → dtype/shape/data_offsets, tensor bytes) replacing the reference's
+ * `load_weights_from_safetensors`.  open reads the file and parses the
+ * header (malformed files return VA_ERR_SHAPE); tensor_info gives the dtype
+ * (VA_ST_*, -1 for others) and shape (up to 8 dims); read_f32 converts an
+ * F32/F16/BF16 tensor to f32 (count must equal its element count);
+ * fold_conv_bn reads `{prefix}.conv.weight` and `{prefix}.bn.{weight, bias,
+ * running_mean, running_var}` and folds them as the reference does
+ * (scale = γ/√(var + eps), w·scale, β − mean·scale; eps 1e-3 for YOLO26,
+ * conv.rs:39,64) into host buffers w_out [c_out][w_count/c_out], b_out
+ * [c_out].  All pointers are host memory. */
+#define VA_ST_F32 0
+#define VA_ST_F16 1
+#define VA_ST_BF16 2
+typedef struct va_safetensors va_safetensors;
+VA_API int va_safetensors_open(const char *path, va_safetensors **out);
+VA_API void va_safetensors_close(va_safetensors *st);
+VA_API int va_safetensors_tensor_info(va_safetensors *st, const char *key, int *dtype, int64_t *shape,
+                                      int *rank);
+VA_API int va_safetensors_read_f32(va_safetensors *st, const char *key, float *dst, size_t count);
+VA_API int va_safetensors_fold_conv_bn(va_safetensors *st, const char *prefix, float eps, float *w_out,
+                                       float *b_out, size_t w_count, int c_out);
+
 /* ── Multi-scale deformable attention (RF-DETR decoder) ──────────────────────
  * No counterpart in the reference (it has no deformable attention); the
  * published MSDeformAttn core with grid_sample(align_corners=False,

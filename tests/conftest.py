@@ -45,6 +45,31 @@ def folded_c2psa(g, eps=1e-5):
     return mat(f["cv1"][0]), f["cv1"][1], [blk], mat(f["cv2"][0]), f["cv2"][1]
 
 
+FIXTURE_STAGES = {"cv1": "cv1", "cv2": "cv2", "m0_attn_qkv": "m.0.attn.qkv", "m0_attn_pe": "m.0.attn.pe",
+                  "m0_attn_proj": "m.0.attn.proj", "m0_ffn0": "m.0.ffn.0", "m0_ffn1": "m.0.ffn.1"}
+
+
+def c2psa_checkpoint(tmp_path, dtype=None, prefix="model.10"):
+    """A safetensors checkpoint with the reference's key layout for a C2PSA
+    (``{prefix}.cv1.conv.weight``, ``{prefix}.m.0.attn.qkv.bn.running_var`` …)
+    holding the golden C2PSA fixture's parameters; returns (path, fixture)."""
+    import torch
+    from safetensors.torch import save_file
+    dtype = dtype or torch.float32
+    g = load_golden("c2psa_fwd.npz")
+    prm = stage_params(g)
+    t = {}
+    for stage, path in FIXTURE_STAGES.items():
+        w, *bn = prm[stage]
+        t[f"{prefix}.{path}.conv.weight"] = torch.as_tensor(np.asarray(w, np.float32)).to(dtype)
+        for name, v in zip(("weight", "bias", "running_mean", "running_var"), bn):
+            t[f"{prefix}.{path}.bn.{name}"] = torch.as_tensor(np.asarray(v, np.float32))
+    t["model.0.conv.weight"] = torch.zeros(4, 3, 3, 3, dtype=torch.float16)  # an unrelated tensor
+    f = os.path.join(str(tmp_path), "yolo26_c2psa.safetensors")
+    save_file(t, f, metadata={"format": "pt"})
+    return f, g
+
+
 def rel_l2(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)

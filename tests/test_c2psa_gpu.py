@@ -24,7 +24,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import BF16_MAX_ABS, BF16_REL_L2, folded_c2psa, load_golden, max_abs, rel_l2
+from conftest import BF16_MAX_ABS, BF16_REL_L2, c2psa_checkpoint, folded_c2psa, load_golden, max_abs, rel_l2
 from oracle import psa_oracle as po
 from vision_rs_b200 import _lib
 
@@ -95,6 +95,16 @@ def test_c2psa_golden_fixture(cuda):
     y = _run_c2psa(x, w_cv1, b_cv1, blocks, w_cv2, b_cv2)
     ref = po.c2psa_forward_folded(x, w_cv1, b_cv1, blocks, w_cv2, b_cv2)
     assert rel_l2(y, ref) < C2PSA_REL_L2 and max_abs(y, ref) < BF16_MAX_ABS * max(1.0, float(np.abs(ref).max()))
+    assert rel_l2(y, g["expected_output"]) < C2PSA_VS_FIXTURE_REL_L2
+
+
+def test_c2psa_from_checkpoint(cuda, tmp_path):
+    """The C2PSA op built from a safetensors checkpoint in the reference's key
+    layout (read and BN-folded by the library; the fixture's BN eps 1e-5)."""
+    from vision_rs_b200 import weights
+    f, g = c2psa_checkpoint(tmp_path)
+    op = weights.C2psa.from_safetensors(f, "model.10", eps=1e-5)
+    y = op(torch.as_tensor(g["x"]).to("cuda", torch.bfloat16)).float().cpu().numpy()
     assert rel_l2(y, g["expected_output"]) < C2PSA_VS_FIXTURE_REL_L2
 
 

@@ -72,6 +72,11 @@ SIGNATURES: dict[str, tuple] = {
     "va_psa_block_fwd_bf16": (I, [P, P, P, I, I, I, I, P, SZ, S]),
     "va_c2psa_workspace_bytes": (SZ, [I, I, I, I, I]),
     "va_c2psa_fwd_bf16": (I, [P, P, P, I, P, P, P, P, I, I, I, I, P, SZ, S]),
+    "va_safetensors_open": (I, [C.c_char_p, C.POINTER(P)]),
+    "va_safetensors_close": (None, [P]),
+    "va_safetensors_tensor_info": (I, [P, C.c_char_p, C.POINTER(C.c_int), I64P, C.POINTER(C.c_int)]),
+    "va_safetensors_read_f32": (I, [P, C.c_char_p, P, SZ]),
+    "va_safetensors_fold_conv_bn": (I, [P, C.c_char_p, F, P, P, SZ, I]),
     "va_dp_comm_create": (I, [I, I, I, I, C.POINTER(P), P]),
     "va_dp_comm_connect": (I, [P, P]),
     "va_dp_comm_status": (I, [P, C.POINTER(C.c_int)]),
