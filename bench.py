@@ -825,9 +825,6 @@ def run_ours(args, ws, rank, local):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:
-        # NCCL reports each rank's communicator set-up (stderr), which shows every rank joined
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         dist.barrier()  # communicator created on every rank before any work
     cls = CONFIGS[args.config]
@@ -945,6 +942,12 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local = dist_env()
+    if ws > 1 and args.impl == "ours":
+        # NCCL reports every rank's communicator set-up (rank, nranks, device) on stderr, which shows
+        # that all ranks joined; it reads these variables when torch first loads it, so set them here
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     if args.impl == "reference":
         run_reference(args, ws, rank)
     else:

@@ -38,7 +38,10 @@ namespace {
 
 constexpr int kC = 128, kQKV = 256, kKD = 32, kHD = 64, kNH = 2;
 constexpr int kRowThreads = 128;
-constexpr int kZFold = 1;  // images per GEMM accumulator in the weight-gradient GEMMs
+#ifndef VA_TRAIN_ZFOLD
+#define VA_TRAIN_ZFOLD 1
+#endif
+constexpr int kZFold = VA_TRAIN_ZFOLD;  // images per GEMM accumulator in the weight-gradient GEMMs
 
 __device__ __forceinline__ float block_sum(float v, float* red) {  // fixed-order reduction, kRowThreads threads
 #pragma unroll
@@ -77,6 +80,43 @@ loss_rows_kernel(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __res
   }
 }
 
+// Same as loss_rows_kernel for N % 8 == 0 (then Np == N): one warp per row,
+// 16-byte loads (8 values) and stores, warp-shuffle sums in a fixed order.
+__global__ void __launch_bounds__(256)
+loss_rows_vec_kernel(const uint4* __restrict__ y, const uint4* __restrict__ t, uint4* __restrict__ r16,
+                     float* __restrict__ rsum, float* __restrict__ rsq, int n8, long long rows) {
+  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float s = 0.f, q = 0.f;
+  for (int c = lane; c < n8; c += 32) {
+    const uint4 uy = __ldg(y + row * n8 + c), ut = __ldg(t + row * n8 + c);
+    const uint32_t* py = &uy.x;
+    const uint32_t* pt = &ut.x;
+    uint4 r;
+    uint32_t* pr = &r.x;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float d0 = __uint_as_float(py[e] << 16) - __uint_as_float(pt[e] << 16);
+      const float d1 = __uint_as_float(py[e] & 0xffff0000u) - __uint_as_float(pt[e] & 0xffff0000u);
+      s += d0 + d1;
+      q = fmaf(d0, d0, fmaf(d1, d1, q));
+      const __half2 h = __floats2half2_rn(d0, d1);
+      pr[e] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    r16[row * n8 + c] = r;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    q += __shfl_xor_sync(0xffffffffu, q, o);
+  }
+  if (lane == 0) {
+    rsum[row] = s;
+    rsq[row] = q;
+  }
+}
+
 // bf16 [rows][N] → f16 [rows][Np] (pad zero)
 __global__ void bf16_to_f16_pad_kernel(const __nv_bfloat16* __restrict__ x, __half* __restrict__ y, long long rows,
                                        int N, int Np) {
@@ -89,10 +129,14 @@ __global__ void bf16_to_f16_pad_kernel(const __nv_bfloat16* __restrict__ x, __ha
   }
 }
 
-// bf16 → f16, 8 elements per thread (16-byte loads and stores)
-__global__ void bf16_to_f16_vec_kernel(const uint4* __restrict__ x, uint4* __restrict__ y, long long n8) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
-    const uint4 u = x[i];
+// bf16 → f16, 8 elements per thread (16-byte loads and stores); a second
+// array (x2 → y2, m8 chunks) rides along in the same launch when given.
+__global__ void bf16_to_f16_vec_kernel(const uint4* __restrict__ x, uint4* __restrict__ y, long long n8,
+                                       const uint4* __restrict__ x2 = nullptr, uint4* __restrict__ y2 = nullptr,
+                                       long long m8 = 0) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8 + m8; i += (long long)gridDim.x * blockDim.x) {
+    const bool second = i >= n8;
+    const uint4 u = second ? x2[i - n8] : x[i];
     const unsigned w[4] = {u.x, u.y, u.z, u.w};
     unsigned o[4];
 #pragma unroll
@@ -100,7 +144,7 @@ __global__ void bf16_to_f16_vec_kernel(const uint4* __restrict__ x, uint4* __res
       const __half2 h = __floats2half2_rn(__uint_as_float(w[k] << 16), __uint_as_float(w[k] & 0xffff0000u));
       o[k] = *reinterpret_cast<const unsigned*>(&h);
     }
-    y[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    (second ? y2[i - n8] : y[i]) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -258,6 +302,58 @@ struct FinalizeArgs {
   float* loss;
 };
 
+// Four consecutive gradients per group of 8 lanes (every block boundary and
+// partial stride is a multiple of 4): lane j sums partials j, j+8, … with
+// 16-byte loads, and the 8 lanes combine with three shuffles (a fixed order).
+__global__ void __launch_bounds__(256) finalize_vec_kernel(FinalizeArgs a) {
+  const int j = threadIdx.x & 7;
+  // warp-uniform loop (the shuffles need every lane): lanes past the end compute nothing
+  for (int t0 = (blockIdx.x * blockDim.x + threadIdx.x) & ~31; t0 < VA_PSA_GRAD_COUNT * 2;
+       t0 += gridDim.x * blockDim.x) {
+    const int i4 = (t0 + (threadIdx.x & 31)) >> 3;
+    const bool live = i4 < VA_PSA_GRAD_COUNT / 4;
+    const int i = live ? 4 * i4 : 0;
+    const float* src;
+    int np, off;
+    size_t stride;
+    if (i < VA_PSA_GRAD_WPROJ) { src = a.part_wqkv; np = a.Pq; off = i; stride = (size_t)kQKV * kC; }
+    else if (i < VA_PSA_GRAD_WPE) { src = a.part_wproj; np = a.Pp; off = i - VA_PSA_GRAD_WPROJ; stride = (size_t)kC * kC; }
+    else if (i < VA_PSA_GRAD_BQKV) { src = a.part_wpe; np = a.B; off = i - VA_PSA_GRAD_WPE; stride = (size_t)kC * 9; }
+    else if (i < VA_PSA_GRAD_BPROJ) { src = a.part_bqkv; np = a.B; off = i - VA_PSA_GRAD_BQKV; stride = kQKV; }
+    else if (i < VA_PSA_GRAD_BPE) { src = a.rsum; np = a.B; off = i - VA_PSA_GRAD_BPROJ; stride = kC; }
+    else { src = a.part_bpe; np = a.B; off = i - VA_PSA_GRAD_BPE; stride = kC; }
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p = j; live && p < np; p += 8) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(src + p * stride + off));
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      s.x += __shfl_xor_sync(0xffffffffu, s.x, o);
+      s.y += __shfl_xor_sync(0xffffffffu, s.y, o);
+      s.z += __shfl_xor_sync(0xffffffffu, s.z, o);
+      s.w += __shfl_xor_sync(0xffffffffu, s.w, o);
+    }
+    if (live && j == 0)
+      *reinterpret_cast<float4*>(a.grads + i) = make_float4(s.x * a.sigma, s.y * a.sigma, s.z * a.sigma, s.w * a.sigma);
+  }
+  if (blockIdx.x == 0) {
+    __shared__ float red[256];
+    float s = 0.f;
+    for (int i = threadIdx.x; i < a.B * kC; i += 256) s += a.rsq[i];
+    red[threadIdx.x] = s;
+    __syncthreads();
+    for (int o = 128; o > 0; o >>= 1) {
+      if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) *a.loss = red[0] * a.inv_numel;
+  }
+}
+
 __global__ void __launch_bounds__(256) finalize_kernel(FinalizeArgs a) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < VA_PSA_GRAD_COUNT; i += gridDim.x * blockDim.x) {
     const float* src;
@@ -377,7 +473,12 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   __half* r16 = static_cast<__half*>(at(L.r16));
   float* rsum = static_cast<float*>(at(L.rsum));
   float* rsq = static_cast<float*>(at(L.rsq));
-  loss_rows_kernel<<<(unsigned)rows, kRowThreads, 0, st>>>(y, target, r16, rsum, rsq, N, Np);
+  if (N % 8 == 0 && !((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(target)) & 15))
+    loss_rows_vec_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+        reinterpret_cast<const uint4*>(y), reinterpret_cast<const uint4*>(target), reinterpret_cast<uint4*>(r16), rsum,
+        rsq, N / 8, rows);
+  else
+    loss_rows_kernel<<<(unsigned)rows, kRowThreads, 0, st>>>(y, target, r16, rsum, rsq, N, Np);
   if (int rc = check_launch("psa train loss")) return rc;
   // dW_proj partials: Pz from O, then Pz from PE (kZFold images per accumulator)
   float* pwp = static_cast<float*>(at(L.part_wproj));
@@ -446,13 +547,15 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   // qkv backward
   __half* x16 = static_cast<__half*>(at(L.x16));
   __half* wq16 = static_cast<__half*>(at(L.wqkv16));
-  if (N == Np && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
-    bf16_to_f16_vec_kernel<<<grid_for(rows * N / 8), 256, 0, st>>>(reinterpret_cast<const uint4*>(x),
-                                                                   reinterpret_cast<uint4*>(x16), rows * N / 8);
-  else
+  if (N == Np && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {  // x and W_qkv in one launch
+    bf16_to_f16_vec_kernel<<<grid_for(rows * N / 8 + kQKV * kC / 8), 256, 0, st>>>(
+        reinterpret_cast<const uint4*>(x), reinterpret_cast<uint4*>(x16), rows * N / 8,
+        reinterpret_cast<const uint4*>(w_qkv), reinterpret_cast<uint4*>(wq16), kQKV * kC / 8);
+  } else {
     bf16_to_f16_pad_kernel<<<grid_for(rows * Np), 256, 0, st>>>(x, x16, rows, N, Np);
-  bf16_to_f16_vec_kernel<<<grid_for(kQKV * kC / 8), 256, 0, st>>>(reinterpret_cast<const uint4*>(w_qkv),
-                                                                  reinterpret_cast<uint4*>(wq16), kQKV * kC / 8);
+    bf16_to_f16_vec_kernel<<<grid_for(kQKV * kC / 8), 256, 0, st>>>(reinterpret_cast<const uint4*>(w_qkv),
+                                                                    reinterpret_cast<uint4*>(wq16), kQKV * kC / 8);
+  }
   if (int rc = check_launch("psa train qkv prep")) return rc;
   float* pwq = static_cast<float*>(at(L.part_wqkv));
   if (int rc = tc_gemm_f16(GemmOperand{dq16, false, Np, (long long)kQKV * Np, false},
@@ -466,7 +569,10 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
       return rc;
   }
   FinalizeArgs fa_args{pwq, pwp, pwe, pbq, rsum, pbe, rsq, Pz, 2 * Pz, B, sigma, (float)(1.0 / numel), grads, loss};
-  finalize_kernel<<<grid_for(VA_PSA_GRAD_COUNT), 256, 0, st>>>(fa_args);
+  if (!(reinterpret_cast<uintptr_t>(grads) & 15))
+    finalize_vec_kernel<<<grid_for(VA_PSA_GRAD_COUNT * 2), 256, 0, st>>>(fa_args);
+  else
+    finalize_kernel<<<grid_for(VA_PSA_GRAD_COUNT), 256, 0, st>>>(fa_args);
   return check_launch("psa train backward");
 }
 

@@ -283,6 +283,39 @@ psa_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_con
 
 // Δ[b·h][n] = Σ_d dO[b][h·64+d][n] · O[b][h·64+d][n]  (f16 channel-major,
 // pitch Np): one thread per token, coalesced across threads.
+// Δ with 16-byte loads, N % 8 == 0: lane = 8·(token chunk) + (channel group);
+// a thread sums its 8 channels for 8 consecutive tokens, and the 8 channel
+// groups of a chunk combine with three shuffles (a fixed order).
+__global__ void __launch_bounds__(256) psa_delta_vec_kernel(const __half* __restrict__ o,
+                                                            const __half* __restrict__ d_o,
+                                                            float* __restrict__ delta, int N, int Np) {
+  const int cg = threadIdx.x & 7, n = 8 * (blockIdx.x * 32 + (threadIdx.x >> 3)), bh = blockIdx.y;
+  const bool live = n < N;
+  const size_t base = (size_t)bh * kHD * Np + (live ? n : 0) + (size_t)cg * 8 * Np;
+  float acc[8] = {};
+#pragma unroll
+  for (int d = 0; d < 8; ++d) {
+    const uint4 uo = live ? __ldg(reinterpret_cast<const uint4*>(o + base + (size_t)d * Np)) : make_uint4(0, 0, 0, 0);
+    const uint4 ud = live ? __ldg(reinterpret_cast<const uint4*>(d_o + base + (size_t)d * Np)) : make_uint4(0, 0, 0, 0);
+    const __half2* ho = reinterpret_cast<const __half2*>(&uo);
+    const __half2* hd = reinterpret_cast<const __half2*>(&ud);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 fo = __half22float2(ho[e]), fd = __half22float2(hd[e]);
+      acc[2 * e] = fmaf(fd.x, fo.x, acc[2 * e]);
+      acc[2 * e + 1] = fmaf(fd.y, fo.y, acc[2 * e + 1]);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], off);
+  if (live && cg == 0) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) delta[(size_t)bh * N + n + e] = acc[e];
+  }
+}
+
 __global__ void psa_delta_kernel(const __half* __restrict__ o, const __half* __restrict__ d_o,
                                  float* __restrict__ delta, int N, int Np) {
   const int n = blockIdx.x * blockDim.x + threadIdx.x, bh = blockIdx.y;
@@ -342,8 +375,12 @@ int psa_attn_bwd_tc(const void* qk, const void* v, const void* o, const void* d_
   cudaError_t e = cudaFuncSetAttribute(psa_attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   const int nt = (N + kT - 1) / kT;
-  psa_delta_kernel<<<dim3((N + 127) / 128, BH), 128, 0, st>>>(static_cast<const __half*>(o),
-                                                               static_cast<const __half*>(d_o), delta, N, Np);
+  if (N % 8 == 0)  // Np == N: rows of 16-byte-aligned 8-token chunks
+    psa_delta_vec_kernel<<<dim3((N / 8 + 31) / 32, BH), 256, 0, st>>>(static_cast<const __half*>(o),
+                                                                      static_cast<const __half*>(d_o), delta, N, Np);
+  else
+    psa_delta_kernel<<<dim3((N + 127) / 128, BH), 128, 0, st>>>(static_cast<const __half*>(o),
+                                                                 static_cast<const __half*>(d_o), delta, N, Np);
   if (int rc = check_launch("psa attention backward (delta)")) return rc;
   psa_attn_bwd_kernel<<<dim3(nt, BH), kBwdThreads, smem, st>>>(mqk, mv, mdo, delta, lse, dk, dv, dq_part, N, Np,
                                                               1.0f / sqrtf((float)kKD));
