@@ -224,6 +224,26 @@ VA_API int va_safetensors_read_f32(va_safetensors *st, const char *key, float *d
 VA_API int va_safetensors_fold_conv_bn(va_safetensors *st, const char *prefix, float eps, float *w_out,
                                        float *b_out, size_t w_count, int c_out);
 
+/* ── Convolution + BN (+ SiLU), NHWC, tcgen05 implicit GEMM ─────────────────
+ * Replaces the reference's `conv` (Conv2d → BN(eps 1e-3) → SiLU) and
+ * `conv_bn` (Conv2d → BN) blocks with groups = 1 (yolo26/blocks/conv.rs:
+ * 31-46, 53-69), BN folded into w and bias (va_fold_bn_f32 or
+ * va_safetensors_fold_conv_bn):
+ *   y[b][oy][ox][o] = act(bias[o] + Σ w[o][ky][kx][c]·x[b][s·oy+ky−k/2][s·ox+kx−k/2][c])
+ * x [B][H][W][Cin] and y [B][Ho][Wo][Cout] bf16 NHWC, w [Cout][k][k][Cin]
+ * bf16 (OHWI), bias f32 [Cout]; k ∈ {1, 3}, stride ∈ {1, 2}, padding k/2,
+ * Ho = (H + 2·(k/2) − k)/stride + 1 (likewise Wo), act 1 = SiLU, 0 = none.
+ * Cin and Cout multiples of 16, x/w/y 16-byte aligned (else
+ * VA_ERR_SHAPE / VA_ERR_ALIGN).  f32 accumulation, one bf16 rounding of the
+ * output.  A stalled pipeline wait sets the device status word
+ * (va_device_status_read).  va_conv_weight_ohwi_bf16 permutes the
+ * reference's OIHW weight layout to OHWI on the device. */
+VA_API int va_conv_nhwc_bf16(const va_bf16 *x, const va_bf16 *w_ohwi, const float *bias, va_bf16 *y,
+                             int B, int H, int W, int Cin, int Cout, int ksize, int stride, int act,
+                             va_stream_t stream);
+VA_API int va_conv_weight_ohwi_bf16(const va_bf16 *w_oihw, va_bf16 *w_ohwi, int Cout, int Cin,
+                                    int ksize, va_stream_t stream);
+
 /* ── Multi-scale deformable attention (RF-DETR decoder) ──────────────────────
  * No counterpart in the reference (it has no deformable attention); the
  * published MSDeformAttn core with grid_sample(align_corners=False,

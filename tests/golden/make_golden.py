@@ -14,6 +14,12 @@ little-endian f32 fixtures under ``tests/fixtures/`` of its crate:
   tolerance 5e-3 at :701)
 * ``conv_grouped/depthwise/``  — the PE-shaped depthwise 3×3 conv fwd/bwd
   (``tests/test_conv_grouped_cuda.rs`` tol 1e-5, ``…_backward_cuda.rs`` 1e-4)
+* ``conv_yolo26/``             — the YOLO26n stem Conv(3→16, k3, s2), BN in
+  training mode, B=2, 16×16 (``generate.py:36-47``; ``tests/test_conv_yolo26.rs``)
+* ``c3k2_yolo26/``             — eval-mode C3k2 blocks, B=2, 4×4
+  (``generate_all.py``): the top-level C3k2(32,64,c3k=F,sc=F,e=0.25),
+  ``shortcut/`` (same, sc=T) and ``deep_st/`` C3k2(128,128,c3k=T,sc=T,e=0.5)
+  → ``conv_c3k2.npz`` with keys ``{variant}/{stage}_{conv_w,bn_w,bn_b,bn_rm,bn_rv}``
 
 The GPU box has no copy of the reference, so the tests read these ``.npz``
 copies.  Usage (in a checkout that has the reference next to it)::
@@ -58,6 +64,51 @@ def load_stages(d):
 def prm_from(arrs):
     return {s: tuple(arrs[f"{s}_{p}"] for p in ("conv_w", "bn_w", "bn_b", "bn_rm", "bn_rv"))
             for s in STAGES}
+
+
+# (directory, C_in, C_out, c3k, shortcut, e) of the C3k2 fixtures copied
+C3K2_VARIANTS = {"shallow_sf": ("", 32, 64, False, False, 0.25),
+                 "shallow_st": ("shortcut", 32, 64, False, True, 0.25),
+                 "deep_st": ("deep_st", 128, 128, True, True, 0.5)}
+
+
+def c3k2_stage_shapes(c_in, c_out, c3k, e):
+    c = int(c_out * e)
+    sh = {"cv1": (2 * c, c_in, 1, 1), "cv2": (c_out, 3 * c, 1, 1)}
+    if c3k:
+        h = c // 2
+        sh.update({"m0_icv1": (h, c, 1, 1), "m0_icv2": (h, c, 1, 1), "m0_icv3": (c, 2 * h, 1, 1)})
+        for m in ("m0_m0_", "m0_m1_"):
+            sh.update({m + "cv1": (h, h, 3, 3), m + "cv2": (h, h, 3, 3)})
+    else:
+        sh.update({"m0_cv1": (c // 2, c, 3, 3), "m0_cv2": (c, c // 2, 3, 3)})
+    return sh
+
+
+def conv_fixtures(fx):
+    from oracle import conv_oracle as co
+    out, worst = {}, 0.0
+    d = os.path.join(fx, "conv_yolo26")
+    stem = dict(x=rd(d, "x.bin", (2, 3, 16, 16)), conv_w=rd(d, "conv_weight.bin", (16, 3, 3, 3)),
+                bn_w=rd(d, "bn_weight.bin"), bn_b=rd(d, "bn_bias.bin"), bn_rm=rd(d, "bn_running_mean.bin"),
+                bn_rv=rd(d, "bn_running_var.bin"), expected_output=rd(d, "expected_output.bin", (2, 16, 8, 8)))
+    y = co.conv_block_train(stem["x"], (stem["conv_w"], stem["bn_w"], stem["bn_b"]), stride=2)
+    worst = max(worst, float(np.abs(y - stem["expected_output"]).max()))
+    out.update({f"stem/{k}": v for k, v in stem.items()})
+    for name, (sub, c_in, c_out, c3k, sc, e) in C3K2_VARIANTS.items():
+        d = os.path.join(fx, "c3k2_yolo26", sub)
+        prm = {}
+        for st, shape in c3k2_stage_shapes(c_in, c_out, c3k, e).items():
+            prm[st] = (rd(d, f"{st}_conv_w.bin", shape),) + tuple(rd(d, f"{st}_bn_{p}.bin") for p in ("w", "b", "rm", "rv"))
+            for p, a in zip(("conv_w", "bn_w", "bn_b", "bn_rm", "bn_rv"), prm[st]):
+                out[f"{name}/{st}_{p}"] = a
+        x = rd(d, "x.bin", (2, c_in, 4, 4))
+        ref = rd(d, "expected_output.bin", (2, c_out, 4, 4))
+        out[f"{name}/x"], out[f"{name}/expected_output"] = x, ref
+        worst = max(worst, float(np.abs(co.c3k2(x, prm, c3k, sc) - ref).max()))
+    assert worst < 1e-5, f"conv oracle does not reproduce the conv/C3k2 fixtures (max-abs {worst})"
+    np.savez_compressed(os.path.join(HERE, "conv_c3k2.npz"), **out)
+    return worst
 
 
 def main(ref_root):
@@ -105,6 +156,7 @@ def main(ref_root):
                         w_qkv=f32(wq), b_qkv=f32(bq), w_pe=f32(wpe), b_pe=f32(bpe),
                         w_proj=f32(wpr), b_proj=f32(bpr), y=f32(attn_out))
     print("golden fixtures written; oracle vs expected_output max-abs", err)
+    print("conv / C3k2 fixtures: oracle max-abs", conv_fixtures(fx))
 
 
 if __name__ == "__main__":

@@ -104,6 +104,15 @@ def test_argument_validation_fails_before_launch():
     assert lib.va_psa_dp_allreduce_sgd(None, *([None] * 2), 0.1, *([None] * 6), None) == 1
     assert lib.va_dp_comm_disconnect(None) == 1
     assert lib.va_dp_comm_destroy(None) == 0
+    # conv: channel counts, kernel size, stride and alignment are checked before any CUDA call
+    conv = lambda x, B, H, W, ci, co, k, s: lib.va_conv_nhwc_bf16(x, 4096, 8192, 12288, B, H, W, ci, co, k, s, 1, None)
+    assert conv(1024, 1, 8, 8, 12, 16, 3, 1) == 1 and b"Cin" in lib.va_get_last_error_string()
+    assert conv(1024, 1, 8, 8, 16, 20, 3, 1) == 1 and b"Cout" in lib.va_get_last_error_string()
+    assert conv(1024, 1, 8, 8, 16, 16, 5, 1) == 1 and b"kernel size" in lib.va_get_last_error_string()
+    assert conv(1024, 1, 8, 8, 16, 16, 3, 3) == 1 and b"stride" in lib.va_get_last_error_string()
+    assert conv(1024, 1, 0, 8, 16, 16, 3, 1) == 1
+    assert conv(None, 1, 8, 8, 16, 16, 3, 1) == 1
+    assert conv(1026, 1, 8, 8, 16, 16, 3, 1) == 4 and b"alignment" in lib.va_get_last_error_string()
 
 
 def test_workspace_query():

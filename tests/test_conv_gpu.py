@@ -1,0 +1,160 @@
+"""Convolution + folded BN (+ SiLU), NHWC bf16 (va_conv_nhwc_bf16), on the GPU
+through the C ABI.
+
+References: the float64 conv oracle (``oracle/conv_oracle.py``, pinned on the
+CPU to the reference's stem and C3k2 fixtures) on the same bf16-rounded
+inputs and weights, and the fixtures' own expected outputs.
+
+Tolerances.  One conv against the oracle on identical bf16 inputs differs
+only by f32 accumulation order and the single bf16 output rounding: rel-L2
+≤ 2e-3 (the north star's bf16 bound) and max-abs ≤ 1e-2 · max(1, max |y|).
+A C3k2 block chains five to eleven convs, each output rounded to bf16;
+emulating exactly those roundings on the CPU gives 3.7-4.0e-3 rel-L2 against
+the fixtures' f32 outputs, so the block is held to 8e-3 against the fixture
+and to 2e-3 against the emulated chain.  The stem fixture (training-mode BN
+applied on the host to the conv output) emulates to 3.1e-3: ≤ 6e-3."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import BF16_MAX_ABS, BF16_REL_L2, load_golden, max_abs, rel_l2
+from oracle import conv_oracle as co
+from vision_rs_b200 import _lib, conv
+
+pytestmark = pytest.mark.gpu
+
+C3K2_VS_FIXTURE_REL_L2 = 8e-3
+STEM_VS_FIXTURE_REL_L2 = 6e-3
+
+
+def _bf(a):
+    return torch.as_tensor(np.asarray(a, np.float32)).bfloat16().double().numpy()
+
+
+def _nhwc(a):
+    """NCHW host array → NHWC bf16 device tensor."""
+    return torch.as_tensor(np.asarray(a, np.float32)).permute(0, 2, 3, 1).contiguous().to("cuda", torch.bfloat16)
+
+
+def _nchw(t):
+    return t.float().permute(0, 3, 1, 2).cpu().double().numpy()
+
+
+def _run(x, w, b, stride, act):
+    op = conv.ConvBnAct(w, b, stride, act)
+    return _nchw(op(_nhwc(x)))
+
+
+CASES = [  # B, Cin, H, W, Cout, k, s, act
+    (2, 16, 16, 16, 16, 3, 1, True),
+    (2, 32, 20, 20, 64, 3, 2, True),      # ragged output tile (Wo = 10)
+    (1, 64, 40, 40, 128, 1, 1, False),
+    (3, 8, 9, 13, 8, 3, 1, True),         # Cin = Cout = 8 (the C3k2 bottleneck of YOLO26n)
+    (2, 24, 11, 7, 40, 3, 2, True),       # Cin % 16 == 8, Cout % 16 == 8, odd sizes
+    (1, 128, 20, 20, 256, 3, 2, True),
+    (2, 256, 20, 20, 256, 1, 1, True),
+    (2, 48, 6, 6, 32, 1, 2, False),       # 1×1 with stride 2
+    (1, 96, 33, 17, 192, 3, 1, True),     # KB = 32, BN = 64
+    (1, 64, 80, 80, 64, 3, 1, True),      # several tiles in both directions
+]
+
+
+@pytest.mark.parametrize("B,Cin,H,W,Cout,k,s,act", CASES)
+def test_conv_vs_oracle(cuda, B, Cin, H, W, Cout, k, s, act):
+    x, w, b = co.conv_synthetic(B, Cin, H, W, Cout, k, seed=Cin + Cout + H)
+    x, w = _bf(x), _bf(w)
+    y = _run(x, w, b, s, act)
+    ref = co.conv2d(x, w, s, np.asarray(b, np.float32))
+    ref = co.silu(ref) if act else ref
+    assert y.shape == ref.shape
+    assert rel_l2(y, ref) < BF16_REL_L2
+    assert max_abs(y, ref) < BF16_MAX_ABS * max(1.0, float(np.abs(ref).max()))
+
+
+def test_weight_permutation_is_exact(cuda):
+    w = torch.randn(40, 24, 3, 3).to("cuda", torch.bfloat16)
+    assert torch.equal(conv.weight_ohwi(w), w.permute(0, 2, 3, 1).contiguous())
+
+
+def test_stem_fixture(cuda):
+    """The reference's YOLO26n stem, Conv(3→16, k3, s2) with training-mode BN:
+    the input is padded to 8 channels (zero weights there), the conv runs on
+    the GPU without bias or SiLU, and BN (batch statistics) + SiLU follow on
+    the host."""
+    g = load_golden("conv_c3k2.npz")
+    x = np.zeros((2, 8, 16, 16))
+    x[:, :3] = g["stem/x"]
+    w = np.zeros((16, 8, 3, 3))
+    w[:, :3] = g["stem/conv_w"]
+    y = _run(_bf(x), _bf(w), np.zeros(16), 2, False)
+    mu, var = y.mean(axis=(0, 2, 3), keepdims=True), y.var(axis=(0, 2, 3), keepdims=True)
+    y = (y - mu) / np.sqrt(var + 1e-5) * g["stem/bn_w"][None, :, None, None] + g["stem/bn_b"][None, :, None, None]
+    assert rel_l2(co.silu(y), g["stem/expected_output"]) < STEM_VS_FIXTURE_REL_L2
+
+
+def _prm(g, v):
+    stages = sorted({k[len(v) + 1:-len("_conv_w")] for k in g if k.startswith(v + "/") and k.endswith("_conv_w")})
+    return {s: tuple(g[f"{v}/{s}_{p}"] for p in ("conv_w", "bn_w", "bn_b", "bn_rm", "bn_rv")) for s in stages}
+
+
+class _Chain:
+    """C3k2 (c3k2.rs:94-127) composed from conv ops; the chunk, cat and
+    residual add are torch glue on the device (bf16), ``emulate`` runs the
+    same chain on the CPU with the same bf16 roundings."""
+
+    def __init__(self, prm, emulate=False):
+        self.prm, self.emulate = prm, emulate
+
+    def cb(self, x, st):
+        w, b = co.fold_bn(*self.prm[st], 1e-5)
+        if self.emulate:
+            return _bf(co.silu(co.conv2d(x, _bf(w), 1, np.asarray(b, np.float32))))
+        return conv.ConvBnAct(w, b, 1, True)(x)
+
+    def cat(self, parts):
+        return np.concatenate(parts, 1) if self.emulate else torch.cat(parts, 3)
+
+    def chunk(self, h):
+        if self.emulate:
+            c = h.shape[1] // 2
+            return h[:, :c], h[:, c:]
+        c = h.shape[3] // 2
+        return h[..., :c].contiguous(), h[..., c:].contiguous()
+
+    def add(self, a, b):
+        return _bf(a + b) if self.emulate else a + b
+
+    def bneck(self, x, pre, sc):
+        y = self.cb(self.cb(x, pre + "cv1"), pre + "cv2")
+        return self.add(x, y) if sc else y
+
+    def __call__(self, x, c3k, sc):
+        y0, y1 = self.chunk(self.cb(x, "cv1"))
+        if c3k:
+            a = self.bneck(self.bneck(self.cb(y1, "m0_icv1"), "m0_m0_", sc), "m0_m1_", sc)
+            last = self.cb(self.cat([a, self.cb(y1, "m0_icv2")]), "m0_icv3")
+        else:
+            last = self.bneck(y1, "m0_", sc)
+        return self.cb(self.cat([y0, y1, last]), "cv2")
+
+
+@pytest.mark.parametrize("variant,c3k,sc", [("shallow_sf", False, False), ("shallow_st", False, True),
+                                            ("deep_st", True, True)])
+def test_c3k2_fixture(cuda, variant, c3k, sc):
+    """The reference's eval-mode C3k2 fixtures (convs of 8 to 128 channels,
+    1×1 and 3×3), every conv through va_conv_nhwc_bf16."""
+    g = load_golden("conv_c3k2.npz")
+    prm = _prm(g, variant)
+    x = _bf(g[f"{variant}/x"])
+    y = _nchw(_Chain(prm)(_nhwc(x), c3k, sc))
+    emu = _Chain(prm, emulate=True)(x, c3k, sc)
+    assert rel_l2(y, emu) < BF16_REL_L2
+    assert rel_l2(y, g[f"{variant}/expected_output"]) < C3K2_VS_FIXTURE_REL_L2
+
+
+def test_device_status_clean_after_convs(cuda):
+    """Every pipeline wait of the conv kernels finished in time."""
+    st = ctypes.c_int(-1)
+    assert _lib.lib().va_device_status_read(ctypes.byref(st), None) == 0 and st.value == 0

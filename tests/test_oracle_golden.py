@@ -2,11 +2,14 @@
 
 Pins ``oracle/psa_oracle.py`` before it is trusted as the parity checker:
 the reference's ultralytics/PyTorch-generated fixtures for the PSA block
-(tests/fixtures/c2psa_yolo26 of the reference crate) and the PE-shaped
-depthwise conv (tests/fixtures/conv_grouped/depthwise)."""
+(tests/fixtures/c2psa_yolo26 of the reference crate), the PE-shaped
+depthwise conv (tests/fixtures/conv_grouped/depthwise), and
+``oracle/conv_oracle.py`` on the YOLO26n stem conv (tests/fixtures/conv_yolo26)
+and three eval-mode C3k2 blocks (tests/fixtures/c3k2_yolo26)."""
 import numpy as np
 
 from conftest import folded_c2psa, load_golden, max_abs, stage_params
+from oracle import conv_oracle as co
 from oracle import psa_oracle as po
 
 SCALE = 1.0 / np.sqrt(np.float32(32))
@@ -104,3 +107,33 @@ def test_torch_cpu_baseline_matches_oracle():
     y = po.psa_attention_torch(t["x"], t["w_qkv"], t["b_qkv"], t["w_pe"], t["b_pe"], t["w_proj"], t["b_proj"], 2, 32)
     ref = po.psa_attention(p["x"], p["w_qkv"], p["b_qkv"], p["w_pe"], p["b_pe"], p["w_proj"], p["b_proj"], 2, 32)
     assert max_abs(y.numpy(), ref) < 1e-5
+
+
+def _conv_prm(g, v):
+    stages = {k[len(v) + 1:-len("_conv_w")] for k in g if k.startswith(v + "/") and k.endswith("_conv_w")}
+    return {s: tuple(g[f"{v}/{s}_{p}"] for p in ("conv_w", "bn_w", "bn_b", "bn_rm", "bn_rv")) for s in stages}
+
+
+def test_stem_conv_fixture():
+    """Conv(3→16, k3, s2) + training-mode BN + SiLU (conv_yolo26/generate.py)."""
+    g = load_golden("conv_c3k2.npz")
+    y = co.conv_block_train(g["stem/x"], (g["stem/conv_w"], g["stem/bn_w"], g["stem/bn_b"]), stride=2)
+    assert max_abs(y, g["stem/expected_output"]) < 1e-5
+
+
+def test_c3k2_fixtures():
+    """C3k2 without / with shortcut and the C3k inner variant (c3k2.rs:46-127)."""
+    g = load_golden("conv_c3k2.npz")
+    for v, c3k, sc in (("shallow_sf", False, False), ("shallow_st", False, True), ("deep_st", True, True)):
+        y = co.c3k2(g[f"{v}/x"], _conv_prm(g, v), c3k, sc)
+        assert max_abs(y, g[f"{v}/expected_output"]) < 1e-5, v
+
+
+def test_conv2d_matches_torch():
+    """The conv restatement against torch's CPU conv2d (f64) for every kernel
+    size and stride the GPU op takes."""
+    import torch
+    for k, s in ((1, 1), (1, 2), (3, 1), (3, 2)):
+        x, w, b = co.conv_synthetic(2, 8, 9, 7, 16, k, seed=k + s)
+        ref = torch.nn.functional.conv2d(torch.tensor(x), torch.tensor(w), torch.tensor(b), stride=s, padding=k // 2)
+        assert max_abs(co.conv2d(x, w, s, b), ref.numpy()) < 1e-12

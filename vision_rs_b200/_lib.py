@@ -72,6 +72,8 @@ SIGNATURES: dict[str, tuple] = {
     "va_psa_block_fwd_bf16": (I, [P, P, P, I, I, I, I, P, SZ, S]),
     "va_c2psa_workspace_bytes": (SZ, [I, I, I, I, I]),
     "va_c2psa_fwd_bf16": (I, [P, P, P, I, P, P, P, P, I, I, I, I, P, SZ, S]),
+    "va_conv_nhwc_bf16": (I, [P, P, P, P, I, I, I, I, I, I, I, I, S]),
+    "va_conv_weight_ohwi_bf16": (I, [P, P, I, I, I, S]),
     "va_safetensors_open": (I, [C.c_char_p, C.POINTER(P)]),
     "va_safetensors_close": (None, [P]),
     "va_safetensors_tensor_info": (I, [P, C.c_char_p, C.POINTER(C.c_int), I64P, C.POINTER(C.c_int)]),

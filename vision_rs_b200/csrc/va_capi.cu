@@ -121,12 +121,14 @@ int va_psa_flash_attention_fwd_f16(const void* qk, const void* v, void* o, float
 
 int va_device_status_read(int* status, va_stream_t s) {  // first non-zero word of the tensor-core kernels
   if (!status) return set_error(VA_ERR_SHAPE, "device_status_read: null output");
-  int v[4] = {0, 0, 0, 0};
+  int v[5] = {0, 0, 0, 0, 0};
   if (int rc = tc_status_read(&v[0], (cudaStream_t)s)) return rc;
   if (int rc = dino_status_read(&v[1], (cudaStream_t)s)) return rc;
   if (int rc = gemm_status_read(&v[2], (cudaStream_t)s)) return rc;
   if (int rc = bwd_status_read(&v[3], (cudaStream_t)s)) return rc;
-  *status = v[0] ? v[0] : (v[1] ? v[1] : (v[2] ? v[2] : v[3]));
+  if (int rc = conv_status_read(&v[4], (cudaStream_t)s)) return rc;
+  *status = 0;
+  for (int i = 0; i < 5 && !*status; ++i) *status = v[i];
   return VA_OK;
 }
 
@@ -134,6 +136,7 @@ int va_device_status_clear(va_stream_t s) {
   if (int rc = tc_status_clear((cudaStream_t)s)) return rc;
   if (int rc = dino_status_clear((cudaStream_t)s)) return rc;
   if (int rc = gemm_status_clear((cudaStream_t)s)) return rc;
+  if (int rc = conv_status_clear((cudaStream_t)s)) return rc;
   return bwd_status_clear((cudaStream_t)s);
 }
 

@@ -88,6 +88,9 @@ int psa_attn_bwd_tc(const void* qk, const void* v, const void* o, const void* d_
 int bwd_status_read(int* out, cudaStream_t st);
 int bwd_status_clear(cudaStream_t st);
 int gemm_status_clear(cudaStream_t st);
+// Status word of the implicit-GEMM convolution kernel (va_conv_nhwc.cu).
+int conv_status_read(int* out, cudaStream_t st);
+int conv_status_clear(cudaStream_t st);
 // Tensor-core forward: any C = 64·nh with key dim 32 (the c2psa widths);
 // the C = 128 kernels of the training step: psa_tc_is_n.
 bool psa_tc_supported(int C, int nh, int kd);
