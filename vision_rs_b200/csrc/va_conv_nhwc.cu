@@ -47,13 +47,16 @@ __device__ int g_conv_status;
 
 namespace {
 
-constexpr int kCvM = 128, kCvTW = 16, kCvTH = 8, kCvStages = 4, kCvThreads = 128;
+constexpr int kCvM = 128, kCvTW = 16, kCvTH = 8, kCvMaxStages = 8;
+constexpr int kCvEpiWarps = 8, kCvThreads = 64 + 32 * kCvEpiWarps;  // producer, MMA, 8 epilogue warps
+constexpr int kCvAcc = 4;  // TMEM accumulator buffers (4 × BN ≤ 512 columns)
 
-template <int KB, int BN>
-struct ConvSmem {
-  uint8_t a[kCvStages][kCvM * KB * 2];  // im2col tile: 128 pixel rows × KB channels, K-major, swizzled
-  uint8_t b[kCvStages][BN * KB * 2];    // weight tile: BN rows × KB, K-major, swizzled
-  uint64_t full[kCvStages], empty[kCvStages], done;
+// Barriers and bookkeeping behind the operand ring in dynamic shared memory.
+struct ConvCtl {
+  uint64_t full[kCvMaxStages], empty[kCvMaxStages];  // operand ring
+  uint64_t acc_full[kCvAcc], acc_empty[kCvAcc];      // rotating TMEM accumulators
+  uint64_t wfull;                                    // resident weights landed
+  uint64_t done;
   uint32_t tmem_base;
   int abort;
 };
@@ -73,110 +76,243 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
+// Geometry of one launch.  linear: a 1×1 stride-1 conv is a plain GEMM over
+// the B·H·W pixels, so a tile is 128 consecutive pixels (x is then a 2-D map
+// [pixels][Cin]); otherwise a tile is 8 output rows × 16 output columns of
+// one image (x a 4-D map, the im2col done by the load's coordinates).
+struct ConvGeom {
+  int Ho, Wo, Cin, Cout, ksize, stride, act, linear;
+  int tiles_w, tiles_h, n_tiles, total_tiles, stages;
+  int wres;          // the CTA's whole weight slice [BN][k·k·Cin] stays in shared memory
+  long long pixels;  // B·Ho·Wo
+};
+
+// Columns one epilogue warp drains (two warps share a TMEM lane quarter when BN ≥ 32).
+template <int BN>
+struct ConvCols {
+  static constexpr int half = BN >= 32 ? BN / 2 : BN;
+};
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* m, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
+// Tile t → (image, first output row, first output column or first pixel, first channel).
+__device__ __forceinline__ void conv_tile(const ConvGeom& g, int t, int bn, int& b, int& oy0, int& ox0, long long& m0,
+                                          int& n0) {
+  n0 = (t % g.n_tiles) * bn;
+  int r = t / g.n_tiles;
+  if (g.linear) {
+    m0 = (long long)r * kCvM;
+    b = oy0 = ox0 = 0;
+    return;
+  }
+  ox0 = (r % g.tiles_w) * kCvTW;
+  r /= g.tiles_w;
+  oy0 = (r % g.tiles_h) * kCvTH;
+  b = r / g.tiles_h;
+  m0 = 0;
+}
+
+// Persistent, warp-specialised: warp 0 streams operands through the ring with
+// TMA, warp 1 issues the MMAs into one of four rotating TMEM accumulators,
+// warps 2-9 drain finished accumulators (bias, SiLU, bf16, NHWC stores), so
+// the epilogues of earlier tiles overlap the main loop of later ones.  One
+// CTA per SM (the launch asks for more than half the shared memory).
+// When the CTA's weight slice fits (wres), it is loaded once and only the
+// activation tiles stream through the ring; the grid is then a multiple of
+// the channel-tile count, so a CTA keeps one channel tile for all its tiles.
 template <int KB, int BN>
 __global__ void __launch_bounds__(kCvThreads, 1)
 conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                 const float* __restrict__ bias, __nv_bfloat16* __restrict__ y, int Ho, int Wo, int Cin, int Cout,
-                 int ksize, int stride, int act, int tiles_w) {
+                 const __grid_constant__ CUtensorMap map_y, const float* __restrict__ bias, const ConvGeom g) {
   extern __shared__ uint8_t smem_raw[];
-  using Sm = ConvSmem<KB, BN>;
-  Sm& sm = *reinterpret_cast<Sm*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  constexpr int kABytes = kCvM * KB * 2, kBBytes = BN * KB * 2;
+  constexpr int kHalfCols = ConvCols<BN>::half, kRowBytes = 2 * kHalfCols;
+  constexpr uint32_t kTmemCols = kCvAcc * BN < 32 ? 32 : kCvAcc * BN;
+  // [staging: 8 warps × 2 × 32 rows × kRowBytes][A ring][B ring or resident slice][barriers]
+  uint8_t* stg = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = stg + kCvEpiWarps * 2 * 32 * kRowBytes;
+  uint8_t* sb = sa + g.stages * kABytes;  // weight ring, or the resident slice
+  const int pad = g.ksize / 2, cblocks = (g.Cin + KB - 1) / KB, nk = g.ksize * g.ksize * cblocks;
+  ConvCtl& c = *reinterpret_cast<ConvCtl*>(sb + (g.wres ? nk : g.stages) * kBBytes);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int ox0 = (blockIdx.x % tiles_w) * kCvTW, oy0 = (blockIdx.x / tiles_w) * kCvTH;
-  const int n0 = blockIdx.y * BN, b = blockIdx.z;
-  const int pad = ksize / 2, cblocks = (Cin + KB - 1) / KB, nk = ksize * ksize * cblocks;
+  const int S = g.stages;
 
   if (tid == 0) {
-    for (int i = 0; i < kCvStages; ++i) {
-      mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], 1);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&c.full[i], 1);
+      mbar_init(&c.empty[i], 1);
     }
-    mbar_init(&sm.done, 1);
-    sm.abort = 0;
+    for (int i = 0; i < kCvAcc; ++i) {
+      mbar_init(&c.acc_full[i], 1);
+      mbar_init(&c.acc_empty[i], kCvEpiWarps);
+    }
+    mbar_init(&c.done, 1);
+    mbar_init(&c.wfull, 1);
+    c.abort = 0;
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(&sm.tmem_base, kTmemCols);
+    tmem_alloc(&c.tmem_base, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = sm.tmem_base;
+  const uint32_t tmem = c.tmem_base;
 
-  if (warp == 0 && lane == 0) {  // ── TMA producer ──
-    tma_prefetch_desc(&map_x);
-    tma_prefetch_desc(&map_w);
-    int issued = 0;
-    bool ok = true;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int st = kb % kCvStages;
-      if (kb >= kCvStages &&
-          !(ok = mbar_wait(&sm.empty[st], ((kb / kCvStages) - 1) & 1, &sm.abort, &g_conv_status, 1)))
-        break;
-      const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * KB, ky = tap / ksize, kx = tap - ky * ksize;
-      mbar_arrive_expect_tx(&sm.full[st], (kCvM + BN) * KB * 2);
-      tma_load_4d(sm.a[st], &map_x, &sm.full[st], c0, stride * ox0 + kx - pad, stride * oy0 + ky - pad, b);
-      tma_load_2d(sm.b[st], &map_w, &sm.full[st], tap * Cin + c0, n0);
-      ++issued;
-    }
-    if (!ok) {  // every load issued here lands (bounded) before the CTA can exit
-      for (int kb = max(0, issued - kCvStages); kb < issued; ++kb) {
-        const long long t0 = clock64();
-        while (!mbar_try_wait(&sm.full[kb % kCvStages], (kb / kCvStages) & 1) && clock64() - t0 < kSpinCycles) {
+  if (warp == 0) {  // ── TMA producer ──
+    if (lane == 0) {
+      tma_prefetch_desc(&map_x);
+      tma_prefetch_desc(&map_w);
+      tma_prefetch_desc(&map_y);
+      long long q = 0;  // operand ring slot counter across tiles
+      bool ok = true;
+      if (g.wres && (int)blockIdx.x < g.total_tiles) {
+        const int n0 = ((int)blockIdx.x % g.n_tiles) * BN;
+        mbar_arrive_expect_tx(&c.wfull, nk * kBBytes);
+        for (int kb = 0; kb < nk; ++kb) {
+          const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * KB;
+          tma_load_2d(sb + kb * kBBytes, &map_w, &c.wfull, tap * g.Cin + c0, n0);
+        }
+      }
+      for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x) {
+        int b, oy0, ox0, n0;
+        long long m0;
+        conv_tile(g, t, BN, b, oy0, ox0, m0, n0);
+        for (int kb = 0; kb < nk; ++kb, ++q) {
+          const int st = (int)(q % S);
+          const long long round = q / S;
+          if (round > 0 && !(ok = mbar_wait(&c.empty[st], (uint32_t)((round - 1) & 1), &c.abort, &g_conv_status, 1)))
+            break;
+          const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * KB, ky = tap / g.ksize, kx = tap - ky * g.ksize;
+          mbar_arrive_expect_tx(&c.full[st], g.wres ? kABytes : kABytes + kBBytes);
+          if (g.linear)
+            tma_load_2d(sa + st * kABytes, &map_x, &c.full[st], c0, (int)m0);
+          else
+            tma_load_4d(sa + st * kABytes, &map_x, &c.full[st], c0, g.stride * ox0 + kx - pad,
+                        g.stride * oy0 + ky - pad, b);
+          if (!g.wres) tma_load_2d(sb + st * kBBytes, &map_w, &c.full[st], tap * g.Cin + c0, n0);
+        }
+      }
+      if (!ok) {  // every load issued here lands (bounded) before the CTA can exit
+        for (long long k = q - S < 0 ? 0 : q - S; k < q; ++k) {
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&c.full[k % S], (uint32_t)((k / S) & 1)) && clock64() - t0 < kSpinCycles) {
+          }
+        }
+        if (g.wres) {
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&c.wfull, 0) && clock64() - t0 < kSpinCycles) {
+          }
         }
       }
     }
-  } else if (warp == 1 && lane == 0) {  // ── MMA issuer ──
-    constexpr uint32_t idesc = idesc_f32acc(kCvM, BN, AB_BF16, false, false);
-    const uint64_t da0 = sdesc(smem_u32(sm.a[0]), 16, KbTraits<KB>::sbo, KbTraits<KB>::swz);
-    const uint64_t db0 = sdesc(smem_u32(sm.b[0]), 16, KbTraits<KB>::sbo, KbTraits<KB>::swz);
-    constexpr uint32_t kAStage = (kCvM * KB * 2) >> 4, kBStage = (BN * KB * 2) >> 4;
-    bool ok = true;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int st = kb % kCvStages;
-      if (!(ok = mbar_wait(&sm.full[st], (kb / kCvStages) & 1, &sm.abort, &g_conv_status, 2))) break;
+  } else if (warp == 1) {  // ── MMA issuer ──
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f32acc(kCvM, BN, AB_BF16, false, false);
+      const uint64_t da0 = sdesc(smem_u32(sa), 16, KbTraits<KB>::sbo, KbTraits<KB>::swz);
+      const uint64_t db0 = sdesc(smem_u32(sb), 16, KbTraits<KB>::sbo, KbTraits<KB>::swz);
+      long long q = 0;
+      bool ok = true;
+      if (g.wres && (int)blockIdx.x < g.total_tiles)
+        ok = mbar_wait(&c.wfull, 0, &c.abort, &g_conv_status, 5);
+      int i = 0;
+      for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x, ++i) {
+        const int buf = i % kCvAcc, use = i / kCvAcc;
+        if (use > 0 && !(ok = mbar_wait(&c.acc_empty[buf], (uint32_t)((use - 1) & 1), &c.abort, &g_conv_status, 2)))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < nk; ++kb, ++q) {
+          const int st = (int)(q % S);
+          if (!(ok = mbar_wait(&c.full[st], (uint32_t)((q / S) & 1), &c.abort, &g_conv_status, 3))) break;
+          tc_fence_after();
+          const uint64_t da = da0 + (uint64_t)((st * kABytes) >> 4);
+          const uint64_t db = db0 + (uint64_t)(((g.wres ? kb : st) * kBBytes) >> 4);
+#pragma unroll
+          for (int s = 0; s < KB / 16; ++s)  // +32 bytes per 16-channel k-step inside the swizzle atom
+            mma_ss(d, da + 2 * s, db + 2 * s, idesc, (kb > 0 || s > 0) ? 1u : 0u);
+          mma_commit(&c.empty[st]);
+        }
+        if (ok) mma_commit(&c.acc_full[buf]);
+      }
+      // Nothing issued here may still be writing TMEM when it is freed.
+      mma_commit(&c.done);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(&c.done, 0) && clock64() - t0 < kSpinCycles) {
+      }
+    }
+  } else {  // ── epilogue: warp (2..9) → TMEM lane quarter warp % 4, column half (warp − 2) / 4 ──
+    const int quarter = warp & 3, half = (warp - 2) >> 2, ew = warp - 2;
+    const bool active = BN >= 32 || half == 0;
+    const int cbase = BN >= 32 ? half * kHalfCols : 0;
+    // Swizzled row of this lane in the staging tile: 16-byte chunk j lands at
+    // chunk j ^ sw, the pattern TMA applies for a kRowBytes-wide swizzle.
+    const int sw = ((lane * kRowBytes) >> 7) & (kRowBytes / 16 - 1);
+    int i = 0;
+    for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++i) {
+      const int buf = i % kCvAcc, use = i / kCvAcc;
+      const bool got = mbar_wait(&c.acc_full[buf], (uint32_t)(use & 1), &c.abort, &g_conv_status, 4);
+      if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform: the TMEM loads below are warp-collective
       tc_fence_after();
-      const uint64_t da = da0 + (uint64_t)(st * kAStage), db = db0 + (uint64_t)(st * kBStage);
+      int b, oy0, ox0, n0;
+      long long m0;
+      conv_tile(g, t, BN, b, oy0, ox0, m0, n0);
+      uint32_t u[kHalfCols];
+      float bv[kHalfCols];
+      if (active) {
+        // Bias first (its loads overlap the TMEM reads), then the TMEM loads and one wait.
+        const int nv = g.Cout - n0 - cbase;
 #pragma unroll
-      for (int s = 0; s < KB / 16; ++s)  // +32 bytes per 16-channel k-step inside the swizzle atom
-        mma_ss(tmem, da + 2 * s, db + 2 * s, idesc, (kb > 0 || s > 0) ? 1u : 0u);
-      mma_commit(&sm.empty[st]);
-    }
-    mma_commit(&sm.done);
-  }
-  __syncwarp();
-  // ── epilogue: thread = pixel row (TMEM lane) ──
-  const bool ok = mbar_wait(&sm.done, 0, &sm.abort, &g_conv_status, 3) && !sm.abort;
-  tc_fence_after();
-  if (ok) {
-    const int r = warp * 32 + lane, oy = oy0 + r / kCvTW, ox = ox0 + r % kCvTW;
-    const bool live = oy < Ho && ox < Wo;
-    __nv_bfloat16* dst = y + (((size_t)b * Ho + (live ? oy : 0)) * Wo + (live ? ox : 0)) * Cout + n0;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      uint32_t u[16];
-      tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c, u);
-      tmem_ld_wait();
-      reg_fence(u);
-      const int nv = min(16, Cout - n0 - c);  // 16 or 8 (Cout % 8 == 0), ≤ 0 past Cout
-      float v[16];
+        for (int k = 0; k < kHalfCols; ++k) bv[k] = k < nv ? __ldg(bias + n0 + cbase + k) : 0.0f;
+        const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + cbase);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        v[i] = __uint_as_float(u[i]) + (i < nv ? bias[n0 + c + i] : 0.0f);
-        if (act) v[i] = v[i] / (1.0f + __expf(-v[i]));
+        for (int cc = 0; cc < kHalfCols; cc += 16) tmem_ld16(ta + cc, *reinterpret_cast<uint32_t(*)[16]>(u + cc));
+        tmem_ld_wait();
+        reg_fence(u);
       }
-      if (live && nv > 0) {
-        uint4* d = reinterpret_cast<uint4*>(dst + c);
-        d[0] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                          pack_bf16x2(v[6], v[7]));
-        if (nv > 8)
-          d[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]), pack_bf16x2(v[12], v[13]),
-                            pack_bf16x2(v[14], v[15]));
+      // The accumulator is in registers: hand it back to the MMA warp now.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c.acc_empty[buf]);
+      if (active) {
+        uint8_t* stage = stg + (ew * 2 + (i & 1)) * (32 * kRowBytes);
+        if (lane == 0) tma_store_wait_read_1();  // this staging buffer's previous store has read it
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < kRowBytes / 16; ++j) {
+          uint32_t q4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int k = 8 * j + 2 * e;
+            float v0 = __uint_as_float(u[k]) + bv[k], v1 = __uint_as_float(u[k + 1]) + bv[k + 1];
+            if (g.act) {  // SiLU; → −0 once exp overflows
+              v0 = __fdividef(v0, 1.0f + __expf(-v0));
+              v1 = __fdividef(v1, 1.0f + __expf(-v1));
+            }
+            q4[e] = pack_bf16x2(v0, v1);
+          }
+          *reinterpret_cast<uint4*>(stage + lane * kRowBytes + ((j ^ sw) << 4)) = make_uint4(q4[0], q4[1], q4[2], q4[3]);
+        }
+        fence_proxy_async_smem();  // the staging writes become visible to the TMA store
+        __syncwarp();
+        if (lane == 0) {  // 32 rows × kHalfCols channels; TMA drops what lies outside y
+          if (g.linear)
+            tma_store_2d(&map_y, stage, n0 + cbase, (int)(m0 + quarter * 32));
+          else
+            tma_store_4d(&map_y, stage, n0 + cbase, ox0, oy0 + 2 * quarter, b);
+          tma_store_commit();
+        }
       }
     }
+    if (lane == 0) tma_store_wait_all();
   }
+  __syncwarp();  // lanes 1-31 of the producer and MMA warps rejoin lane 0
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, kTmemCols);
@@ -216,10 +352,21 @@ CUtensorMapSwizzle tma_swizzle(int kb) {
 namespace va {
 namespace {
 
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev < 64 && cached[dev]) return cached[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
 int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias, __nv_bfloat16* y, int B, int H, int W,
               int Cin, int Cout, int k, int s, int act, cudaStream_t st) {
   VA_CHECK_ARG(x && w && bias && y, "conv nhwc: null pointer");
-  VA_CHECK_ARG(B > 0 && H > 0 && W > 0 && B <= 65535, "conv nhwc: bad sizes");
+  VA_CHECK_ARG(B > 0 && H > 0 && W > 0, "conv nhwc: bad sizes");
   VA_CHECK_ARG(k == 1 || k == 3, "conv nhwc: kernel size %d (1 or 3)", k);
   VA_CHECK_ARG(s == 1 || s == 2, "conv nhwc: stride %d (1 or 2)", s);
   VA_CHECK_ARG(Cin > 0 && Cin % 8 == 0, "conv nhwc: Cin=%d must be a multiple of 8", Cin);
@@ -229,41 +376,88 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
   const int pad = k / 2, Ho = (H + 2 * pad - k) / s + 1, Wo = (W + 2 * pad - k) / s + 1;
   const int KB = Cin % 64 == 0 ? 64 : Cin % 32 == 0 ? 32 : 16;
   const int BN = Cout % 128 == 0 ? 128 : Cout % 64 == 0 ? 64 : Cout % 32 == 0 ? 32 : 16;
+  ConvGeom g{};
+  g.Ho = Ho, g.Wo = Wo, g.Cin = Cin, g.Cout = Cout, g.ksize = k, g.stride = s, g.act = act ? 1 : 0;
+  g.linear = (k == 1 && s == 1) ? 1 : 0;
+  g.pixels = (long long)B * Ho * Wo;
+  g.n_tiles = (Cout + BN - 1) / BN;
+  g.tiles_w = (Wo + kCvTW - 1) / kCvTW;
+  g.tiles_h = (Ho + kCvTH - 1) / kCvTH;
+  const long long tiles = g.linear ? (g.pixels + kCvM - 1) / kCvM * g.n_tiles
+                                   : (long long)g.tiles_w * g.tiles_h * B * g.n_tiles;
+  VA_CHECK_ARG(g.pixels < (1LL << 31) && tiles < (1LL << 31), "conv nhwc: %lld output pixels is too many", g.pixels);
+  g.total_tiles = (int)tiles;
+  const int nk = k * k * ((Cin + KB - 1) / KB), a_bytes = kCvM * KB * 2, b_bytes = BN * KB * 2;
+  const int sms = sm_count();
+  // Resident weight slice when it leaves room for the activation ring.
+  g.wres = (nk * b_bytes <= 96 * 1024 && g.n_tiles <= sms) ? 1 : 0;
+  const int half_cols = BN >= 32 ? BN / 2 : BN, stg_bytes = kCvEpiWarps * 2 * 32 * 2 * half_cols;
+  const int ring_budget = 200 * 1024 - stg_bytes - (g.wres ? nk * b_bytes : 0);
+  const int stage_bytes = g.wres ? a_bytes : a_bytes + b_bytes;
+  g.stages = std::max(2, std::min(kCvMaxStages, ring_budget / stage_bytes));
   auto fn = conv_encode_fn();
   if (!fn) return set_error(VA_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
-  CUtensorMap mx, mw;
-  {
+  CUtensorMap mx, mw, my;
+  CUresult r;
+  if (g.linear) {
+    const uint64_t d[2] = {(uint64_t)Cin, (uint64_t)g.pixels};
+    const uint64_t str[1] = {(uint64_t)Cin * 2};
+    const uint32_t box[2] = {(uint32_t)KB, (uint32_t)kCvM}, es[2] = {1, 1};
+    r = fn(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(x), d, str, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, tma_swizzle(KB), CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
     const uint64_t d[4] = {(uint64_t)Cin, (uint64_t)W, (uint64_t)H, (uint64_t)B};
     const uint64_t str[3] = {(uint64_t)Cin * 2, (uint64_t)W * Cin * 2, (uint64_t)H * W * Cin * 2};
-    const uint32_t box[4] = {(uint32_t)KB, (uint32_t)(16 * s), (uint32_t)(8 * s), 1};
+    const uint32_t box[4] = {(uint32_t)KB, (uint32_t)(kCvTW * s), (uint32_t)(kCvTH * s), 1};
     const uint32_t es[4] = {1, (uint32_t)s, (uint32_t)s, 1};
-    CUresult r = fn(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<__nv_bfloat16*>(x), d, str, box, es,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, tma_swizzle(KB), CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(VA_ERR_ALIGN, "conv nhwc: tensor map for x rejected (CUresult %d)", (int)r);
+    r = fn(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<__nv_bfloat16*>(x), d, str, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, tma_swizzle(KB), CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   }
+  if (r != CUDA_SUCCESS) return set_error(VA_ERR_ALIGN, "conv nhwc: tensor map for x rejected (CUresult %d)", (int)r);
   {
     const uint64_t d[2] = {(uint64_t)k * k * Cin, (uint64_t)Cout};
     const uint64_t str[1] = {(uint64_t)k * k * Cin * 2};
     const uint32_t box[2] = {(uint32_t)KB, (uint32_t)BN}, es[2] = {1, 1};
-    CUresult r = fn(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(w), d, str, box, es,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, tma_swizzle(KB), CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    r = fn(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(w), d, str, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, tma_swizzle(KB), CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(VA_ERR_ALIGN, "conv nhwc: tensor map for w rejected (CUresult %d)", (int)r);
   }
-  const int tiles_w = (Wo + kCvTW - 1) / kCvTW, tiles_h = (Ho + kCvTH - 1) / kCvTH;
-  const dim3 grid((unsigned)(tiles_w * tiles_h), (unsigned)((Cout + BN - 1) / BN), (unsigned)B);
+  // With resident weights a CTA keeps one channel tile: the grid is a multiple of n_tiles.
+  {  // y: tiles of 32 output rows × half_cols channels, stored from the staging buffers
+    const CUtensorMapSwizzle swz = tma_swizzle(half_cols);
+    if (g.linear) {
+      const uint64_t d[2] = {(uint64_t)Cout, (uint64_t)g.pixels};
+      const uint64_t str[1] = {(uint64_t)Cout * 2};
+      const uint32_t box[2] = {(uint32_t)half_cols, 32}, es[2] = {1, 1};
+      r = fn(&my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, d, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+      const uint64_t d[4] = {(uint64_t)Cout, (uint64_t)Wo, (uint64_t)Ho, (uint64_t)B};
+      const uint64_t str[3] = {(uint64_t)Cout * 2, (uint64_t)Wo * Cout * 2, (uint64_t)Ho * Wo * Cout * 2};
+      const uint32_t box[4] = {(uint32_t)half_cols, (uint32_t)kCvTW, 2, 1}, es[4] = {1, 1, 1, 1};
+      r = fn(&my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, y, d, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r != CUDA_SUCCESS) return set_error(VA_ERR_ALIGN, "conv nhwc: tensor map for y rejected (CUresult %d)", (int)r);
+  }
+  const int grid = std::min(g.total_tiles, g.wres ? sms / g.n_tiles * g.n_tiles : sms);
+  // At least 116 KB so that two CTAs never share an SM (each holds 4·BN TMEM columns).
+  const size_t smem = std::max<size_t>(
+      116 * 1024,
+      1024 + (size_t)stg_bytes + (size_t)g.stages * stage_bytes + (g.wres ? (size_t)nk * b_bytes : 0) + sizeof(ConvCtl));
   int rc = VA_ERR_UNSUPPORTED;
   auto launch = [&](auto kb, auto bn) {
     constexpr int KB_ = decltype(kb)::value, BN_ = decltype(bn)::value;
     auto kernel = conv_nhwc_kernel<KB_, BN_>;
-    const size_t smem = sizeof(ConvSmem<KB_, BN_>) + 1024;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) {
       rc = set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       return;
     }
-    kernel<<<grid, kCvThreads, smem, st>>>(mx, mw, bias, y, Ho, Wo, Cin, Cout, k, s, act, tiles_w);
+    kernel<<<grid, kCvThreads, smem, st>>>(mx, mw, my, bias, g);
     rc = check_launch("conv nhwc");
   };
   using std::integral_constant;

@@ -151,7 +151,7 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float v = __uint_as_float(u[i]);
-          u[i] = __float_as_uint(v / (1.0f + __expf(-v)));
+          u[i] = __float_as_uint(__fdividef(v, 1.0f + __expf(-v)));  // SiLU; → −0 once exp overflows
         }
       }
       if (res) {  // + residual (f32, bf16 or f16 by res_type), columns < N
