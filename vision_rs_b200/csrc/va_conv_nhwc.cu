@@ -47,9 +47,10 @@ __device__ int g_conv_status;
 
 namespace {
 
-constexpr int kCvM = 128, kCvTW = 16, kCvTH = 8, kCvMaxStages = 8;
+constexpr int kCvM = 128, kCvTW = 16, kCvTH = 8, kCvMaxStages = 32;
 constexpr int kCvEpiWarps = 8, kCvThreads = 64 + 32 * kCvEpiWarps;  // producer, MMA, 8 epilogue warps
 constexpr int kCvAcc = 4;  // TMEM accumulator buffers (4 × BN ≤ 512 columns)
+constexpr int kHaloRows = (kCvTH + 2) * kCvTW;  // 3×3 stride-1 halo tile: 10 input rows × 16 columns
 
 // Barriers and bookkeeping behind the operand ring in dynamic shared memory.
 struct ConvCtl {
@@ -84,6 +85,7 @@ struct ConvGeom {
   int Ho, Wo, Cin, Cout, ksize, stride, act, linear;
   int tiles_w, tiles_h, n_tiles, total_tiles, stages;
   int wres;          // the CTA's whole weight slice [BN][k·k·Cin] stays in shared memory
+  int halo;          // 3×3 stride 1: one 10-row halo load per (channel block, kx) serves ky = 0, 1, 2
   long long pixels;  // B·Ho·Wo
 };
 
@@ -128,7 +130,8 @@ __device__ __forceinline__ void conv_tile(const ConvGeom& g, int t, int bn, int&
 template <int KB, int BN>
 __global__ void __launch_bounds__(kCvThreads, 1)
 conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                 const __grid_constant__ CUtensorMap map_y, const float* __restrict__ bias, const ConvGeom g) {
+                 const __grid_constant__ CUtensorMap map_y, const float* __restrict__ bias,
+                 __nv_bfloat16* __restrict__ y, const ConvGeom g) {
   extern __shared__ uint8_t smem_raw[];
   constexpr int kABytes = kCvM * KB * 2, kBBytes = BN * KB * 2;
   constexpr int kHalfCols = ConvCols<BN>::half, kRowBytes = 2 * kHalfCols;
@@ -136,8 +139,11 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
   // [staging: 8 warps × 2 × 32 rows × kRowBytes][A ring][B ring or resident slice][barriers]
   uint8_t* stg = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = stg + kCvEpiWarps * 2 * 32 * kRowBytes;
-  uint8_t* sb = sa + g.stages * kABytes;  // weight ring, or the resident slice
+  // A stage: 128 pixel rows, or in halo mode 160 rows (10 input rows × 16 columns).
+  const int aBytes = g.halo ? kHaloRows * KB * 2 : kABytes;
+  uint8_t* sb = sa + g.stages * aBytes;  // weight ring, or the resident slice
   const int pad = g.ksize / 2, cblocks = (g.Cin + KB - 1) / KB, nk = g.ksize * g.ksize * cblocks;
+  const int nq = g.halo ? 3 * cblocks : nk;  // ring stages per tile
   ConvCtl& c = *reinterpret_cast<ConvCtl*>(sb + (g.wres ? nk : g.stages) * kBBytes);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = g.stages;
@@ -184,11 +190,17 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
         int b, oy0, ox0, n0;
         long long m0;
         conv_tile(g, t, BN, b, oy0, ox0, m0, n0);
-        for (int kb = 0; kb < nk; ++kb, ++q) {
+        for (int kb = 0; kb < nq; ++kb, ++q) {
           const int st = (int)(q % S);
           const long long round = q / S;
           if (round > 0 && !(ok = mbar_wait(&c.empty[st], (uint32_t)((round - 1) & 1), &c.abort, &g_conv_status, 1)))
             break;
+          if (g.halo) {  // stage kb = (channel block kb / 3, kx = kb % 3): input rows oy0 − 1 … oy0 + 8
+            const int cb = kb / 3, kx = kb - 3 * cb;
+            mbar_arrive_expect_tx(&c.full[st], aBytes);
+            tma_load_4d(sa + st * aBytes, &map_x, &c.full[st], cb * KB, ox0 + kx - 1, oy0 - 1, b);
+            continue;
+          }
           const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * KB, ky = tap / g.ksize, kx = tap - ky * g.ksize;
           mbar_arrive_expect_tx(&c.full[st], g.wres ? kABytes : kABytes + kBBytes);
           if (g.linear)
@@ -228,11 +240,25 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
           break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * BN);
-        for (int kb = 0; kb < nk; ++kb, ++q) {
+        for (int kb = 0; kb < nq; ++kb, ++q) {
           const int st = (int)(q % S);
           if (!(ok = mbar_wait(&c.full[st], (uint32_t)((q / S) & 1), &c.abort, &g_conv_status, 3))) break;
           tc_fence_after();
-          const uint64_t da = da0 + (uint64_t)((st * kABytes) >> 4);
+          const uint64_t da = da0 + (uint64_t)((st * aBytes) >> 4);
+          if (g.halo) {
+            // Output row r of tap (ky, kx) reads halo row r + 16·ky: the A operand
+            // starts 16·ky rows in (a whole number of swizzle atoms).
+            const int cb = kb / 3, kx = kb - 3 * cb;
+            for (int ky = 0; ky < 3; ++ky) {
+              const uint64_t dak = da + (uint64_t)((16 * ky * KB * 2) >> 4);
+              const uint64_t db = db0 + (uint64_t)((((ky * 3 + kx) * cblocks + cb) * kBBytes) >> 4);
+#pragma unroll
+              for (int s = 0; s < KB / 16; ++s)
+                mma_ss(d, dak + 2 * s, db + 2 * s, idesc, (kb > 0 || ky > 0 || s > 0) ? 1u : 0u);
+            }
+            mma_commit(&c.empty[st]);
+            continue;
+          }
           const uint64_t db = db0 + (uint64_t)(((g.wres ? kb : st) * kBBytes) >> 4);
 #pragma unroll
           for (int s = 0; s < KB / 16; ++s)  // +32 bytes per 16-channel k-step inside the swizzle atom
@@ -281,9 +307,7 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
       __syncwarp();
       if (lane == 0) mbar_arrive(&c.acc_empty[buf]);
       if (active) {
-        uint8_t* stage = stg + (ew * 2 + (i & 1)) * (32 * kRowBytes);
-        if (lane == 0) tma_store_wait_read_1();  // this staging buffer's previous store has read it
-        __syncwarp();
+        uint4 outv[kRowBytes / 16];  // this lane's pixel: kHalfCols channels of bf16
 #pragma unroll
         for (int j = 0; j < kRowBytes / 16; ++j) {
           uint32_t q4[4];
@@ -297,16 +321,43 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
             }
             q4[e] = pack_bf16x2(v0, v1);
           }
-          *reinterpret_cast<uint4*>(stage + lane * kRowBytes + ((j ^ sw) << 4)) = make_uint4(q4[0], q4[1], q4[2], q4[3]);
+          outv[j] = make_uint4(q4[0], q4[1], q4[2], q4[3]);
         }
-        fence_proxy_async_smem();  // the staging writes become visible to the TMA store
-        __syncwarp();
-        if (lane == 0) {  // 32 rows × kHalfCols channels; TMA drops what lies outside y
-          if (g.linear)
-            tma_store_2d(&map_y, stage, n0 + cbase, (int)(m0 + quarter * 32));
-          else
-            tma_store_4d(&map_y, stage, n0 + cbase, ox0, oy0 + 2 * quarter, b);
-          tma_store_commit();
+        if constexpr (kRowBytes >= 64) {  // staged in shared memory, written by a TMA store
+          uint8_t* stage = stg + (ew * 2 + (i & 1)) * (32 * kRowBytes);
+          if (lane == 0) tma_store_wait_read_1();  // this staging buffer's previous store has read it
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < kRowBytes / 16; ++j)
+            *reinterpret_cast<uint4*>(stage + lane * kRowBytes + ((j ^ sw) << 4)) = outv[j];
+          fence_proxy_async_smem();  // the staging writes become visible to the TMA store
+          __syncwarp();
+          if (lane == 0) {  // 32 rows × kHalfCols channels; TMA drops what lies outside y
+            if (g.linear)
+              tma_store_2d(&map_y, stage, n0 + cbase, (int)(m0 + quarter * 32));
+            else
+              tma_store_4d(&map_y, stage, n0 + cbase, ox0, oy0 + 2 * quarter, b);
+            tma_store_commit();
+          }
+        } else {  // rows of 32 bytes: plain stores from registers beat a TMA store of narrow rows
+          const int r = quarter * 32 + lane;
+          long long pix;
+          bool live;
+          if (g.linear) {
+            pix = m0 + r;
+            live = pix < g.pixels;
+          } else {
+            const int oy = oy0 + r / kCvTW, ox = ox0 + r % kCvTW;
+            live = oy < g.Ho && ox < g.Wo;
+            pix = ((long long)b * g.Ho + oy) * g.Wo + ox;
+          }
+          const int nv = g.Cout - n0 - cbase;
+          if (live) {
+            uint4* o = reinterpret_cast<uint4*>(y + pix * g.Cout + n0 + cbase);
+#pragma unroll
+            for (int j = 0; j < kRowBytes / 16; ++j)
+              if (8 * j < nv) o[j] = outv[j];
+          }
         }
       }
     }
@@ -392,8 +443,9 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
   // Resident weight slice when it leaves room for the activation ring.
   g.wres = (nk * b_bytes <= 96 * 1024 && g.n_tiles <= sms) ? 1 : 0;
   const int half_cols = BN >= 32 ? BN / 2 : BN, stg_bytes = kCvEpiWarps * 2 * 32 * 2 * half_cols;
+  g.halo = (k == 3 && s == 1 && g.wres) ? 1 : 0;
   const int ring_budget = 200 * 1024 - stg_bytes - (g.wres ? nk * b_bytes : 0);
-  const int stage_bytes = g.wres ? a_bytes : a_bytes + b_bytes;
+  const int stage_bytes = g.halo ? kHaloRows * KB * 2 : g.wres ? a_bytes : a_bytes + b_bytes;
   g.stages = std::max(2, std::min(kCvMaxStages, ring_budget / stage_bytes));
   auto fn = conv_encode_fn();
   if (!fn) return set_error(VA_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
@@ -409,7 +461,7 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
   } else {
     const uint64_t d[4] = {(uint64_t)Cin, (uint64_t)W, (uint64_t)H, (uint64_t)B};
     const uint64_t str[3] = {(uint64_t)Cin * 2, (uint64_t)W * Cin * 2, (uint64_t)H * W * Cin * 2};
-    const uint32_t box[4] = {(uint32_t)KB, (uint32_t)(kCvTW * s), (uint32_t)(kCvTH * s), 1};
+    const uint32_t box[4] = {(uint32_t)KB, (uint32_t)(kCvTW * s), (uint32_t)(g.halo ? kCvTH + 2 : kCvTH * s), 1};
     const uint32_t es[4] = {1, (uint32_t)s, (uint32_t)s, 1};
     r = fn(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<__nv_bfloat16*>(x), d, str, box, es,
            CU_TENSOR_MAP_INTERLEAVE_NONE, tma_swizzle(KB), CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -457,7 +509,7 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
       rc = set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       return;
     }
-    kernel<<<grid, kCvThreads, smem, st>>>(mx, mw, my, bias, g);
+    kernel<<<grid, kCvThreads, smem, st>>>(mx, mw, my, bias, y, g);
     rc = check_launch("conv nhwc");
   };
   using std::integral_constant;
