@@ -18,6 +18,10 @@ named shapes and distributions, random-init weights):
 * ``cfg5``: PSA Attention training step, bf16 with f32 master weights, 32
   images of 128×20×20 per GPU: forward + backward + NCCL all-reduce of the
   weight gradients + SGD.
+* ``conv``: the convolutions around the block — every Conv+BN+SiLU of the
+  YOLO26n backbone layers 1-8 at 640×640 input (18 convs, 1×1 and 3×3,
+  stride 1 and 2, 8 to 384 channels), bf16 NHWC, batch 64; each conv runs on
+  its own resident input.  Step = the 18 conv launches.
 
 Multi-GPU: one process per GPU (torchrun), image shards (weak scaling); cfg2-4
 have no collective, cfg5 all-reduces its gradients.  Timing: CUDA events on
@@ -76,6 +80,26 @@ DN_NWIN = 1 + DN_WIN * DN_WIN
 DN_FLOP_GLOBAL_ATTN_IMG = 2 * 2 * DN_HEADS * DN_N * DN_N * 64
 DN_FLOP_IMG = (2 * DN_N * DN_HID * 3 * DN_HID + DN_FLOP_GLOBAL_ATTN_IMG
                + 2 * DN_NW * DN_NWIN * DN_HID * 3 * DN_HID + 2 * 2 * DN_HEADS * DN_NW * DN_NWIN * DN_NWIN * 64)
+
+# ── conv stack: YOLO26n backbone layers 1-8 at 640 (name, C_in, C_out, k, stride, input H = W) ──
+CONV_B = 64
+CONV_LAYERS = [("l1", 16, 32, 3, 2, 320), ("l2.cv1", 32, 32, 1, 1, 160), ("l2.m.cv1", 16, 8, 3, 1, 160),
+               ("l2.m.cv2", 8, 16, 3, 1, 160), ("l2.cv2", 48, 64, 1, 1, 160), ("l3", 64, 64, 3, 2, 160),
+               ("l4.cv1", 64, 64, 1, 1, 80), ("l4.m.cv1", 32, 16, 3, 1, 80), ("l4.m.cv2", 16, 32, 3, 1, 80),
+               ("l4.cv2", 96, 128, 1, 1, 80), ("l5", 128, 128, 3, 2, 80), ("l6.cv1", 128, 128, 1, 1, 40),
+               ("l6.m.cv3x3", 32, 32, 3, 1, 40), ("l6.cv2", 192, 128, 1, 1, 40), ("l7", 128, 256, 3, 2, 40),
+               ("l8.cv1", 256, 256, 1, 1, 20), ("l8.m.cv3x3", 64, 64, 3, 1, 20), ("l8.cv2", 384, 256, 1, 1, 20)]
+
+
+def conv_out(h, k, s):
+    return (h + 2 * (k // 2) - k) // s + 1
+
+
+def conv_layer_work(ci, co, k, s, h):
+    """(FLOP, bytes) of one image through one conv: MACs × 2; x in + y out (bf16) + weights."""
+    ho = conv_out(h, k, s)
+    return 2 * ho * ho * co * ci * k * k, 2 * (h * h * ci + ho * ho * co) + 2 * co * ci * k * k
+
 
 # ── cfg5 constants ──────────────────────────────────────────────────────────
 T5_B, T5_H, T5_W = 32, 20, 20
@@ -763,7 +787,97 @@ class Cfg5:
     sample_desc = "images of 128x20x20 fwd+bwd, torch-CPU f32 autograd restatement (the reference has no CPU path)"
 
 
-CONFIGS = {"cfg1": Cfg1, "cfg2": Cfg2, "cfg3": Cfg3, "cfg4": Cfg4, "cfg5": Cfg5}
+class ConvStack:
+    metric = "conv images/sec (YOLO26n backbone Conv+BN+SiLU layers 1-8, bf16 NHWC, 640x640)"
+    unit, dtype, batch = "images/s", "bf16", CONV_B
+    workload = ("conv: the 18 Conv+BN(+SiLU) of YOLO26n backbone layers 1-8 at 640x640 input, batch 64, bf16 "
+                "NHWC, BN folded, each conv on its own resident input")
+
+    def __init__(self, dev, rank, batch, args):
+        import torch
+        from vision_rs_b200 import conv
+        g = torch.Generator(device="cpu").manual_seed(700 + rank)
+        self.B, self.layers = batch, []
+        for name, ci, co, k, s, h in CONV_LAYERS:
+            w = torch.randn(co, ci, k, k, generator=g) / math.sqrt(ci * k * k)
+            b = torch.randn(co, generator=g) * 0.1
+            x = torch.randn(batch, h, h, ci, generator=g).to(dev, torch.bfloat16)
+            op = conv.ConvBnAct(w.numpy(), b.numpy(), s, True, device=dev)
+            y = torch.empty(batch, conv_out(h, k, s), conv_out(h, k, s), co, dtype=torch.bfloat16, device=dev)
+            self.layers.append((name, op, x, y))
+        self.xh = [x.cpu().pin_memory() for _, _, x, _ in self.layers]
+        self.yh = [torch.empty(y.shape, dtype=y.dtype).pin_memory() for _, _, _, y in self.layers]
+        work = [conv_layer_work(ci, co, k, s, h) for _, ci, co, k, s, h in CONV_LAYERS]
+        self.flop_img = sum(f for f, _ in work)
+        self.bytes_img = sum(b for _, b in work)
+
+    def step(self):
+        for _, op, x, y in self.layers:
+            op(x, out=y)
+
+    def e2e_step(self):
+        """Each conv called as a host-buffer op: its input copied in, its output copied out."""
+        for (_, op, x, y), xh, yh in zip(self.layers, self.xh, self.yh):
+            x.copy_(xh, non_blocking=True)
+            op(x, out=y)
+            yh.copy_(y, non_blocking=True)
+
+    def io_bytes(self):
+        return (sum(x.numel() * 2 for _, _, x, _ in self.layers), sum(y.numel() * 2 for _, _, _, y in self.layers))
+
+    def dominant(self, args, stream, flush):
+        """The whole stack against the roofline its arithmetic intensity picks
+        (every launch is the same conv kernel), plus the per-layer times."""
+        pk, src = peaks()
+        per = {}
+        for (name, op, x, y), (_, ci, co, k, s, h) in zip(self.layers, CONV_LAYERS):
+            call = lambda: op(x, out=y)
+            for _ in range(3):
+                call()
+            per[name] = event_time(call, max(5, args.steps), stream, flush) * 1e3
+        ms = sum(per.values()) / 1e3
+        flop, byts = self.flop_img * self.B, self.bytes_img * self.B
+        ridge = pk["bf16_tflops"] * 1e12 / (pk["hbm_gbs"] * 1e9)
+        if flop / byts >= ridge:
+            ach = flop / (ms * 1e-3) / 1e12
+            r = {"bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                 "peak_source": f"{src} bf16_tflops"}
+        else:
+            ach = byts / (ms * 1e-3) / 1e9
+            r = {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                 "peak_source": f"{src} hbm_gbs"}
+        r.update({"kernel": "conv_nhwc_kernel (tcgen05 implicit GEMM, 18 launches: per-layer sum)",
+                  "frac": r["achieved"] / r["peak"], "traffic": None, "flop_per_launch": flop,
+                  "bytes_per_launch": byts, "ms_per_launch": ms, "intensity_flop_per_byte": flop / byts,
+                  "us_per_layer": per})
+        return r
+
+    def extra(self, ms):
+        return {"tflops": self.flop_img * self.B / (ms * 1e-3) / 1e12}
+
+    config = {"layers": len(CONV_LAYERS), "input": "640x640 (layer 1 input 320x320x16)"}
+
+    @staticmethod
+    def cpu_sample(threads, n_img=1, seed=1234):
+        """One image through every layer: torch-CPU f32 conv2d + bias + SiLU, NCHW."""
+        import torch
+        torch.set_num_threads(threads)
+        g = torch.Generator().manual_seed(seed)
+        t = 0.0
+        for _, ci, co, k, s, h in CONV_LAYERS:
+            x = torch.randn(n_img, ci, h, h, generator=g)
+            w = torch.randn(co, ci, k, k, generator=g) / math.sqrt(ci * k * k)
+            b = torch.randn(co, generator=g) * 0.1
+            t0 = time.perf_counter()
+            torch.nn.functional.silu(torch.nn.functional.conv2d(x, w, b, stride=s, padding=k // 2))
+            t += time.perf_counter() - t0
+        return n_img, t
+
+    sample_desc = ("single images through the 18 convs, torch-CPU f32 conv2d + bias + SiLU (NCHW); the reference "
+                   "runs its convs on the GPU only")
+
+
+CONFIGS = {"cfg1": Cfg1, "cfg2": Cfg2, "cfg3": Cfg3, "cfg4": Cfg4, "cfg5": Cfg5, "conv": ConvStack}
 
 
 # ═════════════════════════════ arms ══════════════════════════════════════════
