@@ -111,6 +111,20 @@ VA_API int va_flash_attention2_forward_bf16(const va_bf16 *q, const va_bf16 *k, 
                                      va_bf16 *o, float *l, int n_ctx_q, int n_ctx_k,
                                      float softmax_scale, float neg_inf, int bh, int head_dim,
                                      va_stream_t stream);
+
+/* The same node on the tensor cores (bf16, head_dim 32, n_ctx_q == n_ctx_k as
+ * in the PSA graph): q/k/v/o/l exactly as above, plus a workspace of
+ * va_flash_attention2_tc_workspace_bytes(n_ctx, bh, 32) bytes that a RuntimeOp
+ * declares through param_shapes next to l.  It repacks q, k, v into the
+ * tcgen05 attention kernel's layouts (f16), runs it with the given
+ * softmax_scale and copies the 32 output channels back.  Inputs must satisfy
+ * |x| < 65504 (f16 range).  VA_ERR_SHAPE for other head dims or cross
+ * attention, VA_ERR_WORKSPACE when the workspace is missing or short. */
+VA_API size_t va_flash_attention2_tc_workspace_bytes(int n_ctx, int bh, int head_dim);
+VA_API int va_flash_attention2_forward_tc_bf16(const va_bf16 *q, const va_bf16 *k, const va_bf16 *v,
+                                               va_bf16 *o, float *l, int n_ctx_q, int n_ctx_k,
+                                               float softmax_scale, float neg_inf, int bh, int head_dim,
+                                               void *workspace, size_t ws_bytes, va_stream_t stream);
 /* flash_attention2_backward_dq (flash_attn2.rs:129-187): stores dq. */
 VA_API int va_flash_attention2_backward_dq_f32(const float *q, const float *k, const float *v,
                                         const float *o, const float *d_o, const float *l,

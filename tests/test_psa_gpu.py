@@ -107,6 +107,86 @@ def test_fa_forward_bf16_vs_oracle(cuda):
     assert rel_l2(host(o), ro) < BF16_REL_L2 and max_abs(host(o), ro) < BF16_MAX_ABS
 
 
+def test_fa_forward_tc_golden_fixture(cuda):
+    """The tensor-core node entry on the reference's FA fixture ([4,16,32], lo
+    and hi halves; small enough that the entry runs the FFMA kernel), inputs
+    rounded to bf16: o within the bf16 bound of the oracle on those inputs and
+    of the fixture; l within 1e-3."""
+    g = load_golden("c2psa_bwd.npz")
+    q, k = bf16_round(g["attn_q"]), bf16_round(g["attn_k"])
+    for half in ("lo", "hi"):
+        v = bf16_round(g[f"attn_v_{half}"])
+        o, l = vp.flash_attention2_forward_tc(dev(q, torch.bfloat16), dev(k, torch.bfloat16), dev(v, torch.bfloat16),
+                                              SCALE)
+        ro, rl = po.flash_attention2_forward(q, k, v, SCALE)
+        assert rel_l2(host(o), ro) < BF16_REL_L2 and max_abs(host(o), ro) < BF16_MAX_ABS
+        assert rel_l2(host(o), g[f"attn_o_{half}"]) < 2 * BF16_REL_L2
+        assert max_abs(host(l), rl) < 1e-3
+
+
+# Above 2048 query rows in all the tensor-core kernels run: 100 tokens the short-sequence
+# kernel (one key tile), 400 = cfg1/cfg5, 1600 = cfg2, 1601 and 130 ragged last tiles; (4, 100)
+# and the fixture (4 × 16) are small enough for the FFMA kernel the entry hands them to.
+@pytest.mark.parametrize("bh,n", [(32, 100), (6, 400), (4, 1600), (3, 1601), (24, 130), (128, 400), (4, 100)])
+def test_fa_forward_tc_vs_oracle(cuda, bh, n):
+    rng = np.random.default_rng(bh * n)
+    q, k, v = (bf16_round(rng.standard_normal((bh, n, 32)) * s) for s in (0.8, 0.8, 1.0))
+    o, l = vp.flash_attention2_forward_tc(dev(q, torch.bfloat16), dev(k, torch.bfloat16), dev(v, torch.bfloat16),
+                                          SCALE)
+    idx = [0, bh - 1] if bh > 8 else list(range(bh))
+    ro, rl = po.flash_attention2_forward(q[idx], k[idx], v[idx], SCALE)
+    oh, lh = host(o)[idx], host(l)[idx]
+    assert rel_l2(oh, ro) < BF16_REL_L2 and max_abs(oh, ro) < BF16_MAX_ABS
+    assert max_abs(lh, rl) < 1e-3
+
+
+def test_fa_forward_tc_matches_simt_node(cuda):
+    """Both bf16 entries of the node agree on the same inputs (cfg2's per-call
+    shape, 128 sequences × 1600 tokens), within the bf16 bound."""
+    rng = np.random.default_rng(77)
+    q, k, v = (dev(rng.standard_normal((128, 1600, 32)) * 0.7, torch.bfloat16) for _ in range(3))
+    o1, l1 = vp.flash_attention2_forward_tc(q, k, v, SCALE)
+    o2, l2 = vp.flash_attention2_forward(q, k, v, SCALE)
+    assert rel_l2(host(o1), host(o2)) < BF16_REL_L2
+    assert max_abs(host(l1), host(l2)) < 1e-3
+
+
+def test_fa_forward_tc_rejects(cuda):
+    """Argument errors return before any launch (4096 query rows: the tensor-core route)."""
+    from vision_rs_b200 import _lib
+    lib = _lib.lib()
+    bh, n = 2, 2048
+    x = torch.zeros(bh, n, 32, dtype=torch.bfloat16, device="cuda")
+    lse = torch.zeros(bh, n, device="cuda")
+    ws = torch.empty(int(lib.va_flash_attention2_tc_workspace_bytes(n, bh, 32)), dtype=torch.uint8, device="cuda")
+    p, l, w = x.data_ptr(), lse.data_ptr(), ws.data_ptr()
+    call = lib.va_flash_attention2_forward_tc_bf16
+    assert call(p, p, p, p, l, n, n, SCALE, float("-inf"), bh, 16, w, ws.numel(), None) == 1  # head dim
+    assert call(p, p, p, p, l, n, n // 2, SCALE, float("-inf"), bh, 32, w, ws.numel(), None) == 1  # cross attention
+    assert call(p, p, p, p, None, n, n, SCALE, float("-inf"), bh, 32, w, ws.numel(), None) == 1  # l is required
+    assert call(p, p, p, p, l, n, n, SCALE, float("-inf"), bh, 32, w, ws.numel() - 256, None) == 6  # short workspace
+
+
+def test_reference_node_sequence_bf16_tensor_cores(cuda):
+    """The reference graph's two flash_attention2_forward nodes (lo, hi) with
+    the tensor-core RuntimeOp variant on a bf16 packed buffer: equal, within
+    the bf16 bound, to the oracle's per-half attention."""
+    B, nh, N, kd = 4, 2, 400, 32
+    rng = np.random.default_rng(3)
+    packed = bf16_round(rng.standard_normal((4, B * nh, N, kd)) * 0.8)
+    pd = dev(packed, torch.bfloat16)
+    shp = [B, 4, nh, N, kd]
+    for ctor, sec in ((vp.FlashAttn2PsaOp.new_lo, 2), (vp.FlashAttn2PsaOp.new_hi, 3)):
+        op = ctor(kd, tensor_cores=True).inner
+        shapes = op.param_shapes([shp], None)
+        params = [torch.empty(*shapes[0], device="cuda"), torch.empty(*shapes[1], dtype=torch.uint8, device="cuda")]
+        out = torch.empty(B * nh, N, kd, dtype=torch.bfloat16, device="cuda")
+        op.launch([(pd, shp)], params, out)
+        ro, rl = po.flash_attention2_forward(packed[0], packed[1], packed[sec], SCALE)
+        assert rel_l2(host(out), ro) < BF16_REL_L2 and max_abs(host(out), ro) < BF16_MAX_ABS
+        assert max_abs(host(params[0]).reshape(B * nh, N), rl) < 1e-3
+
+
 @pytest.mark.parametrize("bh,n,d", [(4, 16, 32), (2, 400, 32), (3, 77, 16), (2, 130, 64)])
 def test_psa_fa2_backward_f32(cuda, bh, n, d):
     """psa_fa2_backward (psa.rs:650-725): dq/dk accumulate, dv stored."""

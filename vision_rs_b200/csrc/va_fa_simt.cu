@@ -339,6 +339,8 @@ __global__ void __launch_bounds__(128) fa_bwd_dkv_kernel(const float* __restrict
 template <typename T>
 static int fa_fwd(const T* q, const T* k, const T* v, T* o, float* l, int nq, int nk, float scale, int bh,
                   int hd, cudaStream_t st) {
+  VA_CHECK_ARG(hd == 16 || hd == 32 || hd == 64, "flash_attention2_forward: head_dim %d unsupported (16, 32, 64)", hd);
+  VA_CHECK_ARG(q && k && v && o && l, "flash_attention2_forward: null pointer (q, k, v, o and l are required)");
   VA_CHECK_ARG(nq > 0 && nk > 0 && bh > 0, "flash_attention2_forward: non-positive size");
   VA_CHECK_ARG(bh <= 65535, "flash_attention2_forward: bh=%d exceeds 65535", bh);
   dim3 grid(ceil_div(nq, 128), bh);
@@ -387,6 +389,7 @@ static int fa_fwd(const T* q, const T* k, const T* v, T* o, float* l, int nq, in
 template <bool ACC>
 static int fa_bwd_dq(const float* q, const float* k, const float* v, const float* o, const float* d_o,
                      const float* l, float* dq, int nq, int nk, float scale, int bh, int hd, cudaStream_t st) {
+  VA_CHECK_ARG(q && k && v && o && d_o && l && dq, "flash attention backward (dq): null pointer");
   dim3 grid(ceil_div(nq, 128), bh);
   switch (hd) {
     case 16: fa_bwd_dq_kernel<16, 16, ACC><<<grid, 128, 0, st>>>(q, k, v, o, d_o, l, dq, nq, nk, scale); break;
@@ -401,6 +404,7 @@ template <bool ACC>
 static int fa_bwd_dkv(const float* q, const float* k, const float* v, const float* o, const float* d_o,
                       const float* l, float* dk, float* dv, int nq, int nk, float scale, int bh, int hd,
                       cudaStream_t st) {
+  VA_CHECK_ARG(q && k && v && o && d_o && l && dk && dv, "flash attention backward (dk, dv): null pointer");
   dim3 grid(ceil_div(nk, 128), bh);
   switch (hd) {
     case 16: fa_bwd_dkv_kernel<16, 16, ACC><<<grid, 128, 0, st>>>(q, k, v, o, d_o, l, dk, dv, nq, nk, scale); break;

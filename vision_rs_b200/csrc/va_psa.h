@@ -103,8 +103,9 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
 // qk f16 [2][BH][N][kd] (Q then K), v f16 [BH·64][Np] (Np = N rounded up to 8),
 // head dim 64, kd ∈ {32, 64}; o f16 [BH/nh][nh·64][Np] (channel-major) or,
 // with out_token_major, bf16 [BH/nh][N][nh·64]; lse (optional) f32 [BH][N].
+// scale: softmax scale (0 → 1/√kd).
 int tc_flash_attention(const void* qk, const void* v, void* o, float* lse, int BH, int nh, int N, int kd,
-                       int out_token_major, cudaStream_t st);
+                       int out_token_major, cudaStream_t st, float scale = 0.0f);
 int psa_attention_core_tc(const void* qk, const void* v, void* o, float* lse, int B, int nh, int H, int W,
                           cudaStream_t st);
 int tc_status_read(int* out, cudaStream_t st);

@@ -1642,7 +1642,7 @@ int tc_status_clear(cudaStream_t st) {
 namespace va {
 
 int tc_flash_attention(const void* qk, const void* v, void* o, float* lse, int BH, int nh, int N, int kd,
-                       int out_token_major, cudaStream_t st) {
+                       int out_token_major, cudaStream_t st, float scale) {
   VA_CHECK_ARG(kd == 32 || kd == 64, "flash attention: key dim %d (32 or 64)", kd);
   VA_CHECK_ARG(BH > 0 && nh > 0 && BH % nh == 0 && N > 0 && BH <= 65535, "flash attention: bad sizes");
   if ((reinterpret_cast<uintptr_t>(qk) & 15) || (reinterpret_cast<uintptr_t>(v) & 15) ||
@@ -1664,7 +1664,7 @@ int tc_flash_attention(const void* qk, const void* v, void* o, float* lse, int B
     if (int rc = make_map(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v, d, s, bx, CU_TENSOR_MAP_SWIZZLE_128B, "v"))
       return rc;
   }
-  const float scale_log2 = (1.0f / sqrtf((float)kd)) * 1.4426950408889634f;
+  const float scale_log2 = (scale > 0.0f ? scale : 1.0f / sqrtf((float)kd)) * 1.4426950408889634f;
   if (N <= kTile) {  // one key tile per sequence: persistent short-sequence kernel
     const int ctas = std::min((BH + 1) / 2, 148);
     auto launch_short = [&](auto kernel, size_t smem) -> int {

@@ -193,23 +193,28 @@ class FlashAttn2PsaRuntimeOp:
     """Input: packed ``[4, BH, N, kd]`` (declared shape ``[B,4,nh,N,kd]``);
     output ``[BH, N, kd]``; param: ``[BH*N]`` LSE scratch (psa.rs:958-963)."""
 
-    def __init__(self, key_dim: int, v_section: int):
-        self.key_dim, self.v_section = key_dim, v_section
+    def __init__(self, key_dim: int, v_section: int, tensor_cores: bool = False):
+        self.key_dim, self.v_section, self.tensor_cores = key_dim, v_section, tensor_cores
 
     @classmethod
-    def new_lo(cls, key_dim: int):
-        return cls(key_dim, 2)
+    def new_lo(cls, key_dim: int, tensor_cores: bool = False):
+        return cls(key_dim, 2, tensor_cores)
 
     @classmethod
-    def new_hi(cls, key_dim: int):
-        return cls(key_dim, 3)
+    def new_hi(cls, key_dim: int, tensor_cores: bool = False):
+        return cls(key_dim, 3, tensor_cores)
 
     def n_activation_inputs(self) -> int:
         return 1
 
     def param_shapes(self, input_shapes, output_shape):
+        """psa.rs:958-963: the l scratch [B·nh·N]; the tensor-core variant adds
+        its workspace (bytes) as a second parameter."""
         s = input_shapes[0]
-        return [[s[0] * s[2] * s[3]]]
+        shapes = [[s[0] * s[2] * s[3]]]
+        if self.tensor_cores:
+            shapes.append([int(_lib.lib().va_flash_attention2_tc_workspace_bytes(s[3], s[0] * s[2], s[4]))])
+        return shapes
 
     def _ptrs(self, packed: torch.Tensor, b: int, nh: int, n: int, kd: int):
         sec = b * nh * n * kd * packed.element_size()
@@ -226,6 +231,11 @@ class FlashAttn2PsaRuntimeOp:
 
     def launch(self, inputs, params, output, stream=None):
         packed, shape = inputs[0]
+        if self.tensor_cores:  # bf16, head dim 32: the tcgen05 attention kernel behind the same node
+            ws = params[1]
+            _lib.call("va_flash_attention2_forward_tc_bf16", *self.pack_args(inputs, params, output), _p(ws),
+                      ws.numel() * ws.element_size(), _stream(stream))
+            return
         _lib.call(f"va_flash_attention2_forward_{_sfx(packed)}", *self.pack_args(inputs, params, output),
                   _stream(stream))
 
@@ -245,12 +255,12 @@ class FlashAttn2PsaOp:
         self.inner = inner
 
     @classmethod
-    def new_lo(cls, key_dim: int):
-        return cls(FlashAttn2PsaRuntimeOp.new_lo(key_dim))
+    def new_lo(cls, key_dim: int, tensor_cores: bool = False):
+        return cls(FlashAttn2PsaRuntimeOp.new_lo(key_dim, tensor_cores))
 
     @classmethod
-    def new_hi(cls, key_dim: int):
-        return cls(FlashAttn2PsaRuntimeOp.new_hi(key_dim))
+    def new_hi(cls, key_dim: int, tensor_cores: bool = False):
+        return cls(FlashAttn2PsaRuntimeOp.new_hi(key_dim, tensor_cores))
 
     def name(self) -> str:
         return "flash_attention2_forward"
@@ -276,6 +286,22 @@ def flash_attention2_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     l = torch.empty(bh, nq, device=q.device, dtype=torch.float32)
     _lib.call(f"va_flash_attention2_forward_{_sfx(q)}", _p(q), _p(k), _p(v), _p(o), _p(l), nq, nk,
               float(softmax_scale), float("-inf"), bh, d, _stream())
+    return o, l
+
+
+def flash_attention2_forward_tc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                                softmax_scale: Optional[float] = None, workspace: Optional[torch.Tensor] = None):
+    """The same node on the tensor cores: bf16 ``[BH,N,32]`` self-attention."""
+    bh, n, d = q.shape
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(d)
+    need = int(_lib.lib().va_flash_attention2_tc_workspace_bytes(n, bh, d))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    o = torch.empty(bh, n, v.shape[2], device=q.device, dtype=q.dtype)
+    l = torch.empty(bh, n, device=q.device, dtype=torch.float32)
+    _lib.call("va_flash_attention2_forward_tc_bf16", _p(q), _p(k), _p(v), _p(o), _p(l), n, k.shape[1],
+              float(softmax_scale), float("-inf"), bh, d, _p(workspace), workspace.numel(), _stream())
     return o, l
 
 
