@@ -1056,12 +1056,6 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local = dist_env()
-    if ws > 1 and args.impl == "ours":
-        # NCCL reports every rank's communicator set-up (rank, nranks, device) on stderr, which shows
-        # that all ranks joined; it reads these variables when torch first loads it, so set them here
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     if args.impl == "reference":
         run_reference(args, ws, rank)
     else:
