@@ -374,6 +374,20 @@ VA_API int va_psa_train_fwd_bwd_bf16(const va_bf16 *x, const va_bf16 *target, co
                                      va_bf16 *dx, float *grads, float *loss, int B, int C, int H,
                                      int W, int num_heads, int key_dim, void *workspace,
                                      size_t ws_bytes, va_stream_t stream);
+/* The backward of the fused bf16 op for any loss: given x, the folded weights and dy = ∂L/∂y
+ * [B,C,H,W] bf16, recompute the forward and write grads (f32, the layout and
+ * offsets above, stored) and, if dx is not NULL, dx = ∂L/∂x (bf16).  The
+ * backward runs on dy/dy_scale in f16; pass dy_scale ≈ max|dy| (e.g. 2/numel
+ * for a mean-squared loss) so that the scaled values are O(1); the stored
+ * gradients carry the full scale.  Same kernels, workspace query
+ * (va_psa_attention_bwd_workspace_bytes) and limits as the training step. */
+VA_API size_t va_psa_attention_bwd_workspace_bytes(int B, int H, int W);
+VA_API int va_psa_attention_bwd_bf16(const va_bf16 *x, const va_bf16 *dy, float dy_scale,
+                                     const va_bf16 *w_qkv, const float *b_qkv, const va_bf16 *w_pe,
+                                     const float *b_pe, const va_bf16 *w_proj, const float *b_proj,
+                                     va_bf16 *dx, float *grads, int B, int C, int H, int W,
+                                     int num_heads, int key_dim, void *workspace, size_t ws_bytes,
+                                     va_stream_t stream);
 /* master (f32, gradient layout) -= lr·grad_scale·grads; then the bf16
  * weights and f32 biases the forward reads are rewritten from master. */
 VA_API int va_psa_sgd_update(float *master, const float *grads, float lr, float grad_scale,

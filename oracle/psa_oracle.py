@@ -392,6 +392,25 @@ def psa_attention_torch(x, w_qkv, b_qkv, w_pe, b_pe, w_proj, b_proj, num_heads: 
 GRAD_ORDER = ("w_qkv", "w_proj", "w_pe", "b_qkv", "b_proj", "b_pe")  # flat gradient buffer layout
 
 
+def psa_attention_vjp_torch(x, dy, params: dict, num_heads: int = 2, key_dim: int = 32):
+    """Vector-Jacobian product of the BN-folded PSA Attention block in
+    torch-CPU float64: for an upstream gradient dy = ∂L/∂y, returns
+    ``(grads, dx)`` with ``grads`` flat in ``GRAD_ORDER`` — the backward that
+    a training graph runs through the attention node (the reference's
+    ``psa_fa2_backward``, ``psa_*_backward`` and conv backward kernels,
+    psa.rs:201-327, 650-725)."""
+    import torch
+    t = lambda a: torch.as_tensor(np.asarray(a, F64))
+    p = {k: t(v).requires_grad_(True) for k, v in params.items()}
+    xt = t(x).requires_grad_(True)
+    C = xt.shape[1]
+    y = psa_attention_torch(xt, p["w_qkv"], p["b_qkv"], p["w_pe"].reshape(C, 9), p["b_pe"], p["w_proj"],
+                            p["b_proj"], num_heads, key_dim)
+    y.backward(t(dy))
+    grads = np.concatenate([p[k].grad.numpy().reshape(-1) for k in GRAD_ORDER])
+    return grads, xt.grad.numpy()
+
+
 def psa_train_step_torch(x, target, params: dict, num_heads: int = 2, key_dim: int = 32):
     """Forward + autograd backward of the BN-folded PSA Attention block in
     torch-CPU float64 with loss = mean((y − target)²).  ``params`` holds

@@ -59,14 +59,14 @@ __device__ __forceinline__ float block_sum(float v, float* red) {  // fixed-orde
 // zero), Σr and Σr² of the row.
 __global__ void __launch_bounds__(kRowThreads)
 loss_rows_kernel(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ t, __half* __restrict__ r16,
-                 float* __restrict__ rsum, float* __restrict__ rsq, int N, int Np) {
+                 float* __restrict__ rsum, float* __restrict__ rsq, int N, int Np, float inv_scale) {
   __shared__ float red[kRowThreads / 32];
   const size_t row = blockIdx.x;
   float s = 0.f, q = 0.f;
   for (int n = threadIdx.x; n < Np; n += kRowThreads) {
     float d = 0.f;
     if (n < N) {
-      d = __bfloat162float(y[row * N + n]) - __bfloat162float(t[row * N + n]);
+      d = (__bfloat162float(y[row * N + n]) - (t ? __bfloat162float(t[row * N + n]) : 0.0f)) * inv_scale;
       s += d;
       q = fmaf(d, d, q);
     }
@@ -82,23 +82,24 @@ loss_rows_kernel(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __res
 
 // Same as loss_rows_kernel for N % 8 == 0 (then Np == N): one warp per row,
 // 16-byte loads (8 values) and stores, warp-shuffle sums in a fixed order.
+// With t == nullptr (an upstream gradient given) r = y·inv_scale.
 __global__ void __launch_bounds__(256)
 loss_rows_vec_kernel(const uint4* __restrict__ y, const uint4* __restrict__ t, uint4* __restrict__ r16,
-                     float* __restrict__ rsum, float* __restrict__ rsq, int n8, long long rows) {
+                     float* __restrict__ rsum, float* __restrict__ rsq, int n8, long long rows, float inv_scale) {
   const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   float s = 0.f, q = 0.f;
   for (int c = lane; c < n8; c += 32) {
-    const uint4 uy = __ldg(y + row * n8 + c), ut = __ldg(t + row * n8 + c);
+    const uint4 uy = __ldg(y + row * n8 + c), ut = t ? __ldg(t + row * n8 + c) : make_uint4(0, 0, 0, 0);
     const uint32_t* py = &uy.x;
     const uint32_t* pt = &ut.x;
     uint4 r;
     uint32_t* pr = &r.x;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float d0 = __uint_as_float(py[e] << 16) - __uint_as_float(pt[e] << 16);
-      const float d1 = __uint_as_float(py[e] & 0xffff0000u) - __uint_as_float(pt[e] & 0xffff0000u);
+      const float d0 = (__uint_as_float(py[e] << 16) - __uint_as_float(pt[e] << 16)) * inv_scale;
+      const float d1 = (__uint_as_float(py[e] & 0xffff0000u) - __uint_as_float(pt[e] & 0xffff0000u)) * inv_scale;
       s += d0 + d1;
       q = fmaf(d0, d0, fmaf(d1, d1, q));
       const __half2 h = __floats2half2_rn(d0, d1);
@@ -403,7 +404,7 @@ int grid_for(long long n) { return (int)std::min<long long>(std::max<long long>(
 struct TrainWs {
   PsaTcOffsets fwd;
   size_t lse, r16, rsum, rsq, dA16, part_wproj, part_wqkv, part_wpe, part_bqkv, part_bpe, fa, dqkv16, x16, wqkv16,
-      total;
+      y16, lossd, total;
 };
 
 TrainWs train_layout(int B, int H, int W) {
@@ -428,6 +429,8 @@ TrainWs train_layout(int B, int H, int W) {
   w.dqkv16 = take((size_t)B * kQKV * Np * 2);
   w.x16 = take((size_t)B * kC * Np * 2);
   w.wqkv16 = take((size_t)kQKV * kC * 2);
+  w.y16 = take((size_t)B * kC * N * 2);  // the recomputed forward output when only dy is given
+  w.lossd = take(4);
   w.total = off;
   return w;
 }
@@ -439,13 +442,23 @@ size_t psa_train_workspace_bytes(int B, int H, int W) {
   return train_layout(B, H, W).total;
 }
 
+// Two modes.  Loss mode (target given): loss = mean((y − t)²), r = y − t and
+// σ = 2/numel.  Gradient mode (target == nullptr, dy given): the upstream
+// gradient ∂L/∂y arrives as dy; r = dy / dy_scale keeps it in f16's normal
+// range and σ = dy_scale restores the scale when the gradients are stored;
+// y and loss then go to the workspace.
 int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const __nv_bfloat16* w_qkv,
                       const float* b_qkv, const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
                       const float* b_proj, __nv_bfloat16* y, __nv_bfloat16* dx, float* grads, float* loss, int B,
-                      int C, int H, int W, int nh, int kd, void* ws, size_t ws_bytes, cudaStream_t st) {
+                      int C, int H, int W, int nh, int kd, void* ws, size_t ws_bytes, cudaStream_t st,
+                      const __nv_bfloat16* dy = nullptr, float dy_scale = 1.0f) {
   VA_CHECK_ARG(psa_tc_is_n(C, nh, kd), "psa train: needs C=128, nh=2, kd=32");
   VA_CHECK_ARG(B > 0 && H > 0 && W > 0 && B <= 65535, "psa train: bad sizes");
-  VA_CHECK_ARG(target && grads && loss && y, "psa train: null target/grads/loss/y");
+  const bool grad_mode = target == nullptr;
+  if (grad_mode)
+    VA_CHECK_ARG(x && dy && grads && dy_scale > 0.0f, "psa attention backward: null x/dy/grads or dy_scale <= 0");
+  else
+    VA_CHECK_ARG(x && target && grads && loss && y, "psa train: null x/target/grads/loss/y");
   const int N = H * W, Np = (N + 7) / 8 * 8, BH = B * nh;
   VA_CHECK_ARG(2 * (size_t)N * sizeof(float) <= 200 * 1024, "psa train: %d tokens per image exceed the staged planes",
                N);
@@ -455,6 +468,10 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   if (reinterpret_cast<uintptr_t>(ws) & 255) return set_error(VA_ERR_ALIGN, "psa train: workspace needs 256-byte alignment");
   char* base = static_cast<char*>(ws);
   auto at = [&](size_t o) { return static_cast<void*>(base + o); };
+  if (grad_mode) {
+    y = static_cast<__nv_bfloat16*>(at(L.y16));
+    loss = static_cast<float*>(at(L.lossd));
+  }
   float* lse = static_cast<float*>(at(L.lse));
   // forward, keeping Q/K/V/O/PE and the row LSEs
   if (int rc = psa_attention_fwd_tc(x, w_qkv, b_qkv, w_pe, b_pe, w_proj, b_proj, y, B, C, H, W, nh, kd, ws,
@@ -467,18 +484,20 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   const __half* wp16 = static_cast<const __half*>(at(L.fwd.wproj));
   const long long rows = (long long)B * kC;
   const double numel = (double)rows * N;
-  const float sigma = (float)(2.0 / numel);
+  const float sigma = grad_mode ? dy_scale : (float)(2.0 / numel);
+  const __nv_bfloat16* r_src = grad_mode ? dy : y;  // r = (r_src − target)·inv_scale
+  const float inv_scale = grad_mode ? 1.0f / dy_scale : 1.0f;
   const int Pz = (B + kZFold - 1) / kZFold;
 
   __half* r16 = static_cast<__half*>(at(L.r16));
   float* rsum = static_cast<float*>(at(L.rsum));
   float* rsq = static_cast<float*>(at(L.rsq));
-  if (N % 8 == 0 && !((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(target)) & 15))
+  if (N % 8 == 0 && !((reinterpret_cast<uintptr_t>(r_src) | reinterpret_cast<uintptr_t>(target)) & 15))
     loss_rows_vec_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
-        reinterpret_cast<const uint4*>(y), reinterpret_cast<const uint4*>(target), reinterpret_cast<uint4*>(r16), rsum,
-        rsq, N / 8, rows);
+        reinterpret_cast<const uint4*>(r_src), reinterpret_cast<const uint4*>(target), reinterpret_cast<uint4*>(r16),
+        rsum, rsq, N / 8, rows, inv_scale);
   else
-    loss_rows_kernel<<<(unsigned)rows, kRowThreads, 0, st>>>(y, target, r16, rsum, rsq, N, Np);
+    loss_rows_kernel<<<(unsigned)rows, kRowThreads, 0, st>>>(r_src, target, r16, rsum, rsq, N, Np, inv_scale);
   if (int rc = check_launch("psa train loss")) return rc;
   // dW_proj partials: Pz from O, then Pz from PE (kZFold images per accumulator)
   float* pwp = static_cast<float*>(at(L.part_wproj));
@@ -600,6 +619,18 @@ int va_psa_train_fwd_bwd_bf16(const va_bf16* x, const va_bf16* target, const va_
                            (const __nv_bfloat16*)w_pe, b_pe, (const __nv_bfloat16*)w_proj, b_proj, (__nv_bfloat16*)y,
                            (__nv_bfloat16*)dx, grads, loss, B, C, H, W, num_heads, key_dim, workspace, ws_bytes,
                            (cudaStream_t)stream);
+}
+
+size_t va_psa_attention_bwd_workspace_bytes(int B, int H, int W) { return psa_train_workspace_bytes(B, H, W); }
+
+int va_psa_attention_bwd_bf16(const va_bf16* x, const va_bf16* dy, float dy_scale, const va_bf16* w_qkv,
+                              const float* b_qkv, const va_bf16* w_pe, const float* b_pe, const va_bf16* w_proj,
+                              const float* b_proj, va_bf16* dx, float* grads, int B, int C, int H, int W,
+                              int num_heads, int key_dim, void* workspace, size_t ws_bytes, va_stream_t stream) {
+  return psa_train_fwd_bwd((const __nv_bfloat16*)x, nullptr, (const __nv_bfloat16*)w_qkv, b_qkv,
+                           (const __nv_bfloat16*)w_pe, b_pe, (const __nv_bfloat16*)w_proj, b_proj, nullptr,
+                           (__nv_bfloat16*)dx, grads, nullptr, B, C, H, W, num_heads, key_dim, workspace, ws_bytes,
+                           (cudaStream_t)stream, (const __nv_bfloat16*)dy, dy_scale);
 }
 
 int va_psa_sgd_update(float* master, const float* grads, float lr, float grad_scale, va_bf16* w_qkv, float* b_qkv,

@@ -156,6 +156,25 @@ class PeerGradComm:
             raise RuntimeError(f"peer all-reduce on rank {self.rank}: status {st} at close")
 
 
+def attention_backward(x, dy, params: dict, dy_scale: float = 1.0, want_dx: bool = True, workspace=None,
+                       stream=None):
+    """Backward of the fused bf16 PSA Attention op for an upstream gradient
+    dy = ∂L/∂y (``va_psa_attention_bwd_bf16``): returns ``(grads, dx)`` —
+    grads f32 ``[VA_PSA_GRAD_COUNT]`` in the gradient-buffer layout, dx bf16
+    or None.  Pass dy_scale ≈ max|dy| so that dy/dy_scale is O(1)."""
+    B, C, H, W = x.shape
+    need = int(_lib.lib().va_psa_attention_bwd_workspace_bytes(B, H, W))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    grads = torch.empty(GRAD_COUNT, dtype=torch.float32, device=x.device)
+    dx = torch.empty_like(x) if want_dx else None
+    _lib.call("va_psa_attention_bwd_bf16", _p(x), _p(dy), float(dy_scale), _p(params["w_qkv"]), _p(params["b_qkv"]),
+              _p(params["w_pe"]), _p(params["b_pe"]), _p(params["w_proj"]), _p(params["b_proj"]),
+              _p(dx) if dx is not None else None, _p(grads), B, C, H, W, 2, 32, _p(workspace), workspace.numel(),
+              _stream(stream))
+    return grads, dx
+
+
 def dp_train_step(step: PsaTrainStep, x, target, params: dict, master, lr: float, group=None,
                   comm: PeerGradComm | None = None):
     """One data-parallel step: local fwd+bwd, all-reduce (sum) of the f32
