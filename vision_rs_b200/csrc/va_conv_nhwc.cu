@@ -51,6 +51,9 @@ constexpr int kCvM = 128, kCvTW = 16, kCvTH = 8, kCvMaxStages = 32;
 constexpr int kCvEpiWarps = 8, kCvThreads = 64 + 32 * kCvEpiWarps;  // producer, MMA, 8 epilogue warps
 constexpr int kCvAcc = 4;  // TMEM accumulator buffers (4 × BN ≤ 512 columns)
 constexpr int kHaloRows = (kCvTH + 2) * kCvTW;  // 3×3 stride-1 halo tile: 10 input rows × 16 columns
+// 3×3 stride 2: the even input rows 2·oy0 − 1 … 2·oy0 + 15 (9 rows, taps ky = 0 and 2) and the odd
+// rows 2·oy0 … 2·oy0 + 16 (9 rows loaded, 8 used, tap ky = 1), 16 strided columns each
+constexpr int kHalo2Rows = 9 * kCvTW;
 
 // Barriers and bookkeeping behind the operand ring in dynamic shared memory.
 struct ConvCtl {
@@ -85,7 +88,8 @@ struct ConvGeom {
   int Ho, Wo, Cin, Cout, ksize, stride, act, linear;
   int tiles_w, tiles_h, n_tiles, total_tiles, stages;
   int wres;          // the CTA's whole weight slice [BN][k·k·Cin] stays in shared memory
-  int halo;          // 3×3 stride 1: one 10-row halo load per (channel block, kx) serves ky = 0, 1, 2
+  int halo;          // 1: 3×3 stride 1, one 10-row halo load per (channel block, kx) serves ky = 0, 1, 2;
+                     // 2: 3×3 stride 2, an even-row and an odd-row load per (channel block, kx)
   long long pixels;  // B·Ho·Wo
 };
 
@@ -140,7 +144,7 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
   uint8_t* stg = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = stg + kCvEpiWarps * 2 * 32 * kRowBytes;
   // A stage: 128 pixel rows, or in halo mode 160 rows (10 input rows × 16 columns).
-  const int aBytes = g.halo ? kHaloRows * KB * 2 : kABytes;
+  const int aBytes = g.halo == 1 ? kHaloRows * KB * 2 : g.halo == 2 ? 2 * kHalo2Rows * KB * 2 : kABytes;
   uint8_t* sb = sa + g.stages * aBytes;  // weight ring, or the resident slice
   const int pad = g.ksize / 2, cblocks = (g.Cin + KB - 1) / KB, nk = g.ksize * g.ksize * cblocks;
   const int nq = g.halo ? 3 * cblocks : nk;  // ring stages per tile
@@ -195,10 +199,18 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
           const long long round = q / S;
           if (round > 0 && !(ok = mbar_wait(&c.empty[st], (uint32_t)((round - 1) & 1), &c.abort, &g_conv_status, 1)))
             break;
-          if (g.halo) {  // stage kb = (channel block kb / 3, kx = kb % 3): input rows oy0 − 1 … oy0 + 8
+          if (g.halo == 1) {  // stage kb = (channel block kb / 3, kx = kb % 3): input rows oy0 − 1 … oy0 + 8
             const int cb = kb / 3, kx = kb - 3 * cb;
             mbar_arrive_expect_tx(&c.full[st], aBytes);
             tma_load_4d(sa + st * aBytes, &map_x, &c.full[st], cb * KB, ox0 + kx - 1, oy0 - 1, b);
+            continue;
+          }
+          if (g.halo == 2) {  // even rows from 2·oy0 − 1, odd rows from 2·oy0 (element stride 2 in y and x)
+            const int cb = kb / 3, kx = kb - 3 * cb;
+            mbar_arrive_expect_tx(&c.full[st], aBytes);
+            uint8_t* dst = sa + st * aBytes;
+            tma_load_4d(dst, &map_x, &c.full[st], cb * KB, 2 * ox0 + kx - 1, 2 * oy0 - 1, b);
+            tma_load_4d(dst + kHalo2Rows * KB * 2, &map_x, &c.full[st], cb * KB, 2 * ox0 + kx - 1, 2 * oy0, b);
             continue;
           }
           const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * KB, ky = tap / g.ksize, kx = tap - ky * g.ksize;
@@ -246,11 +258,14 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
           tc_fence_after();
           const uint64_t da = da0 + (uint64_t)((st * aBytes) >> 4);
           if (g.halo) {
-            // Output row r of tap (ky, kx) reads halo row r + 16·ky: the A operand
-            // starts 16·ky rows in (a whole number of swizzle atoms).
+            // Stride 1: output row r of tap (ky, kx) reads halo row r + 16·ky.
+            // Stride 2: ky = 0 → even rows from row 0, ky = 2 → even rows from
+            // row 16, ky = 1 → the odd rows (144 rows in).  Every start is a
+            // whole number of swizzle atoms.
             const int cb = kb / 3, kx = kb - 3 * cb;
             for (int ky = 0; ky < 3; ++ky) {
-              const uint64_t dak = da + (uint64_t)((16 * ky * KB * 2) >> 4);
+              const int row0 = g.halo == 1 ? 16 * ky : ky == 1 ? kHalo2Rows : 8 * ky;
+              const uint64_t dak = da + (uint64_t)((row0 * KB * 2) >> 4);
               const uint64_t db = db0 + (uint64_t)((((ky * 3 + kx) * cblocks + cb) * kBBytes) >> 4);
 #pragma unroll
               for (int s = 0; s < KB / 16; ++s)
@@ -443,9 +458,10 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
   // Resident weight slice when it leaves room for the activation ring.
   g.wres = (nk * b_bytes <= 96 * 1024 && g.n_tiles <= sms) ? 1 : 0;
   const int half_cols = BN >= 32 ? BN / 2 : BN, stg_bytes = kCvEpiWarps * 2 * 32 * 2 * half_cols;
-  g.halo = (k == 3 && s == 1 && g.wres) ? 1 : 0;
+  g.halo = (k == 3 && g.wres) ? s : 0;
   const int ring_budget = 200 * 1024 - stg_bytes - (g.wres ? nk * b_bytes : 0);
-  const int stage_bytes = g.halo ? kHaloRows * KB * 2 : g.wres ? a_bytes : a_bytes + b_bytes;
+  const int stage_bytes = g.halo == 1 ? kHaloRows * KB * 2 : g.halo == 2 ? 2 * kHalo2Rows * KB * 2
+                        : g.wres ? a_bytes : a_bytes + b_bytes;
   g.stages = std::max(2, std::min(kCvMaxStages, ring_budget / stage_bytes));
   auto fn = conv_encode_fn();
   if (!fn) return set_error(VA_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
@@ -461,7 +477,8 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
   } else {
     const uint64_t d[4] = {(uint64_t)Cin, (uint64_t)W, (uint64_t)H, (uint64_t)B};
     const uint64_t str[3] = {(uint64_t)Cin * 2, (uint64_t)W * Cin * 2, (uint64_t)H * W * Cin * 2};
-    const uint32_t box[4] = {(uint32_t)KB, (uint32_t)(kCvTW * s), (uint32_t)(g.halo ? kCvTH + 2 : kCvTH * s), 1};
+    const uint32_t box[4] = {(uint32_t)KB, (uint32_t)(kCvTW * s),
+                             (uint32_t)(g.halo == 1 ? kCvTH + 2 : g.halo == 2 ? 18 : kCvTH * s), 1};
     const uint32_t es[4] = {1, (uint32_t)s, (uint32_t)s, 1};
     r = fn(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<__nv_bfloat16*>(x), d, str, box, es,
            CU_TENSOR_MAP_INTERLEAVE_NONE, tma_swizzle(KB), CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
