@@ -180,7 +180,9 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
       tma_prefetch_desc(&map_x);
       tma_prefetch_desc(&map_w);
       tma_prefetch_desc(&map_y);
-      long long q = 0;  // operand ring slot counter across tiles
+      long long q = 0;      // operand ring slots filled so far (across tiles)
+      int st = 0;           // = q % S, kept incrementally: no 64-bit division per stage
+      uint32_t ph = 0;      // = (q / S) & 1
       bool ok = true;
       if (g.wres && (int)blockIdx.x < g.total_tiles) {
         const int n0 = ((int)blockIdx.x % g.n_tiles) * BN;
@@ -194,11 +196,8 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
         int b, oy0, ox0, n0;
         long long m0;
         conv_tile(g, t, BN, b, oy0, ox0, m0, n0);
-        for (int kb = 0; kb < nq; ++kb, ++q) {
-          const int st = (int)(q % S);
-          const long long round = q / S;
-          if (round > 0 && !(ok = mbar_wait(&c.empty[st], (uint32_t)((round - 1) & 1), &c.abort, &g_conv_status, 1)))
-            break;
+        for (int kb = 0; kb < nq; ++kb, ++q, st = st + 1 == S ? 0 : st + 1, ph ^= st == 0 ? 1u : 0u) {
+          if (q >= S && !(ok = mbar_wait(&c.empty[st], ph ^ 1u, &c.abort, &g_conv_status, 1))) break;
           if (g.halo == 1) {  // stage kb = (channel block kb / 3, kx = kb % 3): input rows oy0 − 1 … oy0 + 8
             const int cb = kb / 3, kx = kb - 3 * cb;
             mbar_arrive_expect_tx(&c.full[st], aBytes);
@@ -237,56 +236,60 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
       }
     }
   } else if (warp == 1) {  // ── MMA issuer ──
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f32acc(kCvM, BN, AB_BF16, false, false);
-      const uint64_t da0 = sdesc(smem_u32(sa), 16, KbTraits<KB>::sbo, KbTraits<KB>::swz);
-      const uint64_t db0 = sdesc(smem_u32(sb), 16, KbTraits<KB>::sbo, KbTraits<KB>::swz);
-      long long q = 0;
-      bool ok = true;
-      if (g.wres && (int)blockIdx.x < g.total_tiles)
-        ok = mbar_wait(&c.wfull, 0, &c.abort, &g_conv_status, 5);
-      int i = 0;
-      for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x, ++i) {
-        const int buf = i % kCvAcc, use = i / kCvAcc;
-        if (use > 0 && !(ok = mbar_wait(&c.acc_empty[buf], (uint32_t)((use - 1) & 1), &c.abort, &g_conv_status, 2)))
-          break;
+    // The whole warp runs the loop converged (waits made warp-uniform) and one
+    // elected lane issues each tcgen05.mma / commit: a lone diverged lane
+    // issues these small MMAs markedly slower.
+    constexpr uint32_t idesc = idesc_f32acc(kCvM, BN, AB_BF16, false, false);
+    const uint64_t da0 = sdesc(smem_u32(sa), 16, KbTraits<KB>::sbo, KbTraits<KB>::swz);
+    const uint64_t db0 = sdesc(smem_u32(sb), 16, KbTraits<KB>::sbo, KbTraits<KB>::swz);
+    int st = 0;       // ring slot, = (stages consumed) % S
+    uint32_t ph = 0;  // its fill parity
+    bool ok = true;
+    if (g.wres && (int)blockIdx.x < g.total_tiles)
+      ok = __all_sync(0xffffffffu, mbar_wait(&c.wfull, 0, &c.abort, &g_conv_status, 5));
+    int i = 0;
+    for (int t = blockIdx.x; t < g.total_tiles && ok; t += gridDim.x, ++i) {
+      const int buf = i % kCvAcc, use = i / kCvAcc;
+      if (use > 0 &&
+          !(ok = __all_sync(0xffffffffu,
+                            mbar_wait(&c.acc_empty[buf], (uint32_t)((use - 1) & 1), &c.abort, &g_conv_status, 2))))
+        break;
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)(buf * BN);
+      for (int kb = 0; kb < nq; ++kb, st = st + 1 == S ? 0 : st + 1, ph ^= st == 0 ? 1u : 0u) {
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&c.full[st], ph, &c.abort, &g_conv_status, 3)))) break;
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * BN);
-        for (int kb = 0; kb < nq; ++kb, ++q) {
-          const int st = (int)(q % S);
-          if (!(ok = mbar_wait(&c.full[st], (uint32_t)((q / S) & 1), &c.abort, &g_conv_status, 3))) break;
-          tc_fence_after();
-          const uint64_t da = da0 + (uint64_t)((st * aBytes) >> 4);
-          if (g.halo) {
-            // Stride 1: output row r of tap (ky, kx) reads halo row r + 16·ky.
-            // Stride 2: ky = 0 → even rows from row 0, ky = 2 → even rows from
-            // row 16, ky = 1 → the odd rows (144 rows in).  Every start is a
-            // whole number of swizzle atoms.
-            const int cb = kb / 3, kx = kb - 3 * cb;
-            for (int ky = 0; ky < 3; ++ky) {
-              const int row0 = g.halo == 1 ? 16 * ky : ky == 1 ? kHalo2Rows : 8 * ky;
-              const uint64_t dak = da + (uint64_t)((row0 * KB * 2) >> 4);
-              const uint64_t db = db0 + (uint64_t)((((ky * 3 + kx) * cblocks + cb) * kBBytes) >> 4);
+        const uint64_t da = da0 + (uint64_t)((st * aBytes) >> 4);
+        if (g.halo) {
+          // Stride 1: output row r of tap (ky, kx) reads halo row r + 16·ky.
+          // Stride 2: ky = 0 → even rows from row 0, ky = 2 → even rows from
+          // row 16, ky = 1 → the odd rows (144 rows in).  Every start is a
+          // whole number of swizzle atoms.
+          const int cb = kb / 3, kx = kb - 3 * cb;
 #pragma unroll
-              for (int s = 0; s < KB / 16; ++s)
-                mma_ss(d, dak + 2 * s, db + 2 * s, idesc, (kb > 0 || ky > 0 || s > 0) ? 1u : 0u);
-            }
-            mma_commit(&c.empty[st]);
-            continue;
+          for (int ky = 0; ky < 3; ++ky) {
+            const int row0 = g.halo == 1 ? 16 * ky : ky == 1 ? kHalo2Rows : 8 * ky;
+            const uint64_t dak = da + (uint64_t)((row0 * KB * 2) >> 4);
+            const uint64_t db = db0 + (uint64_t)((((ky * 3 + kx) * cblocks + cb) * kBBytes) >> 4);
+#pragma unroll
+            for (int s = 0; s < KB / 16; ++s)
+              mma_ss_w(d, dak + 2 * s, db + 2 * s, idesc, (kb > 0 || ky > 0 || s > 0) ? 1u : 0u);
           }
-          const uint64_t db = db0 + (uint64_t)(((g.wres ? kb : st) * kBBytes) >> 4);
-#pragma unroll
-          for (int s = 0; s < KB / 16; ++s)  // +32 bytes per 16-channel k-step inside the swizzle atom
-            mma_ss(d, da + 2 * s, db + 2 * s, idesc, (kb > 0 || s > 0) ? 1u : 0u);
-          mma_commit(&c.empty[st]);
+          mma_commit_w(&c.empty[st]);
+          continue;
         }
-        if (ok) mma_commit(&c.acc_full[buf]);
+        const uint64_t db = db0 + (uint64_t)(((g.wres ? kb : st) * kBBytes) >> 4);
+#pragma unroll
+        for (int s = 0; s < KB / 16; ++s)  // +32 bytes per 16-channel k-step inside the swizzle atom
+          mma_ss_w(d, da + 2 * s, db + 2 * s, idesc, (kb > 0 || s > 0) ? 1u : 0u);
+        mma_commit_w(&c.empty[st]);
       }
-      // Nothing issued here may still be writing TMEM when it is freed.
-      mma_commit(&c.done);
-      const long long t0 = clock64();
-      while (!mbar_try_wait(&c.done, 0) && clock64() - t0 < kSpinCycles) {
-      }
+      if (ok) mma_commit_w(&c.acc_full[buf]);
+    }
+    // Nothing issued here may still be writing TMEM when it is freed.
+    mma_commit_w(&c.done);
+    const long long t0 = clock64();
+    while (!mbar_try_wait(&c.done, 0) && clock64() - t0 < kSpinCycles) {
     }
   } else {  // ── epilogue: warp (2..9) → TMEM lane quarter warp % 4, column half (warp − 2) / 4 ──
     const int quarter = warp & 3, half = (warp - 2) >> 2, ew = warp - 2;
@@ -298,19 +301,22 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
     int i = 0;
     for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++i) {
       const int buf = i % kCvAcc, use = i / kCvAcc;
-      const bool got = mbar_wait(&c.acc_full[buf], (uint32_t)(use & 1), &c.abort, &g_conv_status, 4);
-      if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform: the TMEM loads below are warp-collective
-      tc_fence_after();
       int b, oy0, ox0, n0;
       long long m0;
       conv_tile(g, t, BN, b, oy0, ox0, m0, n0);
-      uint32_t u[kHalfCols];
+      // The tile's bias is loaded before the wait for its accumulator, so the
+      // load latency hides behind the main loop instead of adding to each tile.
       float bv[kHalfCols];
       if (active) {
-        // Bias first (its loads overlap the TMEM reads), then the TMEM loads and one wait.
         const int nv = g.Cout - n0 - cbase;
 #pragma unroll
         for (int k = 0; k < kHalfCols; ++k) bv[k] = k < nv ? __ldg(bias + n0 + cbase + k) : 0.0f;
+      }
+      const bool got = mbar_wait(&c.acc_full[buf], (uint32_t)(use & 1), &c.abort, &g_conv_status, 4);
+      if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform: the TMEM loads below are warp-collective
+      tc_fence_after();
+      uint32_t u[kHalfCols];
+      if (active) {
         const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + cbase);
 #pragma unroll
         for (int cc = 0; cc < kHalfCols; cc += 16) tmem_ld16(ta + cc, *reinterpret_cast<uint32_t(*)[16]>(u + cc));
