@@ -93,10 +93,10 @@ struct ConvGeom {
   long long pixels;  // B·Ho·Wo
 };
 
-// Columns one epilogue warp drains (two warps share a TMEM lane quarter when BN ≥ 32).
+// Columns an epilogue warp drains per TMEM read: the whole tile up to 64, else 64 at a time.
 template <int BN>
 struct ConvCols {
-  static constexpr int half = BN >= 32 ? BN / 2 : BN;
+  static constexpr int chunk = BN < 64 ? BN : 64;
 };
 
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* m, const void* src, int c0, int c1, int c2, int c3) {
@@ -138,7 +138,7 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
                  __nv_bfloat16* __restrict__ y, const ConvGeom g) {
   extern __shared__ uint8_t smem_raw[];
   constexpr int kABytes = kCvM * KB * 2, kBBytes = BN * KB * 2;
-  constexpr int kHalfCols = ConvCols<BN>::half, kRowBytes = 2 * kHalfCols;
+  constexpr int kChunk = ConvCols<BN>::chunk, kRowBytes = 2 * kChunk;
   constexpr uint32_t kTmemCols = kCvAcc * BN < 32 ? 32 : kCvAcc * BN;
   // [staging: 8 warps × 2 × 32 rows × kRowBytes][A ring][B ring or resident slice][barriers]
   uint8_t* stg = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -159,7 +159,7 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
     }
     for (int i = 0; i < kCvAcc; ++i) {
       mbar_init(&c.acc_full[i], 1);
-      mbar_init(&c.acc_empty[i], kCvEpiWarps);
+      mbar_init(&c.acc_empty[i], 4);  // the four warps of the epilogue group that drains it
     }
     mbar_init(&c.done, 1);
     mbar_init(&c.wfull, 1);
@@ -291,44 +291,43 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
     const long long t0 = clock64();
     while (!mbar_try_wait(&c.done, 0) && clock64() - t0 < kSpinCycles) {
     }
-  } else {  // ── epilogue: warp (2..9) → TMEM lane quarter warp % 4, column half (warp − 2) / 4 ──
-    const int quarter = warp & 3, half = (warp - 2) >> 2, ew = warp - 2;
-    const bool active = BN >= 32 || half == 0;
-    const int cbase = BN >= 32 ? half * kHalfCols : 0;
+  } else {
+    // ── epilogue: two groups of four warps (2-5, 6-9) drain alternate tiles, so
+    // two accumulators are read out at once; within a group warp w reads TMEM
+    // lane quarter w % 4 (its 32 pixel rows) and all BN columns, kChunk at a time.
+    const int quarter = warp & 3, grp = (warp - 2) >> 2, ew = warp - 2;
     // Swizzled row of this lane in the staging tile: 16-byte chunk j lands at
     // chunk j ^ sw, the pattern TMA applies for a kRowBytes-wide swizzle.
     const int sw = ((lane * kRowBytes) >> 7) & (kRowBytes / 16 - 1);
-    int i = 0;
-    for (int t = blockIdx.x; t < g.total_tiles; t += gridDim.x, ++i) {
-      const int buf = i % kCvAcc, use = i / kCvAcc;
+    int nstore = 0;  // staging buffer use count of this warp
+    for (int i = grp;; i += 2) {
+      const long long tl = (long long)blockIdx.x + (long long)i * gridDim.x;
+      if (tl >= g.total_tiles) break;
+      const int t = (int)tl, buf = i % kCvAcc, use = i / kCvAcc;
       int b, oy0, ox0, n0;
       long long m0;
       conv_tile(g, t, BN, b, oy0, ox0, m0, n0);
-      // The tile's bias is loaded before the wait for its accumulator, so the
-      // load latency hides behind the main loop instead of adding to each tile.
-      float bv[kHalfCols];
-      if (active) {
-        const int nv = g.Cout - n0 - cbase;
-#pragma unroll
-        for (int k = 0; k < kHalfCols; ++k) bv[k] = k < nv ? __ldg(bias + n0 + cbase + k) : 0.0f;
-      }
       const bool got = mbar_wait(&c.acc_full[buf], (uint32_t)(use & 1), &c.abort, &g_conv_status, 4);
       if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform: the TMEM loads below are warp-collective
       tc_fence_after();
-      uint32_t u[kHalfCols];
-      if (active) {
-        const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + cbase);
+#pragma unroll 1
+      for (int cb = 0; cb < BN; cb += kChunk) {
+        const int nv = g.Cout - n0 - cb;  // live channels of this chunk (multiple of 8)
+        float bv[kChunk];
 #pragma unroll
-        for (int cc = 0; cc < kHalfCols; cc += 16) tmem_ld16(ta + cc, *reinterpret_cast<uint32_t(*)[16]>(u + cc));
+        for (int k = 0; k < kChunk; ++k) bv[k] = k < nv ? __ldg(bias + n0 + cb + k) : 0.0f;
+        uint32_t u[kChunk];
+        const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + cb);
+#pragma unroll
+        for (int cc = 0; cc < kChunk; cc += 16) tmem_ld16(ta + cc, *reinterpret_cast<uint32_t(*)[16]>(u + cc));
         tmem_ld_wait();
         reg_fence(u);
-      }
-      // The accumulator is in registers: hand it back to the MMA warp now.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&c.acc_empty[buf]);
-      if (active) {
-        uint4 outv[kRowBytes / 16];  // this lane's pixel: kHalfCols channels of bf16
+        if (cb + kChunk >= BN) {  // the accumulator is in registers: hand it back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&c.acc_empty[buf]);
+        }
+        uint4 outv[kRowBytes / 16];  // this lane's pixel: kChunk channels of bf16
 #pragma unroll
         for (int j = 0; j < kRowBytes / 16; ++j) {
           uint32_t q4[4];
@@ -345,7 +344,8 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
           outv[j] = make_uint4(q4[0], q4[1], q4[2], q4[3]);
         }
         if constexpr (kRowBytes >= 64) {  // staged in shared memory, written by a TMA store
-          uint8_t* stage = stg + (ew * 2 + (i & 1)) * (32 * kRowBytes);
+          uint8_t* stage = stg + (ew * 2 + (nstore & 1)) * (32 * kRowBytes);
+          ++nstore;
           if (lane == 0) tma_store_wait_read_1();  // this staging buffer's previous store has read it
           __syncwarp();
 #pragma unroll
@@ -353,11 +353,11 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
             *reinterpret_cast<uint4*>(stage + lane * kRowBytes + ((j ^ sw) << 4)) = outv[j];
           fence_proxy_async_smem();  // the staging writes become visible to the TMA store
           __syncwarp();
-          if (lane == 0) {  // 32 rows × kHalfCols channels; TMA drops what lies outside y
+          if (lane == 0) {  // 32 rows × kChunk channels; TMA drops what lies outside y
             if (g.linear)
-              tma_store_2d(&map_y, stage, n0 + cbase, (int)(m0 + quarter * 32));
+              tma_store_2d(&map_y, stage, n0 + cb, (int)(m0 + quarter * 32));
             else
-              tma_store_4d(&map_y, stage, n0 + cbase, ox0, oy0 + 2 * quarter, b);
+              tma_store_4d(&map_y, stage, n0 + cb, ox0, oy0 + 2 * quarter, b);
             tma_store_commit();
           }
         } else {  // rows of 32 bytes: plain stores from registers beat a TMA store of narrow rows
@@ -372,9 +372,8 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
             live = oy < g.Ho && ox < g.Wo;
             pix = ((long long)b * g.Ho + oy) * g.Wo + ox;
           }
-          const int nv = g.Cout - n0 - cbase;
           if (live) {
-            uint4* o = reinterpret_cast<uint4*>(y + pix * g.Cout + n0 + cbase);
+            uint4* o = reinterpret_cast<uint4*>(y + pix * g.Cout + n0 + cb);
 #pragma unroll
             for (int j = 0; j < kRowBytes / 16; ++j)
               if (8 * j < nv) o[j] = outv[j];
@@ -463,7 +462,7 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
   const int sms = sm_count();
   // Resident weight slice when it leaves room for the activation ring.
   g.wres = (nk * b_bytes <= 96 * 1024 && g.n_tiles <= sms) ? 1 : 0;
-  const int half_cols = BN >= 32 ? BN / 2 : BN, stg_bytes = kCvEpiWarps * 2 * 32 * 2 * half_cols;
+  const int chunk_cols = BN < 64 ? BN : 64, stg_bytes = kCvEpiWarps * 2 * 32 * 2 * chunk_cols;
   g.halo = (k == 3 && g.wres) ? s : 0;
   const int ring_budget = 200 * 1024 - stg_bytes - (g.wres ? nk * b_bytes : 0);
   const int stage_bytes = g.halo == 1 ? kHaloRows * KB * 2 : g.halo == 2 ? 2 * kHalo2Rows * KB * 2
@@ -501,18 +500,18 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
     if (r != CUDA_SUCCESS) return set_error(VA_ERR_ALIGN, "conv nhwc: tensor map for w rejected (CUresult %d)", (int)r);
   }
   // With resident weights a CTA keeps one channel tile: the grid is a multiple of n_tiles.
-  {  // y: tiles of 32 output rows × half_cols channels, stored from the staging buffers
-    const CUtensorMapSwizzle swz = tma_swizzle(half_cols);
+  {  // y: tiles of 32 output rows × chunk_cols channels, stored from the staging buffers
+    const CUtensorMapSwizzle swz = tma_swizzle(chunk_cols);
     if (g.linear) {
       const uint64_t d[2] = {(uint64_t)Cout, (uint64_t)g.pixels};
       const uint64_t str[1] = {(uint64_t)Cout * 2};
-      const uint32_t box[2] = {(uint32_t)half_cols, 32}, es[2] = {1, 1};
+      const uint32_t box[2] = {(uint32_t)chunk_cols, 32}, es[2] = {1, 1};
       r = fn(&my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, d, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     } else {
       const uint64_t d[4] = {(uint64_t)Cout, (uint64_t)Wo, (uint64_t)Ho, (uint64_t)B};
       const uint64_t str[3] = {(uint64_t)Cout * 2, (uint64_t)Wo * Cout * 2, (uint64_t)Ho * Wo * Cout * 2};
-      const uint32_t box[4] = {(uint32_t)half_cols, (uint32_t)kCvTW, 2, 1}, es[4] = {1, 1, 1, 1};
+      const uint32_t box[4] = {(uint32_t)chunk_cols, (uint32_t)kCvTW, 2, 1}, es[4] = {1, 1, 1, 1};
       r = fn(&my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, y, d, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
