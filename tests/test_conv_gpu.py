@@ -58,6 +58,8 @@ CASES = [  # B, Cin, H, W, Cout, k, s, act
     (2, 48, 6, 6, 32, 1, 2, False),       # 1×1 with stride 2
     (1, 96, 33, 17, 192, 3, 1, True),     # KB = 32, BN = 64
     (1, 64, 80, 80, 64, 3, 1, True),      # several tiles in both directions
+    (2, 16, 40, 24, 16, 3, 1, True),      # 4 stacked subtiles per tile, ragged last tile row
+    (1, 32, 24, 20, 32, 3, 1, True),      # 2 stacked subtiles per tile
 ]
 
 

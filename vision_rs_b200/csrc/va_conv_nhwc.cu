@@ -50,7 +50,6 @@ namespace {
 constexpr int kCvM = 128, kCvTW = 16, kCvTH = 8, kCvMaxStages = 32;
 constexpr int kCvEpiWarps = 8, kCvThreads = 64 + 32 * kCvEpiWarps;  // producer, MMA, 8 epilogue warps
 constexpr int kCvAcc = 4;  // TMEM accumulator buffers (4 × BN ≤ 512 columns)
-constexpr int kHaloRows = (kCvTH + 2) * kCvTW;  // 3×3 stride-1 halo tile: 10 input rows × 16 columns
 // 3×3 stride 2: the even input rows 2·oy0 − 1 … 2·oy0 + 15 (9 rows, taps ky = 0 and 2) and the odd
 // rows 2·oy0 … 2·oy0 + 16 (9 rows loaded, 8 used, tap ky = 1), 16 strided columns each
 constexpr int kHalo2Rows = 9 * kCvTW;
@@ -88,7 +87,9 @@ struct ConvGeom {
   int Ho, Wo, Cin, Cout, ksize, stride, act, linear;
   int tiles_w, tiles_h, n_tiles, total_tiles, stages;
   int wres;          // the CTA's whole weight slice [BN][k·k·Cin] stays in shared memory
-  int halo;          // 1: 3×3 stride 1, one 10-row halo load per (channel block, kx) serves ky = 0, 1, 2;
+  int th;            // subtiles per tile: 1, or 2 / 4 (stacked 8-row subtiles) in stride-1 halo mode
+  int halo;          // 1: 3×3 stride 1, one (8·th + 2)-row halo load per (channel block, kx) serves every
+                     //    subtile and ky = 0, 1, 2;
                      // 2: 3×3 stride 2, an even-row and an odd-row load per (channel block, kx)
   long long pixels;  // B·Ho·Wo
 };
@@ -118,7 +119,7 @@ __device__ __forceinline__ void conv_tile(const ConvGeom& g, int t, int bn, int&
   }
   ox0 = (r % g.tiles_w) * kCvTW;
   r /= g.tiles_w;
-  oy0 = (r % g.tiles_h) * kCvTH;
+  oy0 = (r % g.tiles_h) * (kCvTH * g.th);
   b = r / g.tiles_h;
   m0 = 0;
 }
@@ -139,12 +140,13 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
   extern __shared__ uint8_t smem_raw[];
   constexpr int kABytes = kCvM * KB * 2, kBBytes = BN * KB * 2;
   constexpr int kChunk = ConvCols<BN>::chunk, kRowBytes = 2 * kChunk;
-  constexpr uint32_t kTmemCols = kCvAcc * BN < 32 ? 32 : kCvAcc * BN;
+  constexpr uint32_t kTmemCols = 512;  // 4 accumulator slots × th subtiles × BN columns ≤ 512 (one CTA per SM)
   // [staging: 8 warps × 2 × 32 rows × kRowBytes][A ring][B ring or resident slice][barriers]
   uint8_t* stg = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = stg + kCvEpiWarps * 2 * 32 * kRowBytes;
   // A stage: 128 pixel rows, or in halo mode 160 rows (10 input rows × 16 columns).
-  const int aBytes = g.halo == 1 ? kHaloRows * KB * 2 : g.halo == 2 ? 2 * kHalo2Rows * KB * 2 : kABytes;
+  const int aBytes = g.halo == 1 ? (kCvTH * g.th + 2) * kCvTW * KB * 2
+                   : g.halo == 2 ? 2 * kHalo2Rows * KB * 2 : kABytes;
   uint8_t* sb = sa + g.stages * aBytes;  // weight ring, or the resident slice
   const int pad = g.ksize / 2, cblocks = (g.Cin + KB - 1) / KB, nk = g.ksize * g.ksize * cblocks;
   const int nq = g.halo ? 3 * cblocks : nk;  // ring stages per tile
@@ -159,7 +161,7 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
     }
     for (int i = 0; i < kCvAcc; ++i) {
       mbar_init(&c.acc_full[i], 1);
-      mbar_init(&c.acc_empty[i], 4);  // the four warps of the epilogue group that drains it
+      mbar_init(&c.acc_empty[i], g.th == 1 ? 4 : 8);  // the epilogue warps that drain it
     }
     mbar_init(&c.done, 1);
     mbar_init(&c.wfull, 1);
@@ -255,7 +257,7 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
                             mbar_wait(&c.acc_empty[buf], (uint32_t)((use - 1) & 1), &c.abort, &g_conv_status, 2))))
         break;
       tc_fence_after();
-      const uint32_t d = tmem + (uint32_t)(buf * BN);
+      const uint32_t d = tmem + (uint32_t)(buf * g.th * BN);
       for (int kb = 0; kb < nq; ++kb, st = st + 1 == S ? 0 : st + 1, ph ^= st == 0 ? 1u : 0u) {
         if (!(ok = __all_sync(0xffffffffu, mbar_wait(&c.full[st], ph, &c.abort, &g_conv_status, 3)))) break;
         tc_fence_after();
@@ -266,14 +268,17 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
           // row 16, ky = 1 → the odd rows (144 rows in).  Every start is a
           // whole number of swizzle atoms.
           const int cb = kb / 3, kx = kb - 3 * cb;
+          for (int sub = 0; sub < g.th; ++sub) {  // subtile sub: output rows 8·sub … 8·sub + 7 of the tile
 #pragma unroll
-          for (int ky = 0; ky < 3; ++ky) {
-            const int row0 = g.halo == 1 ? 16 * ky : ky == 1 ? kHalo2Rows : 8 * ky;
-            const uint64_t dak = da + (uint64_t)((row0 * KB * 2) >> 4);
-            const uint64_t db = db0 + (uint64_t)((((ky * 3 + kx) * cblocks + cb) * kBBytes) >> 4);
+            for (int ky = 0; ky < 3; ++ky) {
+              const int row0 = g.halo == 1 ? 16 * (8 * sub + ky) : ky == 1 ? kHalo2Rows : 8 * ky;
+              const uint64_t dak = da + (uint64_t)((row0 * KB * 2) >> 4);
+              const uint64_t db = db0 + (uint64_t)((((ky * 3 + kx) * cblocks + cb) * kBBytes) >> 4);
 #pragma unroll
-            for (int s = 0; s < KB / 16; ++s)
-              mma_ss_w(d, dak + 2 * s, db + 2 * s, idesc, (kb > 0 || ky > 0 || s > 0) ? 1u : 0u);
+              for (int s = 0; s < KB / 16; ++s)
+                mma_ss_w(d + (uint32_t)(sub * BN), dak + 2 * s, db + 2 * s, idesc,
+                         (kb > 0 || ky > 0 || s > 0) ? 1u : 0u);
+            }
           }
           mma_commit_w(&c.empty[st]);
           continue;
@@ -292,37 +297,44 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
     while (!mbar_try_wait(&c.done, 0) && clock64() - t0 < kSpinCycles) {
     }
   } else {
-    // ── epilogue: two groups of four warps (2-5, 6-9) drain alternate tiles, so
-    // two accumulators are read out at once; within a group warp w reads TMEM
-    // lane quarter w % 4 (its 32 pixel rows) and all BN columns, kChunk at a time.
+    // ── epilogue: two groups of four warps (2-5, 6-9).  With one subtile per
+    // tile they drain alternate tiles, so two accumulators are read out at
+    // once; with th subtiles group e drains subtiles e, e + 2, … of every tile.
+    // Warp w reads TMEM lane quarter w % 4 (32 pixel rows of a subtile) and all
+    // BN columns, kChunk at a time.
     const int quarter = warp & 3, grp = (warp - 2) >> 2, ew = warp - 2;
+    const bool alt = g.th == 1;  // alternate tiles between the groups
     // Swizzled row of this lane in the staging tile: 16-byte chunk j lands at
     // chunk j ^ sw, the pattern TMA applies for a kRowBytes-wide swizzle.
     const int sw = ((lane * kRowBytes) >> 7) & (kRowBytes / 16 - 1);
     int nstore = 0;  // staging buffer use count of this warp
-    for (int i = grp;; i += 2) {
+    for (int i = alt ? grp : 0;; i += alt ? 2 : 1) {
       const long long tl = (long long)blockIdx.x + (long long)i * gridDim.x;
       if (tl >= g.total_tiles) break;
       const int t = (int)tl, buf = i % kCvAcc, use = i / kCvAcc;
-      int b, oy0, ox0, n0;
+      int b, oy0t, ox0, n0;
       long long m0;
-      conv_tile(g, t, BN, b, oy0, ox0, m0, n0);
+      conv_tile(g, t, BN, b, oy0t, ox0, m0, n0);
       const bool got = mbar_wait(&c.acc_full[buf], (uint32_t)(use & 1), &c.abort, &g_conv_status, 4);
       if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform: the TMEM loads below are warp-collective
       tc_fence_after();
+      const int sub0 = alt ? 0 : grp, sstep = alt ? 1 : 2;
+#pragma unroll 1
+      for (int sub = sub0; sub < g.th; sub += sstep)
 #pragma unroll 1
       for (int cb = 0; cb < BN; cb += kChunk) {
+        const int oy0 = oy0t + kCvTH * sub;  // first output row of this subtile
         const int nv = g.Cout - n0 - cb;  // live channels of this chunk (multiple of 8)
         float bv[kChunk];
 #pragma unroll
         for (int k = 0; k < kChunk; ++k) bv[k] = k < nv ? __ldg(bias + n0 + cb + k) : 0.0f;
         uint32_t u[kChunk];
-        const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + cb);
+        const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)((buf * g.th + sub) * BN + cb);
 #pragma unroll
         for (int cc = 0; cc < kChunk; cc += 16) tmem_ld16(ta + cc, *reinterpret_cast<uint32_t(*)[16]>(u + cc));
         tmem_ld_wait();
         reg_fence(u);
-        if (cb + kChunk >= BN) {  // the accumulator is in registers: hand it back to the MMA warp
+        if (cb + kChunk >= BN && sub + sstep >= g.th) {  // this warp's last read of the accumulator
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&c.acc_empty[buf]);
@@ -453,6 +465,7 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
   g.pixels = (long long)B * Ho * Wo;
   g.n_tiles = (Cout + BN - 1) / BN;
   g.tiles_w = (Wo + kCvTW - 1) / kCvTW;
+  g.th = 1;  // set below for the stride-1 halo mode
   g.tiles_h = (Ho + kCvTH - 1) / kCvTH;
   const long long tiles = g.linear ? (g.pixels + kCvM - 1) / kCvM * g.n_tiles
                                    : (long long)g.tiles_w * g.tiles_h * B * g.n_tiles;
@@ -464,8 +477,18 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
   g.wres = (nk * b_bytes <= 96 * 1024 && g.n_tiles <= sms) ? 1 : 0;
   const int chunk_cols = BN < 64 ? BN : 64, stg_bytes = kCvEpiWarps * 2 * 32 * 2 * chunk_cols;
   g.halo = (k == 3 && g.wres) ? s : 0;
+  if (g.halo == 1) {
+    // Narrow convs: stack 2 or 4 subtiles per tile so that each pipeline stage
+    // (one halo load, th·3 MMAs) carries more work; 4 slots × th × BN ≤ 512 TMEM
+    // columns, and no taller than the map needs.
+    g.th = BN <= 16 ? 4 : BN <= 32 ? 2 : 1;
+    while (g.th > 1 && kCvTH * g.th / 2 >= Ho) g.th /= 2;
+    g.tiles_h = (Ho + kCvTH * g.th - 1) / (kCvTH * g.th);
+    const long long t2 = (long long)g.tiles_w * g.tiles_h * B * g.n_tiles;
+    g.total_tiles = (int)t2;
+  }
   const int ring_budget = 200 * 1024 - stg_bytes - (g.wres ? nk * b_bytes : 0);
-  const int stage_bytes = g.halo == 1 ? kHaloRows * KB * 2 : g.halo == 2 ? 2 * kHalo2Rows * KB * 2
+  const int stage_bytes = g.halo == 1 ? (kCvTH * g.th + 2) * kCvTW * KB * 2 : g.halo == 2 ? 2 * kHalo2Rows * KB * 2
                         : g.wres ? a_bytes : a_bytes + b_bytes;
   g.stages = std::max(2, std::min(kCvMaxStages, ring_budget / stage_bytes));
   auto fn = conv_encode_fn();
@@ -483,7 +506,7 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
     const uint64_t d[4] = {(uint64_t)Cin, (uint64_t)W, (uint64_t)H, (uint64_t)B};
     const uint64_t str[3] = {(uint64_t)Cin * 2, (uint64_t)W * Cin * 2, (uint64_t)H * W * Cin * 2};
     const uint32_t box[4] = {(uint32_t)KB, (uint32_t)(kCvTW * s),
-                             (uint32_t)(g.halo == 1 ? kCvTH + 2 : g.halo == 2 ? 18 : kCvTH * s), 1};
+                             (uint32_t)(g.halo == 1 ? kCvTH * g.th + 2 : g.halo == 2 ? 18 : kCvTH * s), 1};
     const uint32_t es[4] = {1, (uint32_t)s, (uint32_t)s, 1};
     r = fn(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<__nv_bfloat16*>(x), d, str, box, es,
            CU_TENSOR_MAP_INTERLEAVE_NONE, tma_swizzle(KB), CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
