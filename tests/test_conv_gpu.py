@@ -60,6 +60,7 @@ CASES = [  # B, Cin, H, W, Cout, k, s, act
     (1, 64, 80, 80, 64, 3, 1, True),      # several tiles in both directions
     (2, 16, 40, 24, 16, 3, 1, True),      # 4 stacked subtiles per tile, ragged last tile row
     (1, 32, 24, 20, 32, 3, 1, True),      # 2 stacked subtiles per tile
+    (2, 48, 20, 20, 64, 1, 1, True),      # 1×1 with 256-pixel tiles (two subtiles), channel block past C_in
 ]
 
 

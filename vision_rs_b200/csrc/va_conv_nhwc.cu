@@ -113,7 +113,7 @@ __device__ __forceinline__ void conv_tile(const ConvGeom& g, int t, int bn, int&
   n0 = (t % g.n_tiles) * bn;
   int r = t / g.n_tiles;
   if (g.linear) {
-    m0 = (long long)r * kCvM;
+    m0 = (long long)r * kCvM * g.th;
     b = oy0 = ox0 = 0;
     return;
   }
@@ -146,7 +146,7 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
   uint8_t* sa = stg + kCvEpiWarps * 2 * 32 * kRowBytes;
   // A stage: 128 pixel rows, or in halo mode 160 rows (10 input rows × 16 columns).
   const int aBytes = g.halo == 1 ? (kCvTH * g.th + 2) * kCvTW * KB * 2
-                   : g.halo == 2 ? 2 * kHalo2Rows * KB * 2 : kABytes;
+                   : g.halo == 2 ? 2 * kHalo2Rows * KB * 2 : kABytes * g.th;
   uint8_t* sb = sa + g.stages * aBytes;  // weight ring, or the resident slice
   const int pad = g.ksize / 2, cblocks = (g.Cin + KB - 1) / KB, nk = g.ksize * g.ksize * cblocks;
   const int nq = g.halo ? 3 * cblocks : nk;  // ring stages per tile
@@ -215,11 +215,11 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
             continue;
           }
           const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * KB, ky = tap / g.ksize, kx = tap - ky * g.ksize;
-          mbar_arrive_expect_tx(&c.full[st], g.wres ? kABytes : kABytes + kBBytes);
-          if (g.linear)
-            tma_load_2d(sa + st * kABytes, &map_x, &c.full[st], c0, (int)m0);
+          mbar_arrive_expect_tx(&c.full[st], g.wres ? aBytes : aBytes + kBBytes);
+          if (g.linear)  // th·128 consecutive pixels
+            tma_load_2d(sa + st * aBytes, &map_x, &c.full[st], c0, (int)m0);
           else
-            tma_load_4d(sa + st * kABytes, &map_x, &c.full[st], c0, g.stride * ox0 + kx - pad,
+            tma_load_4d(sa + st * aBytes, &map_x, &c.full[st], c0, g.stride * ox0 + kx - pad,
                         g.stride * oy0 + ky - pad, b);
           if (!g.wres) tma_load_2d(sb + st * kBBytes, &map_w, &c.full[st], tap * g.Cin + c0, n0);
         }
@@ -284,9 +284,12 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
           continue;
         }
         const uint64_t db = db0 + (uint64_t)(((g.wres ? kb : st) * kBBytes) >> 4);
+        for (int sub = 0; sub < g.th; ++sub) {  // linear mode: subtile sub = pixels 128·sub … of the tile
+          const uint64_t das = da + (uint64_t)((sub * kABytes) >> 4);
 #pragma unroll
-        for (int s = 0; s < KB / 16; ++s)  // +32 bytes per 16-channel k-step inside the swizzle atom
-          mma_ss_w(d, da + 2 * s, db + 2 * s, idesc, (kb > 0 || s > 0) ? 1u : 0u);
+          for (int s = 0; s < KB / 16; ++s)  // +32 bytes per 16-channel k-step inside the swizzle atom
+            mma_ss_w(d + (uint32_t)(sub * BN), das + 2 * s, db + 2 * s, idesc, (kb > 0 || s > 0) ? 1u : 0u);
+        }
         mma_commit_w(&c.empty[st]);
       }
       if (ok) mma_commit_w(&c.acc_full[buf]);
@@ -367,7 +370,7 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
           __syncwarp();
           if (lane == 0) {  // 32 rows × kChunk channels; TMA drops what lies outside y
             if (g.linear)
-              tma_store_2d(&map_y, stage, n0 + cb, (int)(m0 + quarter * 32));
+              tma_store_2d(&map_y, stage, n0 + cb, (int)(m0 + kCvM * sub + quarter * 32));
             else
               tma_store_4d(&map_y, stage, n0 + cb, ox0, oy0 + 2 * quarter, b);
             tma_store_commit();
@@ -377,7 +380,7 @@ conv_nhwc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constan
           long long pix;
           bool live;
           if (g.linear) {
-            pix = m0 + r;
+            pix = m0 + kCvM * sub + r;
             live = pix < g.pixels;
           } else {
             const int oy = oy0 + r / kCvTW, ox = ox0 + r % kCvTW;
@@ -457,7 +460,9 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) & 15)
     return set_error(VA_ERR_ALIGN, "conv nhwc: x, w, y need 16-byte alignment");
   const int pad = k / 2, Ho = (H + 2 * pad - k) / s + 1, Wo = (W + 2 * pad - k) / s + 1;
-  const int KB = Cin % 64 == 0 ? 64 : Cin % 32 == 0 ? 32 : 16;
+  // Channel block: 64 from 40 input channels up, 32 from 24 (the blocks past
+  // C_in read zeros); fewer, wider pipeline stages beat exact-fitting narrow ones.
+  const int KB = Cin >= 40 ? 64 : Cin >= 24 ? 32 : 16;
   const int BN = Cout % 128 == 0 ? 128 : Cout % 64 == 0 ? 64 : Cout % 32 == 0 ? 32 : 16;
   ConvGeom g{};
   g.Ho = Ho, g.Wo = Wo, g.Cin = Cin, g.Cout = Cout, g.ksize = k, g.stride = s, g.act = act ? 1 : 0;
@@ -477,6 +482,11 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
   g.wres = (nk * b_bytes <= 96 * 1024 && g.n_tiles <= sms) ? 1 : 0;
   const int chunk_cols = BN < 64 ? BN : 64, stg_bytes = kCvEpiWarps * 2 * 32 * 2 * chunk_cols;
   g.halo = (k == 3 && g.wres) ? s : 0;
+  if (g.linear && BN <= 64 && g.pixels >= 2 * kCvM) {
+    // 1×1: two 128-pixel subtiles per tile (one 256-row load, two accumulators)
+    g.th = 2;
+    g.total_tiles = (int)((g.pixels + 2 * kCvM - 1) / (2 * kCvM) * g.n_tiles);
+  }
   if (g.halo == 1) {
     // Narrow convs: stack 2 or 4 subtiles per tile so that each pipeline stage
     // (one halo load, th·3 MMAs) carries more work; 4 slots × th × BN ≤ 512 TMEM
@@ -489,7 +499,7 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
   }
   const int ring_budget = 200 * 1024 - stg_bytes - (g.wres ? nk * b_bytes : 0);
   const int stage_bytes = g.halo == 1 ? (kCvTH * g.th + 2) * kCvTW * KB * 2 : g.halo == 2 ? 2 * kHalo2Rows * KB * 2
-                        : g.wres ? a_bytes : a_bytes + b_bytes;
+                        : g.wres ? a_bytes * g.th : a_bytes * g.th + b_bytes;
   g.stages = std::max(2, std::min(kCvMaxStages, ring_budget / stage_bytes));
   auto fn = conv_encode_fn();
   if (!fn) return set_error(VA_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
@@ -498,7 +508,7 @@ int conv_nhwc(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias,
   if (g.linear) {
     const uint64_t d[2] = {(uint64_t)Cin, (uint64_t)g.pixels};
     const uint64_t str[1] = {(uint64_t)Cin * 2};
-    const uint32_t box[2] = {(uint32_t)KB, (uint32_t)kCvM}, es[2] = {1, 1};
+    const uint32_t box[2] = {(uint32_t)KB, (uint32_t)(kCvM * g.th)}, es[2] = {1, 1};
     r = fn(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(x), d, str, box, es,
            CU_TENSOR_MAP_INTERLEAVE_NONE, tma_swizzle(KB), CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
