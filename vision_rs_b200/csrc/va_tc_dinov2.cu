@@ -109,11 +109,11 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
       const int total = my_tiles * nk;
       int issued = 0;
       bool ok = true;
-      for (int g = 0; g < total; ++g) {
-        const int st = g % kWStages, nt = nt_lo + g / nk, kb = g % nk;
-        if (g >= kWStages &&
-            !(ok = mbar_wait(&sm.w_empty[st], ((g / kWStages) - 1) & 1, &sm.abort, &g_dino_status, 1)))
-          break;
+      int st = 0, nt = nt_lo, kb = 0;  // ring slot, N tile and k block of stage g, kept incrementally
+      uint32_t ph = 0;
+      for (int g = 0; g < total; ++g, st = st + 1 == kWStages ? 0 : st + 1, ph ^= st == 0 ? 1u : 0u,
+               kb = kb + 1 == nk ? 0 : kb + 1, nt += kb == 0 ? 1 : 0) {
+        if (g >= kWStages && !(ok = mbar_wait(&sm.w_empty[st], ph ^ 1u, &sm.abort, &g_dino_status, 1))) break;
         mbar_arrive_expect_tx(&sm.w_full[st], kDM * 128 + kDN * 128);
         tma_load_3d(sm.x[st], &map_x, &sm.w_full[st], kb * 64, t0, sq);
         tma_load_2d(sm.w[st], &map_w, &sm.w_full[st], kb * 64, nt * kDN);
@@ -129,31 +129,35 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {  // ── MMA issuer ──
-      constexpr uint32_t idesc = idesc_f32acc(kDM, kDN, AB_BF16, false, false);
-      const uint64_t dx0 = sdesc(smem_u32(sm.x[0]), 16, 1024, SW_128B);
-      const uint64_t dw0 = sdesc(smem_u32(sm.w[0]), 16, 1024, SW_128B);
-      constexpr uint32_t kXS = (kDM * 128) >> 4, kWS = (kDN * 128) >> 4;
-      bool ok = true;
-      for (int t = 0; ok && t < my_tiles; ++t) {
-        const int a = t & 1;
-        if (t >= 2 && !(ok = mbar_wait(&sm.acc_empty[a], ((t >> 1) - 1) & 1, &sm.abort, &g_dino_status, 3))) break;
-        for (int kb = 0; kb < nk; ++kb) {
-          const int g = t * nk + kb, st = g % kWStages;
-          if (!(ok = mbar_wait(&sm.w_full[st], (g / kWStages) & 1, &sm.abort, &g_dino_status, 4))) break;
-          tc_fence_after();
-          const uint64_t da = dx0 + (uint64_t)(st * kXS), db = dw0 + (uint64_t)(st * kWS);
+    // ── MMA issuer: the whole warp runs the loop converged (waits made
+    // warp-uniform) and one elected lane issues each tcgen05 instruction ──
+    constexpr uint32_t idesc = idesc_f32acc(kDM, kDN, AB_BF16, false, false);
+    const uint64_t dx0 = sdesc(smem_u32(sm.x[0]), 16, 1024, SW_128B);
+    const uint64_t dw0 = sdesc(smem_u32(sm.w[0]), 16, 1024, SW_128B);
+    constexpr uint32_t kXS = (kDM * 128) >> 4, kWS = (kDN * 128) >> 4;
+    bool ok = true;
+    int st = 0;       // ring slot of the next stage
+    uint32_t ph = 0;  // its fill parity
+    for (int t = 0; ok && t < my_tiles; ++t) {
+      const int a = t & 1;
+      if (t >= 2 &&
+          !(ok = __all_sync(0xffffffffu,
+                            mbar_wait(&sm.acc_empty[a], ((t >> 1) - 1) & 1, &sm.abort, &g_dino_status, 3))))
+        break;
+      for (int kb = 0; kb < nk; ++kb, st = st + 1 == kWStages ? 0 : st + 1, ph ^= st == 0 ? 1u : 0u) {
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&sm.w_full[st], ph, &sm.abort, &g_dino_status, 4)))) break;
+        tc_fence_after();
+        const uint64_t da = dx0 + (uint64_t)(st * kXS), db = dw0 + (uint64_t)(st * kWS);
 #pragma unroll
-          for (int s = 0; s < 4; ++s)
-            mma_ss(tmem + a * 256, da + 2 * s, db + 2 * s, idesc, (kb > 0 || s > 0) ? 1u : 0u);
-          mma_commit(&sm.w_empty[st]);
-        }
-        if (ok) mma_commit(&sm.acc_full[a]);
+        for (int s = 0; s < 4; ++s)
+          mma_ss_w(tmem + a * 256, da + 2 * s, db + 2 * s, idesc, (kb > 0 || s > 0) ? 1u : 0u);
+        mma_commit_w(&sm.w_empty[st]);
       }
-      mma_commit(&sm.fin);  // every MMA issued here completes before the CTA tears down
-      const long long c0 = clock64();
-      while (!mbar_try_wait(&sm.fin, 0) && clock64() - c0 < kSpinCycles) {
-      }
+      if (ok) mma_commit_w(&sm.acc_full[a]);
+    }
+    mma_commit_w(&sm.fin);  // every MMA issued here completes before the CTA tears down
+    const long long c0 = clock64();
+    while (!mbar_try_wait(&sm.fin, 0) && clock64() - c0 < kSpinCycles) {
     }
     __syncwarp();
   } else {
