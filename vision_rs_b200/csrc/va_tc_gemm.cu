@@ -109,7 +109,7 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         }
       }
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1) {  // the whole warp, converged; one elected lane issues each tcgen05 instruction
     const uint32_t idesc = idesc_f32acc(kGM, kGN, ab_fmt, A_MN, B_MN);
     // K-major SW128: 8-row groups 1024 B apart, a 16-wide k step = +32 B.
     // MN-major SW128: two 64-element blocks 8 KB apart (LBO), 8 k-rows per
@@ -121,15 +121,16 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     bool ok = true;
     for (int kb = 0; kb < nk; ++kb) {
       const int st = kb % kGStages;
-      if (!(ok = mbar_wait(&sm.full[st], (kb / kGStages) & 1, &sm.abort, &g_gemm_status, 2))) break;
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&sm.full[st], (kb / kGStages) & 1, &sm.abort, &g_gemm_status, 2))))
+        break;
       tc_fence_after();
       const uint64_t da = da0 + (uint64_t)(st * kStage), db = db0 + (uint64_t)(st * kStage);
 #pragma unroll
       for (int s = 0; s < kGK / 16; ++s)
-        mma_ss(tmem, da + s * kAStep, db + s * kBStep, idesc, (kb > 0 || s > 0) ? 1u : 0u);
-      mma_commit(&sm.empty[st]);
+        mma_ss_w(tmem, da + s * kAStep, db + s * kBStep, idesc, (kb > 0 || s > 0) ? 1u : 0u);
+      mma_commit_w(&sm.empty[st]);
     }
-    mma_commit(&sm.done);
+    mma_commit_w(&sm.done);
   }
   __syncwarp();
   const bool ok = mbar_wait(&sm.done, 0, &sm.abort, &g_gemm_status, 3) && !sm.abort;
