@@ -92,8 +92,9 @@ psa_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_con
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == 8) {
+    // ── TMA producer (lane 0) + MMA issuer: the whole warp runs the issue
+    // loop converged (waits made warp-uniform), one elected lane issues ──
     if (lane == 0) {
-      // ── TMA producer + MMA issuer ──
       tma_prefetch_desc(&map_qk);
       tma_prefetch_desc(&map_v);
       tma_prefetch_desc(&map_do);
@@ -106,7 +107,9 @@ psa_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_con
       tma_load_3d(sm.k, &map_qk, &sm.load_full, 0, j * kT, BH + bh);
       tma_load_2d(sm.v[0], &map_v, &sm.load_full, j * kT, vrow);
       tma_load_2d(sm.v[1], &map_v, &sm.load_full, j * kT + 64, vrow);
-
+    }
+    __syncwarp();
+    {
       constexpr uint32_t idS = idesc_f32acc(128, 128, AB_F16, false, false);
       constexpr uint32_t idP = idesc_f32acc(128, 128, AB_F16, true, true);
       constexpr uint32_t idV = idesc_f32acc(128, 64, AB_F16, true, false);
@@ -129,43 +132,43 @@ psa_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_con
       auto issue_sdp = [&](int i) {
         const uint64_t a = dq_k(i), b = ddo_mn(i);
 #pragma unroll
-        for (int s = 0; s < kKD / 16; ++s) mma_ss(tmem + kColS, a + 2 * s, dk_k + 2 * s, idS, s > 0);
+        for (int s = 0; s < kKD / 16; ++s) mma_ss_w(tmem + kColS, a + 2 * s, dk_k + 2 * s, idS, s > 0);
 #pragma unroll
-        for (int s = 0; s < kHD / 16; ++s) mma_ss(tmem + kColDP, b + 128 * s, dv_mn + 128 * s, idP, s > 0);
+        for (int s = 0; s < kHD / 16; ++s) mma_ss_w(tmem + kColDP, b + 128 * s, dv_mn + 128 * s, idP, s > 0);
       };
       auto issue_grad = [&](int i) {
         const uint64_t bo = ddo_k(i), bq = dq_mn(i);
 #pragma unroll
         for (int s = 0; s < kT / 16; ++s) {
-          mma_ss(tmem + kColDV, dp_mn + 128 * s, bo + (s >> 2) * 512 + (s & 3) * 2, idV, (i > 0 || s > 0));
-          mma_ss(tmem + kColDK, dds_mn + 128 * s, bq + 64 * s, idK, (i > 0 || s > 0));
-          mma_ss(tmem + kColDQ + 32 * i, dds_k + (s >> 2) * 1024 + (s & 3) * 2, dk_mn + 64 * s, idQ, s > 0);
+          mma_ss_w(tmem + kColDV, dp_mn + 128 * s, bo + (s >> 2) * 512 + (s & 3) * 2, idV, (i > 0 || s > 0));
+          mma_ss_w(tmem + kColDK, dds_mn + 128 * s, bq + 64 * s, idK, (i > 0 || s > 0));
+          mma_ss_w(tmem + kColDQ + 32 * i, dds_k + (s >> 2) * 1024 + (s & 3) * 2, dk_mn + 64 * s, idQ, s > 0);
         }
       };
-      bool ok = mbar_wait(&sm.load_full, 0, &sm.abort, &g_bwd_status, 1);
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.load_full, 0, &sm.abort, &g_bwd_status, 1));
       if (ok) {
         tc_fence_after();
         issue_sdp(0);
-        mma_commit(&sm.s_full);
+        mma_commit_w(&sm.s_full);
       }
       for (int i = 0; ok && i < nt; ++i) {
-        if (!(ok = mbar_wait(&sm.s_free, i & 1, &sm.abort, &g_bwd_status, 2))) break;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_free, i & 1, &sm.abort, &g_bwd_status, 2)))) break;
         tc_fence_after();
         if (i + 1 < nt) {
           issue_sdp(i + 1);
-          mma_commit(&sm.s_full);
+          mma_commit_w(&sm.s_full);
         }
-        if (!(ok = mbar_wait(&sm.p_full, i & 1, &sm.abort, &g_bwd_status, 3))) break;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&sm.p_full, i & 1, &sm.abort, &g_bwd_status, 3)))) break;
         tc_fence_after();
         issue_grad(i);
-        mma_commit(&sm.p_free);
+        mma_commit_w(&sm.p_free);
       }
       if (!ok) {  // the loads issued here land (bounded) before the CTA can exit
         const long long t0 = clock64();
         while (!mbar_try_wait(&sm.load_full, 0) && clock64() - t0 < kSpinCycles) {
         }
       }
-      mma_commit(&sm.done);
+      mma_commit_w(&sm.done);
     }
     __syncwarp();
   } else {
