@@ -703,10 +703,16 @@ class Cfg5:
         import torch.distributed as dist
         multi = dist.is_initialized() and dist.get_world_size() > 1
         self.comm = train.PeerGradComm() if multi and args.allreduce == "peer" else None
+        # with the peer comm the whole step (fwd + bwd + all-reduce + SGD) replays from one graph
+        self.graph_step = train.DpStepGraph(self.step_obj, self.comm) if self.comm is not None else None
         self.allreduce = ("none (one rank)" if not multi else
-                          "peer-memory all-reduce fused with SGD (one kernel)" if self.comm else "NCCL all-reduce")
+                          "peer-memory all-reduce fused with SGD (one kernel), whole step replayed from one CUDA "
+                          "graph" if self.comm else "NCCL all-reduce")
 
     def step(self):
+        if self.graph_step is not None:
+            self.loss = self.graph_step(self.x, self.t, self.params, self.master, self.lr)
+            return
         self.loss = self.train.dp_train_step(self.step_obj, self.x, self.t, self.params, self.master, self.lr,
                                              comm=self.comm)
 
@@ -971,7 +977,8 @@ def run_ours(args, ws, rank, local):
     barrier()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    replayed = lambda: getattr(getattr(wl, "step_obj", None), "replayed_kernels", 0)
+    replayed = lambda: (getattr(getattr(wl, "step_obj", None), "replayed_kernels", 0)
+                        + getattr(getattr(wl, "graph_step", None), "replayed_kernels", 0))
     lc0 = _lib.lib().va_launch_count() + replayed()
     barrier()
     for i in range(args.steps):
@@ -1056,6 +1063,10 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local = dist_env()
+    if ws > 1:
+        # NCCL prints its version line on stdout when its debug level asks for it; the bench's
+        # stdout is one JSON line, so keep NCCL to warnings (read when NCCL initialises)
+        os.environ["NCCL_DEBUG"] = "WARN"
     if args.impl == "reference":
         run_reference(args, ws, rank)
     else:

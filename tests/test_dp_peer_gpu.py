@@ -90,6 +90,22 @@ def _worker(rank, port, world):
         dist.all_gather(peer_g, gp)
         for r in range(1, world):
             assert torch.equal(peer_g[0], peer_g[r]), r
+
+        # the whole step replayed from one CUDA graph (DpStepGraph) equals the eager step:
+        # from the same weights, two eager steps and two graph steps (the first runs eagerly
+        # and captures, the second replays) end in bit-identical weights
+        pe, pg = {k: v.clone() for k, v in pp.items()}, {k: v.clone() for k, v in pp.items()}
+        me, mg = mp_.clone(), mp_.clone()
+        for _ in range(2):
+            train.dp_train_step(step, x, t, pe, me, lr=0.05, comm=comm)
+        gstep = train.DpStepGraph(train.PsaTrainStep(B=B, H=H, W=W, device=dev, graph=True), comm)
+        for _ in range(2):
+            gstep(x, t, pg, mg, 0.05)
+        torch.cuda.synchronize()
+        assert comm.status() == 0 and gstep.graph_kernels > 0
+        assert torch.equal(me, mg)
+        for k in pe:
+            assert torch.equal(pe[k], pg[k]), k
         comm.close()
 
         # failure detection: the last rank never publishes (short limit: 300 ms per wait)

@@ -118,9 +118,17 @@ class PeerGradComm:
     def allreduce_sgd(self, grads, master, params: dict, lr: float, stream=None):
         """grads (in place) = Σ over ranks; master -= lr·grads/world; bf16/f32
         parameters rewritten from master."""
+        self.count_call()
+        self._launch(grads, master, params, lr, stream)
+
+    def count_call(self):
+        """One all-reduce issued (eagerly or by a graph replay): every
+        ``check_every`` calls the sticky status is read (a host sync)."""
         self._calls += 1
         if self.check_every and self._calls % self.check_every == 0:
             self.raise_on_failure()
+
+    def _launch(self, grads, master, params: dict, lr: float, stream=None):
         _lib.call("va_psa_dp_allreduce_sgd", self._h, _p(grads), _p(master), float(lr), _p(params["w_qkv"]),
                   _p(params["b_qkv"]), _p(params["w_pe"]), _p(params["b_pe"]), _p(params["w_proj"]),
                   _p(params["b_proj"]), _stream(stream))
@@ -173,6 +181,43 @@ def attention_backward(x, dy, params: dict, dy_scale: float = 1.0, want_dx: bool
               _p(dx) if dx is not None else None, _p(grads), B, C, H, W, 2, 32, _p(workspace), workspace.numel(),
               _stream(stream))
     return grads, dx
+
+
+class DpStepGraph:
+    """The whole data-parallel step with the peer comm — the local forward +
+    backward and the all-reduce + SGD kernel — replayed from one CUDA graph
+    per rank: one host launch per step instead of two library calls, so a
+    rank's host, sharing the machine's cores with the other ranks, cannot
+    fall behind its GPU.  The all-reduce kernel keeps its step count on the
+    device, so its launch can be replayed.  The first call for a given set of
+    tensors (and lr) runs the step eagerly, then captures it."""
+
+    def __init__(self, step: PsaTrainStep, comm: "PeerGradComm"):
+        self.step, self.comm = step, comm
+        self._graph, self._key = None, None
+        self.graph_kernels = 0     # library kernels one replay launches
+        self.replayed_kernels = 0  # kernels launched by replays so far
+
+    def __call__(self, x, target, params: dict, master, lr: float):
+        key = (x.data_ptr(), target.data_ptr(), master.data_ptr(), float(lr)) + \
+            tuple(params[k].data_ptr() for k in sorted(params))
+        st = self.step
+        if self._graph is None or self._key != key:
+            st._launch(x, target, params, False, None)  # eager step: one-time set-up stays out of the graph
+            self.comm.allreduce_sgd(st.grads, master, params, lr)
+            torch.cuda.current_stream().synchronize()
+            g = torch.cuda.CUDAGraph()
+            n0 = int(_lib.lib().va_launch_count())
+            with torch.cuda.graph(g, capture_error_mode="relaxed"):
+                st._launch(x, target, params, False, None)
+                self.comm._launch(st.grads, master, params, lr)
+            self.graph_kernels = int(_lib.lib().va_launch_count()) - n0
+            self._graph, self._key = g, key
+            return st.loss
+        self.comm.count_call()
+        self._graph.replay()
+        self.replayed_kernels += self.graph_kernels
+        return st.loss
 
 
 def dp_train_step(step: PsaTrainStep, x, target, params: dict, master, lr: float, group=None,
