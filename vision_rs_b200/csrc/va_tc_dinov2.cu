@@ -16,11 +16,12 @@
 // fix the cls handling of windowed layers; this is the choice made here.
 //
 // Kernels:
-//  1. dino_qkv_kernel<EPI>  — per CTA a 128-token tile of one sequence times
-//     half of W_qkv, 192 features per MMA tile (three heads), x and W k
-//     blocks streamed through a TMA ring, two TMEM
-//     accumulators so the epilogue overlaps the next tile's MMAs, output
-//     staged in shared memory and written by TMA stores.  EPI kSplitHeads
+//  1. dino_qkv_kernel<EPI>  — persistent GEMM over work units of a 128-token
+//     tile of one sequence × 192 features (three heads), x and W k blocks
+//     streamed through a TMA ring across unit boundaries, two TMEM
+//     accumulators so the epilogue overlaps the next unit's MMAs, bias
+//     staged in shared memory per unit, output staged in shared memory and
+//     written by TMA stores.  EPI kSplitHeads
 //     writes Q and K f16 [2][S·heads][n][64] and V f16 transposed
 //     [S·heads·64][n_pad] (the flash-attention operands); EPI kPackedRows
 //     writes bf16 [S][n][3·hidden] (torch Linear layout).
@@ -43,7 +44,6 @@ namespace {
 constexpr int kDM = 128;      // tokens per tile (UMMA M)
 constexpr int kDN = 192;      // features per N tile (UMMA N): three heads of 64
 constexpr int kWStages = 4;   // (x, W) k-block ring
-constexpr int kNSplit = 2;    // CTAs sharing one token tile's N tiles
 constexpr int kHead = 64;
 constexpr int kSplitHeads = 0, kPackedRows = 1;
 constexpr int kQkvThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
@@ -52,31 +52,42 @@ struct DinoQkvSmem {
   uint8_t x[kWStages][kDM * 128];     // x block: 128 tokens × 64 features, K-major SW128 (16 KB)
   uint8_t w[kWStages][kDN * 128];     // W block: 192 rows × 64 features (24 KB)
   uint8_t stage[3][kDM * 128];        // epilogue staging: three 16 KB head groups
+  float bias[2][kDN];                 // the bias slice of the accumulator being drained
   uint64_t w_full[kWStages], w_empty[kWStages], acc_full[2], acc_empty[2], fin;
   uint64_t stage_free, stage_full;  // staging handshakes between the epilogue warps and the storing thread
+  uint64_t bias_full[2];            // bias slot a written by all 128 epilogue threads
   uint32_t tmem_base;
   int abort;
 };
 
-// One CTA per (token tile of a sequence, half of the N tiles).  The 64-wide
-// k blocks of x and W stream through a 4-stage TMA ring (x blocks are re-read
-// from L2 for each N tile); two TMEM accumulators (192 columns each) let the
-// epilogue of one N tile overlap the MMAs of the next.  The epilogue stages each 128 × 192
-// tile as three 16 KB head groups and writes them with TMA stores (rows past
-// the sequence end are not written).
+// Work unit u = (N tile nt, token tile tt, sequence sq) with nt fastest, so
+// the CTAs working at one time share few x tiles (read from L2 once per N
+// tile) while W (≤ a few MB) stays L2-resident.
+struct DinoUnit {
+  int nt, t0, sq;
+};
+__device__ __forceinline__ DinoUnit dino_unit(int u, int ntiles, int ntt) {
+  const int nt = u % ntiles, r = u / ntiles;
+  return DinoUnit{nt, (r % ntt) * kDM, r / ntt};
+}
+
+// Persistent: CTA b walks the work units b, b + gridDim.x, …  The 64-wide k
+// blocks of x and W stream through a 4-stage TMA ring across unit boundaries;
+// two TMEM accumulators (192 columns each) let the epilogue of one unit
+// overlap the MMAs of the next.  The epilogue adds the bias (staged in shared
+// memory per unit), stages the 128 × 192 tile as three 16 KB head groups and
+// writes them with TMA stores (rows past the sequence end are not written).
 template <int EPI>
 __global__ void __launch_bounds__(kQkvThreads, 1)
 dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ CUtensorMap map_o1, const __grid_constant__ CUtensorMap map_o2,
-                const float* __restrict__ bias, int hidden, int heads, int BH) {
+                const float* __restrict__ bias, int hidden, int heads, int BH, int ntt, int units) {
   extern __shared__ uint8_t smem_raw[];
   DinoQkvSmem& sm =
       *reinterpret_cast<DinoQkvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t0 = blockIdx.x * kDM, sq = blockIdx.y;
   const int nk = hidden / 64, ntiles = 3 * hidden / kDN;
-  const int nt_lo = blockIdx.z * ntiles / kNSplit, nt_hi = (blockIdx.z + 1) * ntiles / kNSplit;
-  const int my_tiles = nt_hi - nt_lo;
+  const int my_units = blockIdx.x < units ? (units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
 
   if (tid == 0) {
     for (int i = 0; i < kWStages; ++i) {
@@ -90,6 +101,8 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
     mbar_init(&sm.fin, 1);
     mbar_init(&sm.stage_free, 1);
     mbar_init(&sm.stage_full, 128);
+    mbar_init(&sm.bias_full[0], 128);
+    mbar_init(&sm.bias_full[1], 128);
     sm.abort = 0;
     fence_mbar_init();
   }
@@ -106,18 +119,25 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
     if (lane == 0) {  // ── TMA producer ──
       tma_prefetch_desc(&map_x);
       tma_prefetch_desc(&map_w);
-      const int total = my_tiles * nk;
+      const int total = my_units * nk;
       int issued = 0;
       bool ok = true;
-      int st = 0, nt = nt_lo, kb = 0;  // ring slot, N tile and k block of stage g, kept incrementally
+      int st = 0, kb = 0, u = blockIdx.x;  // ring slot, k block and unit of stage g, kept incrementally
       uint32_t ph = 0;
-      for (int g = 0; g < total; ++g, st = st + 1 == kWStages ? 0 : st + 1, ph ^= st == 0 ? 1u : 0u,
-               kb = kb + 1 == nk ? 0 : kb + 1, nt += kb == 0 ? 1 : 0) {
+      DinoUnit w = dino_unit(u, ntiles, ntt);
+      for (int g = 0; g < total; ++g) {
         if (g >= kWStages && !(ok = mbar_wait(&sm.w_empty[st], ph ^ 1u, &sm.abort, &g_dino_status, 1))) break;
         mbar_arrive_expect_tx(&sm.w_full[st], kDM * 128 + kDN * 128);
-        tma_load_3d(sm.x[st], &map_x, &sm.w_full[st], kb * 64, t0, sq);
-        tma_load_2d(sm.w[st], &map_w, &sm.w_full[st], kb * 64, nt * kDN);
+        tma_load_3d(sm.x[st], &map_x, &sm.w_full[st], kb * 64, w.t0, w.sq);
+        tma_load_2d(sm.w[st], &map_w, &sm.w_full[st], kb * 64, w.nt * kDN);
         ++issued;
+        st = st + 1 == kWStages ? 0 : st + 1;
+        ph ^= st == 0 ? 1u : 0u;
+        if (++kb == nk) {
+          kb = 0;
+          u += gridDim.x;
+          w = dino_unit(u, ntiles, ntt);
+        }
       }
       if (!ok) {  // loads issued here land (bounded) before the CTA can exit
         for (int g = max(0, issued - kWStages); g < issued; ++g) {
@@ -138,13 +158,14 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
     bool ok = true;
     int st = 0;       // ring slot of the next stage
     uint32_t ph = 0;  // its fill parity
-    for (int t = 0; ok && t < my_tiles; ++t) {
+    for (int t = 0; ok && t < my_units; ++t) {
       const int a = t & 1;
       if (t >= 2 &&
           !(ok = __all_sync(0xffffffffu,
                             mbar_wait(&sm.acc_empty[a], ((t >> 1) - 1) & 1, &sm.abort, &g_dino_status, 3))))
         break;
-      for (int kb = 0; kb < nk; ++kb, st = st + 1 == kWStages ? 0 : st + 1, ph ^= st == 0 ? 1u : 0u) {
+      tc_fence_after();
+      for (int kb = 0; kb < nk; ++kb) {
         if (!(ok = __all_sync(0xffffffffu, mbar_wait(&sm.w_full[st], ph, &sm.abort, &g_dino_status, 4)))) break;
         tc_fence_after();
         const uint64_t da = dx0 + (uint64_t)(st * kXS), db = dw0 + (uint64_t)(st * kWS);
@@ -152,6 +173,8 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
         for (int s = 0; s < 4; ++s)
           mma_ss_w(tmem + a * 256, da + 2 * s, db + 2 * s, idesc, (kb > 0 || s > 0) ? 1u : 0u);
         mma_commit_w(&sm.w_empty[st]);
+        st = st + 1 == kWStages ? 0 : st + 1;
+        ph ^= st == 0 ? 1u : 0u;
       }
       if (ok) mma_commit_w(&sm.acc_full[a]);
     }
@@ -162,29 +185,37 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
     __syncwarp();
   } else {
     // ── epilogue warps 2-5: TMEM lane quarter = warp % 4 ──
-    const int row = (warp & 3) * 32 + lane;
+    const int row = (warp & 3) * 32 + lane, et = tid - 64;  // et: 0..127
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const bool storer = (warp == 2 && lane == 0);
     bool ok = true;
-    for (int t = 0; t < my_tiles; ++t) {
-      const int a = t & 1, n0 = (nt_lo + t) * kDN;
+    for (int t = 0; t < my_units; ++t) {
+      const int a = t & 1;
+      const DinoUnit w = dino_unit(blockIdx.x + t * gridDim.x, ntiles, ntt);
+      const int n0 = w.nt * kDN;
+      // this unit's bias slice (slot a: the previous unit's epilogue reads slot a ^ 1)
+      sm.bias[a][et] = __ldg(bias + n0 + et);
+      if (et < kDN - 128) sm.bias[a][128 + et] = __ldg(bias + n0 + 128 + et);
+      mbar_arrive(&sm.bias_full[a]);  // release: the slot's values are visible to the waiters
+      if (!(ok = mbar_wait(&sm.bias_full[a], (t >> 1) & 1, &sm.abort, &g_dino_status, 8))) break;
       if (!(ok = mbar_wait(&sm.acc_full[a], (t >> 1) & 1, &sm.abort, &g_dino_status, 5))) break;
       tc_fence_after();
-      if (storer) {  // the previous tile's stores have read the staging buffer
+      if (storer) {  // the previous unit's stores have read the staging buffer
         tma_store_wait_read();
         mbar_arrive(&sm.stage_free);
       }
       if (!(ok = mbar_wait(&sm.stage_free, t & 1, &sm.abort, &g_dino_status, 6))) break;
-#pragma unroll 1
+      const float* bs = sm.bias[a];
+#pragma unroll 2
       for (int c = 0; c < kDN / 32; ++c) {
         uint32_t u[32];
         tmem_ld32(tmem + lane_off + a * 256 + c * 32, u);
         tmem_ld_wait();
         reg_fence(u);
-        const int g = c >> 1, half = c & 1, col = n0 + c * 32;
+        const int g = c >> 1, half = c & 1;
         float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(u[i]) + __ldg(bias + col + i);
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(u[i]) + bs[c * 32 + i];
         uint8_t* tile = sm.stage[g];
         const bool vsec = EPI == kSplitHeads && (n0 + g * kHead) / hidden == 2;
         if (vsec) {
@@ -216,11 +247,11 @@ dino_qkv_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant
         for (int g = 0; g < kDN / kHead; ++g) {
           const int gcol = n0 + g * kHead;
           if constexpr (EPI == kPackedRows) {
-            tma_store_3d(&map_o1, sm.stage[g], gcol, t0, sq);
+            tma_store_3d(&map_o1, sm.stage[g], gcol, w.t0, w.sq);
           } else {
-            const int sec = gcol / hidden, hd = (gcol - sec * hidden) / kHead, bh = sq * heads + hd;
-            if (sec < 2) tma_store_3d(&map_o1, sm.stage[g], 0, t0, sec * BH + bh);
-            else tma_store_3d(&map_o2, sm.stage[g], t0, bh * kHead, 0);
+            const int sec = gcol / hidden, hd = (gcol - sec * hidden) / kHead, bh = w.sq * heads + hd;
+            if (sec < 2) tma_store_3d(&map_o1, sm.stage[g], 0, w.t0, sec * BH + bh);
+            else tma_store_3d(&map_o2, sm.stage[g], w.t0, bh * kHead, 0);
           }
         }
         tma_store_commit();
@@ -360,8 +391,11 @@ int launch_qkv(const __nv_bfloat16* x, const __nv_bfloat16* w, const float* bias
   const size_t smem = sizeof(DinoQkvSmem) + 1024;
   cudaError_t e = cudaFuncSetAttribute(dino_qkv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  dino_qkv_kernel<EPI><<<dim3((n + kDM - 1) / kDM, S, kNSplit), kQkvThreads, smem, st>>>(mx, mw, mo1, mo2, bias,
-                                                                                            hidden, heads, BH);
+  const int ntt = (n + kDM - 1) / kDM;
+  const long long units = (long long)ntt * S * (3 * hidden / kDN);
+  VA_CHECK_ARG(units < (1LL << 31), "dinov2 qkv: too many tiles");
+  dino_qkv_kernel<EPI><<<(unsigned)std::min<long long>(units, 148), kQkvThreads, smem, st>>>(
+      mx, mw, mo1, mo2, bias, hidden, heads, BH, ntt, (int)units);
   return check_launch("dinov2 qkv");
 }
 

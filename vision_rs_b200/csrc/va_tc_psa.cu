@@ -1477,6 +1477,15 @@ int set_smem(K kernel, size_t bytes) {
   return VA_OK;
 }
 
+template <int KD, int OUT>
+int launch_attn(dim3 grid, const CUtensorMap& mqk, const CUtensorMap& mv, void* o, float* lse, int N, int Np,
+                int nh, float sl2, cudaStream_t st) {
+  static PerDeviceOnce attr;  // the shared-memory limit is per device
+  if (int rc = attr.run([] { return set_smem(attn_kernel<KD, OUT>, sizeof(AttnSmem<KD>) + 1024); })) return rc;
+  attn_kernel<KD, OUT><<<grid, kAttnThreads, sizeof(AttnSmem<KD>) + 1024, st>>>(mqk, mv, o, lse, N, Np, nh, sl2);
+  return check_launch("flash attention");
+}
+
 }  // namespace
 
 int pe_dwconv_vec(const __half* v, const __nv_bfloat16* w_pe, const float* b_pe, __half* pe,
@@ -1599,9 +1608,9 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   qkv_proj_kernel<<<std::min(B * ntile, 148), kQpThreads, sm1, st>>>(mx, mw, mvst, b_qkv, qk, N, nh, B, ntile);
   if (int rc = check_launch("psa qkv_proj")) return rc;
   const float scale_log2 = (1.0f / sqrtf((float)kd)) * 1.4426950408889634f;
-  attn_kernel<kKD, kOutChannelMajor>
-      <<<dim3((ntile + 1) / 2, BH), kAttnThreads, sm2, st>>>(mqk, mv, ob, lse_out, N, Np, nh, scale_log2);
-  if (int rc = check_launch("psa attention")) return rc;
+  if (int rc = launch_attn<kKD, kOutChannelMajor>(dim3((ntile + 1) / 2, BH), mqk, mv, ob, lse_out, N, Np, nh,
+                                                  scale_log2, st))
+    return rc;
   const int pe_rc = pe_dwconv_vec(vb, w_pe, b_pe, peb, w_proj, wp16, B, kC, H, W, Np, nullptr, st);
   if (pe_rc == VA_ERR_UNSUPPORTED) {
     pe_dwconv_kernel<<<dim3(kC / kPeCh, B), kPeThreads, sm3, st>>>(vb, w_pe, b_pe, peb, w_proj, wp16, H, W, Np);
@@ -1679,16 +1688,12 @@ int tc_flash_attention(const void* qk, const void* v, void* o, float* lse, int B
                            : launch_short(attn_short_kernel<64, kOutChannelMajor>, sizeof(ShortSmem<64>) + 1024);
   }
   const dim3 grid(((N + kTile - 1) / kTile + 1) / 2, BH);
-  auto launch = [&](auto kernel, size_t smem) -> int {
-    if (int rc = set_smem(kernel, smem)) return rc;
-    kernel<<<grid, kAttnThreads, smem, st>>>(mqk, mv, o, lse, N, Np, nh, scale_log2);
-    return check_launch("flash attention");
-  };
   if (kd == 32)
-    return out_token_major ? launch(attn_kernel<32, kOutTokenMajor>, sizeof(AttnSmem<32>) + 1024)
-                           : launch(attn_kernel<32, kOutChannelMajor>, sizeof(AttnSmem<32>) + 1024);
-  return out_token_major ? launch(attn_kernel<64, kOutTokenMajor>, sizeof(AttnSmem<64>) + 1024)
-                         : launch(attn_kernel<64, kOutChannelMajor>, sizeof(AttnSmem<64>) + 1024);
+    return out_token_major
+               ? launch_attn<32, kOutTokenMajor>(grid, mqk, mv, o, lse, N, Np, nh, scale_log2, st)
+               : launch_attn<32, kOutChannelMajor>(grid, mqk, mv, o, lse, N, Np, nh, scale_log2, st);
+  return out_token_major ? launch_attn<64, kOutTokenMajor>(grid, mqk, mv, o, lse, N, Np, nh, scale_log2, st)
+                         : launch_attn<64, kOutChannelMajor>(grid, mqk, mv, o, lse, N, Np, nh, scale_log2, st);
 }
 
 int psa_attention_core_tc(const void* qk, const void* v, void* o, float* lse, int B, int nh, int H, int W,
