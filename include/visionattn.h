@@ -170,7 +170,14 @@ VA_API int va_dwconv3x3_backward_f32(const float *x, const float *w, const float
  * x, w_qkv, w_proj 16-byte aligned, workspace 256-byte aligned.  f32
  * variant: any C = nh*2*kd.
  * `workspace` holds the qkv/attention intermediates; size from
- * va_psa_attention_workspace_bytes().  dtype: 0 = f32, 1 = bf16. */
+ * va_psa_attention_workspace_bytes().  dtype: 0 = f32, 1 = bf16.
+ * bf16 at C = 128 (and the PSABlock / C2PSA entries below): after the qkv
+ * GEMM the attention kernel runs on a highest-priority and the PE
+ * convolution on a lowest-priority stream of the library's own (ordered
+ * after `stream` by events, joined back before the projection), so PE
+ * blocks fill the SMs the attention grid leaves idle at its end.  The
+ * first such call on a device creates those two streams: make it before
+ * any stream capture. */
 VA_API size_t va_psa_attention_workspace_bytes(int B, int C, int H, int W, int num_heads, int key_dim,
                                         int dtype);
 VA_API int va_psa_attention_fwd_f32(const float *x, const float *w_qkv, const float *b_qkv,

@@ -108,7 +108,8 @@ int psa_block(const __nv_bfloat16* x, const va_psa_block_weights& w, void* out, 
   if (int rc = psa_attention_fwd_tc(x, reinterpret_cast<const __nv_bfloat16*>(w.w_qkv), w.b_qkv,
                                     reinterpret_cast<const __nv_bfloat16*>(w.w_pe), w.b_pe,
                                     reinterpret_cast<const __nv_bfloat16*>(w.w_proj), w.b_proj, t, B, C, H, W, nh,
-                                    kKD, ws + L.attn, psa_tc_workspace_bytes(B, C, H, W, nh), st, nullptr))
+                                    kKD, ws + L.attn, psa_tc_workspace_bytes(B, C, H, W, nh), st, nullptr,
+                                    /*overlap_pe=*/true))
     return rc;
   // y1 = x + t   (`elem_add(b, attn(b))`)
   const long long n8 = (long long)B * C * N / 8;

@@ -95,10 +95,12 @@ int conv_status_clear(cudaStream_t st);
 // the C = 128 kernels of the training step: psa_tc_is_n.
 bool psa_tc_supported(int C, int nh, int kd);
 inline bool psa_tc_is_n(int C, int nh, int kd) { return C == 128 && nh == 2 && kd == 32; }
+// overlap_pe (C = 128): attention and PE on the library's per-device side
+// streams (highest / lowest priority), forked from and joined back to `st`.
 int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,
                          const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
                          const float* b_proj, __nv_bfloat16* y, int B, int C, int H, int W, int nh, int kd,
-                         void* ws, size_t ws_bytes, cudaStream_t st, float* lse_out);
+                         void* ws, size_t ws_bytes, cudaStream_t st, float* lse_out, bool overlap_pe = false);
 // Tensor-core flash attention over BH = sequences·nh heads of N tokens:
 // qk f16 [2][BH][N][kd] (Q then K), v f16 [BH·64][Np] (Np = N rounded up to 8),
 // head dim 64, kd ∈ {32, 64}; o f16 [BH/nh][nh·64][Np] (channel-major) or,

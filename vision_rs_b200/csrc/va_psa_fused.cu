@@ -95,7 +95,7 @@ int psa_attention_fwd_bf16(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, c
                            const float* b_proj, __nv_bfloat16* y, int B, int C, int H, int W, int nh, int kd,
                            void* ws, size_t ws_bytes, cudaStream_t st) {
   return psa_attention_fwd_tc(x, w_qkv, b_qkv, w_pe, b_pe, w_proj, b_proj, y, B, C, H, W, nh, kd, ws, ws_bytes, st,
-                              nullptr);
+                              nullptr, /*overlap_pe=*/true);
 }
 
 }  // namespace va

@@ -1513,10 +1513,56 @@ PsaTcOffsets psa_tc_offsets(int B, int H, int W, int nh) {
 
 bool psa_tc_supported(int C, int nh, int kd) { return kd == kKD && nh >= 1 && C == nh * kHD; }
 
+namespace {
+
+// Side streams of one device for the fused op's fork/join: the attention on
+// the highest stream priority, the PE convolution on the lowest, so the block
+// scheduler places PE blocks only on SMs that no attention block is waiting
+// for — the tail of the attention grid.  Created once per device.
+struct SideStreams {
+  cudaStream_t hi = nullptr, lo = nullptr;
+};
+SideStreams g_side[64];
+PerDeviceOnce g_side_once;
+
+int side_streams(SideStreams** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VA_ERR_UNSUPPORTED;
+  const int rc = g_side_once.run([dev]() -> int {
+    int lo = 0, hi = 0;
+    if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
+        cudaStreamCreateWithPriority(&g_side[dev].hi, cudaStreamNonBlocking, hi) != cudaSuccess ||
+        cudaStreamCreateWithPriority(&g_side[dev].lo, cudaStreamNonBlocking, lo) != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(VA_ERR_LAUNCH, "psa_attention bf16: side stream creation failed");
+    }
+    return VA_OK;
+  });
+  if (rc) return rc;
+  *out = &g_side[dev];
+  return VA_OK;
+}
+
+// Records an event on `from` and makes `to` wait for it (the event is
+// released at once; CUDA keeps it until the wait is resolved).
+int stream_dep(cudaStream_t from, cudaStream_t to) {
+  cudaEvent_t e;
+  cudaError_t r = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+  if (r == cudaSuccess) {
+    r = cudaEventRecord(e, from);
+    if (r == cudaSuccess) r = cudaStreamWaitEvent(to, e, 0);
+    cudaEventDestroy(e);
+  }
+  if (r != cudaSuccess) return set_error(VA_ERR_LAUNCH, "psa_attention bf16: stream dependency: %s", cudaGetErrorString(r));
+  return VA_OK;
+}
+
+}  // namespace
+
 int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,
                          const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
                          const float* b_proj, __nv_bfloat16* y, int B, int C, int H, int W, int nh, int kd,
-                         void* ws, size_t ws_bytes, cudaStream_t st, float* lse_out) {
+                         void* ws, size_t ws_bytes, cudaStream_t st, float* lse_out, bool overlap_pe) {
   VA_CHECK_ARG(psa_tc_supported(C, nh, kd), "psa_attention bf16: tensor-core path needs key_dim 32 and C = 64·num_heads");
   if (!psa_tc_is_n(C, nh, kd))
     return psa_attention_fwd_tc_wide(x, w_qkv, b_qkv, w_pe, b_pe, w_proj, b_proj, y, B, C, H, W, nh, ws, ws_bytes, st);
@@ -1608,15 +1654,28 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   qkv_proj_kernel<<<std::min(B * ntile, 148), kQpThreads, sm1, st>>>(mx, mw, mvst, b_qkv, qk, N, nh, B, ntile);
   if (int rc = check_launch("psa qkv_proj")) return rc;
   const float scale_log2 = (1.0f / sqrtf((float)kd)) * 1.4426950408889634f;
+  // overlap_pe: attention and PE (both read only V and Q/K) run on the side
+  // streams after the qkv GEMM and join before the projection
+  SideStreams* side = nullptr;
+  if (overlap_pe) {
+    if (int rc = side_streams(&side)) return rc;
+    if (int rc = stream_dep(st, side->hi)) return rc;
+    if (int rc = stream_dep(st, side->lo)) return rc;
+  }
+  const cudaStream_t sa = side ? side->hi : st, sp = side ? side->lo : st;
   if (int rc = launch_attn<kKD, kOutChannelMajor>(dim3((ntile + 1) / 2, BH), mqk, mv, ob, lse_out, N, Np, nh,
-                                                  scale_log2, st))
+                                                  scale_log2, sa))
     return rc;
-  const int pe_rc = pe_dwconv_vec(vb, w_pe, b_pe, peb, w_proj, wp16, B, kC, H, W, Np, nullptr, st);
+  const int pe_rc = pe_dwconv_vec(vb, w_pe, b_pe, peb, w_proj, wp16, B, kC, H, W, Np, nullptr, sp);
   if (pe_rc == VA_ERR_UNSUPPORTED) {
-    pe_dwconv_kernel<<<dim3(kC / kPeCh, B), kPeThreads, sm3, st>>>(vb, w_pe, b_pe, peb, w_proj, wp16, H, W, Np);
+    pe_dwconv_kernel<<<dim3(kC / kPeCh, B), kPeThreads, sm3, sp>>>(vb, w_pe, b_pe, peb, w_proj, wp16, H, W, Np);
     if (int rc = check_launch("psa pe")) return rc;
   } else if (pe_rc) {
     return pe_rc;
+  }
+  if (side) {
+    if (int rc = stream_dep(side->hi, st)) return rc;
+    if (int rc = stream_dep(side->lo, st)) return rc;
   }
   if (N % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
     CUtensorMap my;
