@@ -521,7 +521,8 @@ class Cfg3:
         pk, src = peaks()
         work = MS_FWD_BYTES[self.dtype] * self.B // MS_B
         ach = work / (ms * 1e-3) / 1e9
-        r = {"bound": "hbm", "kernel": "msda_fwd_kernel (bilinear gather, 16-byte corner loads)", "achieved": ach,
+        load = "16-byte (4 x f32)" if self.dtype == "f32" else "8-byte (4 x bf16)"
+        r = {"bound": "hbm", "kernel": f"msda_fwd_kernel (bilinear gather, {load} corner loads)", "achieved": ach,
              "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "peak_source": f"{src} hbm_gbs",
              "traffic": None, "bytes_per_launch": work, "ms_per_launch": ms,
              "backward": {"ms": ms_b, "bytes": MS_BWD_BYTES_F32 * self.B // MS_B if self.dtype == "f32" else None,
@@ -935,6 +936,80 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def timed_steps(wl, steps, warmup, min_warm_s, flush, dev, ws, barrier, counter=lambda: 0):
+    """Warm up, then time ``steps`` steps (CUDA events per step on the current
+    stream, L2 evicted before each, outside the events).  Returns the mean ms
+    per step and how far ``counter()`` advanced over the timed steps."""
+    import torch
+    import torch.distributed as dist
+    stream = torch.cuda.current_stream()
+    # Warm up in chunks of `warmup` steps until both the step count and the
+    # minimum duration are reached; with several ranks they agree (MAX) after
+    # every chunk, so all run the same number of steps — a step may hold a
+    # collective (cfg5), and ranks that disagreed on the count would hang.
+    t_w = time.perf_counter()
+    while True:
+        for _ in range(warmup):
+            wl.step()
+        torch.cuda.synchronize()
+        more = torch.tensor([1.0 if time.perf_counter() - t_w < min_warm_s else 0.0], device=dev)
+        if ws > 1:
+            dist.all_reduce(more, op=dist.ReduceOp.MAX)
+        if more.item() == 0.0:
+            break
+    barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    c0 = counter()
+    barrier()
+    for i in range(steps):
+        evict_l2(flush, i)  # between timed steps, outside the events
+        starts[i].record(stream)
+        wl.step()
+        ends[i].record(stream)
+    barrier()
+    return statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends)), counter() - c0
+
+
+# Configurations the default (cfg2) run also measures, briefly, so that one
+# run covers every BASELINE configuration at the run's GPU count.
+SIDE_CONFIGS = (("cfg1", {}), ("cfg3", {"dtype": "f32"}), ("cfg3_bf16", {"dtype": "bf16"}), ("cfg4", {}),
+                ("cfg5", {}))
+
+
+def measure_side(name, overrides, args, ws, rank, dev, flush, barrier):
+    """One side configuration: images/s over a short timed run (max over
+    ranks) and its dominant kernel's roofline fraction; no e2e, no CPU leg."""
+    import copy
+
+    import torch
+    import torch.distributed as dist
+    a = copy.copy(args)
+    for k, v in overrides.items():
+        setattr(a, k, v)
+    a.steps, a.warmup = 10, 3
+    cls = CONFIGS[name.split("_")[0]]
+    wl = cls(dev, rank, cls.batch, a)
+    try:
+        ms, _ = timed_steps(wl, a.steps, a.warmup, 0.3, flush, dev, ws, barrier)
+        dom = wl.dominant(a, torch.cuda.current_stream(), flush)
+        t = torch.tensor([ms, dom["ms_per_launch"]], device=dev, dtype=torch.float64)
+        if ws > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, dom_ms = t.tolist()
+    finally:
+        if hasattr(wl, "close"):
+            wl.close()
+    out = {"workload": wl.workload, "value": cls.batch * ws / (ms * 1e-3), "unit": "images/s",
+           "ms_per_step": ms, "per_gpu_batch": cls.batch, "global_batch": cls.batch * ws, "steps": a.steps,
+           "dtype": getattr(wl, "dtype", "bf16"),
+           "dominant": {"kernel": dom.get("kernel"), "bound": dom.get("bound"), "frac": dom.get("frac"),
+                        "peak_source": dom.get("peak_source"), "ms_per_launch_max_over_ranks": dom_ms}}
+    del wl
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, ws, rank, local):
     import datetime
 
@@ -959,37 +1034,12 @@ def run_ours(args, ws, rank, local):
         torch.cuda.synchronize()
 
     clk = ClockSampler(local).start()
-    # Warm up in chunks of `warmup` steps until both the step count and the
-    # minimum duration are reached; with several ranks they agree (MAX) after
-    # every chunk, so all run the same number of steps — a step may hold a
-    # collective (cfg5), and ranks that disagreed on the count would hang.
-    t_w, nw = time.perf_counter(), 0
-    while True:
-        for _ in range(args.warmup):
-            wl.step()
-            nw += 1
-        torch.cuda.synchronize()
-        more = torch.tensor([1.0 if time.perf_counter() - t_w < args.min_warm_s else 0.0], device=dev)
-        if ws > 1:
-            dist.all_reduce(more, op=dist.ReduceOp.MAX)
-        if more.item() == 0.0:
-            break
-    barrier()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     replayed = lambda: (getattr(getattr(wl, "step_obj", None), "replayed_kernels", 0)
                         + getattr(getattr(wl, "graph_step", None), "replayed_kernels", 0))
-    lc0 = _lib.lib().va_launch_count() + replayed()
-    barrier()
-    for i in range(args.steps):
-        evict_l2(flush, i)  # between timed steps, outside the events
-        starts[i].record(stream)
-        wl.step()
-        ends[i].record(stream)
-    barrier()
+    # kernels launched directly or by graph replays inside the timed steps
+    ms, launches = timed_steps(wl, args.steps, args.warmup, args.min_warm_s, flush, dev, ws, barrier,
+                               counter=lambda: _lib.lib().va_launch_count() + replayed())
     clk.stop()
-    launches = _lib.lib().va_launch_count() + replayed() - lc0  # kernels launched directly or by graph replays
-    ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
 
     dom = wl.dominant(args, stream, flush)
     e2e_ms = float("nan")
@@ -1013,6 +1063,10 @@ def run_ours(args, ws, rank, local):
     ms, e2e_ms, dom_ms = t.tolist()
     dom["ms_per_launch_max_over_ranks"] = dom_ms
 
+    side = {}
+    if args.config == "cfg2" and args.width == "n" and not args.batch and args.side_configs:
+        for name, ov in SIDE_CONFIGS:
+            side[name] = measure_side(name, ov, args, ws, rank, dev, flush, barrier)
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(cls, args)
@@ -1035,6 +1089,8 @@ def run_ours(args, ws, rank, local):
             "clocks": clk.summary(),
         }
         line.update(wl.extra(ms))
+        if side:
+            line["other_configs"] = side
         print(json.dumps(line), flush=True)
     if hasattr(wl, "close"):
         wl.close()
@@ -1060,6 +1116,9 @@ def main():
     ap.add_argument("--min-warm-s", type=float, default=1.5,
                     help="keep warming up at least this long so the clock sampler sees the load")
     ap.add_argument("--batch", type=int, default=0, help="per-GPU batch (default: the config's)")
+    ap.add_argument("--no-side-configs", dest="side_configs", action="store_false",
+                    help="cfg2 only: skip the short runs of cfg1, cfg3 (f32, bf16), cfg4 and cfg5 "
+                         "reported under other_configs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local = dist_env()
