@@ -95,6 +95,14 @@ int conv_status_clear(cudaStream_t st);
 // the C = 128 kernels of the training step: psa_tc_is_n.
 bool psa_tc_supported(int C, int nh, int kd);
 inline bool psa_tc_is_n(int C, int nh, int kd) { return C == 128 && nh == 2 && kd == 32; }
+// Per-device side streams of the library (highest / lowest stream priority),
+// created by the first call on a device; psa_stream_dep(from, to) makes `to`
+// wait for the work issued on `from` so far (an event per call).
+struct SideStreams {
+  cudaStream_t hi = nullptr, lo = nullptr;
+};
+int psa_side_streams(SideStreams** out);
+int psa_stream_dep(cudaStream_t from, cudaStream_t to);
 // overlap_pe (C = 128): attention and PE on the library's per-device side
 // streams (highest / lowest priority), forked from and joined back to `st`.
 int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,

@@ -474,8 +474,10 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   }
   float* lse = static_cast<float*>(at(L.lse));
   // forward, keeping Q/K/V/O/PE and the row LSEs
+  // the forward's PE and the backward's side work run on the library's side streams (psa_side_streams)
+  const bool overlap = true;
   if (int rc = psa_attention_fwd_tc(x, w_qkv, b_qkv, w_pe, b_pe, w_proj, b_proj, y, B, C, H, W, nh, kd, ws,
-                                    L.fwd.total, st, lse))
+                                    L.fwd.total, st, lse, overlap))
     return rc;
   const __half* qk = static_cast<const __half*>(at(L.fwd.qk));
   const __half* vb = static_cast<const __half*>(at(L.fwd.v));
@@ -499,19 +501,31 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   else
     loss_rows_kernel<<<(unsigned)rows, kRowThreads, 0, st>>>(r_src, target, r16, rsum, rsq, N, Np, inv_scale);
   if (int rc = check_launch("psa train loss")) return rc;
+  // Fork: the weight-gradient GEMMs of the projection and the f16 copies of x
+  // and W_qkv need only r and the forward's buffers, so they run on the
+  // lowest-priority side stream beside the attention backward chain (dA →
+  // attention backward → dqkv assembly, highest priority); both join `st`
+  // before the qkv weight gradient.
+  SideStreams* side = nullptr;
+  if (overlap) {
+    if (int rc = psa_side_streams(&side)) return rc;
+    if (int rc = psa_stream_dep(st, side->hi)) return rc;
+    if (int rc = psa_stream_dep(st, side->lo)) return rc;
+  }
+  const cudaStream_t cs = side ? side->hi : st, ss = side ? side->lo : st;
   // dW_proj partials: Pz from O, then Pz from PE (kZFold images per accumulator)
   float* pwp = static_cast<float*>(at(L.part_wproj));
   const GemmOperand a_r{r16, false, Np, (long long)kC * Np, false};
   if (int rc = tc_gemm_f16(a_r, GemmOperand{ob, false, Np, (long long)kC * Np, false}, pwp, 0, kC,
-                           (long long)kC * kC, kC, kC, N, B, st, 1.0f, kZFold))
+                           (long long)kC * kC, kC, kC, N, B, ss, 1.0f, kZFold))
     return rc;
   if (int rc = tc_gemm_f16(a_r, GemmOperand{peb, false, Np, (long long)kC * Np, false}, pwp + (size_t)Pz * kC * kC, 0,
-                           kC, (long long)kC * kC, kC, kC, N, B, st, 1.0f, kZFold))
+                           kC, (long long)kC * kC, kC, kC, N, B, ss, 1.0f, kZFold))
     return rc;
   // dA[b][i][n] = Σ_o W_proj[o][i]·r[b][o][n]  (f16, dO of the attention and dPE)
   __half* dA = static_cast<__half*>(at(L.dA16));
   if (int rc = tc_gemm_f16(GemmOperand{wp16, true, kC, 0, true}, GemmOperand{r16, true, Np, (long long)kC * Np, false},
-                           dA, 2, Np, (long long)kC * Np, kC, N, kC, B, st))
+                           dA, 2, Np, (long long)kC * Np, kC, N, kC, B, cs))
     return rc;
   // attention backward → channel-major dK, dV, dQ partials
   const size_t fsz = (size_t)BH * N * kKD;
@@ -521,31 +535,31 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   int nparts = 1;
   if (N <= 512) {
     float* delta = fa + 7 * fsz;  // [B·nh][N] ≤ fsz floats
-    if (int rc = psa_attn_bwd_tc(qk, vb, ob, dA, lse, delta, dk, dv, dqp, B, nh, N, st)) return rc;
+    if (int rc = psa_attn_bwd_tc(qk, vb, ob, dA, lse, delta, dk, dv, dqp, B, nh, N, cs)) return rc;
     nparts = (N + 127) / 128;
   } else {  // f32 SIMT kernels, one call per V half (dq and dk accumulate), then channel-major
     float *q32 = fa + 4 * fsz, *k32 = fa + 5 * fsz, *vh = fa + 6 * fsz, *oh = fa + 8 * fsz, *doh = fa + 10 * fsz;
     float *dq = fa + 12 * fsz, *dkt = fa + 13 * fsz, *dvh = fa + 14 * fsz;
-    f16_to_f32_kernel<<<grid_for(2 * fsz), 256, 0, st>>>(qk, q32, (long long)(2 * fsz));
-    to_fa_halves_kernel<<<grid_for(2 * fsz), 256, 0, st>>>(vb, vh, B, N, Np);
-    to_fa_halves_kernel<<<grid_for(2 * fsz), 256, 0, st>>>(ob, oh, B, N, Np);
-    to_fa_halves_kernel<<<grid_for(2 * fsz), 256, 0, st>>>(dA, doh, B, N, Np);
+    f16_to_f32_kernel<<<grid_for(2 * fsz), 256, 0, cs>>>(qk, q32, (long long)(2 * fsz));
+    to_fa_halves_kernel<<<grid_for(2 * fsz), 256, 0, cs>>>(vb, vh, B, N, Np);
+    to_fa_halves_kernel<<<grid_for(2 * fsz), 256, 0, cs>>>(ob, oh, B, N, Np);
+    to_fa_halves_kernel<<<grid_for(2 * fsz), 256, 0, cs>>>(dA, doh, B, N, Np);
     if (int rc = check_launch("psa train layouts")) return rc;
-    cudaMemsetAsync(dq, 0, 2 * fsz * sizeof(float), st);
+    cudaMemsetAsync(dq, 0, 2 * fsz * sizeof(float), cs);
     const float scale = 1.0f / sqrtf((float)kd);
     for (int half = 0; half < 2; ++half)
       if (int rc = va_psa_fa2_backward_f32(q32, k32, vh + half * fsz, oh + half * fsz, doh + half * fsz, lse, dq, dkt,
-                                           dvh + half * fsz, N, scale, BH, kKD, st))
+                                           dvh + half * fsz, N, scale, BH, kKD, cs))
         return rc;
-    tm_to_cm_kernel<<<grid_for(fsz), 256, 0, st>>>(dq, dqp, BH, N, kKD);
-    tm_to_cm_kernel<<<grid_for(fsz), 256, 0, st>>>(dkt, dk, BH, N, kKD);
+    tm_to_cm_kernel<<<grid_for(fsz), 256, 0, cs>>>(dq, dqp, BH, N, kKD);
+    tm_to_cm_kernel<<<grid_for(fsz), 256, 0, cs>>>(dkt, dk, BH, N, kKD);
     // dv halves [2][BH][N][32] → [BH][64][N]: channels 0-31 from lo, 32-63 from hi
-    tm_to_cm_kernel<<<grid_for(fsz), 256, 0, st>>>(dvh, q32, BH, N, kKD);            // lo → [BH][32][N]
-    tm_to_cm_kernel<<<grid_for(fsz), 256, 0, st>>>(dvh + fsz, q32 + fsz, BH, N, kKD);  // hi → [BH][32][N]
+    tm_to_cm_kernel<<<grid_for(fsz), 256, 0, cs>>>(dvh, q32, BH, N, kKD);            // lo → [BH][32][N]
+    tm_to_cm_kernel<<<grid_for(fsz), 256, 0, cs>>>(dvh + fsz, q32 + fsz, BH, N, kKD);  // hi → [BH][32][N]
     for (int half = 0; half < 2; ++half)
       cudaMemcpy2DAsync(dv + (size_t)half * kKD * N, (size_t)kHD * N * sizeof(float), q32 + half * fsz,
                         (size_t)kKD * N * sizeof(float), (size_t)kKD * N * sizeof(float), BH,
-                        cudaMemcpyDeviceToDevice, st);
+                        cudaMemcpyDeviceToDevice, cs);
   }
   // dqkv rows (+ PE backward and the bias partials)
   __half* dq16 = static_cast<__half*>(at(L.dqkv16));
@@ -560,22 +574,26 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
     return rc;
   int asm_rows = kAsmRows;  // rows (warps) per CTA: a power of two dividing kQKV whose planes fit
   while (asm_rows > 1 && (size_t)asm_rows * 2 * N * sizeof(float) > 200 * 1024) asm_rows >>= 1;
-  assemble_kernel<<<dim3(kQKV / asm_rows, B), asm_rows * 32, (size_t)asm_rows * 2 * N * sizeof(float), st>>>(
+  assemble_kernel<<<dim3(kQKV / asm_rows, B), asm_rows * 32, (size_t)asm_rows * 2 * N * sizeof(float), cs>>>(
       dqp, nparts, dk, dv, dA, vb, w_pe, dq16, pbq, pwe, pbe, B, H, W, Np);
   if (int rc = check_launch("psa train assemble")) return rc;
   // qkv backward
   __half* x16 = static_cast<__half*>(at(L.x16));
   __half* wq16 = static_cast<__half*>(at(L.wqkv16));
   if (N == Np && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {  // x and W_qkv in one launch
-    bf16_to_f16_vec_kernel<<<grid_for(rows * N / 8 + kQKV * kC / 8), 256, 0, st>>>(
+    bf16_to_f16_vec_kernel<<<grid_for(rows * N / 8 + kQKV * kC / 8), 256, 0, ss>>>(
         reinterpret_cast<const uint4*>(x), reinterpret_cast<uint4*>(x16), rows * N / 8,
         reinterpret_cast<const uint4*>(w_qkv), reinterpret_cast<uint4*>(wq16), kQKV * kC / 8);
   } else {
-    bf16_to_f16_pad_kernel<<<grid_for(rows * Np), 256, 0, st>>>(x, x16, rows, N, Np);
-    bf16_to_f16_vec_kernel<<<grid_for(kQKV * kC / 8), 256, 0, st>>>(reinterpret_cast<const uint4*>(w_qkv),
+    bf16_to_f16_pad_kernel<<<grid_for(rows * Np), 256, 0, ss>>>(x, x16, rows, N, Np);
+    bf16_to_f16_vec_kernel<<<grid_for(kQKV * kC / 8), 256, 0, ss>>>(reinterpret_cast<const uint4*>(w_qkv),
                                                                     reinterpret_cast<uint4*>(wq16), kQKV * kC / 8);
   }
   if (int rc = check_launch("psa train qkv prep")) return rc;
+  if (side) {
+    if (int rc = psa_stream_dep(cs, st)) return rc;
+    if (int rc = psa_stream_dep(ss, st)) return rc;
+  }
   float* pwq = static_cast<float*>(at(L.part_wqkv));
   if (int rc = tc_gemm_f16(GemmOperand{dq16, false, Np, (long long)kQKV * Np, false},
                            GemmOperand{x16, false, Np, (long long)kC * Np, false}, pwq, 0, kC, (long long)kQKV * kC,

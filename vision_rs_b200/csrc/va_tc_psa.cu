@@ -1513,19 +1513,18 @@ PsaTcOffsets psa_tc_offsets(int B, int H, int W, int nh) {
 
 bool psa_tc_supported(int C, int nh, int kd) { return kd == kKD && nh >= 1 && C == nh * kHD; }
 
+// Side streams of one device for the fork/joins inside the library's ops:
+// the critical chain (the fused op's attention, the training step's attention
+// backward) on the highest stream priority, independent side work (PE, the
+// projection's weight gradients) on the lowest, so the block scheduler places
+// side blocks only on SMs that no critical block is waiting for — such as
+// the tail of the attention grid.  Created once per device.
 namespace {
-
-// Side streams of one device for the fused op's fork/join: the attention on
-// the highest stream priority, the PE convolution on the lowest, so the block
-// scheduler places PE blocks only on SMs that no attention block is waiting
-// for — the tail of the attention grid.  Created once per device.
-struct SideStreams {
-  cudaStream_t hi = nullptr, lo = nullptr;
-};
 SideStreams g_side[64];
 PerDeviceOnce g_side_once;
+}  // namespace
 
-int side_streams(SideStreams** out) {
+int psa_side_streams(SideStreams** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VA_ERR_UNSUPPORTED;
   const int rc = g_side_once.run([dev]() -> int {
@@ -1534,7 +1533,7 @@ int side_streams(SideStreams** out) {
         cudaStreamCreateWithPriority(&g_side[dev].hi, cudaStreamNonBlocking, hi) != cudaSuccess ||
         cudaStreamCreateWithPriority(&g_side[dev].lo, cudaStreamNonBlocking, lo) != cudaSuccess) {
       cudaGetLastError();
-      return set_error(VA_ERR_LAUNCH, "psa_attention bf16: side stream creation failed");
+      return set_error(VA_ERR_LAUNCH, "psa: side stream creation failed");
     }
     return VA_OK;
   });
@@ -1545,7 +1544,7 @@ int side_streams(SideStreams** out) {
 
 // Records an event on `from` and makes `to` wait for it (the event is
 // released at once; CUDA keeps it until the wait is resolved).
-int stream_dep(cudaStream_t from, cudaStream_t to) {
+int psa_stream_dep(cudaStream_t from, cudaStream_t to) {
   cudaEvent_t e;
   cudaError_t r = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
   if (r == cudaSuccess) {
@@ -1553,11 +1552,9 @@ int stream_dep(cudaStream_t from, cudaStream_t to) {
     if (r == cudaSuccess) r = cudaStreamWaitEvent(to, e, 0);
     cudaEventDestroy(e);
   }
-  if (r != cudaSuccess) return set_error(VA_ERR_LAUNCH, "psa_attention bf16: stream dependency: %s", cudaGetErrorString(r));
+  if (r != cudaSuccess) return set_error(VA_ERR_LAUNCH, "psa: stream dependency: %s", cudaGetErrorString(r));
   return VA_OK;
 }
-
-}  // namespace
 
 int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,
                          const __nv_bfloat16* w_pe, const float* b_pe, const __nv_bfloat16* w_proj,
@@ -1658,9 +1655,9 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   // streams after the qkv GEMM and join before the projection
   SideStreams* side = nullptr;
   if (overlap_pe) {
-    if (int rc = side_streams(&side)) return rc;
-    if (int rc = stream_dep(st, side->hi)) return rc;
-    if (int rc = stream_dep(st, side->lo)) return rc;
+    if (int rc = psa_side_streams(&side)) return rc;
+    if (int rc = psa_stream_dep(st, side->hi)) return rc;
+    if (int rc = psa_stream_dep(st, side->lo)) return rc;
   }
   const cudaStream_t sa = side ? side->hi : st, sp = side ? side->lo : st;
   if (int rc = launch_attn<kKD, kOutChannelMajor>(dim3((ntile + 1) / 2, BH), mqk, mv, ob, lse_out, N, Np, nh,
@@ -1674,8 +1671,8 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
     return pe_rc;
   }
   if (side) {
-    if (int rc = stream_dep(side->hi, st)) return rc;
-    if (int rc = stream_dep(side->lo, st)) return rc;
+    if (int rc = psa_stream_dep(side->hi, st)) return rc;
+    if (int rc = psa_stream_dep(side->lo, st)) return rc;
   }
   if (N % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
     CUtensorMap my;
