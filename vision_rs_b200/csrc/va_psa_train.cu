@@ -192,7 +192,7 @@ __global__ void tm_to_cm_kernel(const float* __restrict__ src, float* __restrict
 // Writes the f16 row (pad zero), its sum (db_qkv partial) and, on V channels,
 // the dW_pe (9 taps) and db_pe partials of (b, c).  Every sum is a fixed-order
 // warp reduction (no block barrier).  Shared memory: per warp the dA and V
-// planes of (b, c), f32.
+// planes of (b, c), f32, each with a one-pixel zero border.
 constexpr int kAsmRows = 4;
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -215,30 +215,50 @@ assemble_kernel(const float* __restrict__ dq_part, int nparts, const float* __re
   float rs = 0.f;
   if (r < 64) {
     const float* src = r < 32 ? dq_part + ((size_t)bh * kKD + r) * N : dk + ((size_t)bh * kKD + r - 32) * N;
-    for (int n = lane; n < Np; n += 32) {
-      float g = 0.f;
-      if (n < N) {
-        if (r < 32) {
-          for (int p = 0; p < nparts; ++p) g += src[p * part + n];
-        } else {
-          g = src[n];
-        }
-        rs += g;
+    const int np_ = r < 32 ? nparts : 1;
+    // four tokens per lane per pass (n0 + 32u): their loads are in flight together
+    for (int n0 = lane; n0 < Np; n0 += 128) {
+      float g[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int p = 0; p < np_; ++p)  // partials summed in order p = 0, 1, …
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (n0 + 32 * u < N) g[u] += src[p * part + n0 + 32 * u];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int n = n0 + 32 * u;
+        if (n < N) rs += g[u];
+        if (n < Np) out[n] = __float2half_rn(g[u]);
       }
-      out[n] = __float2half_rn(g);
     }
     rs = warp_sum(rs);
     if (lane == 0) part_bqkv[(size_t)b * kQKV + j] = rs;
     return;
   }
   const int dd = r - 64, c = h * kHD + dd;
-  float* pa = planes + (size_t)warp * 2 * N;
-  float* pv = pa + N;
+  // dA and V planes with a one-pixel zero border: pixel (y, x) at (y + 1)·Wp + x + 1, so the
+  // 3×3 taps need no bounds checks (a border tap adds w·0)
+  const int Wp = W + 2, Pp = (H + 2) * Wp;
+  float* pa = planes + (size_t)warp * 2 * Pp;
+  float* pv = pa + Pp;
+  for (int i = lane; i < 2 * Pp; i += 32) pa[i] = 0.f;
+  __syncwarp();
   const __half* arow = dA + ((size_t)b * kC + c) * Np;
   const __half* vrow = vb + ((size_t)b * kC + c) * Np;
-  for (int n = lane; n < N; n += 32) {
-    pa[n] = __half2float(arow[n]);
-    pv[n] = __half2float(vrow[n]);
+  const int dy = 32 / W, dx = 32 - dy * W;
+  {
+    int yy = lane / W, xx = lane - yy * W;
+#pragma unroll 4
+    for (int n = lane; n < N; n += 32) {
+      const int q = (yy + 1) * Wp + xx + 1;
+      pa[q] = __half2float(arow[n]);
+      pv[q] = __half2float(vrow[n]);
+      yy += dy;
+      xx += dx;
+      if (xx >= W) {
+        xx -= W;
+        ++yy;
+      }
+    }
   }
   float w[9];
 #pragma unroll
@@ -247,22 +267,22 @@ assemble_kernel(const float* __restrict__ dq_part, int nparts, const float* __re
   const float* dvr = dv + ((size_t)bh * kHD + dd) * N;
   float tw[9] = {}, ab = 0.f;
   int yy = lane / W, xx = lane - yy * W;  // (y, x) of n, advanced by 32 per iteration
-  const int dy = 32 / W, dx = 32 - dy * W;
+#pragma unroll 2
   for (int n = lane; n < Np; n += 32) {
     float g = 0.f;
     if (n < N) {
-      const float a = pa[n];
+      const int q = (yy + 1) * Wp + xx + 1;
+      const float a = pa[q];
       ab += a;
       float pe = 0.f;
 #pragma unroll
       for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
         for (int kx = 0; kx < 3; ++kx) {
-          // forward: PE[y][x] += w[ky][kx]·V[y+ky−1][x+kx−1]
-          const int sy = yy - ky + 1, sx = xx - kx + 1;  // dV[y][x] += w·dA[y−ky+1][x−kx+1]
-          if (sy >= 0 && sy < H && sx >= 0 && sx < W) pe = fmaf(w[ky * 3 + kx], pa[sy * W + sx], pe);
-          const int vy = yy + ky - 1, vx = xx + kx - 1;  // dW[ky][kx] += dA[y][x]·V[y+ky−1][x+kx−1]
-          if (vy >= 0 && vy < H && vx >= 0 && vx < W) tw[ky * 3 + kx] = fmaf(a, pv[vy * W + vx], tw[ky * 3 + kx]);
+          // forward: PE[y][x] += w[ky][kx]·V[y+ky−1][x+kx−1], so
+          // dV[y][x] += w·dA[y−ky+1][x−kx+1] and dW[ky][kx] += dA[y][x]·V[y+ky−1][x+kx−1]
+          pe = fmaf(w[ky * 3 + kx], pa[q + (1 - ky) * Wp + (1 - kx)], pe);
+          tw[ky * 3 + kx] = fmaf(a, pv[q + (ky - 1) * Wp + (kx - 1)], tw[ky * 3 + kx]);
         }
       g = dvr[n] + pe;
       rs += g;
@@ -460,7 +480,8 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   else
     VA_CHECK_ARG(x && target && grads && loss && y, "psa train: null x/target/grads/loss/y");
   const int N = H * W, Np = (N + 7) / 8 * 8, BH = B * nh;
-  VA_CHECK_ARG(2 * (size_t)N * sizeof(float) <= 200 * 1024, "psa train: %d tokens per image exceed the staged planes",
+  VA_CHECK_ARG(2 * (size_t)(H + 2) * (W + 2) * sizeof(float) <= 200 * 1024,
+               "psa train: %d tokens per image exceed the staged planes",
                N);
   const TrainWs L = train_layout(B, H, W);
   if (!ws || ws_bytes < L.total)
@@ -573,8 +594,9 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
       }))
     return rc;
   int asm_rows = kAsmRows;  // rows (warps) per CTA: a power of two dividing kQKV whose planes fit
-  while (asm_rows > 1 && (size_t)asm_rows * 2 * N * sizeof(float) > 200 * 1024) asm_rows >>= 1;
-  assemble_kernel<<<dim3(kQKV / asm_rows, B), asm_rows * 32, (size_t)asm_rows * 2 * N * sizeof(float), cs>>>(
+  const size_t plane_bytes = 2 * (size_t)(H + 2) * (W + 2) * sizeof(float);  // dA and V with a zero border
+  while (asm_rows > 1 && (size_t)asm_rows * plane_bytes > 200 * 1024) asm_rows >>= 1;
+  assemble_kernel<<<dim3(kQKV / asm_rows, B), asm_rows * 32, (size_t)asm_rows * plane_bytes, cs>>>(
       dqp, nparts, dk, dv, dA, vb, w_pe, dq16, pbq, pwe, pbe, B, H, W, Np);
   if (int rc = check_launch("psa train assemble")) return rc;
   // qkv backward
