@@ -344,6 +344,7 @@ __global__ void __launch_bounds__(256) finalize_vec_kernel(FinalizeArgs a) {
     else if (i < VA_PSA_GRAD_BPE) { src = a.rsum; np = a.B; off = i - VA_PSA_GRAD_BPROJ; stride = kC; }
     else { src = a.part_bpe; np = a.B; off = i - VA_PSA_GRAD_BPE; stride = kC; }
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
     for (int p = j; live && p < np; p += 8) {
       const float4 v = __ldg(reinterpret_cast<const float4*>(src + p * stride + off));
       s.x += v.x;
@@ -364,7 +365,8 @@ __global__ void __launch_bounds__(256) finalize_vec_kernel(FinalizeArgs a) {
   if (blockIdx.x == 0) {
     __shared__ float red[256];
     float s = 0.f;
-    for (int i = threadIdx.x; i < a.B * kC; i += 256) s += a.rsq[i];
+#pragma unroll 8
+    for (int i = threadIdx.x; i < a.B * kC; i += 256) s += a.rsq[i];  // loads in flight, sums in order
     red[threadIdx.x] = s;
     __syncthreads();
     for (int o = 128; o > 0; o >>= 1) {
@@ -393,7 +395,8 @@ __global__ void __launch_bounds__(256) finalize_kernel(FinalizeArgs a) {
   if (blockIdx.x == 0) {
     __shared__ float red[256];
     float s = 0.f;
-    for (int i = threadIdx.x; i < a.B * kC; i += 256) s += a.rsq[i];
+#pragma unroll 8
+    for (int i = threadIdx.x; i < a.B * kC; i += 256) s += a.rsq[i];  // loads in flight, sums in order
     red[threadIdx.x] = s;
     __syncthreads();
     for (int o = 128; o > 0; o >>= 1) {
