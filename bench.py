@@ -635,6 +635,22 @@ class Cfg4:
         qkv = torch_empty_like_qkv(self.x)
         lin = lambda: self.dn.qkv_linear(self.x, self.op.w_qkv, self.op.b_qkv, out=qkv)
         ms_lin = event_time(lin, max(5, args.steps), stream, flush)
+        # the whole global layer (QKV Linear + attention) through the op, and torch's own
+        # F.linear + scaled_dot_product_attention on the same bf16 inputs, for comparison
+        import torch
+        import torch.nn.functional as F
+        ours = lambda: self.op.forward_into(self.x, self.og)
+        wt, bt = self.op.w_qkv, self.op.b_qkv.to(torch.bfloat16)
+        B_, n_ = self.x.shape[0], self.x.shape[1]
+
+        def torch_global():
+            q, k, v = F.linear(self.x, wt, bt).view(B_, n_, 3, DN_HEADS, 64).permute(2, 0, 3, 1, 4)
+            return F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(B_, n_, DN_HID)
+        for _ in range(args.warmup):
+            ours()
+            torch_global()
+        self.global_ms = event_time(ours, max(5, args.steps), stream, flush)
+        self.torch_global_ms = event_time(torch_global, max(5, args.steps), stream, flush)
         pk, src = peaks()
         work = self.B * DN_FLOP_GLOBAL_ATTN_IMG
         ach = work / (ms * 1e-3) / 1e12
@@ -645,7 +661,11 @@ class Cfg4:
                 "qkv_linear_tflops": 2 * self.B * DN_N * DN_HID * 3 * DN_HID / (ms_lin * 1e-3) / 1e12}
 
     def extra(self, ms):
-        return {"tflops_whole_step": DN_FLOP_IMG * self.B / (ms * 1e-3) / 1e12}
+        return {"tflops_whole_step": DN_FLOP_IMG * self.B / (ms * 1e-3) / 1e12,
+                "global_layer_ms": getattr(self, "global_ms", None),
+                "torch_global_layer_ms": getattr(self, "torch_global_ms", None),
+                "torch_global_layer": "torch F.linear + F.scaled_dot_product_attention, bf16, same inputs "
+                                      "(a measurement beside ours, not a path of this library)"}
 
     config = {"seq_len": DN_N, "window_seq_len": DN_NWIN,
               "precision": "bf16 I/O, weights and QKV GEMM; f16 Q/K/V/P; f32 accumulation",

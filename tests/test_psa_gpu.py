@@ -267,6 +267,18 @@ def test_fused_bf16_vs_oracle(cuda, B, H, W):
     assert max_abs(host(y), ref) < BF16_MAX_ABS
 
 
+def test_fused_bf16_large_image_matches_f32_path(cuda):
+    """A 120×120 map (14400 tokens; its PE plane is larger than the shared-memory
+    staging of the fallback PE kernel, so only the register-window PE kernel can
+    run it): the bf16 tensor-core op against the f32 op on the same bf16-rounded
+    inputs (the f32 path is held to the oracle at 1e-5 above), bf16 bound."""
+    p = _bf16_inputs(po.psa_synthetic(1, 120, 120, seed=120))
+    y16 = host(_op(p, torch.bfloat16)(dev(p["x"], torch.bfloat16)))
+    y32 = host(_op(p, torch.float32)(dev(p["x"])))
+    assert rel_l2(y16, y32) < BF16_REL_L2
+    assert max_abs(y16, y32) < BF16_MAX_ABS
+
+
 def test_fused_bf16_full_cfg2_batch(cuda):
     """cfg2 at full size (64×128×40×40): images 0, 31 and 63 against the oracle,
     and a batch-consistency property (an image's output does not depend on its

@@ -1559,12 +1559,20 @@ int launch_attn(dim3 grid, const CUtensorMap& mqk, const CUtensorMap& mv, void* 
 
 }  // namespace
 
+// The register-window PE kernel (no shared-memory plane, any image size) takes
+// rows of 4 or 8 columns; otherwise the plane-staging kernel runs, which
+// holds (H + 2) · pitch floats of a channel in shared memory (kMaxPlane).
+bool pe_vec_supported(int B, int C, int H, int W) {
+  const int cw = (W & 7) == 0 ? 8 : (W & 3) == 0 ? 4 : 0;
+  return cw && (long long)B * C * ((H + kPevRows - 1) / kPevRows) * (W / cw) < (1LL << 31);
+}
+
 int pe_dwconv_vec(const __half* v, const __nv_bfloat16* w_pe, const float* b_pe, __half* pe,
                   const __nv_bfloat16* w_proj, __half* wproj16, int B, int C, int H, int W, int Np,
                   const __half* add, cudaStream_t st) {
   const int cw = (W & 7) == 0 ? 8 : (W & 3) == 0 ? 4 : 0;
   const long long blocks = cw ? (long long)B * C * ((H + kPevRows - 1) / kPevRows) * (W / cw) : 0;
-  if (!cw || blocks >= (1LL << 31)) return VA_ERR_UNSUPPORTED;
+  if (!pe_vec_supported(B, C, H, W)) return VA_ERR_UNSUPPORTED;
   const unsigned grid = (unsigned)((blocks + kPevThreads - 1) / kPevThreads);
   if (cw == 8)
     pe_dwconv_vec_kernel<8><<<grid, kPevThreads, 0, st>>>(v, w_pe, b_pe, pe, w_proj, wproj16, B, H, W, Np, C, add);
@@ -1635,7 +1643,8 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   if (!psa_tc_is_n(C, nh, kd))
     return psa_attention_fwd_tc_wide(x, w_qkv, b_qkv, w_pe, b_pe, w_proj, b_proj, y, B, C, H, W, nh, ws, ws_bytes, st);
   VA_CHECK_ARG(B > 0 && H > 0 && W > 0 && B <= 65535, "psa_attention bf16: bad sizes");
-  VA_CHECK_ARG((H + 2) * ((W + 10) | 1) <= kMaxPlane, "psa_attention bf16: image %dx%d larger than supported", H, W);
+  VA_CHECK_ARG(pe_vec_supported(B, kC, H, W) || (H + 2) * ((W + 10) | 1) <= kMaxPlane,
+               "psa_attention bf16: image %dx%d with W %% 4 != 0 larger than the PE plane staging supports", H, W);
   const TcWs L = tc_layout(B, H, W, nh);
   if (!ws || ws_bytes < L.total)
     return set_error(VA_ERR_WORKSPACE, "psa_attention bf16: workspace %zu < %zu bytes", ws_bytes, L.total);
