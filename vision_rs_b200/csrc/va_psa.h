@@ -103,6 +103,23 @@ struct SideStreams {
 };
 int psa_side_streams(SideStreams** out);
 int psa_stream_dep(cudaStream_t from, cudaStream_t to);
+// Joins both side streams back into `st` once: by join(), or when it goes out
+// of scope (an early error return), so no library work is left unordered
+// against the caller's stream.
+struct SideJoin {
+  SideStreams* side;
+  cudaStream_t st;
+  bool done = false;
+  int join() {
+    done = true;
+    if (!side) return 0;
+    const int a = psa_stream_dep(side->hi, st), b = psa_stream_dep(side->lo, st);
+    return a ? a : b;
+  }
+  ~SideJoin() {
+    if (!done) join();
+  }
+};
 // overlap_pe (C = 128): attention and PE on the library's per-device side
 // streams (highest / lowest priority), forked from and joined back to `st`.
 int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, const float* b_qkv,

@@ -536,6 +536,7 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
     if (int rc = psa_stream_dep(st, side->hi)) return rc;
     if (int rc = psa_stream_dep(st, side->lo)) return rc;
   }
+  SideJoin joiner{side, st};
   const cudaStream_t cs = side ? side->hi : st, ss = side ? side->lo : st;
   // dW_proj partials: Pz from O, then Pz from PE (kZFold images per accumulator)
   float* pwp = static_cast<float*>(at(L.part_wproj));
@@ -615,10 +616,7 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
                                                                     reinterpret_cast<uint4*>(wq16), kQKV * kC / 8);
   }
   if (int rc = check_launch("psa train qkv prep")) return rc;
-  if (side) {
-    if (int rc = psa_stream_dep(cs, st)) return rc;
-    if (int rc = psa_stream_dep(ss, st)) return rc;
-  }
+  if (int rc = joiner.join()) return rc;
   float* pwq = static_cast<float*>(at(L.part_wqkv));
   if (int rc = tc_gemm_f16(GemmOperand{dq16, false, Np, (long long)kQKV * Np, false},
                            GemmOperand{x16, false, Np, (long long)kC * Np, false}, pwq, 0, kC, (long long)kQKV * kC,

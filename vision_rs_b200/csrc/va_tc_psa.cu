@@ -1739,6 +1739,7 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
     if (int rc = psa_stream_dep(st, side->hi)) return rc;
     if (int rc = psa_stream_dep(st, side->lo)) return rc;
   }
+  SideJoin joiner{side, st};
   const cudaStream_t sa = side ? side->hi : st, sp = side ? side->lo : st;
   if (int rc = launch_attn<kKD, kOutChannelMajor>(dim3((ntile + 1) / 2, BH), mqk, mv, ob, lse_out, N, Np, nh,
                                                   scale_log2, sa))
@@ -1750,10 +1751,7 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   } else if (pe_rc) {
     return pe_rc;
   }
-  if (side) {
-    if (int rc = psa_stream_dep(side->hi, st)) return rc;
-    if (int rc = psa_stream_dep(side->lo, st)) return rc;
-  }
+  if (int rc = joiner.join()) return rc;
   if (N % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
     CUtensorMap my;
     uint64_t d[2] = {(uint64_t)N, (uint64_t)B * kC}, s[1] = {(uint64_t)N * 2};
