@@ -388,6 +388,21 @@ VA_API int va_psa_train_fwd_bwd_bf16(const va_bf16 *x, const va_bf16 *target, co
  * for a mean-squared loss) so that the scaled values are O(1); the stored
  * gradients carry the full scale.  Same kernels, workspace query
  * (va_psa_attention_bwd_workspace_bytes) and limits as the training step. */
+/* The backward of the f32 op (va_psa_attention_fwd_f32) for any loss: the
+ * reference graph's backward nodes in f32 on the FFMA kernels
+ * (psa_fa2_backward psa.rs:650-725 for the V_lo and V_hi calls, psa_*_backward
+ * psa.rs:201-327, the conv_bn backwards with BN folded) after recomputing the
+ * forward.  dy = ∂L/∂y [B,C,H,W]; grads (f32, stored) = [w_qkv (nh·4·kd × C) |
+ * w_proj (C × C) | w_pe (C × 9) | b_qkv | b_proj | b_pe], the layout of the
+ * bf16 entry's gradient buffer (the VA_PSA_GRAD_* offsets at C = 128); dx =
+ * ∂L/∂x (optional, may be NULL).  Any C = nh·2·kd; deterministic (no atomics). */
+VA_API size_t va_psa_attention_bwd_f32_workspace_bytes(int B, int C, int H, int W, int num_heads,
+                                                       int key_dim);
+VA_API int va_psa_attention_bwd_f32(const float *x, const float *dy, const float *w_qkv,
+                                    const float *b_qkv, const float *w_pe, const float *b_pe,
+                                    const float *w_proj, const float *b_proj, float *dx, float *grads,
+                                    int B, int C, int H, int W, int num_heads, int key_dim,
+                                    void *workspace, size_t ws_bytes, va_stream_t stream);
 VA_API size_t va_psa_attention_bwd_workspace_bytes(int B, int H, int W);
 VA_API int va_psa_attention_bwd_bf16(const va_bf16 *x, const va_bf16 *dy, float dy_scale,
                                      const va_bf16 *w_qkv, const float *b_qkv, const va_bf16 *w_pe,

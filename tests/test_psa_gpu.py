@@ -251,6 +251,45 @@ def test_fused_f32_vs_oracle(cuda, B, H, W):
     assert max_abs(host(y), _oracle(p)) < F32_MAX_ABS
 
 
+@pytest.mark.parametrize("B,C,nh,H,W", [(2, 128, 2, 7, 9), (1, 128, 2, 20, 20), (1, 256, 4, 8, 8)])
+def test_fused_f32_backward_vs_autograd(cuda, B, C, nh, H, W):
+    """va_psa_attention_bwd_f32 (the reference's backward node sequence in f32)
+    against f64 autograd's vector-Jacobian product of the same block for an
+    upstream gradient dy ~ N(0,1): every gradient block and dx within the f32
+    bound, 1e-5 relative to the block's largest magnitude (weight gradients
+    are sums over B·H·W tokens, up to ≈30 here)."""
+    from vision_rs_b200 import _lib
+    p = po.psa_synthetic(B, H, W, C=C, num_heads=nh, seed=5 + H)
+    dy = np.random.default_rng(H * W).standard_normal((B, C, H, W)).astype(np.float32)
+    prm = {k: p[k] for k in ("w_qkv", "b_qkv", "w_pe", "b_pe", "w_proj", "b_proj")}
+    rg, rdx = po.psa_attention_vjp_torch(p["x"], dy, prm, num_heads=nh, key_dim=32)
+    d = {k: dev(v) for k, v in prm.items()}
+    x, dyd = dev(p["x"]), dev(dy)
+    grads = torch.empty(rg.size, device="cuda")
+    dx = torch.empty_like(x)
+    need = int(_lib.lib().va_psa_attention_bwd_f32_workspace_bytes(B, C, H, W, nh, 32))
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.call("va_psa_attention_bwd_f32", x.data_ptr(), dyd.data_ptr(), d["w_qkv"].data_ptr(), d["b_qkv"].data_ptr(),
+              d["w_pe"].data_ptr(), d["b_pe"].data_ptr(), d["w_proj"].data_ptr(), d["b_proj"].data_ptr(),
+              dx.data_ptr(), grads.data_ptr(), B, C, H, W, nh, 32, ws.data_ptr(), need, st)
+    g = grads.cpu().numpy()
+    qkv_h = nh * 128
+    sizes = {"w_qkv": qkv_h * C, "w_proj": C * C, "w_pe": C * 9, "b_qkv": qkv_h, "b_proj": C, "b_pe": C}
+    off = 0
+    for k, n in sizes.items():
+        ref = rg[off:off + n]
+        assert max_abs(g[off:off + n], ref) <= F32_MAX_ABS * max(1.0, float(np.abs(ref).max())), k
+        off += n
+    assert max_abs(host(dx), rdx) <= F32_MAX_ABS
+    # deterministic: a second call gives the same bits
+    g2 = torch.empty_like(grads)
+    _lib.call("va_psa_attention_bwd_f32", x.data_ptr(), dyd.data_ptr(), d["w_qkv"].data_ptr(), d["b_qkv"].data_ptr(),
+              d["w_pe"].data_ptr(), d["b_pe"].data_ptr(), d["w_proj"].data_ptr(), d["b_proj"].data_ptr(),
+              None, g2.data_ptr(), B, C, H, W, nh, 32, ws.data_ptr(), need, st)
+    assert torch.equal(grads, g2)
+
+
 def _bf16_inputs(p):
     q = dict(p)
     for k in ("x", "w_qkv", "w_pe", "w_proj"):

@@ -73,6 +73,8 @@ SIGNATURES: dict[str, tuple] = {
     "va_c2psa_workspace_bytes": (SZ, [I, I, I, I, I]),
     "va_c2psa_fwd_bf16": (I, [P, P, P, I, P, P, P, P, I, I, I, I, P, SZ, S]),
     "va_conv_nhwc_bf16": (I, [P, P, P, P, I, I, I, I, I, I, I, I, S]),
+    "va_psa_attention_bwd_f32_workspace_bytes": (SZ, [I, I, I, I, I, I]),
+    "va_psa_attention_bwd_f32": (I, [P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, SZ, S]),
     "va_psa_attention_bwd_workspace_bytes": (SZ, [I, I, I]),
     "va_psa_attention_bwd_bf16": (I, [P, P, F, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, SZ, S]),
     "va_flash_attention2_tc_workspace_bytes": (SZ, [I, I, I]),

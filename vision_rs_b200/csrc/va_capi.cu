@@ -105,6 +105,18 @@ int va_psa_attention_fwd_f32(const float* x, const float* w_qkv, const float* b_
                                ws_bytes, (cudaStream_t)s);
 }
 
+size_t va_psa_attention_bwd_f32_workspace_bytes(int B, int C, int H, int W, int num_heads, int key_dim) {
+  return psa_bwd_f32_workspace_bytes(B, C, H, W, num_heads, key_dim);
+}
+
+int va_psa_attention_bwd_f32(const float* x, const float* dy, const float* w_qkv, const float* b_qkv,
+                             const float* w_pe, const float* b_pe, const float* w_proj, const float* b_proj,
+                             float* dx, float* grads, int B, int C, int H, int W, int num_heads, int key_dim,
+                             void* ws, size_t ws_bytes, va_stream_t s) {
+  return psa_attention_bwd_f32(x, dy, w_qkv, b_qkv, w_pe, b_pe, w_proj, b_proj, dx, grads, B, C, H, W, num_heads,
+                               key_dim, ws, ws_bytes, (cudaStream_t)s);
+}
+
 int va_psa_attention_fwd_bf16(const va_bf16* x, const va_bf16* w_qkv, const float* b_qkv, const va_bf16* w_pe,
                               const float* b_pe, const va_bf16* w_proj, const float* b_proj, va_bf16* y, int B,
                               int C, int H, int W, int num_heads, int key_dim, void* ws, size_t ws_bytes,

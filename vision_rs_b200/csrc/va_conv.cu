@@ -155,6 +155,106 @@ __global__ void __launch_bounds__(256) dwconv3x3_dw_kernel(const float* __restri
   if (threadIdx.x < 9) dw[c * 9 + threadIdx.x] = red[threadIdx.x][0];
 }
 
+// Weight gradient of the 1×1 conv (conv_bn backward, BN folded):
+// dW[o][i] = Σ_b Σ_n dY[b][o][n] · (X[b][i][n] + X2[b][i][n]).  64(o) × 64(i)
+// tiles, the (b, n) reduction in 16-token steps through shared memory, in a
+// fixed order — deterministic, no atomics.
+__global__ void __launch_bounds__(256) conv1x1_dw_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                                         const float* __restrict__ x2, float* __restrict__ dw,
+                                                         int B, int cin, int cout, int HW) {
+  __shared__ float Gs[16][64 + 4];
+  __shared__ float Xs[16][64 + 4];
+  const int o0 = blockIdx.y * 64, i0 = blockIdx.x * 64;
+  const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
+  float acc[4][4] = {};
+  for (int b = 0; b < B; ++b) {
+    const float* gb = dy + (long long)b * cout * HW;
+    const float* xb = x + (long long)b * cin * HW;
+    const float* x2b = x2 ? x2 + (long long)b * cin * HW : nullptr;
+    for (int n0 = 0; n0 < HW; n0 += 16) {
+      {  // 64 rows × 16 tokens of dY and of X, one float4-sized strip per thread each
+        const int r = tid / 4, n = (tid % 4) * 4;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int nn = n0 + n + u, oo = o0 + r, ii = i0 + r;
+          Gs[n + u][r] = (oo < cout && nn < HW) ? gb[(long long)oo * HW + nn] : 0.f;
+          float xv = 0.f;
+          if (ii < cin && nn < HW) {
+            xv = xb[(long long)ii * HW + nn];
+            if (x2b) xv += x2b[(long long)ii * HW + nn];
+          }
+          Xs[n + u][r] = xv;
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk) {
+        float a[4], bv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) { a[u] = Gs[kk][ty * 4 + u]; bv[u] = Xs[kk][tx * 4 + u]; }
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[r][c] = fmaf(a[r], bv[c], acc[r][c]);
+      }
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int o = o0 + ty * 4 + r;
+    if (o >= cout) continue;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int i = i0 + tx * 4 + c;
+      if (i < cin) dw[(long long)o * cin + i] = acc[r][c];
+    }
+  }
+}
+
+// db[o] = Σ_b Σ_n dY[b][o][n]: one warp per channel, lanes stride the tokens,
+// then a fixed shuffle tree (deterministic).
+__global__ void __launch_bounds__(256) channel_sum_kernel(const float* __restrict__ dy, float* __restrict__ db, int B,
+                                                          int C, int HW) {
+  const int o = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (o >= C) return;
+  float s = 0.f;
+  for (int b = 0; b < B; ++b) {
+    const float* g = dy + ((long long)b * C + o) * HW;
+    for (int n = lane; n < HW; n += 32) s += g[n];
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) db[o] = s;
+}
+
+// wt[i][o] = w[o][i]
+__global__ void transpose_kernel(const float* __restrict__ w, float* __restrict__ wt, int rows, int cols) {
+  const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (t >= (long long)rows * cols) return;
+  const int r = (int)(t / cols), c = (int)(t % cols);
+  wt[(long long)c * rows + r] = w[t];
+}
+
+int conv1x1_dw_f32(const float* dy, const float* x, const float* x2, float* dw, int B, int cin, int cout, int HW,
+                   cudaStream_t st) {
+  VA_CHECK_ARG(B > 0 && cin > 0 && cout > 0 && HW > 0, "conv1x1 backward: bad sizes");
+  conv1x1_dw_kernel<<<dim3(ceil_div(cin, 64), ceil_div(cout, 64)), 256, 0, st>>>(dy, x, x2, dw, B, cin, cout, HW);
+  return check_launch("conv1x1 dw");
+}
+
+int channel_sum_f32(const float* dy, float* db, int B, int C, int HW, cudaStream_t st) {
+  VA_CHECK_ARG(B > 0 && C > 0 && HW > 0, "channel sum: bad sizes");
+  channel_sum_kernel<<<ceil_div(C, 8), 256, 0, st>>>(dy, db, B, C, HW);
+  return check_launch("channel sum");
+}
+
+int transpose_f32(const float* w, float* wt, int rows, int cols, cudaStream_t st) {
+  const long long n = (long long)rows * cols;
+  transpose_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, wt, rows, cols);
+  return check_launch("transpose");
+}
+
 template <typename T, typename TW>
 int conv1x1(const T* x, const T* x2, const TW* w, const float* bias, T* y, int B, int cin, int cout, int HW,
             cudaStream_t st) {

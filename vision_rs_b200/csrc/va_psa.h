@@ -8,6 +8,11 @@
 namespace va {
 
 size_t psa_workspace_bytes(int B, int C, int H, int W, int nh, int kd, int dtype);
+size_t psa_bwd_f32_workspace_bytes(int B, int C, int H, int W, int nh, int kd);
+int psa_attention_bwd_f32(const float* x, const float* dy, const float* w_qkv, const float* b_qkv,
+                          const float* w_pe, const float* b_pe, const float* w_proj, const float* b_proj, float* dx,
+                          float* grads, int B, int C, int H, int W, int nh, int kd, void* ws, size_t ws_bytes,
+                          cudaStream_t st);
 
 int psa_attention_fwd_f32(const float* x, const float* w_qkv, const float* b_qkv, const float* w_pe,
                           const float* b_pe, const float* w_proj, const float* b_proj, float* y, int B, int C,
@@ -28,6 +33,12 @@ int conv1x1(const T* x, const T* x2, const TW* w, const float* bias, T* y, int B
             cudaStream_t st);
 template <typename T, typename TW>
 int dwconv3x3(const T* x, const TW* w, const float* bias, T* y, int B, int C, int H, int W, cudaStream_t st);
+// f32 1×1-conv backward pieces (va_conv.cu): dW = Σ dY·(X + X2)ᵀ, db = Σ dY
+// (both stored, fixed-order reductions), and a weight transpose.
+int conv1x1_dw_f32(const float* dy, const float* x, const float* x2, float* dw, int B, int cin, int cout, int HW,
+                   cudaStream_t st);
+int channel_sum_f32(const float* dy, float* db, int B, int C, int HW, cudaStream_t st);
+int transpose_f32(const float* w, float* wt, int rows, int cols, cudaStream_t st);
 
 // Workspace of the tensor-core forward (bf16): the specialised C = 128 path
 // or, for other widths C = 64·nh, the general one (va_tc_psa_wide.cu).
