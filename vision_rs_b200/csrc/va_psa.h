@@ -107,8 +107,9 @@ int conv_status_clear(cudaStream_t st);
 bool psa_tc_supported(int C, int nh, int kd);
 inline bool psa_tc_is_n(int C, int nh, int kd) { return C == 128 && nh == 2 && kd == 32; }
 // Per-device side streams of the library (highest / lowest stream priority),
-// created by the first call on a device; psa_stream_dep(from, to) makes `to`
-// wait for the work issued on `from` so far (an event per call).
+// created by the first call on a device (*out = nullptr, run serially, on a
+// device index ≥ 64); psa_stream_dep(from, to) makes `to` wait for the work
+// issued on `from` so far (an event per call).
 struct SideStreams {
   cudaStream_t hi = nullptr, lo = nullptr;
 };

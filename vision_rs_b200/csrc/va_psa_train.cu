@@ -533,8 +533,10 @@ int psa_train_fwd_bwd(const __nv_bfloat16* x, const __nv_bfloat16* target, const
   SideStreams* side = nullptr;
   if (overlap) {
     if (int rc = psa_side_streams(&side)) return rc;
-    if (int rc = psa_stream_dep(st, side->hi)) return rc;
-    if (int rc = psa_stream_dep(st, side->lo)) return rc;
+    if (side) {
+      if (int rc = psa_stream_dep(st, side->hi)) return rc;
+      if (int rc = psa_stream_dep(st, side->lo)) return rc;
+    }
   }
   SideJoin joiner{side, st};
   const cudaStream_t cs = side ? side->hi : st, ss = side ? side->lo : st;

@@ -350,19 +350,20 @@ template <int KD, int OUT>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 attn_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v,
             void* __restrict__ obuf, float* __restrict__ lse, int N, int Np, int nh, float scale_log2,
-            int odd_last) {
+            int linear_bh) {
   static_assert(KD == 32 || KD == 64, "key dim 32 or 64");
   constexpr int kQK = AttnSmem<KD>::kQK;
   extern __shared__ uint8_t smem_raw[];
   AttnSmem<KD>& sm =
       *reinterpret_cast<AttnSmem<KD>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // odd_last (a 1-D grid, odd_last = BH): the two-tile items of every (b, h) first, the
-  // one-tile items of an odd tile count last, so the grid's last wave holds the short ones
+  // linear_bh = 0: grid (tile pair, b·h).  linear_bh = BH: a 1-D grid holding the two-tile
+  // items of every (b, h) first and the one-tile items of an odd tile count last, so the
+  // grid's last wave holds the short ones
   int pair = blockIdx.x, bh = blockIdx.y, BH = gridDim.y;
-  if (odd_last) {
+  if (linear_bh) {
     const int nfull = ((N + kTile - 1) / kTile) / 2;
-    BH = odd_last;
+    BH = linear_bh;
     if ((int)blockIdx.x < nfull * BH) {
       pair = blockIdx.x % nfull;
       bh = blockIdx.x / nfull;
@@ -1605,7 +1606,12 @@ PerDeviceOnce g_side_once;
 
 int psa_side_streams(SideStreams** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VA_ERR_UNSUPPORTED;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(VA_ERR_LAUNCH, "psa: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) {  // no side streams kept for such devices: the caller runs serially
+    *out = nullptr;
+    return VA_OK;
+  }
   const int rc = g_side_once.run([dev]() -> int {
     int lo = 0, hi = 0;
     if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
@@ -1736,8 +1742,10 @@ int psa_attention_fwd_tc(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv, con
   SideStreams* side = nullptr;
   if (overlap_pe) {
     if (int rc = psa_side_streams(&side)) return rc;
-    if (int rc = psa_stream_dep(st, side->hi)) return rc;
-    if (int rc = psa_stream_dep(st, side->lo)) return rc;
+    if (side) {
+      if (int rc = psa_stream_dep(st, side->hi)) return rc;
+      if (int rc = psa_stream_dep(st, side->lo)) return rc;
+    }
   }
   SideJoin joiner{side, st};
   const cudaStream_t sa = side ? side->hi : st, sp = side ? side->lo : st;
