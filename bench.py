@@ -1086,7 +1086,14 @@ def run_ours(args, ws, rank, local):
     side = {}
     if args.config == "cfg2" and args.width == "n" and not args.batch and args.side_configs:
         for name, ov in SIDE_CONFIGS:
-            side[name] = measure_side(name, ov, args, ws, rank, dev, flush, barrier)
+            if ws > 1:  # every rank takes the same collective steps: a failure must end the run on all of them
+                side[name] = measure_side(name, ov, args, ws, rank, dev, flush, barrier)
+                continue
+            try:  # one process: a failing side configuration must not cost the headline line
+                side[name] = measure_side(name, ov, args, ws, rank, dev, flush, barrier)
+            except Exception as e:  # noqa: BLE001 — reported in the line, not hidden
+                torch.cuda.synchronize()
+                side[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(cls, args)
