@@ -1092,7 +1092,6 @@ def run_ours(args, ws, rank, local):
             try:  # one process: a failing side configuration must not cost the headline line
                 side[name] = measure_side(name, ov, args, ws, rank, dev, flush, barrier)
             except Exception as e:  # noqa: BLE001 — reported in the line, not hidden
-                torch.cuda.synchronize()
                 side[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
