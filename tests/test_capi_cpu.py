@@ -113,6 +113,14 @@ def test_argument_validation_fails_before_launch():
     assert conv(1024, 1, 0, 8, 16, 16, 3, 1) == 1
     assert conv(None, 1, 8, 8, 16, 16, 3, 1) == 1
     assert conv(1026, 1, 8, 8, 16, 16, 3, 1) == 4 and b"alignment" in lib.va_get_last_error_string()
+    # f32 fused backward: null pointers, the width rule and the workspace are checked before any launch
+    bwd = lambda x, C, nh, ws, n: lib.va_psa_attention_bwd_f32(x, 64, 128, 192, 256, 320, 384, 448, None, 512, 2,
+                                                                C, 4, 4, nh, 32, ws, n, None)
+    assert bwd(None, 128, 2, 4096, 1 << 20) == 1 and b"null" in lib.va_get_last_error_string()
+    assert bwd(1024, 100, 2, 4096, 1 << 20) == 1 and b"num_heads" in lib.va_get_last_error_string()
+    assert bwd(1024, 128, 2, None, 0) == 6 and b"workspace" in lib.va_get_last_error_string()
+    need = lib.va_psa_attention_bwd_f32_workspace_bytes(2, 128, 4, 4, 2, 32)
+    assert bwd(1024, 128, 2, 4096, need - 1) == 6
 
 
 def test_workspace_query():
@@ -121,3 +129,6 @@ def test_workspace_query():
     n16 = lib.va_psa_attention_workspace_bytes(2, 128, 20, 20, 2, 32, 1)
     assert n32 > 0 and n16 > 0 and n16 < n32
     assert lib.va_psa_attention_workspace_bytes(0, 128, 20, 20, 2, 32, 0) == 0
+    # the f32 backward holds the forward's intermediates plus its own gradient buffers
+    nb = lib.va_psa_attention_bwd_f32_workspace_bytes(2, 128, 20, 20, 2, 32)
+    assert nb > n32 and lib.va_psa_attention_bwd_f32_workspace_bytes(2, 128, 0, 20, 2, 32) == 0
